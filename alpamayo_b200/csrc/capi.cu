@@ -1,0 +1,175 @@
+// capi.cu — the extern "C" entry points declared in include/paro_b200.h.
+//
+// Each entry point validates its arguments on the host (status codes instead
+// of exceptions; the torch shim turns a non-zero status into a RuntimeError,
+// mirroring the reference's TORCH_CHECKs in rotation.cu:117-124,456-493),
+// then launches asynchronously on the caller's stream.  Nothing here
+// allocates device memory or synchronises.
+#include <cstring>
+#include <string>
+
+#include "paro_common.cuh"
+
+namespace paro {
+cudaError_t launch_rotate(int x_dtype, int krot, int group, const void* x, int64_t M, int K, const void* scales,
+                          const void* theta, int pdt, const int16_t* pairs, void* out, cudaStream_t st);
+cudaError_t launch_rotq(int x_dtype, const void* x, int64_t M, int K, const uint16_t* scales, const uint16_t* theta,
+                        const uint8_t* pairs, int fp16_round, int8_t* q, float* s, cudaStream_t st);
+int rotq_max_k();
+cudaError_t launch_quant(int x_dtype, const void* x, int64_t M, int K, int8_t* q, float* s, cudaStream_t st);
+cudaError_t launch_prepare_rotation(const int16_t* pairs, int krot, int K, int group, uint8_t* out, int32_t* bad,
+                                    cudaStream_t st);
+cudaError_t launch_prepare_wq(const int16_t* qweight, const uint16_t* scales, const uint16_t* scaled_zeros, int N,
+                              int K, void* packed, cudaStream_t st);
+cudaError_t launch_prepare_awq(const int32_t* qweight, const uint16_t* scales, const int32_t* qzeros, int N, int K,
+                               void* packed, cudaStream_t st);
+cudaError_t launch_gemm_decode(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
+                               const void* bias, int bias_dtype, void* out, int out_dtype, cudaStream_t st);
+int gemm_tc_supported(int64_t M, int N, int K);
+size_t gemm_tc_workspace(int64_t M, int N, int K);
+cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
+                           const void* bias, int bias_dtype, void* out, int out_dtype, void* ws, size_t ws_bytes,
+                           cudaStream_t st);
+}  // namespace paro
+
+using namespace paro;
+
+namespace {
+thread_local std::string g_last_cuda_error;
+
+int cuda_status(cudaError_t e) {
+  if (e == cudaSuccess) return PARO_OK;
+  g_last_cuda_error = cudaGetErrorString(e);
+  return PARO_ERR_CUDA;
+}
+
+bool valid_dtype(int d) { return d == PARO_F32 || d == PARO_F16 || d == PARO_BF16; }
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int device_check() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return PARO_ERR_DEVICE;
+  int major = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return PARO_ERR_DEVICE;
+  return major == 10 ? PARO_OK : PARO_ERR_DEVICE;
+}
+}  // namespace
+
+extern "C" {
+
+const char* paro_status_string(int s) {
+  switch (s) {
+    case PARO_OK: return "ok";
+    case PARO_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case PARO_ERR_SHAPE: return "unsupported shape";
+    case PARO_ERR_UNSUPPORTED: return "unsupported configuration";
+    case PARO_ERR_MISALIGNED: return "misaligned pointer";
+    case PARO_ERR_CUDA: return "CUDA error";
+    case PARO_ERR_WORKSPACE: return "workspace too small";
+    case PARO_ERR_DEVICE: return "current device is not an sm_100 GPU";
+    case PARO_ERR_TOO_LARGE: return "size beyond compiled limit";
+  }
+  return "unknown status";
+}
+
+int paro_version(void) { return 100; }
+
+const char* paro_last_cuda_error(void) { return g_last_cuda_error.c_str(); }
+
+int paro_prepare_rotation(const int16_t* pairs, int krot, int K, int group, uint8_t* out_u8, int32_t* bad,
+                          paro_stream_t stream) {
+  if (!pairs || !out_u8 || !bad || krot <= 0 || K <= 0) return PARO_ERR_INVALID_ARGUMENT;
+  if (group != 64 && group != 128) return PARO_ERR_UNSUPPORTED;
+  if (K % group) return PARO_ERR_SHAPE;
+  if (int d = device_check()) return d;
+  return cuda_status(launch_prepare_rotation(pairs, krot, K, group, out_u8, bad, (cudaStream_t)stream));
+}
+
+int paro_rotate(const void* x, int x_dtype, int64_t M, int K, const void* scales, const void* theta,
+                int param_dtype, const int16_t* pairs, int krot, int group, void* out, paro_stream_t stream) {
+  if (!x || !theta || !pairs || !out || K <= 0 || M < 0) return PARO_ERR_INVALID_ARGUMENT;
+  if (!valid_dtype(x_dtype) || !valid_dtype(param_dtype)) return PARO_ERR_UNSUPPORTED;
+  if (group != 64 && group != 128) return PARO_ERR_UNSUPPORTED;
+  if (krot != 1 && krot != 2 && krot != 4 && krot != 8 && krot != 16) return PARO_ERR_UNSUPPORTED;
+  if (K % group) return PARO_ERR_SHAPE;
+  if (!aligned(pairs, 4)) return PARO_ERR_MISALIGNED;
+  if (M == 0) return PARO_OK;
+  if (int d = device_check()) return d;
+  return cuda_status(
+      launch_rotate(x_dtype, krot, group, x, M, K, scales, theta, param_dtype, pairs, out, (cudaStream_t)stream));
+}
+
+int paro_rotq_int8(const void* x, int x_dtype, int64_t M, int K, const uint16_t* scales, const uint16_t* theta,
+                   const uint8_t* pairs_u8, int krot, int group, int fp16_round, int8_t* out_q, float* out_scale,
+                   paro_stream_t stream) {
+  if (!x || !theta || !pairs_u8 || !out_q || !out_scale || K <= 0 || M < 0) return PARO_ERR_INVALID_ARGUMENT;
+  if (!valid_dtype(x_dtype)) return PARO_ERR_UNSUPPORTED;
+  if (krot != 8 || group != 128) return PARO_ERR_UNSUPPORTED;  // Rotation supports only these (rotation_linear.py:18-19)
+  if (K % group) return PARO_ERR_SHAPE;
+  if (K > rotq_max_k()) return PARO_ERR_TOO_LARGE;
+  if (!aligned(out_q, 16)) return PARO_ERR_MISALIGNED;
+  if (M == 0) return PARO_OK;
+  if (int d = device_check()) return d;
+  return cuda_status(
+      launch_rotq(x_dtype, x, M, K, scales, theta, pairs_u8, fp16_round ? 1 : 0, out_q, out_scale, (cudaStream_t)stream));
+}
+
+int paro_quant_int8(const void* x, int x_dtype, int64_t M, int K, int8_t* out_q, float* out_scale,
+                    paro_stream_t stream) {
+  if (!x || !out_q || !out_scale || K <= 0 || M < 0) return PARO_ERR_INVALID_ARGUMENT;
+  if (!valid_dtype(x_dtype)) return PARO_ERR_UNSUPPORTED;
+  if (M == 0) return PARO_OK;
+  if (int d = device_check()) return d;
+  return cuda_status(launch_quant(x_dtype, x, M, K, out_q, out_scale, (cudaStream_t)stream));
+}
+
+size_t paro_packed_weight_bytes(int N, int K) {
+  if (N <= 0 || K <= 0 || N % kRecRows || K % kGroup) return 0;
+  return (size_t)(N / kRecRows) * (K / kGroup) * kRecBytes;
+}
+
+int paro_prepare_weights(const int16_t* qweight, const uint16_t* scales, const uint16_t* scaled_zeros, int N, int K,
+                         int G_pad, void* packed, paro_stream_t stream) {
+  if (!qweight || !scales || !scaled_zeros || !packed || N <= 0 || K <= 0) return PARO_ERR_INVALID_ARGUMENT;
+  if (N % kRecRows || K % kGroup || G_pad < K / kGroup) return PARO_ERR_SHAPE;
+  if (!aligned(packed, 16)) return PARO_ERR_MISALIGNED;
+  if (int d = device_check()) return d;
+  return cuda_status(launch_prepare_wq(qweight, scales, scaled_zeros, N, K, packed, (cudaStream_t)stream));
+}
+
+int paro_prepare_weights_awq(const int32_t* awq_qweight, const uint16_t* awq_scales, const int32_t* awq_qzeros, int N,
+                             int K, void* packed, paro_stream_t stream) {
+  if (!awq_qweight || !awq_scales || !awq_qzeros || !packed || N <= 0 || K <= 0) return PARO_ERR_INVALID_ARGUMENT;
+  if (N % kRecRows || K % kGroup) return PARO_ERR_SHAPE;
+  if (!aligned(packed, 16)) return PARO_ERR_MISALIGNED;
+  if (int d = device_check()) return d;
+  return cuda_status(launch_prepare_awq(awq_qweight, awq_scales, awq_qzeros, N, K, packed, (cudaStream_t)stream));
+}
+
+int paro_w4a8_gemm_path(int64_t M, int N, int K) { return gemm_tc_supported(M, N, K) ? 1 : 0; }
+
+size_t paro_w4a8_gemm_workspace_size(int64_t M, int N, int K) {
+  return gemm_tc_supported(M, N, K) ? gemm_tc_workspace(M, N, K) : 0;
+}
+
+int paro_w4a8_gemm(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
+                   const void* bias, int bias_dtype, void* out, int out_dtype, void* workspace, size_t workspace_bytes,
+                   paro_stream_t stream) {
+  if (!xq || !xscale || !packed || !out || M < 0 || N <= 0 || K <= 0) return PARO_ERR_INVALID_ARGUMENT;
+  if (!valid_dtype(out_dtype) || (bias && !valid_dtype(bias_dtype))) return PARO_ERR_UNSUPPORTED;
+  if (N % kRecRows || K % kGroup) return PARO_ERR_SHAPE;
+  if (!aligned(packed, 16) || !aligned(xq, 16)) return PARO_ERR_MISALIGNED;
+  if (M == 0) return PARO_OK;
+  if (int d = device_check()) return d;
+  if (gemm_tc_supported(M, N, K)) {
+    if (workspace_bytes < gemm_tc_workspace(M, N, K) || (gemm_tc_workspace(M, N, K) && !workspace))
+      return PARO_ERR_WORKSPACE;
+    return cuda_status(launch_gemm_tc(xq, xscale, M, N, K, packed, bias, bias_dtype, out, out_dtype, workspace,
+                                      workspace_bytes, (cudaStream_t)stream));
+  }
+  return cuda_status(
+      launch_gemm_decode(xq, xscale, M, N, K, packed, bias, bias_dtype, out, out_dtype, (cudaStream_t)stream));
+}
+
+}  // extern "C"

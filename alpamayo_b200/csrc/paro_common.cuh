@@ -1,0 +1,83 @@
+// paro_common.cuh — shared definitions for the sm_100a ParoQuant W4A8 kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/paro_b200.h"
+
+namespace paro {
+
+constexpr int kGroup = 128;          // int4 quantisation group (K channels)
+constexpr int kRecRows = 16;         // output rows per tile record
+constexpr int kRecCodeBytes = kRecRows * 64;              // 16 rows x 128 nibbles
+constexpr int kRecScaleOff = kRecCodeBytes;               // 16 x fp16 scales
+constexpr int kRecZeroOff = kRecCodeBytes + kRecRows * 2; // 16 x uint8 zero points
+constexpr int kRecBytes = kRecZeroOff + kRecRows;         // 1072 (= 67 x 16)
+
+static_assert(kRecBytes % 16 == 0, "records must stay 16-byte aligned");
+
+// Byte offset of record (row block nb, group g) for a layer with G groups.
+__host__ __device__ __forceinline__ size_t rec_offset(int nb, int g, int G) {
+  return ((size_t)nb * G + g) * kRecBytes;
+}
+
+// Position of code k (0..127 within a group) inside a row's 64 bytes:
+// word index t*4 + j, byte b, nibble h, where k = 32j + 16h + 4t + b.
+__host__ __device__ __forceinline__ int code_byte_pos(int k) {
+  const int j = k >> 5, t = (k >> 2) & 3, b = k & 3;
+  return t * 16 + j * 4 + b;
+}
+__host__ __device__ __forceinline__ int code_nibble(int k) { return (k >> 4) & 1; }
+
+// ---------------------------------------------------------------------------
+// dtype helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float to_f32(float v) { return v; }
+__device__ __forceinline__ float to_f32(__half v) { return __half2float(v); }
+__device__ __forceinline__ float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T> __device__ __forceinline__ T from_f32(float v);
+template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+__device__ __forceinline__ float half_bits_to_f32(uint16_t b) {
+  return __half2float(__ushort_as_half(b));
+}
+
+// Round a float32 to the nearest fp16 value (ties to even) and back.
+__device__ __forceinline__ float round_fp16(float v) {
+  return __half2float(__float2half_rn(v));
+}
+
+// Round half away from zero (libdevice round semantics used by the
+// reference's Triton quantiser); calls the CUDA math library's roundf.
+__device__ __forceinline__ float round_half_away(float v) { return roundf(v); }
+
+// ---------------------------------------------------------------------------
+// small PTX wrappers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ int4 ldg_nc_v4(const void* p) {
+  int4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t ldg_nc_u32(const void* p) {
+  uint32_t r;
+  asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(r) : "l"(p));
+  return r;
+}
+
+}  // namespace paro

@@ -1,0 +1,244 @@
+// torch_ops.cpp — thin TORCH_LIBRARY shim over the C ABI in include/paro_b200.h.
+//
+// Registers the ``paro_b200`` operator namespace (CUDA dispatch key only, like
+// the reference's ``rotation`` namespace, kernels/paroquant_kernels/src/
+// rotation.cu:576-584).  Ops allocate their outputs with the caching
+// allocator, launch on the current stream and never synchronise, so they are
+// CUDA-graph capturable; the Python package registers fake (meta) kernels so
+// torch.compile(fullgraph=True) can trace them.  A non-zero paro_status
+// becomes a RuntimeError, as the reference's TORCH_CHECKs do.
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/library.h>
+
+#include "../../include/paro_b200.h"
+
+namespace {
+
+int to_paro_dtype(at::ScalarType t) {
+  switch (t) {
+    case at::kFloat: return PARO_F32;
+    case at::kHalf: return PARO_F16;
+    case at::kBFloat16: return PARO_BF16;
+    default: TORCH_CHECK(false, "paro_b200: unsupported dtype ", t, " (Float, Half, BFloat16)");
+  }
+  return -1;
+}
+
+void check_status(int s, const char* what) {
+  TORCH_CHECK(s == PARO_OK, "paro_b200::", what, " failed: ", paro_status_string(s),
+              (s == PARO_ERR_CUDA ? std::string(" (") + paro_last_cuda_error() + ")" : std::string()));
+}
+
+paro_stream_t cur_stream() { return reinterpret_cast<paro_stream_t>(at::cuda::getCurrentCUDAStream().stream()); }
+
+void check_cuda(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), "paro_b200: ", name, " must be a CUDA tensor");
+  TORCH_CHECK(t.is_contiguous(), "paro_b200: ", name, " must be contiguous");
+}
+
+// rotation::rotate(Tensor x, Tensor idx_ij, Tensor theta, Tensor? scales, int group_size) -> Tensor
+at::Tensor rotate(const at::Tensor& x_in, const at::Tensor& idx_ij, const at::Tensor& theta,
+                  const c10::optional<at::Tensor>& scales_opt, int64_t group_size) {
+  at::Tensor x = x_in.contiguous();
+  check_cuda(x, "x");
+  check_cuda(idx_ij, "idx_ij");
+  check_cuda(theta, "theta");
+  TORCH_CHECK(idx_ij.scalar_type() == at::kShort, "idx_ij must be int16");
+  TORCH_CHECK(theta.size(0) == idx_ij.size(0), "theta.size(0) must equal idx_ij.size(0)");
+  const int64_t K = x.size(-1);
+  TORCH_CHECK(K % group_size == 0, "h must be divisible by GROUP_SIZE");
+  const void* sp = nullptr;
+  at::Tensor sc;
+  if (scales_opt.has_value() && scales_opt->defined() && scales_opt->numel() > 0) {
+    sc = scales_opt->to(theta.scalar_type()).contiguous();
+    check_cuda(sc, "scales");
+    sp = sc.data_ptr();
+  }
+  c10::cuda::CUDAGuard guard(x.device());
+  at::Tensor out = at::empty_like(x);
+  const int64_t M = x.numel() / K;
+  check_status(paro_rotate(x.data_ptr(), to_paro_dtype(x.scalar_type()), M, (int)K, sp, theta.data_ptr(),
+                           to_paro_dtype(theta.scalar_type()), idx_ij.data_ptr<int16_t>(), (int)idx_ij.size(0),
+                           (int)group_size, out.data_ptr(), cur_stream()),
+               "rotate");
+  return out;
+}
+
+// Validates and narrows the pair table (synchronises once to read the
+// validation count: load-time only).
+at::Tensor prepare_rotation(const at::Tensor& pairs, int64_t group_size) {
+  check_cuda(pairs, "pairs");
+  TORCH_CHECK(pairs.scalar_type() == at::kShort, "pairs must be int16");
+  c10::cuda::CUDAGuard guard(pairs.device());
+  at::Tensor out = at::empty(pairs.sizes(), pairs.options().dtype(at::kByte));
+  at::Tensor bad = at::empty({1}, pairs.options().dtype(at::kInt));
+  check_status(paro_prepare_rotation(pairs.data_ptr<int16_t>(), (int)pairs.size(0), (int)pairs.size(1),
+                                     (int)group_size, out.data_ptr<uint8_t>(), bad.data_ptr<int32_t>(), cur_stream()),
+               "prepare_rotation");
+  const int nbad = bad.item<int32_t>();
+  TORCH_CHECK(nbad == 0, "paro_b200::prepare_rotation: ", nbad,
+              " (layer, group) blocks of rotation.pairs are not permutations of 0..", group_size - 1,
+              " (Givens pairs of one layer must be disjoint)");
+  return out;
+}
+
+std::tuple<at::Tensor, at::Tensor> rotq_int8(const at::Tensor& x_in, const at::Tensor& pairs_u8,
+                                             const at::Tensor& theta, const c10::optional<at::Tensor>& scales_opt,
+                                             int64_t group_size, bool fp16_round) {
+  at::Tensor x = x_in.contiguous();
+  check_cuda(x, "x");
+  check_cuda(pairs_u8, "pairs_u8");
+  check_cuda(theta, "theta");
+  TORCH_CHECK(pairs_u8.scalar_type() == at::kByte, "pairs_u8 must be uint8 (from prepare_rotation)");
+  TORCH_CHECK(theta.scalar_type() == at::kHalf, "theta must be float16");
+  const int64_t K = x.size(-1);
+  const uint16_t* sp = nullptr;
+  at::Tensor sc;
+  if (scales_opt.has_value() && scales_opt->defined() && scales_opt->numel() > 0) {
+    sc = scales_opt->to(at::kHalf).contiguous();
+    check_cuda(sc, "scales");
+    sp = reinterpret_cast<const uint16_t*>(sc.data_ptr());
+  }
+  c10::cuda::CUDAGuard guard(x.device());
+  const int64_t M = x.numel() / K;
+  at::Tensor q = at::empty(x.sizes(), x.options().dtype(at::kChar));
+  auto ssz = x.sizes().vec();
+  ssz.back() = 1;
+  at::Tensor s = at::empty(ssz, x.options().dtype(at::kFloat));
+  check_status(paro_rotq_int8(x.data_ptr(), to_paro_dtype(x.scalar_type()), M, (int)K, sp,
+                              reinterpret_cast<const uint16_t*>(theta.data_ptr()), pairs_u8.data_ptr<uint8_t>(),
+                              (int)pairs_u8.size(0), (int)group_size, fp16_round ? 1 : 0, q.data_ptr<int8_t>(),
+                              s.data_ptr<float>(), cur_stream()),
+               "rotq_int8");
+  return {q, s};
+}
+
+// per_token_quant_int8 (vllm int8_utils.py:131-156): returns (int8 codes, float32 scales [..., 1])
+std::tuple<at::Tensor, at::Tensor> quant_int8(const at::Tensor& x_in) {
+  at::Tensor x = x_in.contiguous();
+  check_cuda(x, "x");
+  const int64_t K = x.size(-1);
+  const int64_t M = x.numel() / K;
+  c10::cuda::CUDAGuard guard(x.device());
+  at::Tensor q = at::empty(x.sizes(), x.options().dtype(at::kChar));
+  auto ssz = x.sizes().vec();
+  ssz.back() = 1;
+  at::Tensor s = at::empty(ssz, x.options().dtype(at::kFloat));
+  check_status(paro_quant_int8(x.data_ptr(), to_paro_dtype(x.scalar_type()), M, (int)K, q.data_ptr<int8_t>(),
+                               s.data_ptr<float>(), cur_stream()),
+               "quant_int8");
+  return {q, s};
+}
+
+at::Tensor prepare_weights(const at::Tensor& qweight, const at::Tensor& scales, const at::Tensor& scaled_zeros,
+                           int64_t N, int64_t K) {
+  check_cuda(qweight, "qweight");
+  check_cuda(scales, "scales");
+  check_cuda(scaled_zeros, "scaled_zeros");
+  TORCH_CHECK(qweight.scalar_type() == at::kShort, "qweight must be int16 (WQLinear layout)");
+  TORCH_CHECK(scales.scalar_type() == at::kHalf && scaled_zeros.scalar_type() == at::kHalf,
+              "scales / scaled_zeros must be float16");
+  TORCH_CHECK(qweight.size(0) * 4 == N && qweight.size(1) == K, "qweight must be [N/4, K]");
+  TORCH_CHECK(scales.size(1) == N && scaled_zeros.sizes() == scales.sizes(), "scales must be [G_pad, N]");
+  c10::cuda::CUDAGuard guard(qweight.device());
+  const size_t bytes = paro_packed_weight_bytes((int)N, (int)K);
+  TORCH_CHECK(bytes > 0, "paro_b200::prepare_weights: N must be a multiple of 16 and K of 128");
+  at::Tensor packed = at::empty({(int64_t)bytes}, qweight.options().dtype(at::kByte));
+  check_status(paro_prepare_weights(qweight.data_ptr<int16_t>(), reinterpret_cast<const uint16_t*>(scales.data_ptr()),
+                                    reinterpret_cast<const uint16_t*>(scaled_zeros.data_ptr()), (int)N, (int)K,
+                                    (int)scales.size(0), packed.data_ptr(), cur_stream()),
+               "prepare_weights");
+  return packed;
+}
+
+at::Tensor prepare_weights_awq(const at::Tensor& qweight, const at::Tensor& scales, const at::Tensor& qzeros,
+                               int64_t N, int64_t K) {
+  check_cuda(qweight, "qweight");
+  check_cuda(scales, "scales");
+  check_cuda(qzeros, "qzeros");
+  TORCH_CHECK(qweight.scalar_type() == at::kInt && qzeros.scalar_type() == at::kInt, "AWQ buffers must be int32");
+  TORCH_CHECK(scales.scalar_type() == at::kHalf, "scales must be float16");
+  TORCH_CHECK(qweight.size(0) == K && qweight.size(1) * 8 == N, "qweight must be [K, N/8]");
+  c10::cuda::CUDAGuard guard(qweight.device());
+  const size_t bytes = paro_packed_weight_bytes((int)N, (int)K);
+  TORCH_CHECK(bytes > 0, "paro_b200::prepare_weights_awq: N must be a multiple of 16 and K of 128");
+  at::Tensor packed = at::empty({(int64_t)bytes}, qweight.options().dtype(at::kByte));
+  check_status(paro_prepare_weights_awq(qweight.data_ptr<int32_t>(),
+                                        reinterpret_cast<const uint16_t*>(scales.data_ptr()),
+                                        qzeros.data_ptr<int32_t>(), (int)N, (int)K, packed.data_ptr(), cur_stream()),
+               "prepare_weights_awq");
+  return packed;
+}
+
+at::Tensor w4a8_gemm(const at::Tensor& xq_in, const at::Tensor& xscale_in, const at::Tensor& packed, int64_t N,
+                     const c10::optional<at::Tensor>& bias_opt, at::ScalarType out_dtype) {
+  at::Tensor xq = xq_in.contiguous();
+  at::Tensor xscale = xscale_in.contiguous();
+  check_cuda(xq, "xq");
+  check_cuda(xscale, "xscale");
+  check_cuda(packed, "packed");
+  TORCH_CHECK(xq.scalar_type() == at::kChar, "xq must be int8");
+  TORCH_CHECK(xscale.scalar_type() == at::kFloat, "xscale must be float32");
+  const int64_t K = xq.size(-1);
+  const int64_t M = xq.numel() / K;
+  TORCH_CHECK(xscale.numel() == M, "xscale must hold one scale per token");
+  TORCH_CHECK((size_t)packed.numel() == paro_packed_weight_bytes((int)N, (int)K), "packed weight size mismatch");
+  const void* bp = nullptr;
+  int bdt = PARO_F32;
+  at::Tensor bias;
+  if (bias_opt.has_value() && bias_opt->defined()) {
+    bias = bias_opt->contiguous();
+    check_cuda(bias, "bias");
+    TORCH_CHECK(bias.numel() == N, "bias must have N elements");
+    bp = bias.data_ptr();
+    bdt = to_paro_dtype(bias.scalar_type());
+  }
+  c10::cuda::CUDAGuard guard(xq.device());
+  auto osz = xq.sizes().vec();
+  osz.back() = N;
+  at::Tensor out = at::empty(osz, xq.options().dtype(out_dtype));
+  const size_t ws = paro_w4a8_gemm_workspace_size(M, (int)N, (int)K);
+  at::Tensor wst;
+  if (ws) wst = at::empty({(int64_t)ws}, xq.options().dtype(at::kByte));
+  check_status(paro_w4a8_gemm(xq.data_ptr<int8_t>(), xscale.data_ptr<float>(), M, (int)N, (int)K, packed.data_ptr(),
+                              bp, bdt, out.data_ptr(), to_paro_dtype(out_dtype), ws ? wst.data_ptr() : nullptr, ws,
+                              cur_stream()),
+               "w4a8_gemm");
+  return out;
+}
+
+// One W4A8 rotated linear: fused activation kernel + GEMM (two launches).
+at::Tensor linear_w4a8(const at::Tensor& x, const at::Tensor& pairs_u8, const at::Tensor& theta,
+                       const c10::optional<at::Tensor>& channel_scales, const at::Tensor& packed, int64_t N,
+                       const c10::optional<at::Tensor>& bias, bool fp16_round, at::ScalarType out_dtype) {
+  auto qs = rotq_int8(x, pairs_u8, theta, channel_scales, 128, fp16_round);
+  return w4a8_gemm(std::get<0>(qs), std::get<1>(qs), packed, N, bias, out_dtype);
+}
+
+}  // namespace
+
+TORCH_LIBRARY(paro_b200, m) {
+  m.def("rotate(Tensor x, Tensor idx_ij, Tensor theta, Tensor? scales, int group_size) -> Tensor");
+  m.def("prepare_rotation(Tensor pairs, int group_size) -> Tensor");
+  m.def("rotq_int8(Tensor x, Tensor pairs_u8, Tensor theta, Tensor? scales, int group_size, bool fp16_round) -> "
+        "(Tensor, Tensor)");
+  m.def("quant_int8(Tensor x) -> (Tensor, Tensor)");
+  m.def("prepare_weights(Tensor qweight, Tensor scales, Tensor scaled_zeros, int N, int K) -> Tensor");
+  m.def("prepare_weights_awq(Tensor qweight, Tensor scales, Tensor qzeros, int N, int K) -> Tensor");
+  m.def("w4a8_gemm(Tensor xq, Tensor xscale, Tensor packed, int N, Tensor? bias, ScalarType out_dtype) -> Tensor");
+  m.def("linear_w4a8(Tensor x, Tensor pairs_u8, Tensor theta, Tensor? channel_scales, Tensor packed, int N, "
+        "Tensor? bias, bool fp16_round, ScalarType out_dtype) -> Tensor");
+}
+
+TORCH_LIBRARY_IMPL(paro_b200, CUDA, m) {
+  m.impl("rotate", &rotate);
+  m.impl("prepare_rotation", &prepare_rotation);
+  m.impl("rotq_int8", &rotq_int8);
+  m.impl("quant_int8", &quant_int8);
+  m.impl("prepare_weights", &prepare_weights);
+  m.impl("prepare_weights_awq", &prepare_weights_awq);
+  m.impl("w4a8_gemm", &w4a8_gemm);
+  m.impl("linear_w4a8", &linear_w4a8);
+}

@@ -1,0 +1,106 @@
+"""Python entry points for the ``torch.ops.paro_b200`` operators.
+
+Each function is a direct call into the native operator (CUDA only).  Fake
+(meta) kernels are registered so the operators trace under
+``torch.compile(fullgraph=True)`` and CUDA-graph capture, the way the
+reference registers ``rotation::rotate`` (kernels/paroquant_kernels/
+__init__.py:7-28).
+"""
+from __future__ import annotations
+
+import torch
+
+from ._native import load_ops
+
+load_ops()
+
+_ops = torch.ops.paro_b200
+
+
+@torch.library.register_fake("paro_b200::rotate")
+def _rotate_fake(x, idx_ij, theta, scales, group_size):
+    return torch.empty_like(x)
+
+
+@torch.library.register_fake("paro_b200::prepare_rotation")
+def _prepare_rotation_fake(pairs, group_size):
+    return torch.empty(pairs.shape, dtype=torch.uint8, device=pairs.device)
+
+
+@torch.library.register_fake("paro_b200::rotq_int8")
+def _rotq_fake(x, pairs_u8, theta, scales, group_size, fp16_round):
+    q = torch.empty(x.shape, dtype=torch.int8, device=x.device)
+    s = torch.empty(tuple(x.shape[:-1]) + (1,), dtype=torch.float32, device=x.device)
+    return q, s
+
+
+@torch.library.register_fake("paro_b200::quant_int8")
+def _quant_fake(x):
+    q = torch.empty(x.shape, dtype=torch.int8, device=x.device)
+    s = torch.empty(tuple(x.shape[:-1]) + (1,), dtype=torch.float32, device=x.device)
+    return q, s
+
+
+def packed_weight_bytes(N: int, K: int) -> int:
+    """Bytes of the tile-record weight buffer (16-row x 128-channel records of
+    1072 bytes)."""
+    if N % 16 or K % 128:
+        raise ValueError("N must be a multiple of 16 and K a multiple of 128")
+    return (N // 16) * (K // 128) * 1072
+
+
+@torch.library.register_fake("paro_b200::prepare_weights")
+def _prep_fake(qweight, scales, scaled_zeros, N, K):
+    return torch.empty(packed_weight_bytes(N, K), dtype=torch.uint8, device=qweight.device)
+
+
+@torch.library.register_fake("paro_b200::prepare_weights_awq")
+def _prep_awq_fake(qweight, scales, qzeros, N, K):
+    return torch.empty(packed_weight_bytes(N, K), dtype=torch.uint8, device=qweight.device)
+
+
+@torch.library.register_fake("paro_b200::w4a8_gemm")
+def _gemm_fake(xq, xscale, packed, N, bias, out_dtype):
+    return torch.empty(tuple(xq.shape[:-1]) + (N,), dtype=out_dtype, device=xq.device)
+
+
+@torch.library.register_fake("paro_b200::linear_w4a8")
+def _linear_fake(x, pairs_u8, theta, channel_scales, packed, N, bias, fp16_round, out_dtype):
+    return torch.empty(tuple(x.shape[:-1]) + (N,), dtype=out_dtype, device=x.device)
+
+
+def rotate(x, idx_ij, theta, scales=None, group_size=128):
+    """Drop-in for ``torch.ops.rotation.rotate`` (rotation.cu:576-584)."""
+    return _ops.rotate(x, idx_ij, theta, scales, group_size)
+
+
+def prepare_rotation(pairs, group_size=128):
+    """Validate (each layer-group a permutation) and narrow pairs to uint8."""
+    return _ops.prepare_rotation(pairs, group_size)
+
+
+def rotq_int8(x, pairs_u8, theta, scales=None, group_size=128, fp16_round=True):
+    """Fused channel scale + Givens rotation + per-token int8 quantisation."""
+    return _ops.rotq_int8(x, pairs_u8, theta, scales, group_size, fp16_round)
+
+
+def per_token_quant_int8(x):
+    """Drop-in for vLLM ``per_token_quant_int8`` (int8_utils.py:131-156)."""
+    return _ops.quant_int8(x)
+
+
+def prepare_weights(qweight, scales, scaled_zeros, N, K):
+    return _ops.prepare_weights(qweight, scales, scaled_zeros, N, K)
+
+
+def prepare_weights_awq(qweight, scales, qzeros, N, K):
+    return _ops.prepare_weights_awq(qweight, scales, qzeros, N, K)
+
+
+def w4a8_gemm(xq, xscale, packed, N, bias=None, out_dtype=torch.bfloat16):
+    return _ops.w4a8_gemm(xq, xscale, packed, N, bias, out_dtype)
+
+
+def linear_w4a8(x, pairs_u8, theta, channel_scales, packed, N, bias=None, fp16_round=True, out_dtype=None):
+    return _ops.linear_w4a8(x, pairs_u8, theta, channel_scales, packed, N, bias, fp16_round,
+                            out_dtype if out_dtype is not None else x.dtype)

@@ -1,0 +1,128 @@
+"""Rotation and RotateLinearInt4 — the ParoQuant rotated int4 linear.
+
+Mirrors src/alpamayo_r1/utils/quantization/rotation_linear.py (reference):
+same constructors, buffers (``rotation.theta`` fp16 [8, K/2],
+``rotation.pairs`` int16 [8, K], ``rotation.channel_scales`` fp16 [1, K]) and
+``buffer_name`` accessor, so state dicts load unchanged.
+
+Forward paths (all CUDA, through torch.ops.paro_b200):
+  * ``Rotation.forward`` is ``rotation::rotate`` (rotation.cu:456-493).
+  * ``RotateLinearInt4.forward`` with a W4A8 ``qlinear`` runs the fused
+    activation kernel (channel scale + 8 Givens layers + per-token int8, the
+    rotated value rounded to fp16 first as the reference's rotate kernel
+    stores it) and the int4 x int8 GEMM: two launches instead of the
+    reference's six (paroquant_marlin_w4a8.py:59-65 + rotation.cu + vLLM).
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+
+from .. import ops
+from .qmodule import WQLinear
+from .rotation_utils import quantizer, rotate_tensor
+from .quantization_utils import pseudo_quantize_tensor
+
+
+def _default_device():
+    return "cuda" if torch.cuda.is_available() else "cpu"
+
+
+class Rotation(nn.Module):
+    def __init__(self, dim, krot=8, group_size=128, rotation_angles=None, rotation_pairs=None,
+                 channel_scales=None):
+        super().__init__()
+        if krot != 8 or group_size != 128:
+            raise NotImplementedError()
+        assert dim % group_size == 0
+        num_groups = dim // group_size
+        device = _default_device()
+        if rotation_angles is None:
+            rotation_angles = torch.zeros(krot, dim // 2, device=device, dtype=torch.float16)
+        if rotation_pairs is None:
+            one = torch.randperm(group_size, dtype=torch.int, device=device)
+            rotation_pairs = one.repeat(num_groups).unsqueeze(0).expand(krot, -1)
+        if channel_scales is None:
+            channel_scales = torch.ones(1, dim, dtype=torch.half)
+        self.register_buffer("theta", rotation_angles.clone().contiguous())
+        self.register_buffer("pairs", rotation_pairs.clone().short().contiguous())
+        self.register_buffer("channel_scales", channel_scales.clone().contiguous())
+        self._pairs_u8 = None
+        self._pairs_key = None
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return ops.rotate(x, self.pairs, self.theta, self.channel_scales, 128)
+
+    def pairs_u8(self) -> torch.Tensor:
+        """uint8 pair table validated as disjoint pairs (derived, cached)."""
+        key = (self.pairs.data_ptr(), self.pairs._version, self.pairs.device)
+        if self._pairs_u8 is None or self._pairs_key != key:
+            self._pairs_u8 = ops.prepare_rotation(self.pairs.contiguous(), 128)
+            self._pairs_key = key
+        return self._pairs_u8
+
+    def quantize_activations(self, x: torch.Tensor, fp16_round: bool = True):
+        """x -> (int8 codes, float32 per-token scales) in one kernel."""
+        cs = self.channel_scales.reshape(-1).to(torch.float16)
+        return ops.rotq_int8(x, self.pairs_u8(), self.theta.to(torch.float16).contiguous(), cs, 128, fp16_round)
+
+
+class RotateLinearInt4(nn.Module):
+    def __init__(self, in_feat, out_feat, bias, dtype, rotation_angles=None, rotation_pairs=None,
+                 channel_scales=None):
+        super().__init__()
+        self.in_features = in_feat
+        self.out_features = out_feat
+        self.rotation = Rotation(in_feat, rotation_angles=rotation_angles, rotation_pairs=rotation_pairs,
+                                 channel_scales=channel_scales)
+        self.qlinear = WQLinear(4, 128, self.in_features, self.out_features, bias, dtype=dtype)
+
+    @classmethod
+    def from_linear(cls, linear, rotation_angles=None, rotation_pairs=None, channel_scales=None, qscales=None,
+                    qzeros=None, rotate_weight=False, init_only=True):
+        rl = cls(linear.in_features, linear.out_features, linear.bias is not None, linear.weight.dtype,
+                 rotation_angles, rotation_pairs, channel_scales)
+        if rotate_weight:
+            with torch.no_grad():
+                w = linear.weight.data.detach().clone()
+                w = rotate_tensor(w, rotation_angles, rotation_pairs, channel_scales)
+                if qscales is not None:
+                    w = pseudo_quantize_tensor(w, 4, q_group_size=128, qzeros=qzeros, qscales=qscales)
+                    qzeros = qzeros.view(w.size(0), -1)
+                    qscales = qscales.view(w.size(0), -1)
+                linear.weight.copy_(w)
+        if init_only:
+            return rl
+        linear.to(torch.half)
+        assert (qscales is None) == (qzeros is None)
+        rl.qlinear = quantizer(linear, 4, 128, qscales=qscales, qzeros=qzeros)
+        return rl
+
+    def _packed_and_bias(self):
+        q = self.qlinear
+        if hasattr(q, "packed_weight"):
+            return q.packed_weight(), q.bias
+        return q.packed(), q.bias
+
+    @torch.no_grad()
+    def forward(self, x, out_dtype=None):
+        packed, bias = self._packed_and_bias()
+        cs = self.rotation.channel_scales.reshape(-1).to(torch.float16)
+        return ops.linear_w4a8(x, self.rotation.pairs_u8(), self.rotation.theta.to(torch.float16).contiguous(),
+                               cs, packed, self.out_features, bias, True,
+                               out_dtype if out_dtype is not None else x.dtype)
+
+    def buffer_name(self, buffer_name: str):
+        if buffer_name == "qlinear.qweight":
+            return self.qlinear.qweight
+        elif buffer_name == "qlinear.scaled_zeros":
+            return self.qlinear.scaled_zeros
+        elif buffer_name == "qlinear.scales":
+            return self.qlinear.scales
+        elif buffer_name == "rotation.theta":
+            return self.rotation.theta
+        elif buffer_name == "rotation.pairs":
+            return self.rotation.pairs
+        elif buffer_name == "rotation.channel_scales":
+            return self.rotation.channel_scales
+        raise ValueError(f"Invalid buffer name: {buffer_name}")

@@ -1,0 +1,409 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 W4A8 rotated-linear path (one JSON line on rank 0).
+
+Headline workload ("decode sweep"): the four
+projection shapes of one 7B-class decoder layer (qkv 3584->4608, o 3584->3584,
+gate_up 3584->37888, down 18944->3584) at M = 1, 4 and 8 tokens; each linear
+is the fused rotation + int8 activation kernel followed by the int4 x int8
+GEMM.  One step = STEP_SWEEPS passes over the 12 (shape, M) cases.  Three
+weight replicas (one per M) make the per-pass weight working set 363 MB
+(> 126 MB L2), so every GEMM streams its weights from HBM.  The metric value
+is weight-stream GB/s (algorithmic int4 code + fp16 scale + int4 zero bytes
+per second), whole job.
+
+Timing: CUDA graph of one step, replayed; CUDA events around the timed
+replays, barrier + synchronize on both sides, max over ranks.  Per-kernel
+launch durations for the roofline come from an eager pass in which the host
+runs ahead of the device (a device sleep is queued first), with events
+between launches.
+
+--impl reference: the reference's CPU fake-quant path (oracle/cpu_baseline.py,
+a port, since the reference's own Python cannot run here) on the host cores,
+same metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+SHAPES = [("qkv", 4608, 3584), ("o_proj", 3584, 3584), ("gate_up", 37888, 3584), ("down", 3584, 18944)]
+DECODE_M = [1, 4, 8]
+STEP_SWEEPS = 16
+L2_BYTES = 126 * 2 ** 20
+METRIC = "W4A8 rot-GEMM decode weight GB/s & prefill int8 TOPS vs roofline, 1-8 B200"
+
+
+def args_():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+def weight_bytes(N, K):
+    G = K // 128
+    return N * K // 2 + G * N * 2 + G * N // 2
+
+
+def gemm_alg_bytes(M, N, K):
+    """Algorithmic bytes of one decode GEMM launch: weights + int8 activations
+    + fp32 token scales + bf16 output."""
+    return weight_bytes(N, K) + M * K + 4 * M + 2 * M * N
+
+
+def act_alg_bytes(M, K):
+    """Activation kernel: bf16 in, int8 + fp32 scale out, fp16 angles,
+    uint8 pairs and fp16 channel scales."""
+    return 2 * M * K + M * K + 4 * M + 8 * (K // 2) * 2 + 8 * K + 2 * K
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profile_traffic(name):
+    """dram bytes per launch recorded from an ncu capture (profiles/*.md line
+    'traffic_bytes_per_launch: <n>'), or None."""
+    p = os.path.join(ROOT, "profiles", name)
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+class Clocks:
+    """nvidia-smi clock / throttle-reason sampling while the timed region runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_uuid=None):
+        self.uuid = device_uuid
+        self.proc = None
+        self.f = None
+
+    def start(self):
+        try:
+            self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            cmd = ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "20"]
+            if self.uuid:
+                cmd += ["-i", self.uuid]
+            self.proc = subprocess.Popen(cmd, stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.flush()
+        rows = [l.split(",") for l in open(self.f.name).read().strip().splitlines() if l.count(",") >= 8]
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def dist_setup(n):
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        from datetime import timedelta
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier_sync(world):
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def max_over_ranks(v, world):
+    import torch
+    import torch.distributed as dist
+    if world == 1:
+        return v
+    t = torch.tensor([v], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def cpu_baseline_sample(budget_s=10.0):
+    """The reference's CPU fake-quant path on config 0 (M=16, K=N=3584)."""
+    from oracle.cpu_baseline import make_case, time_cases
+    case = make_case(3584, 3584, 16, seed=0)
+    calls, sec, threads = time_cases([case], budget_s=budget_s)
+    gbs = calls * weight_bytes(3584, 3584) / sec / 1e9
+    return {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"config 0 (M=16, K=N=3584) fake-quant linear x{calls} in {sec:.1f} s, torch CPU, "
+                      f"{threads} threads"}
+
+
+def run_reference(a):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import torch
+    from oracle.cpu_baseline import make_case, time_cases
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cases = {(name, M): make_case(N, K, M, seed=i * 10 + M)
+             for i, (name, N, K) in enumerate(SHAPES) for M in DECODE_M}
+    keys = list(cases)
+
+    def step(i):
+        # bounded sample: one M value's four shapes per step, cycling M
+        M = DECODE_M[i % len(DECODE_M)]
+        sel = [cases[k] for k in keys if k[1] == M]
+        t0 = time.perf_counter()
+        from oracle.cpu_baseline import fake_quant_linear
+        for c in sel:
+            fake_quant_linear(c["x"], c["pairs"], c["theta"], c["cs"], c["w_dq"])
+        return time.perf_counter() - t0, sum(weight_bytes(N, K) for (_, N, K) in SHAPES)
+
+    for i in range(a.warmup):
+        step(i)
+    tot_t, tot_b = 0.0, 0
+    for i in range(a.steps):
+        t, b = step(i)
+        tot_t += t
+        tot_b += b
+    val = tot_b / tot_t / 1e9
+    line = {"metric": METRIC, "value": val, "unit": "GB/s", "impl": "reference", "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": 1e3 * tot_t / a.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "decode sweep (configs[1]): qkv/o/gate_up/down x M in {1,4,8}; one M per step",
+                       "parallelism": "cpu"},
+            "cpu_baseline": {"value": val, "unit": "GB/s", "cores": threads, "kind": "port",
+                             "sample": "per step the four shapes at one M (cycling 1, 4, 8), torch CPU fake-quant"},
+            "e2e": {"value": val, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main():
+    a = args_()
+    if a.impl == "reference":
+        return run_reference(a)
+    import torch
+    world, rank, local = dist_setup(a.gpus)
+    import alpamayo_b200.ops as ops
+    from alpamayo_b200 import synthetic as syn
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    # --- inputs: three weight replicas (one per M), activations per (M, K)
+    reps = []
+    for ri, M in enumerate(DECODE_M):
+        reps.append({name: syn.make_layer(N, K, seed=1000 * rank + 100 * ri + si, checkpoint=False)
+                     for si, (name, N, K) in enumerate(SHAPES)})
+    xs = {(M, K): syn.make_activations(M, K, seed=7 * M + K + rank) for M in DECODE_M for K in {3584, 18944}}
+    torch.cuda.synchronize()
+    wset = sum(weight_bytes(N, K) for (_, N, K) in SHAPES) * len(DECODE_M)
+
+    def linear(L, x, M):
+        q, s = ops.rotq_int8(x, L["pairs_u8"], L["theta"], L["cs_vec"], 128, True)
+        return ops.w4a8_gemm(q, s, L["packed"], L["N"], None, torch.bfloat16)
+
+    def sweep():
+        for ri, M in enumerate(DECODE_M):
+            for (name, N, K) in SHAPES:
+                linear(reps[ri][name], xs[(M, K)], M)
+
+    def step():
+        for _ in range(STEP_SWEEPS):
+            sweep()
+
+    bytes_per_step = STEP_SWEEPS * wset
+    launches_per_step = STEP_SWEEPS * len(DECODE_M) * len(SHAPES) * 2
+
+    # --- capture one step as a CUDA graph
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    for _ in range(a.warmup):
+        g.replay()
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        pass
+    clocks = Clocks(uuid)
+    clocks.start()
+    time.sleep(0.2)
+    barrier_sync(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(a.steps):
+        g.replay()
+    e1.record()
+    barrier_sync(world)
+    ms = e0.elapsed_time(e1) / a.steps
+    clk = clocks.stop()
+    ms = max_over_ranks(ms, world)
+    value = world * bytes_per_step / (ms * 1e-3) / 1e9
+
+    # --- per-kernel launch durations (eager, host ahead of the device)
+    gemm_t, gemm_b, act_t, act_b, cases = 0.0, 0, 0.0, 0, {}
+    for _ in range(3):
+        torch.cuda._sleep(int(2e7))
+        evs = []
+        for ri, M in enumerate(DECODE_M):
+            for (name, N, K) in SHAPES:
+                L = reps[ri][name]
+                ea, eb, ec = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+                ea.record()
+                q, sc = ops.rotq_int8(xs[(M, K)], L["pairs_u8"], L["theta"], L["cs_vec"], 128, True)
+                eb.record()
+                ops.w4a8_gemm(q, sc, L["packed"], N, None, torch.bfloat16)
+                ec.record()
+                evs.append((name, M, N, K, ea, eb, ec))
+        torch.cuda.synchronize()
+        for (name, M, N, K, ea, eb, ec) in evs:
+            ta, tg = ea.elapsed_time(eb) * 1e-3, eb.elapsed_time(ec) * 1e-3
+            act_t += ta
+            act_b += act_alg_bytes(M, K)
+            gemm_t += tg
+            gemm_b += gemm_alg_bytes(M, N, K)
+            c = cases.setdefault(f"{name}_m{M}", {"gemm_us": [], "act_us": []})
+            c["gemm_us"].append(tg * 1e6)
+            c["act_us"].append(ta * 1e6)
+    hbm, peak_kind = peaks()
+    gemm_gbs = gemm_b / gemm_t / 1e9
+    case_out = {}
+    for (name, N, K) in SHAPES:
+        for M in DECODE_M:
+            c = cases[f"{name}_m{M}"]
+            gu = statistics.median(c["gemm_us"])
+            case_out[f"{name}_m{M}"] = {"gemm_us": round(gu, 2), "act_us": round(statistics.median(c["act_us"]), 2),
+                                       "weight_GBps": round(weight_bytes(N, K) / gu / 1e3, 1)}
+    traffic = profile_traffic("gemm_decode_gate_up_m8.md")
+
+    # --- end to end through the public op with host buffers (graph of the step)
+    e2e = None
+    if not a.no_e2e:
+        hx = {k: v.cpu().pin_memory() for k, v in xs.items()}
+        dx = {k: torch.empty_like(v) for k, v in xs.items()}
+        hy = {(ri, name): torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
+              for ri, M in enumerate(DECODE_M) for (name, N, K) in SHAPES}
+        h2d = sum(v.numel() * 2 for v in xs.values())
+        d2h = sum(v.numel() * 2 for v in hy.values())
+
+        def e2e_step():
+            for k in dx:
+                dx[k].copy_(hx[k], non_blocking=True)
+            for ri, M in enumerate(DECODE_M):
+                for (name, N, K) in SHAPES:
+                    L = reps[ri][name]
+                    y = ops.linear_w4a8(dx[(M, K)], L["pairs_u8"], L["theta"], L["cs_vec"], L["packed"], N, None,
+                                        True, torch.bfloat16)
+                    hy[(ri, name)].copy_(y, non_blocking=True)
+
+        s2 = torch.cuda.Stream()
+        s2.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s2):
+            e2e_step()
+        torch.cuda.current_stream().wait_stream(s2)
+        g2 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g2):
+            e2e_step()
+        for _ in range(a.warmup):
+            g2.replay()
+        barrier_sync(world)
+        t0 = time.perf_counter()
+        for _ in range(a.steps):
+            g2.replay()
+            torch.cuda.synchronize()  # the step's results are read on the host
+        barrier_sync(world)
+        el = max_over_ranks((time.perf_counter() - t0) / a.steps, world)
+        e2e = {"value": world * wset / el / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
+               "d2h_bytes_per_step": d2h, "ms_per_step": el * 1e3,
+               "path": "torch.ops.paro_b200.linear_w4a8 per linear, pinned host inputs/outputs, one sweep per "
+                       "step, CUDA graph replay + host sync per step"}
+        del g2
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        cpu = cpu_baseline_sample()
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int4xint8->int32 (bf16 act/out)", "data": "synthetic",
+            "config": {"workload": "decode sweep, BASELINE configs[1]: qkv 3584->4608, o 3584->3584, "
+                                   "gate_up 3584->37888, down 18944->3584 at M=1,4,8; rotation+int8 quant kernel "
+                                   "+ W4A8 GEMM per linear",
+                       "step": f"{STEP_SWEEPS} sweeps of the 12 (shape, M) linears, CUDA graph",
+                       "l2": f"weight working set {wset / 2**20:.0f} MiB per sweep > L2 {L2_BYTES / 2**20:.0f} MiB "
+                             "(3 replicas, one per M); inputs not flushed",
+                       "parallelism": f"dp{world} (independent replicas, no collective)"},
+            "roofline": {"kernel": "gemm_decode (int4 x int8 mma.sync streaming)", "bound": "hbm",
+                         "achieved": round(gemm_gbs, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(gemm_gbs / hbm, 4), "peak_kind": peak_kind,
+                         "traffic": traffic,
+                         "alg_bytes": "N*K/2 + G*N*2 + G*N/2 + M*K + 4M + 2*M*N per launch"},
+            "activation_kernel": {"achieved_GBps": round(act_b / act_t / 1e9, 1),
+                                  "frac": round(act_b / act_t / 1e9 / hbm, 4)},
+            "cases": case_out,
+            "gpu_launches": launches_per_step * a.steps,
+            "clocks": clk,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+        }
+        print(json.dumps(line), flush=True)
+    del g
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

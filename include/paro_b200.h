@@ -1,0 +1,195 @@
+/*
+ * paro_b200.h — C ABI of the B200 (sm_100a) ParoQuant W4A8 rotated-linear
+ * kernels.
+ *
+ * Every entry point takes raw device pointers, sizes and a CUDA stream,
+ * launches asynchronously on that stream, never synchronises, never
+ * allocates, and returns a paro_status code (0 = success).  Outputs are
+ * written only on success.  No torch types appear here: the torch operator
+ * shim (alpamayo_b200/csrc/torch_ops.cpp) and any FFI binding (ctypes, cgo,
+ * JNI) call these functions directly.
+ *
+ * Reference interfaces replaced (paths relative to the reference project):
+ *   rotation::rotate            kernels/paroquant_kernels/src/rotation.cu:456-493,576-584
+ *   rotation::rotate_and_quant  kernels/paroquant_kernels/src/rotation.cu:495-536 (the
+ *                               build's fused quantiser is per-token int8, the format
+ *                               the W4A8 path consumes, not NVFP4)
+ *   per_token_quant_int8        vllm/model_executor/layers/quantization/utils/int8_utils.py:131-156
+ *   marlin_gemm (uint4 x int8)  vllm/_custom_ops.py:1277-1318 via
+ *                               src/alpamayo_r1/utils/quantization/paroquant_marlin_w4a8.py:314-333
+ *   WQLinear -> Marlin repack   src/alpamayo_r1/utils/quantization/paroquant_marlin_w4a8.py:95-209,274-312
+ */
+#ifndef PARO_B200_H_
+#define PARO_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same object as cudaStream_t; NULL means the legacy default stream. */
+typedef struct CUstream_st* paro_stream_t;
+
+typedef enum paro_status {
+  PARO_OK = 0,
+  PARO_ERR_INVALID_ARGUMENT = 1, /* null pointer where one is required, size <= 0   */
+  PARO_ERR_SHAPE = 2,            /* K % group != 0, N % 16 != 0, ...                */
+  PARO_ERR_UNSUPPORTED = 3,      /* krot / group / dtype combination not built      */
+  PARO_ERR_MISALIGNED = 4,       /* pointer not aligned as the entry point requires */
+  PARO_ERR_CUDA = 5,             /* a CUDA runtime call or launch failed            */
+  PARO_ERR_WORKSPACE = 6,        /* workspace smaller than *_workspace_size()       */
+  PARO_ERR_DEVICE = 7,           /* current device is not sm_100                    */
+  PARO_ERR_TOO_LARGE = 8         /* size beyond a compiled limit                    */
+} paro_status;
+
+typedef enum paro_dtype {
+  PARO_F32 = 0,
+  PARO_F16 = 1,
+  PARO_BF16 = 2
+} paro_dtype;
+
+/* Human-readable name of a status code (static storage). */
+const char* paro_status_string(int status);
+
+/* Library ABI version (major * 100 + minor). */
+int paro_version(void);
+
+/* Last CUDA error string seen by the library on this thread ("" if none). */
+const char* paro_last_cuda_error(void);
+
+/* ------------------------------------------------------------------------
+ * Rotation tables
+ * ------------------------------------------------------------------------ */
+
+/*
+ * Validate and pack the Givens pair table.
+ *   pairs  : int16 [krot, K] group-local channel indices; entries 2p, 2p+1 of
+ *            each group form pair p (reference layout, rotation_linear.py:32-44,
+ *            read by rotation.cuh:280-297).
+ *   out_u8 : uint8 [krot, K] the same indices as bytes (group <= 128).
+ *   bad    : device int32, set to the number of (layer, group) blocks that are
+ *            not a permutation of 0..group-1 (must be zero before the call is
+ *            trusted: overlapping pairs make the rotation order-dependent).
+ * Replaces nothing in the reference (it has no validator); it guards the
+ * disjointness invariant rotation.cu:48-54 relies on.
+ */
+int paro_prepare_rotation(const int16_t* pairs, int krot, int K, int group,
+                          uint8_t* out_u8, int32_t* bad, paro_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Activation kernels
+ * ------------------------------------------------------------------------ */
+
+/*
+ * rotation::rotate (rotation.cu:456-493): out = R_krot...R_1 (x * scales)
+ * per group, float32 math, stored in x's dtype.
+ *   x, out       : [M, K] of x_dtype (F32 / F16 / BF16), row-major.
+ *   scales       : [K] of param_dtype or NULL (no scaling).
+ *   theta        : [krot, K/2] of param_dtype.
+ *   pairs        : int16 [krot, K].
+ *   krot in {1,2,4,8,16}, group in {64,128}.
+ */
+int paro_rotate(const void* x, int x_dtype, int64_t M, int K,
+                const void* scales, const void* theta, int param_dtype,
+                const int16_t* pairs, int krot, int group,
+                void* out, paro_stream_t stream);
+
+/*
+ * Fused channel scale + Givens rotation + per-token symmetric int8
+ * quantisation: the activation half of one W4A8 linear, replacing
+ * rotation::rotate (rotation.cu:15-60) followed by per_token_quant_int8
+ * (int8_utils.py:106-128).
+ *   x            : [M, K] of x_dtype (F32 / F16 / BF16).
+ *   scales       : fp16 [K] channel scales or NULL.
+ *   theta        : fp16 [krot, K/2].
+ *   pairs_u8     : uint8 [krot, K] from paro_prepare_rotation.
+ *   fp16_round   : 1 = round the rotated value to fp16 before quantising,
+ *                  as the reference does (its rotate kernel stores fp16,
+ *                  rotation.cuh:333-334); 0 = quantise the float32 value.
+ *   out_q        : int8 [M, K];  out_scale : float32 [M] (= absmax / 127).
+ */
+int paro_rotq_int8(const void* x, int x_dtype, int64_t M, int K,
+                   const uint16_t* scales, const uint16_t* theta,
+                   const uint8_t* pairs_u8, int krot, int group, int fp16_round,
+                   int8_t* out_q, float* out_scale, paro_stream_t stream);
+
+/*
+ * per_token_quant_int8 (int8_utils.py:131-156): absmax = max(max|x|, 1e-10),
+ * scale = absmax / 127, q = round_half_away(x * (127 / absmax)).
+ *   x : [M, K] of x_dtype;  out_q : int8 [M, K];  out_scale : float32 [M].
+ */
+int paro_quant_int8(const void* x, int x_dtype, int64_t M, int K,
+                    int8_t* out_q, float* out_scale, paro_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Weights
+ * ------------------------------------------------------------------------ */
+
+/*
+ * Size in bytes of the packed weight buffer for an N x K layer.  The layout
+ * ("tile records"): for each block of 16 output rows and each 128-channel
+ * group one 1072-byte record = 16 rows x 64 bytes of int4 codes, then the
+ * 16 fp16 group scales, then the 16 uint8 zero points.
+ */
+size_t paro_packed_weight_bytes(int N, int K);
+
+/*
+ * WQLinear checkpoint buffers -> packed tile records.
+ *   qweight       : int16 [N/4, K] (qmodule.py:39-78 layout).
+ *   scales        : fp16 [G_pad, N];  scaled_zeros : fp16 [G_pad, N] (= -s*z),
+ *                   G_pad >= K/128 (qmodule.py:123-142).
+ *   zero points are recovered as clamp(round(-sz / s), 0, 15) with |s| < 1e-10
+ *   treated as 1 (paroquant_marlin_w4a8.py:197-204).
+ *   packed        : paro_packed_weight_bytes(N, K) bytes, 16-byte aligned.
+ * Requires N % 16 == 0, K % 128 == 0.
+ */
+int paro_prepare_weights(const int16_t* qweight, const uint16_t* scales,
+                         const uint16_t* scaled_zeros, int N, int K, int G_pad,
+                         void* packed, paro_stream_t stream);
+
+/*
+ * AWQ int32 buffers (the input of MarlinW4A8Linear.load_from_awq,
+ * paroquant_marlin_w4a8.py:274-312) -> packed tile records.
+ *   awq_qweight : int32 [K, N/8], nibble order [0,2,4,6,1,3,5,7] (:149-164).
+ *   awq_scales  : fp16 [K/128, N];  awq_qzeros : int32 [K/128, N/8].
+ */
+int paro_prepare_weights_awq(const int32_t* awq_qweight, const uint16_t* awq_scales,
+                             const int32_t* awq_qzeros, int N, int K,
+                             void* packed, paro_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * The int4 x int8 GEMM
+ * ------------------------------------------------------------------------ */
+
+/*
+ * y[m, n] = xscale[m] * sum_g s[g, n] * sum_{k in g} (q[k, n] - z[g, n]) * xq[m, k]
+ *           (+ bias[n]),
+ * int32-exact per 128-channel group, float32 across groups, stored in
+ * out_dtype (F16 / BF16 / F32).  Replaces marlin_gemm as called by
+ * apply_awq_marlin_linear (vllm/.../marlin_utils.py:577-630).
+ *   xq        : int8 [M, K];  xscale : float32 [M].
+ *   packed    : tile records from paro_prepare_weights*.
+ *   bias      : [N] of bias_dtype (F16 / BF16 / F32) or NULL.
+ *   out       : [M, N] of out_dtype.
+ *   workspace : at least paro_w4a8_gemm_workspace_size(M, N, K) bytes
+ *               (may be NULL when that size is 0).
+ * Requires N % 16 == 0, K % 128 == 0, M >= 1.
+ */
+size_t paro_w4a8_gemm_workspace_size(int64_t M, int N, int K);
+
+int paro_w4a8_gemm(const int8_t* xq, const float* xscale, int64_t M, int N, int K,
+                   const void* packed, const void* bias, int bias_dtype,
+                   void* out, int out_dtype, void* workspace, size_t workspace_bytes,
+                   paro_stream_t stream);
+
+/* Which GEMM kernel paro_w4a8_gemm would launch for this shape
+ * (0 = streaming decode kernel, 1 = tcgen05 tensor-core kernel). */
+int paro_w4a8_gemm_path(int64_t M, int N, int K);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PARO_B200_H_ */

@@ -1,0 +1,155 @@
+"""Activation-side kernels against the CPU oracle (which is pinned bit-exact
+to the reference's own rotation in test_oracle.py).
+
+Tolerances (north_star): int8 activation codes may differ from the
+reference's by at most 1 LSB on at most 0.1% of elements; per-token scales
+follow from the same absolute maximum.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import paro_oracle as O
+from tests.helpers import make_activations, make_rotation
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+CODE_LSB_FRAC = 1e-3
+
+
+@pytest.fixture(scope="module")
+def ops():
+    import alpamayo_b200.ops as ops
+    return ops
+
+
+def dev(a, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    return t.to(dtype) if dtype is not None else t
+
+
+def check_codes(q, q_ref, s, s_ref):
+    q = q.astype(np.int32)
+    d = np.abs(q - q_ref.astype(np.int32))
+    assert d.max() <= 1, f"code difference {d.max()} LSB"
+    frac = (d > 0).mean()
+    assert frac <= CODE_LSB_FRAC, f"{frac:.2e} of codes differ"
+    assert np.allclose(s, s_ref, rtol=2 ** -10, atol=0)
+    return frac
+
+
+@pytest.mark.parametrize("name", ["rot_m16_k1024.npz", "rot_m4_k3584.npz"])
+def test_rotate_matches_reference_golden_fp32(ops, name):
+    d = np.load(os.path.join(GOLD, name))
+    out = ops.rotate(dev(d["x"]), dev(d["pairs"]), dev(d["theta"]), dev(d["channel_scales"]), 128)
+    out = out.cpu().numpy()
+    ref = d["rotated"]
+    # float32 chain; the device uses __sincosf like the reference's kernel
+    assert np.abs(out - ref).max() <= 2e-5 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_rotate_half_types_round_like_reference(ops, dtype):
+    d = np.load(os.path.join(GOLD, "rot_m16_k1024.npz"))
+    x = torch.from_numpy(d["x"]).to(dtype)
+    theta = torch.from_numpy(d["theta"]).to(dtype)
+    cs = torch.from_numpy(d["channel_scales"]).to(dtype)
+    out = ops.rotate(x.cuda(), dev(d["pairs"]), theta.cuda(), cs.cuda(), 128).float().cpu().numpy()
+    ref = O.rotate_activations(x.float().numpy(), d["pairs"], theta.float().numpy(), cs.float().numpy())
+    ref = torch.from_numpy(ref).to(dtype).float().numpy()
+    ulp = 2 ** -10 if dtype == torch.float16 else 2 ** -7
+    diff = np.abs(out - ref)
+    assert (diff > 0).mean() < 0.01
+    assert (diff <= ulp * np.abs(ref) + 1e-6).all()
+
+
+@pytest.mark.parametrize("krot,group", [(1, 128), (2, 128), (4, 128), (16, 128), (8, 64), (2, 64)])
+def test_rotate_krot_group_variants(ops, krot, group):
+    rng = np.random.default_rng(krot * 10 + group)
+    K, M = 512, 7
+    G = K // group
+    pairs = np.stack([np.concatenate([rng.permutation(group) for _ in range(G)]) for _ in range(krot)]).astype(np.int16)
+    theta = ((rng.random((krot, K // 2)) * 2 - 1) * np.pi).astype(np.float32)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    out = ops.rotate(dev(x), dev(pairs), dev(theta), None, group).cpu().numpy()
+    ref = O.rotate_activations(x, pairs, theta, None, group_size=group)
+    assert np.abs(out - ref).max() <= 2e-5 * np.abs(ref).max()
+
+
+@pytest.mark.parametrize("M,K,xdt", [(1, 3584, torch.bfloat16), (4, 3584, torch.bfloat16),
+                                     (8, 18944, torch.bfloat16), (37, 1024, torch.float16),
+                                     (64, 3584, torch.bfloat16), (16, 2048, torch.float32),
+                                     (300, 3584, torch.bfloat16)])
+def test_rotq_int8_matches_reference_chain(ops, M, K, xdt):
+    pairs, theta, cs = make_rotation(K, seed=M + K)
+    x = make_activations(M, K, seed=7 * M + K)
+    xt = torch.from_numpy(x).to(xdt)
+    pu8 = ops.prepare_rotation(dev(pairs), 128)
+    q, s = ops.rotq_int8(xt.cuda(), pu8, dev(theta), dev(cs.reshape(-1)), 128, True)
+    q_ref, s_ref, _ = O.rot_quant_reference(xt.float().numpy(), pairs, theta.astype(np.float32),
+                                            cs.astype(np.float32))
+    assert tuple(q.shape) == (M, K) and tuple(s.shape) == (M, 1)
+    check_codes(q.cpu().numpy(), q_ref, s.cpu().numpy().reshape(-1), s_ref)
+
+
+def test_rotq_int8_golden_fixture(ops):
+    d = np.load(os.path.join(GOLD, "rot_m4_k3584.npz"))
+    pu8 = ops.prepare_rotation(dev(d["pairs"]), 128)
+    q, s = ops.rotq_int8(dev(d["x"]), pu8, dev(d["theta"]), dev(d["channel_scales"].reshape(-1)), 128, True)
+    # reference chain: its rotation (fixture), fp16 store, vLLM int8 quant
+    q_ref, s_ref = O.per_token_quant_int8(O.round_to_fp16(d["rotated"]))
+    check_codes(q.cpu().numpy(), q_ref, s.cpu().numpy().reshape(-1), s_ref)
+
+
+def test_rotq_int8_without_fp16_rounding(ops):
+    M, K = 16, 1024
+    pairs, theta, cs = make_rotation(K, seed=3)
+    x = make_activations(M, K, seed=4)
+    pu8 = ops.prepare_rotation(dev(pairs), 128)
+    q, s = ops.rotq_int8(dev(x), pu8, dev(theta), dev(cs.reshape(-1)), 128, False)
+    q_ref, s_ref, _ = O.rot_quant_reference(x, pairs, theta.astype(np.float32), cs.astype(np.float32),
+                                            fp16_intermediate=False)
+    check_codes(q.cpu().numpy(), q_ref, s.cpu().numpy().reshape(-1), s_ref)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+def test_quant_int8_bit_exact(ops, dtype):
+    x = make_activations(33, 3584, seed=9)
+    x[3] = 0.0  # all-zero row: absmax clamps to 1e-10
+    x[5, :8] = np.array([127, 0.5, -0.5, 1.5, -2.5, 63.49, -126.5, 0], dtype=np.float32)
+    x[5, 8:] = 0
+    xt = torch.from_numpy(x).to(dtype)
+    q, s = ops.per_token_quant_int8(xt.cuda())
+    q_ref, s_ref = O.per_token_quant_int8(xt.float().numpy())
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+    assert np.array_equal(s.cpu().numpy().reshape(-1), s_ref)
+    assert q[5, :8].tolist() == [127, 1, -1, 2, -3, 63, -127, 0]
+
+
+def test_prepare_rotation_rejects_overlapping_pairs(ops):
+    pairs, _, _ = make_rotation(256, seed=1)
+    ok = ops.prepare_rotation(dev(pairs), 128)
+    assert torch.equal(ok.cpu(), torch.from_numpy(pairs.astype(np.uint8)))
+    pairs[2, 130] = pairs[2, 131]
+    with pytest.raises(RuntimeError, match="not permutations"):
+        ops.prepare_rotation(dev(pairs), 128)
+
+
+def test_empty_batch(ops):
+    pairs, theta, cs = make_rotation(256, seed=1)
+    pu8 = ops.prepare_rotation(dev(pairs), 128)
+    q, s = ops.rotq_int8(torch.zeros(0, 256, device="cuda", dtype=torch.bfloat16), pu8, dev(theta),
+                         dev(cs.reshape(-1)), 128, True)
+    assert q.shape == (0, 256) and s.shape == (0, 1)
+
+
+def test_leading_batch_dims(ops):
+    pairs, theta, cs = make_rotation(512, seed=2)
+    x = make_activations(6, 512, seed=3).reshape(2, 3, 512)
+    pu8 = ops.prepare_rotation(dev(pairs), 128)
+    q, s = ops.rotq_int8(dev(x, torch.bfloat16), pu8, dev(theta), dev(cs.reshape(-1)), 128, True)
+    assert q.shape == (2, 3, 512) and s.shape == (2, 3, 1)
+    q2, s2 = ops.rotq_int8(dev(x.reshape(6, 512), torch.bfloat16), pu8, dev(theta), dev(cs.reshape(-1)), 128, True)
+    assert torch.equal(q.reshape(6, 512), q2) and torch.equal(s.reshape(6, 1), s2)

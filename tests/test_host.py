@@ -1,0 +1,155 @@
+"""Host-side checks that need no GPU: the C-ABI library exports every entry
+point declared in include/paro_b200.h, argument validation returns status
+codes before any launch, and the Python API mirror reproduces the
+reference's load-time conversions (against the golden fixtures)."""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+GOLD = os.path.join(ROOT, "tests", "golden")
+
+
+def header_functions():
+    src = open(os.path.join(ROOT, "include", "paro_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(paro_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    from alpamayo_b200._native import capi
+    L = capi()
+    names = header_functions()
+    assert len(names) >= 12
+    for n in names:
+        assert hasattr(L, n), f"{n} declared in include/paro_b200.h but not exported"
+
+
+def test_status_strings_and_version():
+    from alpamayo_b200._native import capi
+    L = capi()
+    assert L.paro_version() >= 100
+    assert L.paro_status_string(0) == b"ok"
+    assert L.paro_status_string(6) == b"workspace too small"
+    assert L.paro_packed_weight_bytes(3584, 3584) == (3584 // 16) * 28 * 1072
+    assert L.paro_packed_weight_bytes(3585, 3584) == 0
+
+
+def test_argument_validation_before_launch():
+    """Invalid arguments are rejected on the host with a status code (no
+    device work is attempted)."""
+    from alpamayo_b200._native import capi
+    L = capi()
+    dummy = ctypes.c_void_p(16)
+    # null x
+    assert L.paro_rotate(None, 1, 4, 256, None, dummy, 1, dummy, 8, 128, dummy, None) == 1
+    # K not a multiple of the group
+    assert L.paro_rotate(dummy, 1, 4, 200, None, dummy, 1, dummy, 8, 128, dummy, None) == 2
+    # unsupported krot / group
+    assert L.paro_rotate(dummy, 1, 4, 256, None, dummy, 1, dummy, 3, 128, dummy, None) == 3
+    assert L.paro_rotate(dummy, 1, 4, 256, None, dummy, 1, dummy, 8, 32, dummy, None) == 3
+    # bad dtype
+    assert L.paro_quant_int8(dummy, 7, 4, 256, dummy, dummy, None) == 3
+    # fused kernel only for krot 8, group 128 (rotation_linear.py:18-19)
+    assert L.paro_rotq_int8(dummy, 2, 4, 256, None, dummy, dummy, 4, 128, 1, dummy, dummy, None) == 3
+    # GEMM shape checks
+    assert L.paro_w4a8_gemm(dummy, dummy, 4, 100, 256, dummy, None, 0, dummy, 2, None, 0, None) == 2
+    assert L.paro_w4a8_gemm(dummy, dummy, 4, 256, 200, dummy, None, 0, dummy, 2, None, 0, None) == 2
+    # misaligned packed weights
+    assert L.paro_w4a8_gemm(dummy, dummy, 4, 256, 256, ctypes.c_void_p(8), None, 0, dummy, 2, None, 0,
+                            None) == 4
+    assert L.paro_prepare_weights(dummy, dummy, dummy, 256, 256, 0, dummy, None) == 2  # G_pad < K/128
+    # M == 0 is a no-op success
+    assert L.paro_quant_int8(dummy, 2, 0, 256, dummy, dummy, None) == 0
+
+
+def test_header_has_reference_citations():
+    src = open(os.path.join(ROOT, "include", "paro_b200.h")).read()
+    for cite in ["rotation.cu:456-493", "int8_utils.py", "_custom_ops.py:1277-1318", "paroquant_marlin_w4a8.py"]:
+        assert cite in src
+
+
+def test_python_api_mirror_matches_reference_conversions():
+    from alpamayo_b200.quantization import (calculate_zeros_width, pack_awq_int32, pack_intweight,
+                                            unpack_wqlinear_qweight, wqlinear_to_awq, dequant_awq,
+                                            dequant_wqlinear)
+    w = np.load(os.path.join(GOLD, "wq_n128_k1024.npz"))
+    codes = torch.from_numpy(w["codes"])
+    assert torch.equal(pack_intweight(codes), torch.from_numpy(w["qweight"]))
+    qw = torch.from_numpy(w["qweight"])
+    assert torch.equal(unpack_wqlinear_qweight(qw, 128, 1024), torch.from_numpy(w["unpacked"]))
+    awq = wqlinear_to_awq(qw, torch.from_numpy(w["wq_scales"]), torch.from_numpy(w["wq_scaled_zeros"]),
+                          128, 1024, 128)
+    assert torch.equal(awq.qweight, torch.from_numpy(w["awq_qweight"]))
+    assert torch.equal(awq.qzeros, torch.from_numpy(w["awq_qzeros"]))
+    assert torch.equal(awq.zeros, torch.from_numpy(w["awq_zeros"]))
+    assert torch.equal(pack_awq_int32(awq.zeros), awq.qzeros)
+    a = dequant_wqlinear(awq.int4_values, torch.from_numpy(w["wq_scales"]), torch.from_numpy(w["wq_scaled_zeros"]),
+                         128)[:32]
+    assert torch.equal(a, torch.from_numpy(w["dequant_wqlinear"]))
+    b = dequant_awq(awq.int4_values, awq.zeros, awq.scales, 128)[:32]
+    assert torch.equal(b, torch.from_numpy(w["dequant_awq"]))
+    assert calculate_zeros_width(3584) * 8 == 32 and calculate_zeros_width(18944) * 8 == 152
+
+
+def test_module_state_dict_keys_match_reference():
+    from alpamayo_b200.quantization import RotateLinearInt4
+    m = RotateLinearInt4(1024, 128, True, torch.float16)
+    sd = m.state_dict()
+    expect = {"rotation.theta": ((8, 512), torch.float16), "rotation.pairs": ((8, 1024), torch.int16),
+              "rotation.channel_scales": ((1, 1024), torch.float16), "qlinear.qweight": ((32, 1024), torch.int16),
+              "qlinear.scales": ((8, 128), torch.float16), "qlinear.scaled_zeros": ((8, 128), torch.float16),
+              "qlinear.bias": ((128,), torch.float16)}
+    assert set(sd) == set(expect)
+    for k, (shape, dt) in expect.items():
+        assert tuple(sd[k].shape) == shape and sd[k].dtype == dt, k
+    assert m.buffer_name("rotation.pairs") is m.rotation.pairs
+    with pytest.raises(ValueError):
+        m.buffer_name("nope")
+
+
+def test_rotation_rejects_unsupported_config():
+    from alpamayo_b200.quantization import Rotation
+    with pytest.raises(NotImplementedError):
+        Rotation(256, krot=4)
+
+
+def test_replace_and_wrap_on_fake_model():
+    """Module surgery of the loader on a stand-in model with the Alpamayo
+    layer path (model.vlm.model.language_model.layers)."""
+    import torch.nn as nn
+    from alpamayo_b200.quantization import RotateLinearInt4, replace_linears_with_rotate_linear
+    from alpamayo_b200.quantization.paroquant_marlin_w4a8 import (_sanitise_channel_scales, _wrap_rotate_linears,
+                                                                  BF16RotateLinearWrapper)
+
+    class Attn(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.q_proj = nn.Linear(256, 256, bias=False)
+            self.lm_head = nn.Linear(256, 32, bias=False)
+
+    class Layer(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.self_attn = Attn()
+
+    model = nn.Module()
+    model.vlm = nn.Module()
+    model.vlm.model = nn.Module()
+    model.vlm.model.language_model = nn.Module()
+    model.vlm.model.language_model.layers = nn.ModuleList([Layer(), Layer()])
+    replace_linears_with_rotate_linear(model)
+    layer0 = model.vlm.model.language_model.layers[0]
+    assert isinstance(layer0.self_attn.q_proj, RotateLinearInt4)
+    assert isinstance(layer0.self_attn.lm_head, nn.Linear)
+    layer0.self_attn.q_proj.rotation.channel_scales[0, :3] = torch.tensor([float("inf"), float("nan"), 1e4])
+    assert _sanitise_channel_scales(model) == 1
+    cs = layer0.self_attn.q_proj.rotation.channel_scales
+    assert torch.isfinite(cs).all() and cs.abs().max() <= 65504 / 128
+    _wrap_rotate_linears(model)
+    w = layer0.self_attn.q_proj
+    assert isinstance(w, BF16RotateLinearWrapper) and w.in_features == 256
