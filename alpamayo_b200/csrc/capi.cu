@@ -8,7 +8,7 @@
 #include <cstring>
 #include <string>
 
-#include "paro_common.cuh"
+#include "tc_ptx.cuh"
 
 namespace paro {
 cudaError_t launch_rotate(int x_dtype, int krot, int group, const void* x, int64_t M, int K, const void* scales,
@@ -24,13 +24,19 @@ cudaError_t launch_prepare_wq(const int16_t* qweight, const uint16_t* scales, co
 cudaError_t launch_prepare_awq(const int32_t* qweight, const uint16_t* scales, const int32_t* qzeros, int N, int K,
                                void* packed, cudaStream_t st);
 cudaError_t launch_gemm_decode(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
-                               const void* bias, int bias_dtype, void* out, int out_dtype, cudaStream_t st);
+                               const void* bias, int bias_dtype, void* out, int out_dtype, void* ws,
+                               cudaStream_t st);
+size_t gemm_decode_workspace(int64_t M, int N);
 int gemm_tc_supported(int64_t M, int N, int K);
 size_t gemm_tc_workspace(int64_t M, int N, int K);
 cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
                            const void* bias, int bias_dtype, void* out, int out_dtype, void* ws, size_t ws_bytes,
                            cudaStream_t st);
 }  // namespace paro
+
+namespace paro {
+uint32_t error_word_decode(int clear);
+}
 
 using namespace paro;
 
@@ -88,6 +94,7 @@ int paro_prepare_rotation(const int16_t* pairs, int krot, int K, int group, uint
 
 int paro_rotate(const void* x, int x_dtype, int64_t M, int K, const void* scales, const void* theta,
                 int param_dtype, const int16_t* pairs, int krot, int group, void* out, paro_stream_t stream) {
+  if (M == 0 && K > 0) return PARO_OK;
   if (!x || !theta || !pairs || !out || K <= 0 || M < 0) return PARO_ERR_INVALID_ARGUMENT;
   if (!valid_dtype(x_dtype) || !valid_dtype(param_dtype)) return PARO_ERR_UNSUPPORTED;
   if (group != 64 && group != 128) return PARO_ERR_UNSUPPORTED;
@@ -103,12 +110,15 @@ int paro_rotate(const void* x, int x_dtype, int64_t M, int K, const void* scales
 int paro_rotq_int8(const void* x, int x_dtype, int64_t M, int K, const uint16_t* scales, const uint16_t* theta,
                    const uint8_t* pairs_u8, int krot, int group, int fp16_round, int8_t* out_q, float* out_scale,
                    paro_stream_t stream) {
+  if (M == 0 && K > 0) return PARO_OK;
   if (!x || !theta || !pairs_u8 || !out_q || !out_scale || K <= 0 || M < 0) return PARO_ERR_INVALID_ARGUMENT;
   if (!valid_dtype(x_dtype)) return PARO_ERR_UNSUPPORTED;
   if (krot != 8 || group != 128) return PARO_ERR_UNSUPPORTED;  // Rotation supports only these (rotation_linear.py:18-19)
   if (K % group) return PARO_ERR_SHAPE;
   if (K > rotq_max_k()) return PARO_ERR_TOO_LARGE;
-  if (!aligned(out_q, 16)) return PARO_ERR_MISALIGNED;
+  if (!aligned(out_q, 16) || !aligned(x, x_dtype == PARO_F32 ? 16 : 8) || (scales && !aligned(scales, 8)) ||
+      !aligned(pairs_u8, 2) || !aligned(theta, 2))
+    return PARO_ERR_MISALIGNED;
   if (M == 0) return PARO_OK;
   if (int d = device_check()) return d;
   return cuda_status(
@@ -117,6 +127,7 @@ int paro_rotq_int8(const void* x, int x_dtype, int64_t M, int K, const uint16_t*
 
 int paro_quant_int8(const void* x, int x_dtype, int64_t M, int K, int8_t* out_q, float* out_scale,
                     paro_stream_t stream) {
+  if (M == 0 && K > 0) return PARO_OK;
   if (!x || !out_q || !out_scale || K <= 0 || M < 0) return PARO_ERR_INVALID_ARGUMENT;
   if (!valid_dtype(x_dtype)) return PARO_ERR_UNSUPPORTED;
   if (M == 0) return PARO_OK;
@@ -150,12 +161,20 @@ int paro_prepare_weights_awq(const int32_t* awq_qweight, const uint16_t* awq_sca
 int paro_w4a8_gemm_path(int64_t M, int N, int K) { return gemm_tc_supported(M, N, K) ? 1 : 0; }
 
 size_t paro_w4a8_gemm_workspace_size(int64_t M, int N, int K) {
-  return gemm_tc_supported(M, N, K) ? gemm_tc_workspace(M, N, K) : 0;
+  if (M <= 0 || N <= 0 || K <= 0 || N % kRecRows || K % kGroup) return 0;
+  return gemm_tc_supported(M, N, K) ? gemm_tc_workspace(M, N, K) : gemm_decode_workspace(M, N);
+}
+
+int paro_device_error_word(int clear) {
+  const uint32_t a = error_word_decode(clear);
+  if (a == ~0u) return -1;
+  return (int)a;
 }
 
 int paro_w4a8_gemm(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
                    const void* bias, int bias_dtype, void* out, int out_dtype, void* workspace, size_t workspace_bytes,
                    paro_stream_t stream) {
+  if (M == 0 && N > 0 && K > 0) return PARO_OK;
   if (!xq || !xscale || !packed || !out || M < 0 || N <= 0 || K <= 0) return PARO_ERR_INVALID_ARGUMENT;
   if (!valid_dtype(out_dtype) || (bias && !valid_dtype(bias_dtype))) return PARO_ERR_UNSUPPORTED;
   if (N % kRecRows || K % kGroup) return PARO_ERR_SHAPE;
@@ -168,8 +187,11 @@ int paro_w4a8_gemm(const int8_t* xq, const float* xscale, int64_t M, int N, int 
     return cuda_status(launch_gemm_tc(xq, xscale, M, N, K, packed, bias, bias_dtype, out, out_dtype, workspace,
                                       workspace_bytes, (cudaStream_t)stream));
   }
-  return cuda_status(
-      launch_gemm_decode(xq, xscale, M, N, K, packed, bias, bias_dtype, out, out_dtype, (cudaStream_t)stream));
+  const size_t need = gemm_decode_workspace(M, N);
+  if (!workspace || workspace_bytes < need) return PARO_ERR_WORKSPACE;
+  if (!aligned(workspace, 256)) return PARO_ERR_MISALIGNED;
+  return cuda_status(launch_gemm_decode(xq, xscale, M, N, K, packed, bias, bias_dtype, out, out_dtype, workspace,
+                                        (cudaStream_t)stream));
 }
 
 }  // extern "C"

@@ -14,6 +14,8 @@
 // layer are disjoint, so a layer needs only a __syncwarp between reads and
 // writes).  rotq keeps every rotated row in shared memory until the row's
 // absolute maximum is known, then writes int8 codes with 16-byte stores.
+#include <cooperative_groups.h>
+
 #include "paro_common.cuh"
 
 namespace paro {
@@ -168,6 +170,214 @@ rot_kernel(const InT* __restrict__ x, int64_t M, int K,
   }
 }
 
+// ---------------------------------------------------------------------------
+// Fused rotation + int8 quantisation, cluster version.
+//
+// A thread-block cluster of C CTAs owns R consecutive rows; CTA c of the
+// cluster owns groups [c*gpc, (c+1)*gpc) and one warp per group, so all
+// groups of a row block rotate in parallel.  Each warp loads its group's pair
+// indices and angles once, then rotates all R rows together in a per-warp
+// shared buffer laid out channel-major ([128][R], R floats per channel, so a
+// Givens update moves R rows with vector loads).  The rotated values (fp16-
+// rounded like the reference's rotate kernel output) stay in shared memory;
+// each CTA's per-row absolute maxima are exchanged through distributed shared
+// memory, and every warp then quantises its own group with the row scale.
+// ---------------------------------------------------------------------------
+template <int R>
+struct RowVec;
+template <> struct RowVec<1> { using T = float; };
+template <> struct RowVec<2> { using T = float2; };
+template <> struct RowVec<4> { using T = float4; };
+
+template <int R>
+__device__ __forceinline__ void ld_rows(const float* p, float (&v)[R]) {
+  if constexpr (R == 1) {
+    v[0] = p[0];
+  } else if constexpr (R == 2) {
+    const float2 a = *reinterpret_cast<const float2*>(p);
+    v[0] = a.x; v[1] = a.y;
+  } else {
+#pragma unroll
+    for (int q = 0; q < R / 4; ++q) {
+      const float4 a = reinterpret_cast<const float4*>(p)[q];
+      v[4 * q] = a.x; v[4 * q + 1] = a.y; v[4 * q + 2] = a.z; v[4 * q + 3] = a.w;
+    }
+  }
+}
+
+template <int R>
+__device__ __forceinline__ void st_rows(float* p, const float (&v)[R]) {
+  if constexpr (R == 1) {
+    p[0] = v[0];
+  } else if constexpr (R == 2) {
+    *reinterpret_cast<float2*>(p) = make_float2(v[0], v[1]);
+  } else {
+#pragma unroll
+    for (int q = 0; q < R / 4; ++q)
+      reinterpret_cast<float4*>(p)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  }
+}
+
+template <typename InT>
+__device__ __forceinline__ void load4(const InT* p, float (&v)[4]) {
+  if constexpr (sizeof(InT) == 4) {
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  } else {
+    const uint2 a = *reinterpret_cast<const uint2*>(p);
+    const InT* h = reinterpret_cast<const InT*>(&a);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) v[e] = to_f32(h[e]);
+  }
+}
+
+template <typename InT, int R>
+__global__ void __launch_bounds__(512)
+rotq_cluster_kernel(const InT* __restrict__ x, int64_t M, int K, const uint16_t* __restrict__ scales,
+                    const uint16_t* __restrict__ theta, const uint8_t* __restrict__ pairs, int fp16_round, int gpc,
+                    int8_t* __restrict__ out_q, float* __restrict__ out_scale) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  extern __shared__ __align__(16) float gbuf[];  // [gpc][128][R]
+  __shared__ float wmax[32][R];
+  __shared__ float cta_max[R];
+  __shared__ float row_inv[R];
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  const int crank = (int)cluster.block_rank();
+  const int csize = (int)cluster.num_blocks();
+  const int G = K >> 7;
+  const int64_t row0 = (int64_t)blockIdx.y * R;
+  const int nrows = (M - row0 < R) ? (int)(M - row0) : R;
+  float rmax[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) rmax[r] = 0.f;
+
+  for (int gl = warp; gl < gpc; gl += nwarps) {
+    const int g = crank * gpc + gl;
+    if (g >= G) break;
+    float* gb = gbuf + (size_t)gl * 128 * R;
+    // this lane's pairs p = lane, lane + 32 for every layer
+    uint32_t pij[8][2];  // (i * R) | (j * R) << 16
+    float cs[8][2], sn[8][2];
+#pragma unroll
+    for (int l = 0; l < 8; ++l) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int pp = lane + 32 * h;
+        const uint16_t pr = *reinterpret_cast<const uint16_t*>(pairs + (size_t)l * K + (size_t)g * 128 + 2 * pp);
+        pij[l][h] = ((uint32_t)(pr & 0x7F) * R) | (((uint32_t)(pr >> 8) & 0x7F) * R << 16);
+        __sincosf(half_bits_to_f32(theta[(size_t)l * (K / 2) + (size_t)g * 64 + pp]), &sn[l][h], &cs[l][h]);
+      }
+    }
+    float sc[4];
+    if (scales) {
+      const uint2 s2 = *reinterpret_cast<const uint2*>(scales + (size_t)g * 128 + 4 * lane);
+      const uint16_t* sh = reinterpret_cast<const uint16_t*>(&s2);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sc[e] = half_bits_to_f32(sh[e]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sc[e] = 1.f;
+    }
+    // load and scale R rows of this group: lane owns channels 4*lane..+3
+    float xv[R][4];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      if (r < nrows) {
+        load4(x + (row0 + r) * (int64_t)K + (size_t)g * 128 + 4 * lane, xv[r]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) xv[r][e] = 0.f;
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float col[R];
+#pragma unroll
+      for (int r = 0; r < R; ++r) col[r] = xv[r][e] * sc[e];
+      st_rows<R>(gb + (4 * lane + e) * R, col);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int l = 0; l < 8; ++l) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float a[R], b[R];
+        const int oi = pij[l][h] & 0xFFFF, oj = pij[l][h] >> 16;
+        ld_rows<R>(gb + oi, a);
+        ld_rows<R>(gb + oj, b);
+        const float c_ = cs[l][h], s_ = sn[l][h];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          const float xi = a[r], xj = b[r];
+          a[r] = xi * c_ + xj * s_;
+          b[r] = xi * (-s_) + xj * c_;
+        }
+        st_rows<R>(gb + oi, a);
+        st_rows<R>(gb + oj, b);
+      }
+      __syncwarp();
+    }
+    // fp16 store rounding of the reference and the per-row maxima
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float col[R];
+      ld_rows<R>(gb + (4 * lane + e) * R, col);
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        if (fp16_round) col[r] = round_fp16(col[r]);
+        rmax[r] = fmaxf(rmax[r], fabsf(col[r]));
+      }
+      if (fp16_round) st_rows<R>(gb + (4 * lane + e) * R, col);
+    }
+  }
+
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    float a = rmax[r];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    if (lane == 0) wmax[warp][r] = a;
+  }
+  __syncthreads();
+  if (threadIdx.x < R) {
+    float a = 0.f;
+    for (int w = 0; w < nwarps; ++w) a = fmaxf(a, wmax[w][threadIdx.x]);
+    cta_max[threadIdx.x] = a;
+  }
+  cluster.sync();
+  if (threadIdx.x < R) {
+    float a = 0.f;
+    for (int c = 0; c < csize; ++c) a = fmaxf(a, cluster.map_shared_rank(cta_max, c)[threadIdx.x]);
+    a = fmaxf(a, 1e-10f);
+    row_inv[threadIdx.x] = __fdiv_rn(127.0f, a);
+    if (crank == 0 && threadIdx.x < nrows) out_scale[row0 + threadIdx.x] = __fdiv_rn(a, 127.0f);
+  }
+  // every remote read of cta_max is done before any CTA may exit, and
+  // row_inv is visible to the whole CTA
+  cluster.sync();
+
+  for (int gl = warp; gl < gpc; gl += nwarps) {
+    const int g = crank * gpc + gl;
+    if (g >= G) break;
+    const float* gb = gbuf + (size_t)gl * 128 * R;
+    float col[4][R];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) ld_rows<R>(gb + (4 * lane + e) * R, col[e]);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      if (r < nrows) {
+        const float inv = row_inv[r];
+        uint32_t w = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) w |= ((uint32_t)(int)round_half_away(col[e][r] * inv) & 0xFFu) << (8 * e);
+        *reinterpret_cast<uint32_t*>(out_q + (row0 + r) * (int64_t)K + (size_t)g * 128 + 4 * lane) = w;
+      }
+    }
+  }
+}
+
 // Per-token int8 quantisation of an [M, K] tensor: one CTA per row.
 template <typename InT>
 __global__ void __launch_bounds__(256)
@@ -236,19 +446,52 @@ cudaError_t launch_rotate(int x_dtype, int krot, int group, const void* x, int64
   return cudaErrorInvalidValue;
 }
 
+// Cluster geometry of the fused kernel: C CTAs (<= 8, portable) split the
+// groups; each CTA runs one warp per group it owns.
+struct RotqGeom {
+  int csize, gpc, warps;
+};
+
+static RotqGeom rotq_geom(int K) {
+  const int G = K / kGroup;
+  RotqGeom g;
+  g.csize = G < 8 ? G : 8;
+  g.gpc = (G + g.csize - 1) / g.csize;
+  g.warps = g.gpc < 16 ? g.gpc : 16;
+  return g;
+}
+
+template <typename InT, int R>
+static cudaError_t launch_rotq_r(const void* x, int64_t M, int K, const uint16_t* scales, const uint16_t* theta,
+                                 const uint8_t* pairs, int fp16_round, int8_t* q, float* s, cudaStream_t st) {
+  const RotqGeom geo = rotq_geom(K);
+  const size_t smem = (size_t)geo.gpc * 128 * R * sizeof(float);
+  auto kern = rotq_cluster_kernel<InT, R>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)geo.csize, (unsigned)((M + R - 1) / R), 1);
+  cfg.blockDim = dim3((unsigned)(32 * geo.warps), 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = (unsigned)geo.csize;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<const InT*>(x), M, K, scales, theta, pairs, fp16_round, geo.gpc,
+                            q, s);
+}
+
 template <typename InT>
 static cudaError_t launch_rotq_t(const void* x, int64_t M, int K, const uint16_t* scales, const uint16_t* theta,
                                  const uint8_t* pairs, int fp16_round, int8_t* q, float* s, cudaStream_t st) {
-  const int rows = rows_for(K, sizeof(float));
-  if (rows < 1) return cudaErrorInvalidValue;
-  const size_t smem = kRotWarps * kGroup * sizeof(float) + (size_t)rows * K * sizeof(float);
-  auto kern = rot_kernel<InT, InT, uint8_t, 8, 128, 1>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
-  dim3 grid((unsigned)((M + rows - 1) / rows));
-  kern<<<grid, kRotThreads, smem, st>>>(static_cast<const InT*>(x), M, K, scales, theta, PARO_F16, pairs, rows,
-                                        fp16_round, nullptr, q, s);
-  return cudaGetLastError();
+  if (M <= 1) return launch_rotq_r<InT, 1>(x, M, K, scales, theta, pairs, fp16_round, q, s, st);
+  if (M <= 2) return launch_rotq_r<InT, 2>(x, M, K, scales, theta, pairs, fp16_round, q, s, st);
+  if (M <= 4) return launch_rotq_r<InT, 4>(x, M, K, scales, theta, pairs, fp16_round, q, s, st);
+  return launch_rotq_r<InT, 8>(x, M, K, scales, theta, pairs, fp16_round, q, s, st);
 }
 
 cudaError_t launch_rotq(int x_dtype, const void* x, int64_t M, int K, const uint16_t* scales, const uint16_t* theta,
@@ -261,7 +504,9 @@ cudaError_t launch_rotq(int x_dtype, const void* x, int64_t M, int K, const uint
   return cudaErrorInvalidValue;
 }
 
-int rotq_max_k() { return (int)((160 * 1024 - kRotWarps * kGroup * sizeof(float)) / sizeof(float)); }
+// Largest K the fused kernel accepts: the rows it keeps resident
+// (gpc groups x 128 channels x 8 rows x 4 bytes per CTA) must fit in 200 KB.
+int rotq_max_k() { return 8 * 48 * kGroup; }
 
 cudaError_t launch_quant(int x_dtype, const void* x, int64_t M, int K, int8_t* q, float* s, cudaStream_t st) {
   dim3 grid((unsigned)M);

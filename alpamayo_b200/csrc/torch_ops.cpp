@@ -12,6 +12,10 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/library.h>
 
+#include <map>
+#include <mutex>
+#include <utility>
+
 #include "../../include/paro_b200.h"
 
 namespace {
@@ -32,6 +36,27 @@ void check_status(int s, const char* what) {
 }
 
 paro_stream_t cur_stream() { return reinterpret_cast<paro_stream_t>(at::cuda::getCurrentCUDAStream().stream()); }
+
+// GEMM workspace: one zero-filled buffer per (device, stream), kept for the
+// life of the process (the kernels leave it zero-filled after every call, so
+// it is reused without clearing; separate streams get separate buffers so
+// concurrent calls do not share it).  It is allocated with at least 16 MiB on
+// first use so later, larger calls (and CUDA graphs captured after a warm-up
+// call) keep a stable address; it only grows for larger shapes.
+void* workspace_for(const c10::Device& dev, size_t bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<int, cudaStream_t>, at::Tensor> cache;
+  std::lock_guard<std::mutex> lock(mu);
+  const auto key = std::make_pair((int)dev.index(), at::cuda::getCurrentCUDAStream().stream());
+  auto it = cache.find(key);
+  if (it == cache.end() || (size_t)it->second.numel() < bytes) {
+    const size_t want = std::max(bytes, (size_t)16 << 20);
+    at::Tensor t = at::zeros({(int64_t)want}, at::TensorOptions().device(dev).dtype(at::kByte));
+    cache[key] = t;
+    return t.data_ptr();
+  }
+  return it->second.data_ptr();
+}
 
 void check_cuda(const at::Tensor& t, const char* name) {
   TORCH_CHECK(t.is_cuda(), "paro_b200: ", name, " must be a CUDA tensor");
@@ -200,11 +225,9 @@ at::Tensor w4a8_gemm(const at::Tensor& xq_in, const at::Tensor& xscale_in, const
   osz.back() = N;
   at::Tensor out = at::empty(osz, xq.options().dtype(out_dtype));
   const size_t ws = paro_w4a8_gemm_workspace_size(M, (int)N, (int)K);
-  at::Tensor wst;
-  if (ws) wst = at::empty({(int64_t)ws}, xq.options().dtype(at::kByte));
+  void* wsp = ws ? workspace_for(xq.device(), ws) : nullptr;
   check_status(paro_w4a8_gemm(xq.data_ptr<int8_t>(), xscale.data_ptr<float>(), M, (int)N, (int)K, packed.data_ptr(),
-                              bp, bdt, out.data_ptr(), to_paro_dtype(out_dtype), ws ? wst.data_ptr() : nullptr, ws,
-                              cur_stream()),
+                              bp, bdt, out.data_ptr(), to_paro_dtype(out_dtype), wsp, ws, cur_stream()),
                "w4a8_gemm");
   return out;
 }

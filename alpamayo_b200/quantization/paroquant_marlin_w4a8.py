@@ -184,7 +184,10 @@ class MarlinW4A8Linear(nn.Module):
         self.register_buffer("g_idx", torch.empty(0, dtype=torch.int32))
         self.register_buffer("g_idx_sort_indices", torch.empty(0, dtype=torch.int32))
         self.register_buffer("input_global_scale", torch.ones(1, dtype=torch.float32))
-        self.bias = None
+        # registered up front so a bias tensor can be assigned later (the
+        # reference sets a plain attribute and then registers over it, which
+        # torch rejects for layers that do have a bias)
+        self.register_buffer("bias", None)
 
     def load_from_awq(self, awq_qweight, awq_scales, awq_qzeros, bias=None):
         K, N = self.in_features, self.out_features
@@ -194,10 +197,7 @@ class MarlinW4A8Linear(nn.Module):
         self.qzeros = awq_qzeros.contiguous()
         self.workspace = torch.empty(0, dtype=torch.int32, device=awq_qweight.device)
         self.input_global_scale = torch.ones(1, dtype=torch.float32, device=awq_qweight.device)
-        if bias is not None:
-            self.register_buffer("bias", bias)
-        else:
-            self.bias = None
+        self.bias = bias
 
     def load_from_wqlinear(self, qweight_i16, scales, scaled_zeros, bias=None):
         """Direct WQLinear -> tile records (same codes and zero points as the
@@ -207,10 +207,7 @@ class MarlinW4A8Linear(nn.Module):
         self.qweight = ops.prepare_weights(qweight_i16.contiguous(), scales.to(torch.float16).contiguous(),
                                            scaled_zeros.to(torch.float16).contiguous(), N, K)
         self.scales = scales[:G, :N].to(torch.float16).contiguous()
-        if bias is not None:
-            self.register_buffer("bias", bias)
-        else:
-            self.bias = None
+        self.bias = bias
 
     def packed_weight(self):
         return self.qweight

@@ -173,8 +173,11 @@ int paro_prepare_weights_awq(const int32_t* awq_qweight, const uint16_t* awq_sca
  *   packed    : tile records from paro_prepare_weights*.
  *   bias      : [N] of bias_dtype (F16 / BF16 / F32) or NULL.
  *   out       : [M, N] of out_dtype.
- *   workspace : at least paro_w4a8_gemm_workspace_size(M, N, K) bytes
- *               (may be NULL when that size is 0).
+ *   workspace : at least paro_w4a8_gemm_workspace_size(M, N, K) bytes,
+ *               256-byte aligned, ZERO-FILLED before its first use.  Every
+ *               call leaves it zero-filled again (the kernels clear what they
+ *               use), so one buffer serves all calls on one stream; calls that
+ *               may run concurrently need separate workspaces.
  * Requires N % 16 == 0, K % 128 == 0, M >= 1.
  */
 size_t paro_w4a8_gemm_workspace_size(int64_t M, int N, int K);
@@ -183,6 +186,11 @@ int paro_w4a8_gemm(const int8_t* xq, const float* xscale, int64_t M, int N, int 
                    const void* packed, const void* bias, int bias_dtype,
                    void* out, int out_dtype, void* workspace, size_t workspace_bytes,
                    paro_stream_t stream);
+
+/* Error bits kernels raise instead of hanging (1 = a pipeline wait timed
+ * out, 2 = tensor-memory allocation failed); synchronises with the device to
+ * read them.  clear != 0 resets the word.  Returns -1 if it cannot be read. */
+int paro_device_error_word(int clear);
 
 /* Which GEMM kernel paro_w4a8_gemm would launch for this shape
  * (0 = streaming decode kernel, 1 = tcgen05 tensor-core kernel). */

@@ -90,7 +90,7 @@ def test_marlin_module_from_awq_buffers():
     y = mod(xr)
     assert y.dtype == torch.float16
     q, s = O.per_token_quant_int8(xr.float().cpu().numpy())
-    ref = O.w4a8_linear(q, s, d["unpacked"], d["awq_zeros"].T, d["awq_scales"].astype(np.float32))
+    ref = O.w4a8_linear(q, s, d["unpacked"], d["awq_zeros"], d["awq_scales"].astype(np.float32))
     assert rel_l2(y.float().cpu().numpy(), O.round_to_fp16(ref)) <= 1e-3
     mod2, awq = convert_wqlinear_layer(torch.from_numpy(d["qweight"]), torch.from_numpy(d["wq_scales"]),
                                        torch.from_numpy(d["wq_scaled_zeros"]), N, K, 128)
