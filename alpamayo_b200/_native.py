@@ -54,9 +54,9 @@ def capi() -> ctypes.CDLL:
         "paro_status_string": (ctypes.c_char_p, [i32]),
         "paro_version": (i32, []),
         "paro_last_cuda_error": (ctypes.c_char_p, []),
-        "paro_prepare_rotation": (i32, [vp, i32, i32, i32, vp, vp, vp]),
+        "paro_prepare_rotation": (i32, [vp, vp, i32, i32, i32, vp, vp, vp]),
         "paro_rotate": (i32, [vp, i32, i64, i32, vp, vp, i32, vp, i32, i32, vp, vp]),
-        "paro_rotq_int8": (i32, [vp, i32, i64, i32, vp, vp, vp, i32, i32, i32, vp, vp, vp]),
+        "paro_rotq_int8": (i32, [vp, i32, i64, i32, vp, vp, i32, i32, i32, vp, vp, vp]),
         "paro_quant_int8": (i32, [vp, i32, i64, i32, vp, vp, vp]),
         "paro_packed_weight_bytes": (sz, [i32, i32]),
         "paro_prepare_weights": (i32, [vp, vp, vp, i32, i32, i32, vp, vp]),

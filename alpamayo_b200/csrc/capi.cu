@@ -13,12 +13,12 @@
 namespace paro {
 cudaError_t launch_rotate(int x_dtype, int krot, int group, const void* x, int64_t M, int K, const void* scales,
                           const void* theta, int pdt, const int16_t* pairs, void* out, cudaStream_t st);
-cudaError_t launch_rotq(int x_dtype, const void* x, int64_t M, int K, const uint16_t* scales, const uint16_t* theta,
-                        const uint8_t* pairs, int fp16_round, int8_t* q, float* s, cudaStream_t st);
+cudaError_t launch_rotq(int x_dtype, const void* x, int64_t M, int K, const uint16_t* scales, const uint32_t* rtab,
+                        int fp16_round, int8_t* q, float* s, cudaStream_t st);
 int rotq_max_k();
 cudaError_t launch_quant(int x_dtype, const void* x, int64_t M, int K, int8_t* q, float* s, cudaStream_t st);
-cudaError_t launch_prepare_rotation(const int16_t* pairs, int krot, int K, int group, uint8_t* out, int32_t* bad,
-                                    cudaStream_t st);
+cudaError_t launch_prepare_rotation(const int16_t* pairs, const uint16_t* theta, int krot, int K, int group,
+                                    uint32_t* out, int32_t* bad, cudaStream_t st);
 cudaError_t launch_prepare_wq(const int16_t* qweight, const uint16_t* scales, const uint16_t* scaled_zeros, int N,
                               int K, void* packed, cudaStream_t st);
 cudaError_t launch_prepare_awq(const int32_t* qweight, const uint16_t* scales, const int32_t* qzeros, int N, int K,
@@ -83,13 +83,13 @@ int paro_version(void) { return 100; }
 
 const char* paro_last_cuda_error(void) { return g_last_cuda_error.c_str(); }
 
-int paro_prepare_rotation(const int16_t* pairs, int krot, int K, int group, uint8_t* out_u8, int32_t* bad,
-                          paro_stream_t stream) {
-  if (!pairs || !out_u8 || !bad || krot <= 0 || K <= 0) return PARO_ERR_INVALID_ARGUMENT;
-  if (group != 64 && group != 128) return PARO_ERR_UNSUPPORTED;
+int paro_prepare_rotation(const int16_t* pairs, const uint16_t* theta, int krot, int K, int group,
+                          uint32_t* out_table, int32_t* bad, paro_stream_t stream) {
+  if (!pairs || !theta || !out_table || !bad || krot <= 0 || K <= 0) return PARO_ERR_INVALID_ARGUMENT;
+  if (group != 128) return PARO_ERR_UNSUPPORTED;
   if (K % group) return PARO_ERR_SHAPE;
   if (int d = device_check()) return d;
-  return cuda_status(launch_prepare_rotation(pairs, krot, K, group, out_u8, bad, (cudaStream_t)stream));
+  return cuda_status(launch_prepare_rotation(pairs, theta, krot, K, group, out_table, bad, (cudaStream_t)stream));
 }
 
 int paro_rotate(const void* x, int x_dtype, int64_t M, int K, const void* scales, const void* theta,
@@ -107,22 +107,20 @@ int paro_rotate(const void* x, int x_dtype, int64_t M, int K, const void* scales
       launch_rotate(x_dtype, krot, group, x, M, K, scales, theta, param_dtype, pairs, out, (cudaStream_t)stream));
 }
 
-int paro_rotq_int8(const void* x, int x_dtype, int64_t M, int K, const uint16_t* scales, const uint16_t* theta,
-                   const uint8_t* pairs_u8, int krot, int group, int fp16_round, int8_t* out_q, float* out_scale,
-                   paro_stream_t stream) {
+int paro_rotq_int8(const void* x, int x_dtype, int64_t M, int K, const uint16_t* scales, const uint32_t* rot_table,
+                   int krot, int group, int fp16_round, int8_t* out_q, float* out_scale, paro_stream_t stream) {
   if (M == 0 && K > 0) return PARO_OK;
-  if (!x || !theta || !pairs_u8 || !out_q || !out_scale || K <= 0 || M < 0) return PARO_ERR_INVALID_ARGUMENT;
+  if (!x || !rot_table || !out_q || !out_scale || K <= 0 || M < 0) return PARO_ERR_INVALID_ARGUMENT;
   if (!valid_dtype(x_dtype)) return PARO_ERR_UNSUPPORTED;
   if (krot != 8 || group != 128) return PARO_ERR_UNSUPPORTED;  // Rotation supports only these (rotation_linear.py:18-19)
   if (K % group) return PARO_ERR_SHAPE;
   if (K > rotq_max_k()) return PARO_ERR_TOO_LARGE;
-  if (!aligned(out_q, 16) || !aligned(x, x_dtype == PARO_F32 ? 16 : 8) || (scales && !aligned(scales, 8)) ||
-      !aligned(pairs_u8, 2) || !aligned(theta, 2))
+  if (!aligned(x, x_dtype == PARO_F32 ? 4 : 2) || (scales && !aligned(scales, 2)) || !aligned(rot_table, 4))
     return PARO_ERR_MISALIGNED;
   if (M == 0) return PARO_OK;
   if (int d = device_check()) return d;
   return cuda_status(
-      launch_rotq(x_dtype, x, M, K, scales, theta, pairs_u8, fp16_round ? 1 : 0, out_q, out_scale, (cudaStream_t)stream));
+      launch_rotq(x_dtype, x, M, K, scales, rot_table, fp16_round ? 1 : 0, out_q, out_scale, (cudaStream_t)stream));
 }
 
 int paro_quant_int8(const void* x, int x_dtype, int64_t M, int K, int8_t* out_q, float* out_scale,

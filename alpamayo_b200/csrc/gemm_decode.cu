@@ -7,34 +7,44 @@
 //  * Persistent, load-balanced grid ("stream-K"): the layer's tile records —
 //    one per (16-row block nb, 128-channel group g), stored nb-major so each
 //    row block's K strip is contiguous — are split into one contiguous range
-//    per CTA.  A CTA's range spans parts of a few row blocks (segments).
-//  * TMA bulk copies: one producer thread streams the range through an
-//    8-stage shared-memory ring (cp.async.bulk + mbarrier complete_tx).  A
-//    chunk holds up to 8 records of one row block, one per consumer warp.
-//  * 8 consumer warps expand each record's int4 codes to int8 (q - z) in
-//    registers and run int8 mma.sync m16n8k32 against the token tile
-//    (B fragments read from the L1-cached activations).  Each group's int32
-//    accumulator is exact and is scaled into float32 per group.
-//  * Segment end: the warps' partial sums are reduced in shared memory.  A
-//    segment covering the whole row block is finished in place (token scale,
-//    bias, store).  A boundary segment shared with a neighbouring CTA adds its
-//    partial into a float32 workspace (red.global.add) and bumps the row
+//    per CTA.  A CTA's range covers parts of a few row blocks (segments).
+//  * TMA bulk copies: one producer thread streams the range through a shared
+//    memory ring (cp.async.bulk + mbarrier complete_tx).  A chunk holds the
+//    records of up to 16 consecutive groups of one row block, aligned to
+//    16-group boundaries.
+//  * 8 consumer warps; warp w owns the groups g = w (mod 8), so each chunk
+//    gives every warp up to two independent records, and the activation
+//    fragments a warp needs are the same for every row block.  The token
+//    activations are staged once per CTA in shared memory in mma fragment
+//    order (falls back to L1-cached global loads when they do not fit).
+//  * Each record's int4 codes are expanded to int8 (q - z) in registers and
+//    fed to int8 mma.sync m16n8k32 (A = 16 weight rows x 32 channels, B = 8
+//    tokens); each group's int32 sum is exact and is scaled into float32.
+//  * Segment end: partial sums of the 8 warps are reduced in shared memory.
+//    A segment covering a whole row block is finished in place (token scale,
+//    bias, store).  A boundary segment shared with a neighbouring CTA adds
+//    its partial into a float32 workspace (red.global.add) and bumps the row
 //    block's unit counter; the CTA that completes the count applies the
 //    epilogue and returns the workspace slice and counter to zero, so the
 //    workspace is zero again after every call.
+//  * Programmatic dependent launch: the weight stream starts before the
+//    activation kernel that produces this GEMM's input has finished; only
+//    the reads of the activations wait (griddepcontrol.wait).
 //
-// The record layout puts, for lane (gid = lane/4, tig = lane%4), the A
-// fragment words of rows gid and gid+8 for all four 32-channel steps of a
-// group in one 16-byte chunk each: low nibbles give a0/a1, high nibbles a2/a3.
+// Record layout: for lane (gid = lane/4, tig = lane%4), the A fragment words
+// of rows gid and gid+8 for the four 32-channel steps of a group are one
+// 16-byte chunk each: low nibbles give a0/a1, high nibbles a2/a3.
 #include "tc_ptx.cuh"
 
 namespace paro {
 
 constexpr int kDecConsumers = 8;
 constexpr int kDecThreads = 32 * (kDecConsumers + 1);
-constexpr int kDecStages = 8;
-constexpr int kDecStageBytes = kDecConsumers * kRecBytes;
-constexpr int kDecMaxTokens = 64;  // tokens per CTA slice (8 tiles of 8)
+constexpr int kDecChunkGroups = 16;
+constexpr int kDecStageBytes = kDecChunkGroups * kRecBytes;  // 17152
+constexpr int kDecMaxStages = 8;
+constexpr int kDecMaxTokens = 64;   // tokens per CTA slice (8 tiles of 8)
+constexpr int kDecSmemBudget = 220 * 1024;
 
 struct DecParams {
   const int8_t* xq;
@@ -50,7 +60,11 @@ struct DecParams {
   uint32_t* cnt;    // [token slices][N/16] unit counters, zero between calls
   int64_t units;    // (N/16) * G
   int ctas;
+  int stages;
 };
+
+__host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
+__host__ __device__ __forceinline__ int64_t max64(int64_t a, int64_t b) { return a > b ? a : b; }
 
 __device__ __forceinline__ uint32_t expand_lo(uint32_t w, uint32_t zz) {
   // bytes 0x80 + q - z (no borrows since q, z <= 15), then flip the bias bit
@@ -69,6 +83,8 @@ __device__ __forceinline__ void mma_s8(int (&c)[4], uint32_t a0, uint32_t a1, ui
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ float bias_at(const void* bias, int dtype, int n) {
   if (!bias) return 0.f;
   if (dtype == PARO_F16) return __half2float(static_cast<const __half*>(bias)[n]);
@@ -82,33 +98,82 @@ __device__ __forceinline__ void store_out(void* out, int dtype, size_t idx, floa
   else static_cast<float*>(out)[idx] = v;
 }
 
-// End of the chunk that starts at unit u: at most one record per consumer
-// warp and never past the end of u's row block or of the CTA's range.
-__host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
-__host__ __device__ __forceinline__ int64_t max64(int64_t a, int64_t b) { return a > b ? a : b; }
-
+// End of the chunk starting at unit u: the next 16-group boundary of u's
+// row block, the row block's end, or the CTA range end.
 __device__ __forceinline__ int64_t chunk_end(int64_t u, int64_t u1, int G) {
-  const int64_t seg_end = min64(u1, (u / G + 1) * (int64_t)G);
-  return min64(u + kDecConsumers, seg_end);
+  const int64_t nb = u / G;
+  const int g = (int)(u - nb * G);
+  const int gend = min(G, (g / kDecChunkGroups + 1) * kDecChunkGroups);
+  return min64(u1, nb * G + gend);
+}
+
+// The 8 B-fragment words of (token tile, group g) for this lane: b0/b1 of
+// the four 32-channel steps.
+__device__ __forceinline__ void load_bfrag_global(const int8_t* xrow, bool valid, int g, uint32_t (&b)[8]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int8_t* xp = xrow + (size_t)g * kGroup + 32 * j;
+    b[2 * j] = valid ? ldg_nc_u32(xp) : 0u;
+    b[2 * j + 1] = valid ? ldg_nc_u32(xp + 16) : 0u;
+  }
 }
 
 template <int MT>
+__device__ __forceinline__ void process_record(const uint8_t* rec, const uint32_t (&bf)[MT][8], int gid, int tig,
+                                               float (&y)[MT][4]) {
+  const uint4 wa = *reinterpret_cast<const uint4*>(rec + gid * 64 + tig * 16);
+  const uint4 wb = *reinterpret_cast<const uint4*>(rec + (gid + 8) * 64 + tig * 16);
+  const uint16_t* sp = reinterpret_cast<const uint16_t*>(rec + kRecScaleOff);
+  const float s_lo = half_bits_to_f32(sp[gid]), s_hi = half_bits_to_f32(sp[gid + 8]);
+  const uint32_t zz_lo = (uint32_t)rec[kRecZeroOff + gid] * 0x01010101u;
+  const uint32_t zz_hi = (uint32_t)rec[kRecZeroOff + gid + 8] * 0x01010101u;
+  const uint32_t wA[4] = {wa.x, wa.y, wa.z, wa.w};
+  const uint32_t wB[4] = {wb.x, wb.y, wb.z, wb.w};
+  // two independent accumulator chains (k-steps 0,1 and 2,3)
+  int acc[2][MT][4];
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[h][mt][i] = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t a0 = expand_lo(wA[j], zz_lo), a2 = expand_hi(wA[j], zz_lo);
+    const uint32_t a1 = expand_lo(wB[j], zz_hi), a3 = expand_hi(wB[j], zz_hi);
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) mma_s8(acc[j >> 1][mt], a0, a1, a2, a3, bf[mt][2 * j], bf[mt][2 * j + 1]);
+  }
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) {
+    y[mt][0] = fmaf(s_lo, (float)(acc[0][mt][0] + acc[1][mt][0]), y[mt][0]);
+    y[mt][1] = fmaf(s_lo, (float)(acc[0][mt][1] + acc[1][mt][1]), y[mt][1]);
+    y[mt][2] = fmaf(s_hi, (float)(acc[0][mt][2] + acc[1][mt][2]), y[mt][2]);
+    y[mt][3] = fmaf(s_hi, (float)(acc[0][mt][3] + acc[1][mt][3]), y[mt][3]);
+  }
+}
+
+// XS: activations staged in shared memory (fragment order) instead of read
+// from global memory per record.
+template <int MT, bool XS>
 __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kDecStages * kDecStageBytes);
-  uint64_t* empty = full + kDecStages;
-  float* red = reinterpret_cast<float*>(empty + kDecStages);  // [consumers][MT*4][32]
+  const int S = p.stages;
+  const int G = p.K / kGroup;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * kDecStageBytes);
+  uint64_t* empty = full + kDecMaxStages;
+  float* red = reinterpret_cast<float*>(empty + kDecMaxStages);                 // [8][MT*4][32]
+  uint4* xs = reinterpret_cast<uint4*>(red + kDecConsumers * MT * 4 * 32);    // [G][MT][32][2]
   __shared__ int last_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int G = p.K / kGroup;
   const int64_t u0 = (int64_t)blockIdx.x * p.units / p.ctas;
   const int64_t u1 = (int64_t)(blockIdx.x + 1) * p.units / p.ctas;
   const int64_t tok0 = (int64_t)blockIdx.y * kDecMaxTokens;
   uint32_t* cnt = p.cnt + (size_t)blockIdx.y * (p.N / kRecRows);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kDecStages; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kDecConsumers);
     }
@@ -116,13 +181,13 @@ __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p
   }
   __syncthreads();
 
-  if (warp == 0) {  // producer
+  if (warp == 0) {  // producer: weights do not depend on the previous kernel
     if (lane == 0) {
       int64_t u = u0;
       for (int k = 0; u < u1; ++k) {
         const int64_t ce = chunk_end(u, u1, G);
-        const int s = k % kDecStages;
-        if (k >= kDecStages && !mbar_wait(&empty[s], ((k / kDecStages) - 1) & 1)) break;
+        const int s = k % S;
+        if (k >= S && !mbar_wait(&empty[s], ((k / S) - 1) & 1)) break;
         const uint32_t bytes = (uint32_t)(ce - u) * kRecBytes;
         mbar_arrive_expect_tx(&full[s], bytes);
         bulk_g2s(smem + (size_t)s * kDecStageBytes, p.packed + u * kRecBytes, bytes, &full[s]);
@@ -144,6 +209,20 @@ __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p
     xvalid[mt] = t < p.M;
     xrow[mt] = p.xq + (xvalid[mt] ? t : 0) * (int64_t)p.K + 4 * tig;
   }
+  grid_dependency_wait();  // the activations come from the previous kernel
+  if constexpr (XS) {
+    for (int e = ctid; e < G * MT * 32; e += kDecConsumers * 32) {
+      const int l = e & 31, gm = e >> 5, mt = gm % MT, g = gm / MT;
+      const int lgid = l >> 2, ltig = l & 3;
+      const int64_t t = tok0 + mt * 8 + lgid;
+      uint32_t b[8];
+      load_bfrag_global(p.xq + (t < p.M ? t : 0) * (int64_t)p.K + 4 * ltig, t < p.M, g, b);
+      xs[2 * e] = make_uint4(b[0], b[1], b[2], b[3]);
+      xs[2 * e + 1] = make_uint4(b[4], b[5], b[6], b[7]);
+    }
+    named_barrier(1, kDecConsumers * 32);
+  }
+
   float y[MT][4];
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt)
@@ -153,50 +232,28 @@ __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p
   int64_t u = u0;
   for (int k = 0; u < u1; ++k) {
     const int64_t ce = chunk_end(u, u1, G);
-    const int s = k % kDecStages;
-    const int64_t my = u + cw;
-    const bool have = my < ce;
-    const int g = (int)(my % G);
-    // activation fragments of this warp's group (independent of the stage)
-    uint32_t bf[MT][4][2];
+    const int s = k % S;
+    const int64_t nb = u / G;
+    const int gbase = (int)(u - nb * G) / kDecChunkGroups * kDecChunkGroups;
+    if (!mbar_wait(&full[s], (k / S) & 1)) return;
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
+    for (int slot = 0; slot < 2; ++slot) {
+      const int g = gbase + slot * 8 + cw;
+      const int64_t ur = nb * G + g;
+      if (ur >= u && ur < ce) {
+        uint32_t bf[MT][8];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int8_t* xp = xrow[mt] + (size_t)g * kGroup + 32 * j;
-        const bool v = have && xvalid[mt];
-        bf[mt][j][0] = v ? ldg_nc_u32(xp) : 0u;
-        bf[mt][j][1] = v ? ldg_nc_u32(xp + 16) : 0u;
-      }
-    if (!mbar_wait(&full[s], (k / kDecStages) & 1)) return;
-    if (have) {
-      const uint8_t* rec = smem + (size_t)s * kDecStageBytes + cw * kRecBytes;
-      const uint4 wa = *reinterpret_cast<const uint4*>(rec + gid * 64 + tig * 16);
-      const uint4 wb = *reinterpret_cast<const uint4*>(rec + (gid + 8) * 64 + tig * 16);
-      const uint16_t* sp = reinterpret_cast<const uint16_t*>(rec + kRecScaleOff);
-      const float s_lo = half_bits_to_f32(sp[gid]), s_hi = half_bits_to_f32(sp[gid + 8]);
-      const uint32_t zz_lo = (uint32_t)rec[kRecZeroOff + gid] * 0x01010101u;
-      const uint32_t zz_hi = (uint32_t)rec[kRecZeroOff + gid + 8] * 0x01010101u;
-      const uint32_t wA[4] = {wa.x, wa.y, wa.z, wa.w};
-      const uint32_t wB[4] = {wb.x, wb.y, wb.z, wb.w};
-      int acc[MT][4];
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) acc[mt][i] = 0;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint32_t a0 = expand_lo(wA[j], zz_lo), a2 = expand_hi(wA[j], zz_lo);
-        const uint32_t a1 = expand_lo(wB[j], zz_hi), a3 = expand_hi(wB[j], zz_hi);
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt) mma_s8(acc[mt], a0, a1, a2, a3, bf[mt][j][0], bf[mt][j][1]);
-      }
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        y[mt][0] = fmaf(s_lo, (float)acc[mt][0], y[mt][0]);
-        y[mt][1] = fmaf(s_lo, (float)acc[mt][1], y[mt][1]);
-        y[mt][2] = fmaf(s_hi, (float)acc[mt][2], y[mt][2]);
-        y[mt][3] = fmaf(s_hi, (float)acc[mt][3], y[mt][3]);
+        for (int mt = 0; mt < MT; ++mt) {
+          if constexpr (XS) {
+            const uint4* xp = xs + 2 * ((g * MT + mt) * 32 + lane);
+            const uint4 lo = xp[0], hi = xp[1];
+            bf[mt][0] = lo.x; bf[mt][1] = lo.y; bf[mt][2] = lo.z; bf[mt][3] = lo.w;
+            bf[mt][4] = hi.x; bf[mt][5] = hi.y; bf[mt][6] = hi.z; bf[mt][7] = hi.w;
+          } else {
+            load_bfrag_global(xrow[mt], xvalid[mt], g, bf[mt]);
+          }
+        }
+        process_record<MT>(smem + (size_t)s * kDecStageBytes + (size_t)(ur - u) * kRecBytes, bf, gid, tig, y);
       }
     }
     __syncwarp();
@@ -204,7 +261,6 @@ __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p
 
     const bool seg_done = (ce == u1) || (ce % G == 0);
     if (seg_done) {
-      const int64_t nb = (ce - 1) / G;
       const int64_t seg_begin = max64(u0, nb * (int64_t)G);
       const int seg_units = (int)(ce - seg_begin);
       const bool whole = seg_units == G;
@@ -221,8 +277,10 @@ __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p
         const int64_t t = tok0 + mt * 8 + 2 * tig + (i & 1);
         const int n = (int)nb * kRecRows + gid + ((i >> 1) << 3);
         if (t < p.M) {
-          if (whole) store_out(p.out, p.out_dtype, (size_t)t * p.N + n, v * p.xscale[t] + bias_at(p.bias, p.bias_dtype, n));
-          else red_add_f32(p.ws + (size_t)n * p.M + t, v);
+          if (whole)
+            store_out(p.out, p.out_dtype, (size_t)t * p.N + n, v * p.xscale[t] + bias_at(p.bias, p.bias_dtype, n));
+          else
+            red_add_f32(p.ws + (size_t)n * p.M + t, v);
         }
       }
       if (!whole) {
@@ -269,19 +327,41 @@ size_t gemm_decode_workspace(int64_t M, int N) {
   return ws + (size_t)slices * (N / kRecRows) * sizeof(uint32_t);
 }
 
-size_t gemm_decode_smem(int MT) {
-  return (size_t)kDecStages * kDecStageBytes + 2 * kDecStages * sizeof(uint64_t) +
-         (size_t)kDecConsumers * MT * 4 * 32 * sizeof(float);
+static size_t fixed_smem(int MT) {
+  return 2 * kDecMaxStages * sizeof(uint64_t) + (size_t)kDecConsumers * MT * 4 * 32 * sizeof(float);
+}
+
+template <int MT, bool XS>
+static cudaError_t launch_mt(DecParams p, size_t xs_bytes, cudaStream_t st) {
+  const size_t smem = (size_t)p.stages * kDecStageBytes + fixed_smem(MT) + (XS ? xs_bytes : 0);
+  auto kern = gemm_stream_kernel<MT, XS>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)p.ctas, (unsigned)((p.M + kDecMaxTokens - 1) / kDecMaxTokens), 1);
+  cfg.blockDim = dim3(kDecThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
 template <int MT>
-static cudaError_t launch_mt(DecParams p, cudaStream_t st) {
-  const size_t smem = gemm_decode_smem(MT);
-  cudaError_t e = cudaFuncSetAttribute(gemm_stream_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
-  dim3 grid(p.ctas, (unsigned)((p.M + kDecMaxTokens - 1) / kDecMaxTokens));
-  gemm_stream_kernel<MT><<<grid, kDecThreads, smem, st>>>(p);
-  return cudaGetLastError();
+static cudaError_t launch_pick(DecParams p, cudaStream_t st) {
+  const int G = p.K / kGroup;
+  const size_t xs_bytes = (size_t)G * MT * 32 * 32;
+  const size_t base = fixed_smem(MT);
+  const bool xs = base + xs_bytes + 3 * (size_t)kDecStageBytes <= (size_t)kDecSmemBudget;
+  const size_t avail = kDecSmemBudget - base - (xs ? xs_bytes : 0);
+  int stages = (int)(avail / kDecStageBytes);
+  stages = stages > kDecMaxStages ? kDecMaxStages : stages;
+  if (stages < 2) return cudaErrorInvalidValue;
+  p.stages = stages;
+  return xs ? launch_mt<MT, true>(p, xs_bytes, st) : launch_mt<MT, false>(p, xs_bytes, st);
 }
 
 cudaError_t launch_gemm_decode(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
@@ -304,15 +384,16 @@ cudaError_t launch_gemm_decode(const int8_t* xq, const float* xscale, int64_t M,
   p.bias_dtype = bias_dtype;
   p.out = out;
   p.out_dtype = out_dtype;
-  size_t wsf = ((size_t)N * (size_t)M * sizeof(float) + 255) & ~(size_t)255;
+  const size_t wsf = ((size_t)N * (size_t)M * sizeof(float) + 255) & ~(size_t)255;
   p.ws = static_cast<float*>(ws);
   p.cnt = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(ws) + wsf);
   p.units = (int64_t)(N / kRecRows) * (K / kGroup);
   p.ctas = (int)min64(g_num_sms, p.units);
-  if (M <= 8) return launch_mt<1>(p, st);
-  if (M <= 16) return launch_mt<2>(p, st);
-  if (M <= 32) return launch_mt<4>(p, st);
-  return launch_mt<8>(p, st);
+  p.stages = 0;
+  if (M <= 8) return launch_pick<1>(p, st);
+  if (M <= 16) return launch_pick<2>(p, st);
+  if (M <= 32) return launch_pick<4>(p, st);
+  return launch_pick<8>(p, st);
 }
 
 }  // namespace paro

@@ -17,20 +17,30 @@
 
 namespace paro {
 
-__global__ void prepare_rotation_kernel(const int16_t* __restrict__ pairs, int K, int group,
-                                        uint8_t* __restrict__ out, int32_t* __restrict__ bad) {
-  // one CTA per (layer, group) block
+// One CTA per (layer, group) block.  Entry t of the block is element (t & 1)
+// of pair t / 2.  Output, indexed by channel c: the partner channel
+// (bits 0-6, group-local), the role (bit 7: 0 = first element i of the pair,
+// 1 = second element j) and the pair's fp16 angle (bits 16-31), so the thread
+// owning channel c applies its half of the Givens update
+//   i' = c*i + s*j,  j' = -s*i + c*j
+// with one 32-bit load.
+__global__ void prepare_rotation_kernel(const int16_t* __restrict__ pairs, const uint16_t* __restrict__ theta,
+                                        int K, int group, uint32_t* __restrict__ out, int32_t* __restrict__ bad) {
   __shared__ int cnt[128];
-  const int blk = blockIdx.x;
+  const int blk = blockIdx.x;  // = layer * (K / group) + g
+  const int layer = blk / (K / group), g = blk - layer * (K / group);
   const size_t base = (size_t)blk * group;
   const int t = threadIdx.x;
   if (t < group) cnt[t] = 0;
   __syncthreads();
-  int v = -1;
   if (t < group) {
-    v = pairs[base + t];
-    if (v >= 0 && v < group) atomicAdd(&cnt[v], 1);
-    out[base + t] = (uint8_t)(v & 0xFF);
+    const int v = pairs[base + t];
+    const int w = pairs[base + (t ^ 1)];
+    if (v >= 0 && v < group) {
+      atomicAdd(&cnt[v], 1);
+      const uint32_t th = theta[(size_t)layer * (K / 2) + (size_t)g * (group / 2) + (t >> 1)];
+      out[base + v] = (uint32_t)(w & 0x7F) | ((uint32_t)(t & 1) << 7) | (th << 16);
+    }
   }
   __syncthreads();
   const int ok = (t >= group) || (cnt[t] == 1);
@@ -114,11 +124,11 @@ prepare_kernel(const void* __restrict__ qweight, const uint16_t* __restrict__ sc
   }
 }
 
-cudaError_t launch_prepare_rotation(const int16_t* pairs, int krot, int K, int group, uint8_t* out, int32_t* bad,
-                                    cudaStream_t st) {
+cudaError_t launch_prepare_rotation(const int16_t* pairs, const uint16_t* theta, int krot, int K, int group,
+                                    uint32_t* out, int32_t* bad, cudaStream_t st) {
   cudaError_t e = cudaMemsetAsync(bad, 0, sizeof(int32_t), st);
   if (e != cudaSuccess) return e;
-  prepare_rotation_kernel<<<krot * (K / group), 128, 0, st>>>(pairs, K, group, out, bad);
+  prepare_rotation_kernel<<<krot * (K / group), 128, 0, st>>>(pairs, theta, K, group, out, bad);
   return cudaGetLastError();
 }
 

@@ -91,16 +91,22 @@ at::Tensor rotate(const at::Tensor& x_in, const at::Tensor& idx_ij, const at::Te
   return out;
 }
 
-// Validates and narrows the pair table (synchronises once to read the
-// validation count: load-time only).
-at::Tensor prepare_rotation(const at::Tensor& pairs, int64_t group_size) {
+// Validates the pair table and builds the per-channel rotation table
+// (synchronises once to read the validation count: load-time only).  The
+// uint32 table is returned in an int32 tensor.
+at::Tensor prepare_rotation(const at::Tensor& pairs, const at::Tensor& theta, int64_t group_size) {
   check_cuda(pairs, "pairs");
+  check_cuda(theta, "theta");
   TORCH_CHECK(pairs.scalar_type() == at::kShort, "pairs must be int16");
+  TORCH_CHECK(theta.scalar_type() == at::kHalf, "theta must be float16");
+  TORCH_CHECK(theta.size(0) == pairs.size(0) && theta.size(1) * 2 == pairs.size(1), "theta must be [krot, K/2]");
   c10::cuda::CUDAGuard guard(pairs.device());
-  at::Tensor out = at::empty(pairs.sizes(), pairs.options().dtype(at::kByte));
+  at::Tensor out = at::empty(pairs.sizes(), pairs.options().dtype(at::kInt));
   at::Tensor bad = at::empty({1}, pairs.options().dtype(at::kInt));
-  check_status(paro_prepare_rotation(pairs.data_ptr<int16_t>(), (int)pairs.size(0), (int)pairs.size(1),
-                                     (int)group_size, out.data_ptr<uint8_t>(), bad.data_ptr<int32_t>(), cur_stream()),
+  check_status(paro_prepare_rotation(pairs.data_ptr<int16_t>(), reinterpret_cast<const uint16_t*>(theta.data_ptr()),
+                                     (int)pairs.size(0), (int)pairs.size(1), (int)group_size,
+                                     reinterpret_cast<uint32_t*>(out.data_ptr<int32_t>()), bad.data_ptr<int32_t>(),
+                                     cur_stream()),
                "prepare_rotation");
   const int nbad = bad.item<int32_t>();
   TORCH_CHECK(nbad == 0, "paro_b200::prepare_rotation: ", nbad,
@@ -109,15 +115,14 @@ at::Tensor prepare_rotation(const at::Tensor& pairs, int64_t group_size) {
   return out;
 }
 
-std::tuple<at::Tensor, at::Tensor> rotq_int8(const at::Tensor& x_in, const at::Tensor& pairs_u8,
-                                             const at::Tensor& theta, const c10::optional<at::Tensor>& scales_opt,
-                                             int64_t group_size, bool fp16_round) {
+std::tuple<at::Tensor, at::Tensor> rotq_int8(const at::Tensor& x_in, const at::Tensor& rot_table,
+                                             const c10::optional<at::Tensor>& scales_opt, int64_t group_size,
+                                             bool fp16_round) {
   at::Tensor x = x_in.contiguous();
   check_cuda(x, "x");
-  check_cuda(pairs_u8, "pairs_u8");
-  check_cuda(theta, "theta");
-  TORCH_CHECK(pairs_u8.scalar_type() == at::kByte, "pairs_u8 must be uint8 (from prepare_rotation)");
-  TORCH_CHECK(theta.scalar_type() == at::kHalf, "theta must be float16");
+  check_cuda(rot_table, "rot_table");
+  TORCH_CHECK(rot_table.scalar_type() == at::kInt, "rot_table must be the int32 tensor from prepare_rotation");
+  TORCH_CHECK(rot_table.size(-1) == x.size(-1), "rot_table must be [krot, K]");
   const int64_t K = x.size(-1);
   const uint16_t* sp = nullptr;
   at::Tensor sc;
@@ -133,8 +138,8 @@ std::tuple<at::Tensor, at::Tensor> rotq_int8(const at::Tensor& x_in, const at::T
   ssz.back() = 1;
   at::Tensor s = at::empty(ssz, x.options().dtype(at::kFloat));
   check_status(paro_rotq_int8(x.data_ptr(), to_paro_dtype(x.scalar_type()), M, (int)K, sp,
-                              reinterpret_cast<const uint16_t*>(theta.data_ptr()), pairs_u8.data_ptr<uint8_t>(),
-                              (int)pairs_u8.size(0), (int)group_size, fp16_round ? 1 : 0, q.data_ptr<int8_t>(),
+                              reinterpret_cast<const uint32_t*>(rot_table.data_ptr<int32_t>()),
+                              (int)rot_table.size(0), (int)group_size, fp16_round ? 1 : 0, q.data_ptr<int8_t>(),
                               s.data_ptr<float>(), cur_stream()),
                "rotq_int8");
   return {q, s};
@@ -233,10 +238,10 @@ at::Tensor w4a8_gemm(const at::Tensor& xq_in, const at::Tensor& xscale_in, const
 }
 
 // One W4A8 rotated linear: fused activation kernel + GEMM (two launches).
-at::Tensor linear_w4a8(const at::Tensor& x, const at::Tensor& pairs_u8, const at::Tensor& theta,
-                       const c10::optional<at::Tensor>& channel_scales, const at::Tensor& packed, int64_t N,
-                       const c10::optional<at::Tensor>& bias, bool fp16_round, at::ScalarType out_dtype) {
-  auto qs = rotq_int8(x, pairs_u8, theta, channel_scales, 128, fp16_round);
+at::Tensor linear_w4a8(const at::Tensor& x, const at::Tensor& rot_table, const c10::optional<at::Tensor>& channel_scales,
+                       const at::Tensor& packed, int64_t N, const c10::optional<at::Tensor>& bias, bool fp16_round,
+                       at::ScalarType out_dtype) {
+  auto qs = rotq_int8(x, rot_table, channel_scales, 128, fp16_round);
   return w4a8_gemm(std::get<0>(qs), std::get<1>(qs), packed, N, bias, out_dtype);
 }
 
@@ -244,15 +249,14 @@ at::Tensor linear_w4a8(const at::Tensor& x, const at::Tensor& pairs_u8, const at
 
 TORCH_LIBRARY(paro_b200, m) {
   m.def("rotate(Tensor x, Tensor idx_ij, Tensor theta, Tensor? scales, int group_size) -> Tensor");
-  m.def("prepare_rotation(Tensor pairs, int group_size) -> Tensor");
-  m.def("rotq_int8(Tensor x, Tensor pairs_u8, Tensor theta, Tensor? scales, int group_size, bool fp16_round) -> "
-        "(Tensor, Tensor)");
+  m.def("prepare_rotation(Tensor pairs, Tensor theta, int group_size) -> Tensor");
+  m.def("rotq_int8(Tensor x, Tensor rot_table, Tensor? scales, int group_size, bool fp16_round) -> (Tensor, Tensor)");
   m.def("quant_int8(Tensor x) -> (Tensor, Tensor)");
   m.def("prepare_weights(Tensor qweight, Tensor scales, Tensor scaled_zeros, int N, int K) -> Tensor");
   m.def("prepare_weights_awq(Tensor qweight, Tensor scales, Tensor qzeros, int N, int K) -> Tensor");
   m.def("w4a8_gemm(Tensor xq, Tensor xscale, Tensor packed, int N, Tensor? bias, ScalarType out_dtype) -> Tensor");
-  m.def("linear_w4a8(Tensor x, Tensor pairs_u8, Tensor theta, Tensor? channel_scales, Tensor packed, int N, "
-        "Tensor? bias, bool fp16_round, ScalarType out_dtype) -> Tensor");
+  m.def("linear_w4a8(Tensor x, Tensor rot_table, Tensor? channel_scales, Tensor packed, int N, Tensor? bias, "
+        "bool fp16_round, ScalarType out_dtype) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(paro_b200, CUDA, m) {

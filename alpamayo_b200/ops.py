@@ -23,12 +23,12 @@ def _rotate_fake(x, idx_ij, theta, scales, group_size):
 
 
 @torch.library.register_fake("paro_b200::prepare_rotation")
-def _prepare_rotation_fake(pairs, group_size):
-    return torch.empty(pairs.shape, dtype=torch.uint8, device=pairs.device)
+def _prepare_rotation_fake(pairs, theta, group_size):
+    return torch.empty(pairs.shape, dtype=torch.int32, device=pairs.device)
 
 
 @torch.library.register_fake("paro_b200::rotq_int8")
-def _rotq_fake(x, pairs_u8, theta, scales, group_size, fp16_round):
+def _rotq_fake(x, rot_table, scales, group_size, fp16_round):
     q = torch.empty(x.shape, dtype=torch.int8, device=x.device)
     s = torch.empty(tuple(x.shape[:-1]) + (1,), dtype=torch.float32, device=x.device)
     return q, s
@@ -65,7 +65,7 @@ def _gemm_fake(xq, xscale, packed, N, bias, out_dtype):
 
 
 @torch.library.register_fake("paro_b200::linear_w4a8")
-def _linear_fake(x, pairs_u8, theta, channel_scales, packed, N, bias, fp16_round, out_dtype):
+def _linear_fake(x, rot_table, channel_scales, packed, N, bias, fp16_round, out_dtype):
     return torch.empty(tuple(x.shape[:-1]) + (N,), dtype=out_dtype, device=x.device)
 
 
@@ -74,14 +74,16 @@ def rotate(x, idx_ij, theta, scales=None, group_size=128):
     return _ops.rotate(x, idx_ij, theta, scales, group_size)
 
 
-def prepare_rotation(pairs, group_size=128):
-    """Validate (each layer-group a permutation) and narrow pairs to uint8."""
-    return _ops.prepare_rotation(pairs, group_size)
+def prepare_rotation(pairs, theta, group_size=128):
+    """Validate the pair table (each layer-group a permutation of 0..127) and
+    build the per-channel rotation table (int32 [krot, K]: partner channel,
+    role bit, fp16 angle bits) the fused kernel reads."""
+    return _ops.prepare_rotation(pairs, theta.to(torch.float16).contiguous(), group_size)
 
 
-def rotq_int8(x, pairs_u8, theta, scales=None, group_size=128, fp16_round=True):
+def rotq_int8(x, rot_table, scales=None, group_size=128, fp16_round=True):
     """Fused channel scale + Givens rotation + per-token int8 quantisation."""
-    return _ops.rotq_int8(x, pairs_u8, theta, scales, group_size, fp16_round)
+    return _ops.rotq_int8(x, rot_table, scales, group_size, fp16_round)
 
 
 def per_token_quant_int8(x):
@@ -101,6 +103,7 @@ def w4a8_gemm(xq, xscale, packed, N, bias=None, out_dtype=torch.bfloat16):
     return _ops.w4a8_gemm(xq, xscale, packed, N, bias, out_dtype)
 
 
-def linear_w4a8(x, pairs_u8, theta, channel_scales, packed, N, bias=None, fp16_round=True, out_dtype=None):
-    return _ops.linear_w4a8(x, pairs_u8, theta, channel_scales, packed, N, bias, fp16_round,
+def linear_w4a8(x, rot_table, channel_scales, packed, N, bias=None, fp16_round=True, out_dtype=None):
+    """One W4A8 rotated linear: fused activation kernel + GEMM."""
+    return _ops.linear_w4a8(x, rot_table, channel_scales, packed, N, bias, fp16_round,
                             out_dtype if out_dtype is not None else x.dtype)

@@ -47,24 +47,27 @@ class Rotation(nn.Module):
         self.register_buffer("theta", rotation_angles.clone().contiguous())
         self.register_buffer("pairs", rotation_pairs.clone().short().contiguous())
         self.register_buffer("channel_scales", channel_scales.clone().contiguous())
-        self._pairs_u8 = None
-        self._pairs_key = None
+        self._rot_table = None
+        self._rot_key = None
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         return ops.rotate(x, self.pairs, self.theta, self.channel_scales, 128)
 
-    def pairs_u8(self) -> torch.Tensor:
-        """uint8 pair table validated as disjoint pairs (derived, cached)."""
-        key = (self.pairs.data_ptr(), self.pairs._version, self.pairs.device)
-        if self._pairs_u8 is None or self._pairs_key != key:
-            self._pairs_u8 = ops.prepare_rotation(self.pairs.contiguous(), 128)
-            self._pairs_key = key
-        return self._pairs_u8
+    def rot_table(self) -> torch.Tensor:
+        """Per-channel rotation table (partner, role, fp16 angle) built from
+        ``pairs`` / ``theta`` after checking that every layer's pairs are
+        disjoint; derived and cached, rebuilt if the buffers change."""
+        key = (self.pairs.data_ptr(), self.pairs._version, self.theta.data_ptr(), self.theta._version,
+               self.pairs.device)
+        if self._rot_table is None or self._rot_key != key:
+            self._rot_table = ops.prepare_rotation(self.pairs.contiguous(), self.theta, 128)
+            self._rot_key = key
+        return self._rot_table
 
     def quantize_activations(self, x: torch.Tensor, fp16_round: bool = True):
         """x -> (int8 codes, float32 per-token scales) in one kernel."""
         cs = self.channel_scales.reshape(-1).to(torch.float16)
-        return ops.rotq_int8(x, self.pairs_u8(), self.theta.to(torch.float16).contiguous(), cs, 128, fp16_round)
+        return ops.rotq_int8(x, self.rot_table(), cs, 128, fp16_round)
 
 
 class RotateLinearInt4(nn.Module):
@@ -108,8 +111,7 @@ class RotateLinearInt4(nn.Module):
     def forward(self, x, out_dtype=None):
         packed, bias = self._packed_and_bias()
         cs = self.rotation.channel_scales.reshape(-1).to(torch.float16)
-        return ops.linear_w4a8(x, self.rotation.pairs_u8(), self.rotation.theta.to(torch.float16).contiguous(),
-                               cs, packed, self.out_features, bias, True,
+        return ops.linear_w4a8(x, self.rotation.rot_table(), cs, packed, self.out_features, bias, True,
                                out_dtype if out_dtype is not None else x.dtype)
 
     def buffer_name(self, buffer_name: str):

@@ -109,7 +109,7 @@ def make_layer(N, K, seed, device="cuda", checkpoint=True):
         layer["packed"] = ops.prepare_weights_awq(pack_awq_gpu(codes.t().contiguous()), scales[:G].contiguous(),
                                                   pack_awq_gpu(zq.to(torch.uint8)), N, K)
     del codes
-    layer["pairs_u8"] = ops.prepare_rotation(pairs, GROUP)
+    layer["rot_table"] = ops.prepare_rotation(pairs, theta, GROUP)
     layer["cs_vec"] = cs.reshape(-1).contiguous()
     return layer
 

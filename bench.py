@@ -243,7 +243,7 @@ def main():
     wset = sum(weight_bytes(N, K) for (_, N, K) in SHAPES) * len(DECODE_M)
 
     def linear(L, x, M):
-        q, s = ops.rotq_int8(x, L["pairs_u8"], L["theta"], L["cs_vec"], 128, True)
+        q, s = ops.rotq_int8(x, L["rot_table"], L["cs_vec"], 128, True)
         return ops.w4a8_gemm(q, s, L["packed"], L["N"], None, torch.bfloat16)
 
     def sweep():
@@ -299,7 +299,7 @@ def main():
                 L = reps[ri][name]
                 ea, eb, ec = (torch.cuda.Event(enable_timing=True) for _ in range(3))
                 ea.record()
-                q, sc = ops.rotq_int8(xs[(M, K)], L["pairs_u8"], L["theta"], L["cs_vec"], 128, True)
+                q, sc = ops.rotq_int8(xs[(M, K)], L["rot_table"], L["cs_vec"], 128, True)
                 eb.record()
                 ops.w4a8_gemm(q, sc, L["packed"], N, None, torch.bfloat16)
                 ec.record()
@@ -341,8 +341,8 @@ def main():
             for ri, M in enumerate(DECODE_M):
                 for (name, N, K) in SHAPES:
                     L = reps[ri][name]
-                    y = ops.linear_w4a8(dx[(M, K)], L["pairs_u8"], L["theta"], L["cs_vec"], L["packed"], N, None,
-                                        True, torch.bfloat16)
+                    y = ops.linear_w4a8(dx[(M, K)], L["rot_table"], L["cs_vec"], L["packed"], N, None, True,
+                                        torch.bfloat16)
                     hy[(ri, name)].copy_(y, non_blocking=True)
 
         s2 = torch.cuda.Stream()

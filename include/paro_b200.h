@@ -64,19 +64,26 @@ const char* paro_last_cuda_error(void);
  * ------------------------------------------------------------------------ */
 
 /*
- * Validate and pack the Givens pair table.
- *   pairs  : int16 [krot, K] group-local channel indices; entries 2p, 2p+1 of
- *            each group form pair p (reference layout, rotation_linear.py:32-44,
- *            read by rotation.cuh:280-297).
- *   out_u8 : uint8 [krot, K] the same indices as bytes (group <= 128).
- *   bad    : device int32, set to the number of (layer, group) blocks that are
- *            not a permutation of 0..group-1 (must be zero before the call is
- *            trusted: overlapping pairs make the rotation order-dependent).
- * Replaces nothing in the reference (it has no validator); it guards the
- * disjointness invariant rotation.cu:48-54 relies on.
+ * Validate the Givens pair table and build the per-channel rotation table
+ * the fused activation kernel reads.
+ *   pairs     : int16 [krot, K] group-local channel indices; entries 2p, 2p+1
+ *               of each group form pair p (reference layout,
+ *               rotation_linear.py:32-44, read by rotation.cuh:280-297).
+ *   theta     : fp16 [krot, K/2] angle of each pair.
+ *   out_table : uint32 [krot, K] indexed by channel: partner channel (bits
+ *               0-6, group-local), role (bit 7: 0 = first element of its
+ *               pair, 1 = second) and the pair's fp16 angle bits (16-31).
+ *   bad       : device int32, set to the number of (layer, group) blocks that
+ *               are not a permutation of 0..group-1 (must be zero before the
+ *               table is trusted: overlapping pairs make a layer
+ *               order-dependent and leave table entries unwritten).
+ * group must be 128 (Rotation supports only krot 8 / group 128,
+ * rotation_linear.py:18-19; any krot is accepted here).  The reference has no
+ * validator; this guards the disjointness invariant rotation.cu:48-54 relies on.
  */
-int paro_prepare_rotation(const int16_t* pairs, int krot, int K, int group,
-                          uint8_t* out_u8, int32_t* bad, paro_stream_t stream);
+int paro_prepare_rotation(const int16_t* pairs, const uint16_t* theta, int krot, int K,
+                          int group, uint32_t* out_table, int32_t* bad,
+                          paro_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Activation kernels
@@ -103,17 +110,16 @@ int paro_rotate(const void* x, int x_dtype, int64_t M, int K,
  * (int8_utils.py:106-128).
  *   x            : [M, K] of x_dtype (F32 / F16 / BF16).
  *   scales       : fp16 [K] channel scales or NULL.
- *   theta        : fp16 [krot, K/2].
- *   pairs_u8     : uint8 [krot, K] from paro_prepare_rotation.
+ *   rot_table    : uint32 [krot, K] from paro_prepare_rotation.
  *   fp16_round   : 1 = round the rotated value to fp16 before quantising,
  *                  as the reference does (its rotate kernel stores fp16,
  *                  rotation.cuh:333-334); 0 = quantise the float32 value.
  *   out_q        : int8 [M, K];  out_scale : float32 [M] (= absmax / 127).
  */
 int paro_rotq_int8(const void* x, int x_dtype, int64_t M, int K,
-                   const uint16_t* scales, const uint16_t* theta,
-                   const uint8_t* pairs_u8, int krot, int group, int fp16_round,
-                   int8_t* out_q, float* out_scale, paro_stream_t stream);
+                   const uint16_t* scales, const uint32_t* rot_table, int krot,
+                   int group, int fp16_round, int8_t* out_q, float* out_scale,
+                   paro_stream_t stream);
 
 /*
  * per_token_quant_int8 (int8_utils.py:131-156): absmax = max(max|x|, 1e-10),

@@ -87,8 +87,8 @@ def test_rotq_int8_matches_reference_chain(ops, M, K, xdt):
     pairs, theta, cs = make_rotation(K, seed=M + K)
     x = make_activations(M, K, seed=7 * M + K)
     xt = torch.from_numpy(x).to(xdt)
-    pu8 = ops.prepare_rotation(dev(pairs), 128)
-    q, s = ops.rotq_int8(xt.cuda(), pu8, dev(theta), dev(cs.reshape(-1)), 128, True)
+    pu8 = ops.prepare_rotation(dev(pairs), dev(theta), 128)
+    q, s = ops.rotq_int8(xt.cuda(), pu8, dev(cs.reshape(-1)), 128, True)
     q_ref, s_ref, _ = O.rot_quant_reference(xt.float().numpy(), pairs, theta.astype(np.float32),
                                             cs.astype(np.float32))
     assert tuple(q.shape) == (M, K) and tuple(s.shape) == (M, 1)
@@ -97,8 +97,8 @@ def test_rotq_int8_matches_reference_chain(ops, M, K, xdt):
 
 def test_rotq_int8_golden_fixture(ops):
     d = np.load(os.path.join(GOLD, "rot_m4_k3584.npz"))
-    pu8 = ops.prepare_rotation(dev(d["pairs"]), 128)
-    q, s = ops.rotq_int8(dev(d["x"]), pu8, dev(d["theta"]), dev(d["channel_scales"].reshape(-1)), 128, True)
+    pu8 = ops.prepare_rotation(dev(d["pairs"]), dev(d["theta"]), 128)
+    q, s = ops.rotq_int8(dev(d["x"]), pu8, dev(d["channel_scales"].reshape(-1)), 128, True)
     # reference chain: its rotation (fixture), fp16 store, vLLM int8 quant
     q_ref, s_ref = O.per_token_quant_int8(O.round_to_fp16(d["rotated"]))
     check_codes(q.cpu().numpy(), q_ref, s.cpu().numpy().reshape(-1), s_ref)
@@ -108,8 +108,8 @@ def test_rotq_int8_without_fp16_rounding(ops):
     M, K = 16, 1024
     pairs, theta, cs = make_rotation(K, seed=3)
     x = make_activations(M, K, seed=4)
-    pu8 = ops.prepare_rotation(dev(pairs), 128)
-    q, s = ops.rotq_int8(dev(x), pu8, dev(theta), dev(cs.reshape(-1)), 128, False)
+    pu8 = ops.prepare_rotation(dev(pairs), dev(theta), 128)
+    q, s = ops.rotq_int8(dev(x), pu8, dev(cs.reshape(-1)), 128, False)
     q_ref, s_ref, _ = O.rot_quant_reference(x, pairs, theta.astype(np.float32), cs.astype(np.float32),
                                             fp16_intermediate=False)
     check_codes(q.cpu().numpy(), q_ref, s.cpu().numpy().reshape(-1), s_ref)
@@ -129,28 +129,58 @@ def test_quant_int8_bit_exact(ops, dtype):
     assert q[5, :8].tolist() == [127, 1, -1, 2, -3, 63, -127, 0]
 
 
-def test_prepare_rotation_rejects_overlapping_pairs(ops):
-    pairs, _, _ = make_rotation(256, seed=1)
-    ok = ops.prepare_rotation(dev(pairs), 128)
-    assert torch.equal(ok.cpu(), torch.from_numpy(pairs.astype(np.uint8)))
+def expected_rot_table(pairs, theta):
+    """Per-channel table restated from the pair list: partner channel, role
+    bit (second element of its pair), fp16 angle bits of the pair."""
+    L, K = pairs.shape
+    out = np.zeros((L, K), dtype=np.uint32)
+    tb = theta.view(np.uint16).astype(np.uint32)
+    for l in range(L):
+        for g in range(K // 128):
+            blk = pairs[l, g * 128:(g + 1) * 128].astype(np.int64)
+            for t in range(128):
+                v, w = blk[t], blk[t ^ 1]
+                out[l, g * 128 + v] = w | ((t & 1) << 7) | (tb[l, g * 64 + t // 2] << 16)
+    return out.view(np.int32)
+
+
+def test_prepare_rotation_table_and_rejects_overlapping_pairs(ops):
+    pairs, theta, _ = make_rotation(256, seed=1)
+    ok = ops.prepare_rotation(dev(pairs), dev(theta), 128)
+    assert np.array_equal(ok.cpu().numpy(), expected_rot_table(pairs, theta))
     pairs[2, 130] = pairs[2, 131]
     with pytest.raises(RuntimeError, match="not permutations"):
-        ops.prepare_rotation(dev(pairs), 128)
+        ops.prepare_rotation(dev(pairs), dev(theta), 128)
 
 
 def test_empty_batch(ops):
     pairs, theta, cs = make_rotation(256, seed=1)
-    pu8 = ops.prepare_rotation(dev(pairs), 128)
-    q, s = ops.rotq_int8(torch.zeros(0, 256, device="cuda", dtype=torch.bfloat16), pu8, dev(theta),
-                         dev(cs.reshape(-1)), 128, True)
+    pu8 = ops.prepare_rotation(dev(pairs), dev(theta), 128)
+    q, s = ops.rotq_int8(torch.zeros(0, 256, device="cuda", dtype=torch.bfloat16), pu8, dev(cs.reshape(-1)), 128,
+                         True)
     assert q.shape == (0, 256) and s.shape == (0, 1)
 
 
 def test_leading_batch_dims(ops):
     pairs, theta, cs = make_rotation(512, seed=2)
     x = make_activations(6, 512, seed=3).reshape(2, 3, 512)
-    pu8 = ops.prepare_rotation(dev(pairs), 128)
-    q, s = ops.rotq_int8(dev(x, torch.bfloat16), pu8, dev(theta), dev(cs.reshape(-1)), 128, True)
+    pu8 = ops.prepare_rotation(dev(pairs), dev(theta), 128)
+    q, s = ops.rotq_int8(dev(x, torch.bfloat16), pu8, dev(cs.reshape(-1)), 128, True)
     assert q.shape == (2, 3, 512) and s.shape == (2, 3, 1)
-    q2, s2 = ops.rotq_int8(dev(x.reshape(6, 512), torch.bfloat16), pu8, dev(theta), dev(cs.reshape(-1)), 128, True)
+    q2, s2 = ops.rotq_int8(dev(x.reshape(6, 512), torch.bfloat16), pu8, dev(cs.reshape(-1)), 128, True)
     assert torch.equal(q.reshape(6, 512), q2) and torch.equal(s.reshape(6, 1), s2)
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 5, 8, 9, 17])
+def test_rotq_ragged_rows_and_large_k(ops, M):
+    """Row counts that do not fill a cluster's row block, at the down_proj K
+    (several groups per thread)."""
+    K = 18944
+    pairs, theta, cs = make_rotation(K, seed=M)
+    x = make_activations(M, K, seed=M + 1)
+    xt = torch.from_numpy(x).to(torch.bfloat16)
+    table = ops.prepare_rotation(dev(pairs), dev(theta), 128)
+    q, s = ops.rotq_int8(xt.cuda(), table, dev(cs.reshape(-1)), 128, True)
+    q_ref, s_ref, _ = O.rot_quant_reference(xt.float().numpy(), pairs, theta.astype(np.float32),
+                                            cs.astype(np.float32))
+    check_codes(q.cpu().numpy(), q_ref, s.cpu().numpy().reshape(-1), s_ref)

@@ -55,7 +55,9 @@ def test_argument_validation_before_launch():
     # bad dtype
     assert L.paro_quant_int8(dummy, 7, 4, 256, dummy, dummy, None) == 3
     # fused kernel only for krot 8, group 128 (rotation_linear.py:18-19)
-    assert L.paro_rotq_int8(dummy, 2, 4, 256, None, dummy, dummy, 4, 128, 1, dummy, dummy, None) == 3
+    assert L.paro_rotq_int8(dummy, 2, 4, 256, None, dummy, 4, 128, 1, dummy, dummy, None) == 3
+    # the rotation table is only built for 128-channel groups
+    assert L.paro_prepare_rotation(dummy, dummy, 8, 256, 64, dummy, dummy, None) == 3
     # GEMM shape checks
     assert L.paro_w4a8_gemm(dummy, dummy, 4, 100, 256, dummy, None, 0, dummy, 2, None, 0, None) == 2
     assert L.paro_w4a8_gemm(dummy, dummy, 4, 256, 200, dummy, None, 0, dummy, 2, None, 0, None) == 2
