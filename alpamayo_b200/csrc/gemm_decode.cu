@@ -66,21 +66,23 @@ struct DecParams {
 __host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
 __host__ __device__ __forceinline__ int64_t max64(int64_t a, int64_t b) { return a > b ? a : b; }
 
-__device__ __forceinline__ uint32_t expand_lo(uint32_t w, uint32_t zz) {
-  // bytes 0x80 + q - z (no borrows since q, z <= 15), then flip the bias bit
-  return (((w & 0x0F0F0F0Fu) | 0x80808080u) - zz) ^ 0x80808080u;
-}
-__device__ __forceinline__ uint32_t expand_hi(uint32_t w, uint32_t zz) {
-  return ((((w >> 4) & 0x0F0F0F0Fu) | 0x80808080u) - zz) ^ 0x80808080u;
-}
-
-__device__ __forceinline__ void mma_s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                       uint32_t b0, uint32_t b1) {
+// A = unsigned 8-bit codes (q, or 16*q from a high nibble), B = signed int8
+// activations, int32 accumulate.
+__device__ __forceinline__ void mma_u8s8(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
   asm volatile(
-      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};\n"
       : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Sum of the 32 int8 activations in a lane's 8 fragment words.
+__device__ __forceinline__ int frag_sum(const uint32_t (&b)[8]) {
+  int s = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) s = __dp4a((int)b[i], 0x01010101, s);
+  return s;
 }
 
 __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -118,38 +120,46 @@ __device__ __forceinline__ void load_bfrag_global(const int8_t* xrow, bool valid
   }
 }
 
+// One record: 16 rows x 128 channels against MT token tiles.
+//   bf[mt][2s], bf[mt][2s+1] : B fragment of k-step s (channels 32s..32s+31)
+//   sx[mt][0..1]             : group sums of this lane's two tokens
+// The low nibbles of the lane's four words per row are, as unsigned bytes,
+// the A fragments of k-steps 0-1; masked in place, the high nibbles are
+// 16*q, the A fragments of k-steps 2-3 (a separate accumulator).  So
+//   16 * sum_k (q - z) x = 16*lo + hi - 16*z*sum_k x,
+// exact in int32 (and below 2^24, so the float conversion is exact), and
+// scaled by s/16 it equals s * sum_k (q - z) x bit for bit.
 template <int MT>
-__device__ __forceinline__ void process_record(const uint8_t* rec, const uint32_t (&bf)[MT][8], int gid, int tig,
-                                               float (&y)[MT][4]) {
+__device__ __forceinline__ void process_record(const uint8_t* rec, const uint32_t (&bf)[MT][8],
+                                               const int (&sx)[MT][2], int gid, int tig, float (&y)[MT][4]) {
   const uint4 wa = *reinterpret_cast<const uint4*>(rec + gid * 64 + tig * 16);
   const uint4 wb = *reinterpret_cast<const uint4*>(rec + (gid + 8) * 64 + tig * 16);
   const uint16_t* sp = reinterpret_cast<const uint16_t*>(rec + kRecScaleOff);
-  const float s_lo = half_bits_to_f32(sp[gid]), s_hi = half_bits_to_f32(sp[gid + 8]);
-  const uint32_t zz_lo = (uint32_t)rec[kRecZeroOff + gid] * 0x01010101u;
-  const uint32_t zz_hi = (uint32_t)rec[kRecZeroOff + gid + 8] * 0x01010101u;
-  const uint32_t wA[4] = {wa.x, wa.y, wa.z, wa.w};
-  const uint32_t wB[4] = {wb.x, wb.y, wb.z, wb.w};
-  // two independent accumulator chains (k-steps 0,1 and 2,3)
-  int acc[2][MT][4];
+  const float s16_lo = half_bits_to_f32(sp[gid]) * 0.0625f, s16_hi = half_bits_to_f32(sp[gid + 8]) * 0.0625f;
+  const int nz_lo = -16 * (int)rec[kRecZeroOff + gid], nz_hi = -16 * (int)rec[kRecZeroOff + gid + 8];
+  constexpr uint32_t LO = 0x0F0F0F0Fu, HI = 0xF0F0F0F0u;
+  int lo[MT][4], hi[MT][4];
 #pragma unroll
-  for (int h = 0; h < 2; ++h)
+  for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
+    for (int i = 0; i < 4; ++i) lo[mt][i] = hi[mt][i] = 0;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) acc[h][mt][i] = 0;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const uint32_t a0 = expand_lo(wA[j], zz_lo), a2 = expand_hi(wA[j], zz_lo);
-    const uint32_t a1 = expand_lo(wB[j], zz_hi), a3 = expand_hi(wB[j], zz_hi);
-#pragma unroll
-    for (int mt = 0; mt < MT; ++mt) mma_s8(acc[j >> 1][mt], a0, a1, a2, a3, bf[mt][2 * j], bf[mt][2 * j + 1]);
+  for (int mt = 0; mt < MT; ++mt) {
+    mma_u8s8(lo[mt], wa.x & LO, wb.x & LO, wa.y & LO, wb.y & LO, bf[mt][0], bf[mt][1]);
+    mma_u8s8(hi[mt], wa.x & HI, wb.x & HI, wa.y & HI, wb.y & HI, bf[mt][4], bf[mt][5]);
+    mma_u8s8(lo[mt], wa.z & LO, wb.z & LO, wa.w & LO, wb.w & LO, bf[mt][2], bf[mt][3]);
+    mma_u8s8(hi[mt], wa.z & HI, wb.z & HI, wa.w & HI, wb.w & HI, bf[mt][6], bf[mt][7]);
   }
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt) {
-    y[mt][0] = fmaf(s_lo, (float)(acc[0][mt][0] + acc[1][mt][0]), y[mt][0]);
-    y[mt][1] = fmaf(s_lo, (float)(acc[0][mt][1] + acc[1][mt][1]), y[mt][1]);
-    y[mt][2] = fmaf(s_hi, (float)(acc[0][mt][2] + acc[1][mt][2]), y[mt][2]);
-    y[mt][3] = fmaf(s_hi, (float)(acc[0][mt][3] + acc[1][mt][3]), y[mt][3]);
+    const int t0 = 16 * lo[mt][0] + hi[mt][0] + nz_lo * sx[mt][0];
+    const int t1 = 16 * lo[mt][1] + hi[mt][1] + nz_lo * sx[mt][1];
+    const int t2 = 16 * lo[mt][2] + hi[mt][2] + nz_hi * sx[mt][0];
+    const int t3 = 16 * lo[mt][3] + hi[mt][3] + nz_hi * sx[mt][1];
+    y[mt][0] = fmaf(s16_lo, (float)t0, y[mt][0]);
+    y[mt][1] = fmaf(s16_lo, (float)t1, y[mt][1]);
+    y[mt][2] = fmaf(s16_hi, (float)t2, y[mt][2]);
+    y[mt][3] = fmaf(s16_hi, (float)t3, y[mt][3]);
   }
 }
 
@@ -164,6 +174,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p
   uint64_t* empty = full + kDecMaxStages;
   float* red = reinterpret_cast<float*>(empty + kDecMaxStages);                 // [8][MT*4][32]
   uint4* xs = reinterpret_cast<uint4*>(red + kDecConsumers * MT * 4 * 32);    // [G][MT][32][2]
+  int* sxs = reinterpret_cast<int*>(xs + (XS ? 2 * G * MT * 32 : 0));         // [G][MT][8] group sums
   __shared__ int last_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -219,6 +230,12 @@ __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p
       load_bfrag_global(p.xq + (t < p.M ? t : 0) * (int64_t)p.K + 4 * ltig, t < p.M, g, b);
       xs[2 * e] = make_uint4(b[0], b[1], b[2], b[3]);
       xs[2 * e + 1] = make_uint4(b[4], b[5], b[6], b[7]);
+      // the 4 lanes of one token row cover the group's 128 channels (the
+      // trip count is uniform across a warp, so the shuffles are safe)
+      int part = frag_sum(b);
+      part += __shfl_xor_sync(0xffffffffu, part, 1);
+      part += __shfl_xor_sync(0xffffffffu, part, 2);
+      if (ltig == 0) sxs[(g * MT + mt) * 8 + lgid] = part;
     }
     named_barrier(1, kDecConsumers * 32);
   }
@@ -242,6 +259,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p
       const int64_t ur = nb * G + g;
       if (ur >= u && ur < ce) {
         uint32_t bf[MT][8];
+        int sx[MT][2];
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
           if constexpr (XS) {
@@ -249,11 +267,20 @@ __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p
             const uint4 lo = xp[0], hi = xp[1];
             bf[mt][0] = lo.x; bf[mt][1] = lo.y; bf[mt][2] = lo.z; bf[mt][3] = lo.w;
             bf[mt][4] = hi.x; bf[mt][5] = hi.y; bf[mt][6] = hi.z; bf[mt][7] = hi.w;
+            const int2 s2 = *reinterpret_cast<const int2*>(sxs + (g * MT + mt) * 8 + 2 * tig);
+            sx[mt][0] = s2.x;
+            sx[mt][1] = s2.y;
           } else {
             load_bfrag_global(xrow[mt], xvalid[mt], g, bf[mt]);
+            // token row gid's sum, then the sums of this lane's C columns
+            int part = frag_sum(bf[mt]);
+            part += __shfl_xor_sync(0xffffffffu, part, 1);
+            part += __shfl_xor_sync(0xffffffffu, part, 2);
+            sx[mt][0] = __shfl_sync(0xffffffffu, part, 8 * tig);
+            sx[mt][1] = __shfl_sync(0xffffffffu, part, 8 * tig + 4);
           }
         }
-        process_record<MT>(smem + (size_t)s * kDecStageBytes + (size_t)(ur - u) * kRecBytes, bf, gid, tig, y);
+        process_record<MT>(smem + (size_t)s * kDecStageBytes + (size_t)(ur - u) * kRecBytes, bf, sx, gid, tig, y);
       }
     }
     __syncwarp();
@@ -284,15 +311,18 @@ __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p
         }
       }
       if (!whole) {
-        __threadfence();
+        // release: the CTA's partial adds (ordered before thread 0 by the
+        // barrier) become visible before the counter moves; the CTA that
+        // completes the count acquires them all
         named_barrier(1, kDecConsumers * 32);
         if (ctid == 0) {
+          asm volatile("fence.acq_rel.gpu;" ::: "memory");
           const uint32_t old = atomicAdd(&cnt[nb], (uint32_t)seg_units);
           last_flag = (old + (uint32_t)seg_units == (uint32_t)G);
+          if (last_flag) asm volatile("fence.acq_rel.gpu;" ::: "memory");
         }
         named_barrier(1, kDecConsumers * 32);
         if (last_flag) {
-          __threadfence();
           const int ntok = (int)min64(kDecMaxTokens, p.M - tok0);
           for (int idx = ctid; idx < kRecRows * ntok; idx += kDecConsumers * 32) {
             const int r = idx / ntok, tt = idx - r * ntok;
@@ -353,7 +383,7 @@ static cudaError_t launch_mt(DecParams p, size_t xs_bytes, cudaStream_t st) {
 template <int MT>
 static cudaError_t launch_pick(DecParams p, cudaStream_t st) {
   const int G = p.K / kGroup;
-  const size_t xs_bytes = (size_t)G * MT * 32 * 32;
+  const size_t xs_bytes = (size_t)G * MT * 32 * 32 + (size_t)G * MT * 8 * sizeof(int);
   const size_t base = fixed_smem(MT);
   const bool xs = base + xs_bytes + 3 * (size_t)kDecStageBytes <= (size_t)kDecSmemBudget;
   const size_t avail = kDecSmemBudget - base - (xs ? xs_bytes : 0);

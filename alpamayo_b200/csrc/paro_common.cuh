@@ -24,13 +24,14 @@ __host__ __device__ __forceinline__ size_t rec_offset(int nb, int g, int G) {
   return ((size_t)nb * G + g) * kRecBytes;
 }
 
-// Position of code k (0..127 within a group) inside a row's 64 bytes:
-// word index t*4 + j, byte b, nibble h, where k = 32j + 16h + 4t + b.
+// Position of code k (0..127 within a group) inside a row's 64 bytes: with
+// k = 64h + 32s + 16f + 4t + b it is byte t*16 + (2s + f)*4 + b, low nibble
+// for h = 0 and high nibble for h = 1.
 __host__ __device__ __forceinline__ int code_byte_pos(int k) {
-  const int j = k >> 5, t = (k >> 2) & 3, b = k & 3;
-  return t * 16 + j * 4 + b;
+  const int s = (k >> 5) & 1, f = (k >> 4) & 1, t = (k >> 2) & 3, b = k & 3;
+  return t * 16 + (2 * s + f) * 4 + b;
 }
-__host__ __device__ __forceinline__ int code_nibble(int k) { return (k >> 4) & 1; }
+__host__ __device__ __forceinline__ int code_nibble(int k) { return k >> 6; }
 
 // ---------------------------------------------------------------------------
 // dtype helpers

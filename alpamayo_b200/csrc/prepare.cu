@@ -9,8 +9,11 @@
 //
 // Tile record (one per 16-row block nb and 128-channel group g, 1072 bytes):
 //   [0, 1024)    codes: row r's 64 bytes at r*64; word t*4+j (t,j in 0..3) byte b
-//                holds code k = 32j+4t+b in its low nibble and k+16 in its high
-//                nibble (k relative to the group start);
+//                holds code k = 32*(j>>1) + 16*(j&1) + 4t + b in its low nibble
+//                and code k + 64 in its high nibble (k relative to the group
+//                start), so the low nibbles of a lane's four words are the A
+//                fragments of mma k-steps 0-1 and the high nibbles (as 16*q)
+//                those of k-steps 2-3;
 //   [1024, 1056) fp16 group scales of the 16 rows;
 //   [1056, 1072) uint8 zero points of the 16 rows.
 #include "paro_common.cuh"
@@ -89,7 +92,7 @@ prepare_kernel(const void* __restrict__ qweight, const uint16_t* __restrict__ sc
   uint32_t word = 0;
 #pragma unroll
   for (int b = 0; b < 4; ++b) {
-    const int klo = g * kGroup + 32 * j + 4 * tt + b, khi = klo + 16;
+    const int klo = g * kGroup + 32 * (j >> 1) + 16 * (j & 1) + 4 * tt + b, khi = klo + 64;
     uint32_t lo, hi;
     if constexpr (AWQ) {
       const int32_t* aq = static_cast<const int32_t*>(qweight);

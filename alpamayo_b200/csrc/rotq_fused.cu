@@ -88,7 +88,9 @@ rotq_fused_kernel(const InT* __restrict__ x, int64_t M, int K, const uint16_t* _
   // let the GEMM that consumes these codes start its weight stream now
   asm volatile("griddepcontrol.launch_dependents;");
   cg::cluster_group cluster = cg::this_cluster();
-  extern __shared__ __align__(16) float xb[];  // [2][P][GB][128][R]
+  extern __shared__ __align__(16) float smem_f[];
+  uint32_t* tabs = reinterpret_cast<uint32_t*>(smem_f);      // [8][P][GB][128] rotation table slice
+  float* xb = smem_f + (size_t)8 * P * GB * 128;             // [2][P][GB][128][R]
   __shared__ float wred[16][R];
   __shared__ float cta_max[R];
   __shared__ float row_inv[R];
@@ -110,6 +112,21 @@ rotq_fused_kernel(const InT* __restrict__ x, int64_t M, int K, const uint16_t* _
     goff[p] = (p < P && gl < gpc && g < G) ? g * 128 + ch : -1;
   }
 
+  // every layer's table entry of this thread's channels, copied to shared
+  // memory asynchronously so all the loads are in flight at once; each
+  // thread reads back only its own entries (no barrier needed)
+  const size_t tslot = (size_t)gs * 128 + ch;
+#pragma unroll
+  for (int l = 0; l < 8; ++l)
+#pragma unroll
+    for (int p = 0; p < PM; ++p)
+      if (goff[p] >= 0) {
+        const uint32_t dst = smem_u32(tabs + ((size_t)l * P + p) * GB * 128 + tslot);
+        asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(rtab + (size_t)l * K + goff[p])
+                     : "memory");
+      }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+
   float v[PM][R];
 #pragma unroll
   for (int p = 0; p < PM; ++p) {
@@ -118,16 +135,11 @@ rotq_fused_kernel(const InT* __restrict__ x, int64_t M, int K, const uint16_t* _
     for (int r = 0; r < R; ++r)
       v[p][r] = (goff[p] >= 0 && r < nrows) ? to_f32(x[(row0 + r) * (int64_t)K + goff[p]]) * sc : 0.f;
   }
-  uint32_t tab[PM];
-#pragma unroll
-  for (int p = 0; p < PM; ++p) tab[p] = goff[p] >= 0 ? rtab[goff[p]] : 0u;
+  asm volatile("cp.async.wait_all;" ::: "memory");
 
 #pragma unroll
   for (int l = 0; l < 8; ++l) {
     float* buf = xb + (l & 1) * plane;
-    uint32_t nxt[PM];
-#pragma unroll
-    for (int p = 0; p < PM; ++p) nxt[p] = (l < 7 && goff[p] >= 0) ? rtab[(size_t)(l + 1) * K + goff[p]] : 0u;
 #pragma unroll
     for (int p = 0; p < PM; ++p)
       if (p < P) st_vec<R>(buf + ((size_t)(p * GB + gs) * 128 + ch) * R, v[p]);
@@ -135,10 +147,11 @@ rotq_fused_kernel(const InT* __restrict__ x, int64_t M, int K, const uint16_t* _
 #pragma unroll
     for (int p = 0; p < PM; ++p) {
       if (goff[p] >= 0) {
-        const int partner = tab[p] & 0x7F;
-        const bool role_j = (tab[p] >> 7) & 1;
+        const uint32_t tab = tabs[((size_t)l * P + p) * GB * 128 + tslot];
+        const int partner = tab & 0x7F;
+        const bool role_j = (tab >> 7) & 1;
         float s_, c_;
-        __sincosf(half_bits_to_f32((uint16_t)(tab[p] >> 16)), &s_, &c_);
+        __sincosf(half_bits_to_f32((uint16_t)(tab >> 16)), &s_, &c_);
         float w[R];
         ld_vec<R>(buf + ((size_t)(p * GB + gs) * 128 + partner) * R, w);
         const float ca = role_j ? -s_ : c_, cb = role_j ? c_ : s_;
@@ -150,8 +163,6 @@ rotq_fused_kernel(const InT* __restrict__ x, int64_t M, int K, const uint16_t* _
         }
       }
     }
-#pragma unroll
-    for (int p = 0; p < PM; ++p) tab[p] = nxt[p];
   }
 
   // fp16 store rounding of the reference's rotate kernel, row maxima
@@ -206,7 +217,7 @@ rotq_fused_kernel(const InT* __restrict__ x, int64_t M, int K, const uint16_t* _
 template <typename InT, int R, int PM>
 static cudaError_t launch_fused(const FusedGeom& f, const void* x, int64_t M, int K, const uint16_t* scales,
                                 const uint32_t* rtab, int fp16_round, int8_t* q, float* s, cudaStream_t st) {
-  const size_t smem = 2 * (size_t)f.P * f.GB * 128 * R * sizeof(float);
+  const size_t smem = (8 + 2 * (size_t)R) * f.P * f.GB * 128 * sizeof(float);
   auto kern = rotq_fused_kernel<InT, R, PM>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
@@ -230,11 +241,12 @@ static cudaError_t launch_fused(const FusedGeom& f, const void* x, int64_t M, in
 template <typename InT, int PM>
 static cudaError_t launch_fused_r(const FusedGeom& f, const void* x, int64_t M, int K, const uint16_t* scales,
                                   const uint32_t* rtab, int fp16_round, int8_t* q, float* s, cudaStream_t st) {
-  const size_t per_row = 2 * (size_t)f.P * f.GB * 128 * sizeof(float);
+  const size_t unit = (size_t)f.P * f.GB * 128 * sizeof(float);  // tables take 8 units, rows 2 units each
   const size_t budget = 200 * 1024;
-  if (M <= 1 || per_row * 2 > budget) return launch_fused<InT, 1, PM>(f, x, M, K, scales, rtab, fp16_round, q, s, st);
-  if (M <= 2 || per_row * 4 > budget) return launch_fused<InT, 2, PM>(f, x, M, K, scales, rtab, fp16_round, q, s, st);
-  if (M <= 4 || per_row * 8 > budget) return launch_fused<InT, 4, PM>(f, x, M, K, scales, rtab, fp16_round, q, s, st);
+  auto fits = [&](int r) { return (8 + 2 * (size_t)r) * unit <= budget; };
+  if (M <= 1 || !fits(2)) return launch_fused<InT, 1, PM>(f, x, M, K, scales, rtab, fp16_round, q, s, st);
+  if (M <= 2 || !fits(4)) return launch_fused<InT, 2, PM>(f, x, M, K, scales, rtab, fp16_round, q, s, st);
+  if (M <= 4 || !fits(8)) return launch_fused<InT, 4, PM>(f, x, M, K, scales, rtab, fp16_round, q, s, st);
   return launch_fused<InT, 8, PM>(f, x, M, K, scales, rtab, fp16_round, q, s, st);
 }
 

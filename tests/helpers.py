@@ -66,17 +66,19 @@ def rel_l2(a, b):
 def expected_records(codes, scales_gn, zeros_gn):
     """The tile-record layout, restated independently of the kernel: per
     16-row block nb and group g, 1072 bytes = codes (row r at r*64; word
-    t*4+j byte b = code 32j+4t+b | code 32j+16+4t+b << 4), 16 fp16 scales,
-    16 uint8 zero points."""
+    t*4+j byte b = code k | code (k+64) << 4 with k = 32*(j>>1) + 16*(j&1) +
+    4t + b), 16 fp16 scales, 16 uint8 zero points."""
     codes = np.asarray(codes)
     N, K = codes.shape
     G = K // GROUP
     out = np.zeros(((N // 16) * G, 1072), dtype=np.uint8)
-    c = codes.reshape(N // 16, 16, G, 4, 2, 4, 4)  # nb, r, g, j, h, t, b   (k = 32j + 16h + 4t + b)
-    lo = c[:, :, :, :, 0]
-    hi = c[:, :, :, :, 1]
-    byte = (lo | (hi << 4)).astype(np.uint8)          # nb, r, g, j, t, b
-    byte = byte.transpose(0, 2, 1, 4, 3, 5)           # nb, g, r, t, j, b
+    # k = 64h + 32s + 16half + 4t + b, word j = 2s + half
+    c = codes.reshape(N // 16, 16, G, 2, 2, 2, 4, 4)  # nb, r, g, h, s, half, t, b
+    lo = c[:, :, :, 0]
+    hi = c[:, :, :, 1]
+    byte = (lo | (hi << 4)).astype(np.uint8)            # nb, r, g, s, half, t, b
+    byte = byte.reshape(N // 16, 16, G, 4, 4, 4)        # nb, r, g, j, t, b
+    byte = byte.transpose(0, 2, 1, 4, 3, 5)             # nb, g, r, t, j, b
     out[:, :1024] = byte.reshape((N // 16) * G, 1024)
     s16 = np.asarray(scales_gn, dtype=np.float32).astype(np.float16)  # [G, N]
     out[:, 1024:1056] = s16.T.reshape(N // 16, 16, G).transpose(0, 2, 1).reshape(-1, 16).view(np.uint8).reshape(-1, 32)
