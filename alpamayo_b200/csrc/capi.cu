@@ -34,9 +34,26 @@ cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int
                            cudaStream_t st);
 }  // namespace paro
 
+#include <map>
+#include <mutex>
+
 namespace paro {
 uint32_t error_word_decode(int clear);
+
+cudaError_t ensure_smem_limit(const void* kernel, int bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  int& have = done[std::make_pair(kernel, dev)];
+  if (have >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) have = bytes;
+  return e;
 }
+}  // namespace paro
 
 using namespace paro;
 

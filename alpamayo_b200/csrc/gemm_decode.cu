@@ -39,7 +39,7 @@
 namespace paro {
 
 constexpr int kDecConsumers = 8;
-constexpr int kDecThreads = 32 * (kDecConsumers + 1);
+constexpr int kDecThreads = 32 * (kDecConsumers + 2);  // producer + consumers + epilogue
 constexpr int kDecChunkGroups = 16;
 constexpr int kDecStageBytes = kDecChunkGroups * kRecBytes;  // 17152
 constexpr int kDecMaxStages = 8;
@@ -100,15 +100,6 @@ __device__ __forceinline__ void store_out(void* out, int dtype, size_t idx, floa
   else static_cast<float*>(out)[idx] = v;
 }
 
-// End of the chunk starting at unit u: the next 16-group boundary of u's
-// row block, the row block's end, or the CTA range end.
-__device__ __forceinline__ int64_t chunk_end(int64_t u, int64_t u1, int G) {
-  const int64_t nb = u / G;
-  const int g = (int)(u - nb * G);
-  const int gend = min(G, (g / kDecChunkGroups + 1) * kDecChunkGroups);
-  return min64(u1, nb * G + gend);
-}
-
 // The 8 B-fragment words of (token tile, group g) for this lane: b0/b1 of
 // the four 32-channel steps.
 __device__ __forceinline__ void load_bfrag_global(const int8_t* xrow, bool valid, int g, uint32_t (&b)[8]) {
@@ -163,46 +154,165 @@ __device__ __forceinline__ void process_record(const uint8_t* rec, const uint32_
   }
 }
 
-// XS: activations staged in shared memory (fragment order) instead of read
+// Walks a CTA's unit range in chunks: a chunk is the records of up to 16
+// consecutive groups of one row block, aligned to 16-group boundaries.
+struct ChunkIter {
+  int64_t u, u1;
+  int nb, g, G;
+  __device__ __forceinline__ ChunkIter(int64_t u0, int64_t u1_, int G_) : u(u0), u1(u1_), G(G_) {
+    nb = (int)(u0 / G_);
+    g = (int)(u0 - (int64_t)nb * G_);
+  }
+  __device__ __forceinline__ bool more() const { return u < u1; }
+  __device__ __forceinline__ int count() const {
+    const int gend = min(G, ((g >> 4) + 1) << 4);
+    return (int)min64(gend - g, u1 - u);
+  }
+  // advance past a chunk of n records; true if that ended a segment
+  __device__ __forceinline__ bool advance(int n) {
+    u += n;
+    g += n;
+    if (g == G) {
+      g = 0;
+      ++nb;
+      return true;
+    }
+    return u == u1;
+  }
+};
+
+// XS: the token slice's int8 rows are bulk-copied into shared memory (rows
+// padded by 16 bytes so the B-fragment reads of a warp hit 32 distinct
+// banks) and the per-group sums computed there; otherwise fragments are read
 // from global memory per record.
 template <int MT, bool XS>
 __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int S = p.stages;
   const int G = p.K / kGroup;
+  constexpr int MP = 8 * MT;  // token rows of the slice
+  const int xstride = p.K + 16;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)S * kDecStageBytes);
   uint64_t* empty = full + kDecMaxStages;
-  float* red = reinterpret_cast<float*>(empty + kDecMaxStages);                 // [8][MT*4][32]
-  uint4* xs = reinterpret_cast<uint4*>(red + kDecConsumers * MT * 4 * 32);    // [G][MT][32][2]
-  int* sxs = reinterpret_cast<int*>(xs + (XS ? 2 * G * MT * 32 : 0));         // [G][MT][8] group sums
-  __shared__ int last_flag;
+  uint64_t* seg_full = empty + kDecMaxStages;   // [2]: all consumer slices written
+  uint64_t* seg_free = seg_full + 2;             // [2]: epilogue has read them
+  uint64_t* xbar = seg_free + 2;                 // activation rows landed
+  float* red = reinterpret_cast<float*>(xbar + 2);                                    // [2][8][MT*4][32]
+  uint8_t* xrows = reinterpret_cast<uint8_t*>(red + 2 * kDecConsumers * MT * 4 * 32);  // [MP][K + 16]
+  int* sxs = reinterpret_cast<int*>(xrows + (XS ? (size_t)MP * xstride : 0));          // [G][MP] group sums
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t u0 = (int64_t)blockIdx.x * p.units / p.ctas;
   const int64_t u1 = (int64_t)(blockIdx.x + 1) * p.units / p.ctas;
   const int64_t tok0 = (int64_t)blockIdx.y * kDecMaxTokens;
-  uint32_t* cnt = p.cnt + (size_t)blockIdx.y * (p.N / kRecRows);
+  const int ntok_slice = (int)min64(MP, p.M - tok0);
+  const int gid = lane >> 2, tig = lane & 3;
+  constexpr int kSlice = MT * 4 * 32;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kDecConsumers);
     }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&seg_full[b], kDecConsumers);
+      mbar_init(&seg_free[b], 1);
+    }
+    mbar_init(xbar, 1);
     fence_mbar_init();
   }
   __syncthreads();
 
   if (warp == 0) {  // producer: weights do not depend on the previous kernel
     if (lane == 0) {
-      int64_t u = u0;
-      for (int k = 0; u < u1; ++k) {
-        const int64_t ce = chunk_end(u, u1, G);
+      ChunkIter it(u0, u1, G);
+      for (int k = 0; it.more(); ++k) {
+        const int n = it.count();
         const int s = k % S;
         if (k >= S && !mbar_wait(&empty[s], ((k / S) - 1) & 1)) break;
-        const uint32_t bytes = (uint32_t)(ce - u) * kRecBytes;
+        const uint32_t bytes = (uint32_t)n * kRecBytes;
         mbar_arrive_expect_tx(&full[s], bytes);
-        bulk_g2s(smem + (size_t)s * kDecStageBytes, p.packed + u * kRecBytes, bytes, &full[s]);
-        u = ce;
+        bulk_g2s(smem + (size_t)s * kDecStageBytes, p.packed + it.u * kRecBytes, bytes, &full[s]);
+        it.advance(n);
+        if (XS && (k == S - 1 || (!it.more() && k < S - 1))) {
+          // the ring is full of weights: now fetch the activations, which
+          // the previous kernel may still be writing
+          grid_dependency_wait();
+          mbar_arrive_expect_tx(xbar, (uint32_t)ntok_slice * p.K);
+          for (int r = 0; r < ntok_slice; ++r)
+            bulk_g2s(xrows + (size_t)r * xstride, p.xq + (tok0 + r) * (int64_t)p.K, (uint32_t)p.K, xbar);
+        }
+      }
+      if (XS && u1 <= u0) {  // no weights to stream: still complete xbar
+        grid_dependency_wait();
+        mbar_arrive_expect_tx(xbar, (uint32_t)ntok_slice * p.K);
+        for (int r = 0; r < ntok_slice; ++r)
+          bulk_g2s(xrows + (size_t)r * xstride, p.xq + (tok0 + r) * (int64_t)p.K, (uint32_t)p.K, xbar);
+      }
+    }
+    return;
+  }
+
+  if (warp == kDecConsumers + 1) {  // epilogue warp
+    grid_dependency_wait();         // token scales come from the previous kernel
+    uint32_t* cnt = p.cnt + (size_t)blockIdx.y * (p.N / kRecRows);
+    const int nb0 = (int)(u0 / G);
+    const int nseg = u1 > u0 ? (int)((u1 - 1) / G) - nb0 + 1 : 0;
+    const int ntok = (int)min64(kDecMaxTokens, p.M - tok0);
+    for (int q = 0; q < nseg; ++q) {
+      const int par = q & 1, nb = nb0 + q;
+      const int64_t seg_b = max64(u0, (int64_t)nb * G), seg_e = min64(u1, (int64_t)(nb + 1) * G);
+      const int seg_units = (int)(seg_e - seg_b);
+      if (!mbar_wait(&seg_full[par], (q >> 1) & 1)) return;
+      float v[MT * 4];
+#pragma unroll
+      for (int sl = 0; sl < MT * 4; ++sl) {
+        float a = 0.f;
+#pragma unroll
+        for (int w = 0; w < kDecConsumers; ++w) a += red[(size_t)(par * kDecConsumers + w) * kSlice + sl * 32 + lane];
+        v[sl] = a;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&seg_free[par]);
+      const bool whole = seg_units == G;
+#pragma unroll
+      for (int sl = 0; sl < MT * 4; ++sl) {
+        const int mt = sl >> 2, i = sl & 3;
+        const int64_t t = tok0 + mt * 8 + 2 * tig + (i & 1);
+        const int n = nb * kRecRows + gid + ((i >> 1) << 3);
+        if (t < p.M) {
+          if (whole)
+            store_out(p.out, p.out_dtype, (size_t)t * p.N + n,
+                      v[sl] * p.xscale[t] + bias_at(p.bias, p.bias_dtype, n));
+          else
+            red_add_f32(p.ws + (size_t)n * p.M + t, v[sl]);
+        }
+      }
+      if (!whole) {
+        // release the warp's partial adds, count the units; the CTA that
+        // completes the row block acquires every partial and finishes it
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) {
+          asm volatile("fence.acq_rel.gpu;" ::: "memory");
+          const uint32_t old = atomicAdd(&cnt[nb], (uint32_t)seg_units);
+          last = (old + (uint32_t)seg_units == (uint32_t)G);
+          if (last) asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+          for (int idx = lane; idx < kRecRows * ntok; idx += 32) {
+            const int r = idx / ntok, tt = idx - r * ntok;
+            const int n = nb * kRecRows + r;
+            const int64_t t = tok0 + tt;
+            float* wp = p.ws + (size_t)n * p.M + t;
+            const float a = __ldcg(wp);
+            __stcg(wp, 0.f);
+            store_out(p.out, p.out_dtype, (size_t)t * p.N + n, a * p.xscale[t] + bias_at(p.bias, p.bias_dtype, n));
+          }
+          __syncwarp();
+          if (lane == 0) cnt[nb] = 0u;
+        }
       }
     }
     return;
@@ -211,7 +321,6 @@ __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p
   // consumers
   const int cw = warp - 1;
   const int ctid = threadIdx.x - 32;
-  const int gid = lane >> 2, tig = lane & 3;
   const int8_t* xrow[MT];
   bool xvalid[MT];
 #pragma unroll
@@ -220,24 +329,29 @@ __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p
     xvalid[mt] = t < p.M;
     xrow[mt] = p.xq + (xvalid[mt] ? t : 0) * (int64_t)p.K + 4 * tig;
   }
-  grid_dependency_wait();  // the activations come from the previous kernel
   if constexpr (XS) {
-    for (int e = ctid; e < G * MT * 32; e += kDecConsumers * 32) {
-      const int l = e & 31, gm = e >> 5, mt = gm % MT, g = gm / MT;
-      const int lgid = l >> 2, ltig = l & 3;
-      const int64_t t = tok0 + mt * 8 + lgid;
-      uint32_t b[8];
-      load_bfrag_global(p.xq + (t < p.M ? t : 0) * (int64_t)p.K + 4 * ltig, t < p.M, g, b);
-      xs[2 * e] = make_uint4(b[0], b[1], b[2], b[3]);
-      xs[2 * e + 1] = make_uint4(b[4], b[5], b[6], b[7]);
-      // the 4 lanes of one token row cover the group's 128 channels (the
-      // trip count is uniform across a warp, so the shuffles are safe)
-      int part = frag_sum(b);
-      part += __shfl_xor_sync(0xffffffffu, part, 1);
-      part += __shfl_xor_sync(0xffffffffu, part, 2);
-      if (ltig == 0) sxs[(g * MT + mt) * 8 + lgid] = part;
+    // rows beyond the slice's tokens hold stale bytes; they only feed output
+    // columns that are never stored
+    if (!mbar_wait(xbar, 0)) return;
+    for (int e = ctid; e < G * MP; e += kDecConsumers * 32) {
+      const int g = e / MP, r = e - g * MP;
+      int sum = 0;
+      if (r < ntok_slice) {
+        const uint4* src = reinterpret_cast<const uint4*>(xrows + (size_t)r * xstride + (size_t)g * kGroup);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const uint4 v = src[c];
+          sum = __dp4a((int)v.x, 0x01010101, sum);
+          sum = __dp4a((int)v.y, 0x01010101, sum);
+          sum = __dp4a((int)v.z, 0x01010101, sum);
+          sum = __dp4a((int)v.w, 0x01010101, sum);
+        }
+      }
+      sxs[e] = sum;
     }
     named_barrier(1, kDecConsumers * 32);
+  } else {
+    grid_dependency_wait();  // the activations come from the previous kernel
   }
 
   float y[MT][4];
@@ -246,28 +360,29 @@ __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p
 #pragma unroll
     for (int i = 0; i < 4; ++i) y[mt][i] = 0.f;
 
-  int64_t u = u0;
-  for (int k = 0; u < u1; ++k) {
-    const int64_t ce = chunk_end(u, u1, G);
+  ChunkIter it(u0, u1, G);
+  int q = 0;
+  for (int k = 0; it.more(); ++k) {
+    const int n = it.count();
     const int s = k % S;
-    const int64_t nb = u / G;
-    const int gbase = (int)(u - nb * G) / kDecChunkGroups * kDecChunkGroups;
+    const int gfirst = it.g, gbase = (it.g >> 4) << 4;
     if (!mbar_wait(&full[s], (k / S) & 1)) return;
 #pragma unroll
     for (int slot = 0; slot < 2; ++slot) {
       const int g = gbase + slot * 8 + cw;
-      const int64_t ur = nb * G + g;
-      if (ur >= u && ur < ce) {
+      if (g >= gfirst && g < gfirst + n) {
         uint32_t bf[MT][8];
         int sx[MT][2];
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt) {
           if constexpr (XS) {
-            const uint4* xp = xs + 2 * ((g * MT + mt) * 32 + lane);
-            const uint4 lo = xp[0], hi = xp[1];
-            bf[mt][0] = lo.x; bf[mt][1] = lo.y; bf[mt][2] = lo.z; bf[mt][3] = lo.w;
-            bf[mt][4] = hi.x; bf[mt][5] = hi.y; bf[mt][6] = hi.z; bf[mt][7] = hi.w;
-            const int2 s2 = *reinterpret_cast<const int2*>(sxs + (g * MT + mt) * 8 + 2 * tig);
+            const uint8_t* xb = xrows + (size_t)(mt * 8 + gid) * xstride + (size_t)g * kGroup + 4 * tig;
+#pragma unroll
+            for (int s4 = 0; s4 < 4; ++s4) {
+              bf[mt][2 * s4] = *reinterpret_cast<const uint32_t*>(xb + 32 * s4);
+              bf[mt][2 * s4 + 1] = *reinterpret_cast<const uint32_t*>(xb + 32 * s4 + 16);
+            }
+            const int2 s2 = *reinterpret_cast<const int2*>(sxs + (size_t)g * MP + mt * 8 + 2 * tig);
             sx[mt][0] = s2.x;
             sx[mt][1] = s2.y;
           } else {
@@ -280,69 +395,28 @@ __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p
             sx[mt][1] = __shfl_sync(0xffffffffu, part, 8 * tig + 4);
           }
         }
-        process_record<MT>(smem + (size_t)s * kDecStageBytes + (size_t)(ur - u) * kRecBytes, bf, sx, gid, tig, y);
+        process_record<MT>(smem + (size_t)s * kDecStageBytes + (size_t)(g - gfirst) * kRecBytes, bf, sx, gid, tig,
+                           y);
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
 
-    const bool seg_done = (ce == u1) || (ce % G == 0);
-    if (seg_done) {
-      const int64_t seg_begin = max64(u0, nb * (int64_t)G);
-      const int seg_units = (int)(ce - seg_begin);
-      const bool whole = seg_units == G;
+    if (it.advance(n)) {  // segment end: hand this warp's partial to the epilogue warp
+      const int par = q & 1;
+      if (q >= 2 && !mbar_wait(&seg_free[par], ((q >> 1) - 1) & 1)) return;
+      float* sl = red + (size_t)(par * kDecConsumers + cw) * kSlice;
 #pragma unroll
       for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) red[(cw * MT * 4 + mt * 4 + i) * 32 + lane] = y[mt][i];
-      named_barrier(1, kDecConsumers * 32);
-      for (int slot = cw; slot < MT * 4; slot += kDecConsumers) {
-        float v = 0.f;
-#pragma unroll
-        for (int w = 0; w < kDecConsumers; ++w) v += red[(w * MT * 4 + slot) * 32 + lane];
-        const int mt = slot >> 2, i = slot & 3;
-        const int64_t t = tok0 + mt * 8 + 2 * tig + (i & 1);
-        const int n = (int)nb * kRecRows + gid + ((i >> 1) << 3);
-        if (t < p.M) {
-          if (whole)
-            store_out(p.out, p.out_dtype, (size_t)t * p.N + n, v * p.xscale[t] + bias_at(p.bias, p.bias_dtype, n));
-          else
-            red_add_f32(p.ws + (size_t)n * p.M + t, v);
+        for (int i = 0; i < 4; ++i) {
+          sl[(mt * 4 + i) * 32 + lane] = y[mt][i];
+          y[mt][i] = 0.f;
         }
-      }
-      if (!whole) {
-        // release: the CTA's partial adds (ordered before thread 0 by the
-        // barrier) become visible before the counter moves; the CTA that
-        // completes the count acquires them all
-        named_barrier(1, kDecConsumers * 32);
-        if (ctid == 0) {
-          asm volatile("fence.acq_rel.gpu;" ::: "memory");
-          const uint32_t old = atomicAdd(&cnt[nb], (uint32_t)seg_units);
-          last_flag = (old + (uint32_t)seg_units == (uint32_t)G);
-          if (last_flag) asm volatile("fence.acq_rel.gpu;" ::: "memory");
-        }
-        named_barrier(1, kDecConsumers * 32);
-        if (last_flag) {
-          const int ntok = (int)min64(kDecMaxTokens, p.M - tok0);
-          for (int idx = ctid; idx < kRecRows * ntok; idx += kDecConsumers * 32) {
-            const int r = idx / ntok, tt = idx - r * ntok;
-            const int n = (int)nb * kRecRows + r;
-            const int64_t t = tok0 + tt;
-            float* wp = p.ws + (size_t)n * p.M + t;
-            const float v = __ldcg(wp);
-            __stcg(wp, 0.f);
-            store_out(p.out, p.out_dtype, (size_t)t * p.N + n, v * p.xscale[t] + bias_at(p.bias, p.bias_dtype, n));
-          }
-          if (ctid == 0) cnt[nb] = 0u;
-        }
-      }
-      named_barrier(1, kDecConsumers * 32);
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) y[mt][i] = 0.f;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&seg_full[par]);
+      ++q;
     }
-    u = ce;
   }
 }
 
@@ -358,14 +432,16 @@ size_t gemm_decode_workspace(int64_t M, int N) {
 }
 
 static size_t fixed_smem(int MT) {
-  return 2 * kDecMaxStages * sizeof(uint64_t) + (size_t)kDecConsumers * MT * 4 * 32 * sizeof(float);
+  // full/empty rings, seg_full/seg_free pairs, xbar (+1 slot keeps 16-byte
+  // alignment), then the epilogue slices
+  return (2 * kDecMaxStages + 6) * sizeof(uint64_t) + 2 * (size_t)kDecConsumers * MT * 4 * 32 * sizeof(float);
 }
 
 template <int MT, bool XS>
 static cudaError_t launch_mt(DecParams p, size_t xs_bytes, cudaStream_t st) {
   const size_t smem = (size_t)p.stages * kDecStageBytes + fixed_smem(MT) + (XS ? xs_bytes : 0);
   auto kern = gemm_stream_kernel<MT, XS>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = ensure_smem_limit((const void*)kern, kDecSmemBudget + 4096);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)p.ctas, (unsigned)((p.M + kDecMaxTokens - 1) / kDecMaxTokens), 1);
@@ -383,7 +459,7 @@ static cudaError_t launch_mt(DecParams p, size_t xs_bytes, cudaStream_t st) {
 template <int MT>
 static cudaError_t launch_pick(DecParams p, cudaStream_t st) {
   const int G = p.K / kGroup;
-  const size_t xs_bytes = (size_t)G * MT * 32 * 32 + (size_t)G * MT * 8 * sizeof(int);
+  const size_t xs_bytes = (size_t)8 * MT * (p.K + 16) + (size_t)G * 8 * MT * sizeof(int);
   const size_t base = fixed_smem(MT);
   const bool xs = base + xs_bytes + 3 * (size_t)kDecStageBytes <= (size_t)kDecSmemBudget;
   const size_t avail = kDecSmemBudget - base - (xs ? xs_bytes : 0);

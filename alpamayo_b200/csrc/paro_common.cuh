@@ -60,6 +60,10 @@ __device__ __forceinline__ float round_fp16(float v) {
 // reference's Triton quantiser); calls the CUDA math library's roundf.
 __device__ __forceinline__ float round_half_away(float v) { return roundf(v); }
 
+// Raise a kernel's dynamic shared-memory limit to `bytes` once per (kernel,
+// device); later calls are a map lookup instead of a driver call.
+cudaError_t ensure_smem_limit(const void* kernel, int bytes);
+
 // ---------------------------------------------------------------------------
 // small PTX wrappers
 // ---------------------------------------------------------------------------

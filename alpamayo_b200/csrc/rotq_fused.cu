@@ -219,7 +219,7 @@ static cudaError_t launch_fused(const FusedGeom& f, const void* x, int64_t M, in
                                 const uint32_t* rtab, int fp16_round, int8_t* q, float* s, cudaStream_t st) {
   const size_t smem = (8 + 2 * (size_t)R) * f.P * f.GB * 128 * sizeof(float);
   auto kern = rotq_fused_kernel<InT, R, PM>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  cudaError_t e = ensure_smem_limit((const void*)kern, 200 * 1024);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)f.C, (unsigned)((M + R - 1) / R), 1);
