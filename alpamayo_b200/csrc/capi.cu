@@ -39,6 +39,7 @@ cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int
 
 namespace paro {
 uint32_t error_word_decode(int clear);
+uint32_t error_word_tc(int clear);
 
 cudaError_t ensure_smem_limit(const void* kernel, int bytes) {
   static std::mutex mu;
@@ -181,9 +182,9 @@ size_t paro_w4a8_gemm_workspace_size(int64_t M, int N, int K) {
 }
 
 int paro_device_error_word(int clear) {
-  const uint32_t a = error_word_decode(clear);
-  if (a == ~0u) return -1;
-  return (int)a;
+  const uint32_t a = error_word_decode(clear), b = error_word_tc(clear);
+  if (a == ~0u || b == ~0u) return -1;
+  return (int)(a | b);
 }
 
 int paro_w4a8_gemm(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
@@ -197,6 +198,7 @@ int paro_w4a8_gemm(const int8_t* xq, const float* xscale, int64_t M, int N, int 
   if (M == 0) return PARO_OK;
   if (int d = device_check()) return d;
   if (gemm_tc_supported(M, N, K)) {
+    if (!aligned(out, 16)) return PARO_ERR_MISALIGNED;
     if (workspace_bytes < gemm_tc_workspace(M, N, K) || (gemm_tc_workspace(M, N, K) && !workspace))
       return PARO_ERR_WORKSPACE;
     return cuda_status(launch_gemm_tc(xq, xscale, M, N, K, packed, bias, bias_dtype, out, out_dtype, workspace,
@@ -210,3 +212,4 @@ int paro_w4a8_gemm(const int8_t* xq, const float* xscale, int64_t M, int N, int 
 }
 
 }  // extern "C"
+

@@ -1,13 +1,438 @@
-// gemm_tc.cu — tcgen05 (kind::i8, TMEM accumulators) int4 x int8 GEMM for
-// prefill shapes, sm_100a.  (Kernel body added in the following change; until
-// then no shape is routed here.)
-#include "paro_common.cuh"
+// gemm_tc.cu — int4 x int8 GEMM on the 5th-generation tensor cores (tcgen05,
+// kind::i8, int32 accumulators in tensor memory) for prefill shapes, sm_100a.
+//
+// y[m, n] = xscale[m] * sum_g s[g, n] * sum_{k in g} (q[n, k] - z[g, n]) x[m, k] (+ bias[n])
+//
+// One CTA computes a 128 (tokens) x 256 (output rows) tile, walking K one
+// 128-channel group per pipeline stage:
+//
+//  * warp 0 (producer): per group, one tensor TMA of the activation tile
+//    (128 rows x 128 int8 channels, 128-byte swizzle = the UMMA K-major
+//    canonical layout) and 16 bulk copies of the weight tile records
+//    (16 rows x 128 channels each).
+//  * warpgroup 1 (expansion): unpacks each record's int4 codes to signed
+//    int8 (q - z) and writes them in the same swizzled K-major layout.
+//  * warp 1 (MMA): issues 4 tcgen05.mma (K = 32 each) per group into one of
+//    two 256-column TMEM buffers and commits completion to mbarriers.
+//  * warpgroups 2-3 (epilogue): fold each finished group into float32
+//    registers while the tensor core works on the next group.  Each TMEM
+//    buffer is pre-seeded with the integer bit pattern of 1.5 * 2^23, so after
+//    the group's MMAs the int32 word reinterpreted as float32 is exactly
+//    1.5 * 2^23 + acc (|acc| < 2^22); one packed subtract and one packed FMA
+//    per two elements apply the group scale, then the buffer is re-seeded.
+//    After the last group: token scale, bias, convert, store.
+//
+// All mbarrier waits are bounded (report kErrMbarTimeout and drop out), and
+// the tensor memory is freed on every path out of the kernel.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "tc_ptx.cuh"
 
 namespace paro {
-int gemm_tc_supported(int64_t, int, int) { return 0; }
-size_t gemm_tc_workspace(int64_t, int, int) { return 0; }
-cudaError_t launch_gemm_tc(const int8_t*, const float*, int64_t, int, int, const void*, const void*, int, void*, int,
-                           void*, size_t, cudaStream_t) {
-  return cudaErrorNotSupported;
+
+PARO_DEFINE_ERROR_ACCESSOR(tc)
+
+constexpr int kTcBM = 128;
+constexpr int kTcBN = 256;
+constexpr int kTcStages = 3;
+constexpr int kTcThreads = 512;
+constexpr int kTcRecs = kTcBN / kRecRows;                // 16 records per group
+constexpr int kTcABytes = kTcBM * kGroup;                 // 16 KB
+constexpr int kTcBBytes = kTcBN * kGroup;                 // 32 KB
+constexpr int kTcRawBytes = kTcRecs * kRecBytes;          // 17152
+constexpr uint32_t kMagic = 0x4B400000u;                  // bits of 12582912.0f = 1.5 * 2^23
+constexpr float kMagicF = 12582912.0f;
+
+// shared memory plan (offsets from a 1024-byte aligned base)
+constexpr int kOffA = 0;
+constexpr int kOffB = kOffA + kTcStages * kTcABytes;
+constexpr int kOffRaw = kOffB + kTcStages * kTcBBytes;
+constexpr int kOffScale = kOffRaw + kTcStages * kTcRawBytes;          // [3][256] float
+constexpr int kOffBar = kOffScale + 3 * kTcBN * 4;
+constexpr int kTcSmem = kOffBar + 256 + 1024;                         // + alignment slack
+
+struct TcParams {
+  const float* xscale;
+  int64_t M;
+  int N, K;
+  const uint8_t* packed;
+  const void* bias;
+  int bias_dtype;
+  void* out;
+  int out_dtype;
+};
+
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+  // K-major, 128-byte swizzle: 8-row atoms of 1024 bytes (stride byte offset
+  // 1024), leading byte offset unused (1), descriptor version 1 (sm_100)
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
+
+// instruction descriptor: s32 accumulate, A s8, B s8, both K-major, N = 256, M = 128
+constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTcBN >> 3) << 17) |
+                            ((uint32_t)(kTcBM >> 4) << 24);
+
+__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(kIdesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr));
+}
+
+// Seeds 8 consecutive columns of this warp's 32 lanes with the magic value
+// (the .x8 shape keeps the source register block small).
+__device__ __forceinline__ void tmem_st8_magic(uint32_t taddr) {
+  const uint32_t m = kMagic;
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr), "r"(m)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// packed float32 pair arithmetic (sm_100)
+__device__ __forceinline__ uint64_t pack2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float2 unpack2(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t expand_signed(uint32_t nib4, uint32_t zz) {
+  // bytes 0x80 + q - z (no borrows: q, z <= 15), then flip the bias bit
+  return ((nib4 | 0x80808080u) - zz) ^ 0x80808080u;
+}
+
+__device__ __forceinline__ float tc_bias(const void* bias, int dtype, int n) {
+  if (!bias) return 0.f;
+  if (dtype == PARO_F16) return __half2float(static_cast<const __half*>(bias)[n]);
+  if (dtype == PARO_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(bias)[n]);
+  return static_cast<const float*>(bias)[n];
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap amap, TcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint64_t* full_raw = reinterpret_cast<uint64_t*>(smem + kOffBar);     // [3] A + records landed
+  uint64_t* bexp_full = full_raw + kTcStages;                            // [3] expanded B written
+  uint64_t* smem_empty = bexp_full + kTcStages;                          // [3] MMA done with the stage
+  uint64_t* acc_full = smem_empty + kTcStages;                           // [2] group's MMAs complete
+  uint64_t* acc_empty = acc_full + 2;                                    // [2] epilogue read + re-seeded
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  float* scale_ring = reinterpret_cast<float*>(smem + kOffScale);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = p.K / kGroup;
+  const int n0 = blockIdx.x * kTcBN;
+  const int64_t m0 = (int64_t)blockIdx.y * kTcBM;
+  const int nrec = min(kTcRecs, (p.N - n0) / kRecRows);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTcStages; ++s) {
+      mbar_init(&full_raw[s], 1);
+      mbar_init(&bexp_full[s], 128);
+      mbar_init(&smem_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 8);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot))
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool failed = false;
+
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 56;");
+    if (warp == 0 && lane == 0) {
+      // producer
+      for (int g = 0; g < G && !failed; ++g) {
+        const int s = g % kTcStages;
+        if (g >= kTcStages && !mbar_wait(&smem_empty[s], ((g / kTcStages) - 1) & 1)) {
+          failed = true;
+          break;
+        }
+        mbar_arrive_expect_tx(&full_raw[s], (uint32_t)(kTcABytes + nrec * kRecBytes));
+        tma_load_2d(smem + kOffA + s * kTcABytes, &amap, g * kGroup, (int)m0, &full_raw[s]);
+        uint8_t* raw = smem + kOffRaw + s * kTcRawBytes;
+        for (int i = 0; i < nrec; ++i)
+          bulk_g2s(raw + i * kRecBytes, p.packed + rec_offset(n0 / kRecRows + i, g, G), kRecBytes, &full_raw[s]);
+      }
+    } else if (warp == 1 && lane == 0) {
+      // MMA issuer
+      const uint32_t a_base = smem_u32(smem + kOffA), b_base = smem_u32(smem + kOffB);
+      for (int g = 0; g < G && !failed; ++g) {
+        const int s = g % kTcStages, b = g & 1;
+        if (!mbar_wait(&full_raw[s], (g / kTcStages) & 1) || !mbar_wait(&bexp_full[s], (g / kTcStages) & 1) ||
+            !mbar_wait(&acc_empty[b], (g >> 1) & 1)) {
+          failed = true;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t da = umma_desc_sw128(a_base + s * kTcABytes);
+        const uint64_t db = umma_desc_sw128(b_base + s * kTcBBytes);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) mma_i8(tmem + b * kTcBN, da + 2 * kk, db + 2 * kk, 1u);
+        umma_commit(&smem_empty[s]);
+        umma_commit(&acc_full[b]);
+      }
+    }
+  } else if (warp < 8) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 88;");
+    // expansion: thread t writes rows t and t + 128 of the 256-row B tile
+    const int t = threadIdx.x - 128;
+    for (int g = 0; g < G && !failed; ++g) {
+      const int s = g % kTcStages;
+      if (!mbar_wait(&full_raw[s], (g / kTcStages) & 1)) {
+        failed = true;
+        break;
+      }
+      const uint8_t* raw = smem + kOffRaw + s * kTcRawBytes;
+      uint8_t* bt = smem + kOffB + s * kTcBBytes;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int n = t + 128 * h;
+        const int i = n >> 4, r = n & 15;
+        uint8_t* row = bt + n * 128;
+        const int sw = n & 7;
+        if (i < nrec) {
+          const uint8_t* rec = raw + i * kRecBytes;
+          const uint32_t zz = (uint32_t)rec[kRecZeroOff + r] * 0x01010101u;
+          uint32_t w[4][4];  // [t][j]
+#pragma unroll
+          for (int tt = 0; tt < 4; ++tt) {
+            const uint4 v = *reinterpret_cast<const uint4*>(rec + r * 64 + tt * 16);
+            w[tt][0] = v.x; w[tt][1] = v.y; w[tt][2] = v.z; w[tt][3] = v.w;
+          }
+          // 16-channel chunk c < 4 holds the low nibbles of words (t, c) for
+          // t = 0..3; chunk c + 4 holds their high nibbles
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            *reinterpret_cast<uint4*>(row + ((c ^ sw) << 4)) =
+                make_uint4(expand_signed(w[0][c] & 0x0F0F0F0Fu, zz), expand_signed(w[1][c] & 0x0F0F0F0Fu, zz),
+                           expand_signed(w[2][c] & 0x0F0F0F0Fu, zz), expand_signed(w[3][c] & 0x0F0F0F0Fu, zz));
+            *reinterpret_cast<uint4*>(row + (((c + 4) ^ sw) << 4)) =
+                make_uint4(expand_signed((w[0][c] >> 4) & 0x0F0F0F0Fu, zz),
+                           expand_signed((w[1][c] >> 4) & 0x0F0F0F0Fu, zz),
+                           expand_signed((w[2][c] >> 4) & 0x0F0F0F0Fu, zz),
+                           expand_signed((w[3][c] >> 4) & 0x0F0F0F0Fu, zz));
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(row + (c << 4)) = make_uint4(0, 0, 0, 0);
+        }
+      }
+      fence_proxy_async_smem();  // make the generic-proxy writes visible to the tensor core
+      mbar_arrive(&bexp_full[s]);
+    }
+  } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 184;");
+    // epilogue: 8 warps; warp (w % 4) owns TMEM lanes 32*(w%4).., and
+    // column half (w - 8) / 4
+    const int ew = warp - 8;
+    const int q4 = warp & 3, half = ew >> 2;
+    const int et = threadIdx.x - 256;  // 0..255: the column this thread fetches scales for
+    const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
+    const int col0 = half * 128;
+    // scale prefetch: column et's scale of a group, from its tile record
+    auto fetch_scale = [&](int g) -> float {
+      const int i = et >> 4, r = et & 15;
+      if (g >= G || i >= nrec) return 0.f;
+      const uint16_t* sp = reinterpret_cast<const uint16_t*>(p.packed + rec_offset(n0 / kRecRows + i, g, G) +
+                                                             kRecScaleOff);
+      return half_bits_to_f32(__ldg(sp + r));
+    };
+    scale_ring[0 * kTcBN + et] = fetch_scale(0);
+    scale_ring[1 * kTcBN + et] = fetch_scale(1);
+    float pending = fetch_scale(2);
+    // seed both accumulator buffers
+#pragma unroll
+    for (int c = 0; c < 128; c += 8) {
+      tmem_st8_magic(tmem + lane_base + col0 + c);
+      tmem_st8_magic(tmem + lane_base + kTcBN + col0 + c);
+    }
+    tmem_wait_st();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) {
+      mbar_arrive(&acc_empty[0]);
+      mbar_arrive(&acc_empty[1]);
+    }
+    uint64_t y[64];
+#pragma unroll
+    for (int j = 0; j < 64; ++j) y[j] = 0ull;  // (+0.0f, +0.0f)
+    const uint64_t negc = pack2(-kMagicF, -kMagicF);
+    for (int g = 0; g < G && !failed; ++g) {
+      const int b = g & 1;
+      if (g >= 1) scale_ring[((g + 1) % 3) * kTcBN + et] = pending;
+      pending = fetch_scale(g + 2);
+      named_barrier(2, 256);
+      if (!mbar_wait(&acc_full[b], (g >> 1) & 1)) {
+        failed = true;
+        break;
+      }
+      tc_fence_after();
+      const float* sc = scale_ring + (g % 3) * kTcBN + col0;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        uint32_t v[16];
+        tmem_ld16(tmem + lane_base + b * kTcBN + col0 + c * 16, v);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float2 s2 = *reinterpret_cast<const float2*>(sc + c * 16 + 2 * j);
+          const uint64_t t2 = add2(pack2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1])), negc);
+          y[c * 8 + j] = fma2(pack2(s2.x, s2.y), t2, y[c * 8 + j]);
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 16; ++c) tmem_st8_magic(tmem + lane_base + b * kTcBN + col0 + c * 8);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+    }
+    // token scale, bias, convert, store: this thread holds row m0 + 32*q4 + lane
+    const int64_t m = m0 + q4 * 32 + lane;
+    if (!failed && m < p.M) {
+      const float a = p.xscale[m];
+#pragma unroll
+      for (int c8 = 0; c8 < 16; ++c8) {
+        const int nb = n0 + col0 + c8 * 8;
+        if (nb >= p.N) break;
+        float o[8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = unpack2(y[c8 * 4 + e]);
+          o[2 * e] = f.x * a + tc_bias(p.bias, p.bias_dtype, nb + 2 * e);
+          o[2 * e + 1] = f.y * a + tc_bias(p.bias, p.bias_dtype, nb + 2 * e + 1);
+        }
+        if (p.out_dtype == PARO_BF16) {
+          __nv_bfloat162 h[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(o[2 * e], o[2 * e + 1]);
+          *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + m * p.N + nb) = *reinterpret_cast<uint4*>(h);
+        } else if (p.out_dtype == PARO_F16) {
+          __half2 h[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) h[e] = __floats2half2_rn(o[2 * e], o[2 * e + 1]);
+          *reinterpret_cast<uint4*>(static_cast<__half*>(p.out) + m * p.N + nb) = *reinterpret_cast<uint4*>(h);
+        } else {
+          float* dst = static_cast<float*>(p.out) + m * p.N + nb;
+          *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+          *reinterpret_cast<float4*>(dst + 4) = make_float4(o[4], o[5], o[6], o[7]);
+        }
+      }
+    }
+  }
+
+  // every role reaches this point; the tensor memory is freed once nobody
+  // reads it any more
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// The tensor-core kernel handles token counts above the decode range.
+int gemm_tc_supported(int64_t M, int N, int K) { return M > 64 && N % kRecRows == 0 && K % kGroup == 0; }
+
+size_t gemm_tc_workspace(int64_t, int, int) { return 0; }
+
+cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
+                           const void* bias, int bias_dtype, void* out, int out_dtype, void*, size_t,
+                           cudaStream_t st) {
+  auto encode = get_encode();
+  if (!encode) return cudaErrorNotSupported;
+  if (M > 0x7FFFFFFF) return cudaErrorInvalidValue;
+  CUtensorMap amap;
+  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+  const cuuint64_t strides[1] = {(cuuint64_t)K};
+  const cuuint32_t box[2] = {(cuuint32_t)kGroup, (cuuint32_t)kTcBM};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode(&amap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(xq), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  TcParams p;
+  p.xscale = xscale;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.packed = static_cast<const uint8_t*>(packed);
+  p.bias = bias;
+  p.bias_dtype = bias_dtype;
+  p.out = out;
+  p.out_dtype = out_dtype;
+  cudaError_t e = ensure_smem_limit((const void*)gemm_tc_kernel, kTcSmem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((unsigned)((N + kTcBN - 1) / kTcBN), (unsigned)((M + kTcBM - 1) / kTcBM));
+  gemm_tc_kernel<<<grid, kTcThreads, kTcSmem, st>>>(amap, p);
+  return cudaGetLastError();
+}
+
 }  // namespace paro

@@ -69,10 +69,12 @@ def test_single_group_int32_exact(ops, M):
     assert np.array_equal(y, P)
 
 
-def test_multi_group_int32_exact_with_power_of_two_scales(ops):
+@pytest.mark.parametrize("M", [8, 256])
+def test_multi_group_int32_exact_with_power_of_two_scales(ops, M):
     """Scales 2^-g keep every product and sum exact in fp32, so the output
-    must equal the exact per-group partials combined."""
-    N, K, M = 128, 512, 8   # 18-bit partials x 2^-3 stay within fp32's 24 bits
+    must equal the exact per-group partials combined (M = 8: decode kernel,
+    M = 256: tensor-core kernel)."""
+    N, K = 128, 512   # 18-bit partials x 2^-3 stay within fp32's 24 bits
     G = K // 128
     rng = np.random.default_rng(1)
     codes = rng.integers(0, 16, (N, K))
@@ -154,3 +156,27 @@ def test_gemm_linearity_in_token_scale(ops):
     y1 = _run(ops, xq, xs, packed, N).cpu().numpy()
     y2 = _run(ops, xq, 2 * xs, packed, N).cpu().numpy()
     assert np.array_equal(2 * y1, y2)
+
+
+@pytest.mark.parametrize("N,K,M", [(272, 256, 65), (512, 128, 129), (768, 1024, 300), (4608, 3584, 2048),
+                                   (3584, 18944, 256), (37888, 3584, 160)])
+def test_tensor_core_gemm_tiles_match_oracle(ops, N, K, M):
+    """The tcgen05 kernel (M > 64): full and partial 128-token x 256-row
+    tiles, against the oracle on sampled rows and columns."""
+    from alpamayo_b200 import _native
+    assert _native.capi().paro_w4a8_gemm_path(M, N, K) == 1
+    codes, scales, zeros, packed = records_layer(N, K, seed=N // 16 + K + M)
+    rng = np.random.default_rng(N + K + M)
+    xq = rng.integers(-127, 128, (M, K)).astype(np.int8)
+    xs = (rng.random(M) * 0.1 + 0.01).astype(np.float32)
+    bias = (rng.standard_normal(N) * 0.1).astype(np.float32)
+    bias_bf = dev(bias).to(torch.bfloat16)
+    rows = np.sort(rng.choice(M, size=min(M, 192), replace=False))
+    cols = np.sort(rng.choice(N, size=min(N, 512), replace=False))
+    ref = O.w4a8_linear(xq[rows], xs[rows], codes[cols], zeros[:, cols], scales[:, cols],
+                        bias=bias_bf.float().cpu().numpy()[cols])
+    y = ops.w4a8_gemm(dev(xq), dev(xs), packed, N, bias_bf, torch.bfloat16).float().cpu().numpy()
+    assert rel_l2(y[rows][:, cols], O.round_to_bf16(ref)) <= OUT_REL_L2
+    y32 = ops.w4a8_gemm(dev(xq), dev(xs), packed, N, bias_bf, torch.float32).cpu().numpy()
+    assert rel_l2(y32[rows][:, cols], ref) <= 1e-6
+    assert _native.capi().paro_device_error_word(1) == 0
