@@ -213,3 +213,59 @@ int paro_w4a8_gemm(const int8_t* xq, const float* xscale, int64_t M, int N, int 
 
 }  // extern "C"
 
+// ---------------------------------------------------------------------------
+// paro_w4a8_gemm_noalloc: the GEMM with its scratch in a fixed array compiled
+// into this library, for callers that may not allocate device memory.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_noalloc_scratch[PARO_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int kNoallocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kNoallocMaxDevices];  // device address of the array, per device
+
+// Set-up, once per device and with that device current: look up the array's
+// device address.  Nothing is allocated.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoallocMaxDevices) return PARO_ERR_DEVICE;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_status(e);
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return PARO_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int paro_w4a8_gemm_noalloc(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
+                           const void* bias, int bias_dtype, void* out, int out_dtype, paro_stream_t stream) {
+  if (M == 0 && N > 0 && K > 0) return PARO_OK;
+  if (!xq || !xscale || !packed || !out || M < 0 || N <= 0 || K <= 0) return PARO_ERR_INVALID_ARGUMENT;
+  if (!valid_dtype(out_dtype) || (bias && !valid_dtype(bias_dtype))) return PARO_ERR_UNSUPPORTED;
+  if (N % kRecRows || K % kGroup) return PARO_ERR_SHAPE;
+  if (!aligned(packed, 16) || !aligned(xq, 16)) return PARO_ERR_MISALIGNED;
+  if (int d = device_check()) return d;
+  if (gemm_tc_supported(M, N, K)) {
+    if (!aligned(out, 16)) return PARO_ERR_MISALIGNED;
+    return cuda_status(
+        launch_gemm_tc(xq, xscale, M, N, K, packed, bias, bias_dtype, out, out_dtype, nullptr, 0, (cudaStream_t)stream));
+  }
+  const size_t need = gemm_decode_workspace(M, N);
+  if (need > (size_t)PARO_NOALLOC_SCRATCH_BYTES) return PARO_ERR_TOO_LARGE;
+  void* scratch = nullptr;
+  if (int st = noalloc_scratch(&scratch)) return st;
+  // the decode kernel expects a zero-filled workspace; the array holds
+  // whatever the previous call left, so clear the part this call uses
+  cudaError_t e = cudaMemsetAsync(scratch, 0, need, (cudaStream_t)stream);
+  if (e != cudaSuccess) return cuda_status(e);
+  return cuda_status(launch_gemm_decode(xq, xscale, M, N, K, packed, bias, bias_dtype, out, out_dtype, scratch,
+                                        (cudaStream_t)stream));
+}
+
+}  // extern "C"

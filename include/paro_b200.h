@@ -204,6 +204,39 @@ int paro_device_error_word(int clear);
  * (0 = streaming decode kernel, 1 = tcgen05 tensor-core kernel). */
 int paro_w4a8_gemm_path(int64_t M, int N, int K);
 
+/* ---- Allocation-free GEMM (no counterpart in the reference) --------------
+ * paro_w4a8_gemm without a caller-provided workspace, for callers that may
+ * not allocate device memory when they run a layer: an engine whose memory
+ * pool already owns the whole device, a latency-critical loop that cannot
+ * afford cudaMalloc's implicit device-wide synchronisation, or a foreign
+ * binding with no device allocator of its own.  It allocates nothing: no
+ * cudaMalloc / cudaFree and no allocating library routine.
+ *
+ * The decode kernel's scratch lives in one fixed array of
+ * PARO_NOALLOC_SCRATCH_BYTES compiled into this library (one copy per
+ * device).
+ *  - Set-up: the first call on a device, with that device current, looks
+ *    up the array's device address (cudaGetSymbolAddress).  Make that first
+ *    call before any stream capture.
+ *  - Limit: shapes that run the decode kernel (M <= 64) need
+ *    paro_w4a8_gemm_workspace_size(M, N, K) bytes, about 4 * M * N; a call
+ *    needing more than PARO_NOALLOC_SCRATCH_BYTES returns
+ *    PARO_ERR_TOO_LARGE and launches nothing.  The tensor-core range
+ *    (M > 64) needs no scratch.
+ *  - State: the array keeps whatever the previous call left, so every call
+ *    first clears the part it uses (cudaMemsetAsync on `stream`).
+ *  - Concurrency: all calls on a device share the one array.  Calls whose
+ *    work can overlap on the GPU (different streams with no ordering between
+ *    them) race on it and give wrong results; order them on one stream, or
+ *    use paro_w4a8_gemm with a workspace per stream.
+ * Arguments, results and errors are otherwise those of paro_w4a8_gemm.
+ */
+#define PARO_NOALLOC_SCRATCH_BYTES (8u << 20)
+
+int paro_w4a8_gemm_noalloc(const int8_t* xq, const float* xscale, int64_t M, int N, int K,
+                           const void* packed, const void* bias, int bias_dtype,
+                           void* out, int out_dtype, paro_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
