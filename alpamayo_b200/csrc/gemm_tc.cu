@@ -3,14 +3,17 @@
 //
 // y[m, n] = xscale[m] * sum_g s[g, n] * sum_{k in g} (q[n, k] - z[g, n]) x[m, k] (+ bias[n])
 //
-// One CTA computes a 128 (tokens) x 256 (output rows) tile, walking K one
-// 128-channel group per pipeline stage:
+// One CTA computes a 128 (output rows n) x 256 (tokens m) tile of y^T: the
+// weights are the MMA's M operand and the tokens its N operand, so a TMEM
+// lane is one output row and each epilogue thread owns one row (its group
+// scale is one scalar per group).  K is walked one 128-channel group per
+// pipeline stage:
 //
 //  * warp 0 (producer): per group, one tensor TMA of the activation tile
-//    (128 rows x 128 int8 channels, 128-byte swizzle = the UMMA K-major
-//    canonical layout) and 16 bulk copies of the weight tile records
+//    (256 tokens x 128 int8 channels, 128-byte swizzle = the UMMA K-major
+//    canonical layout) and 8 bulk copies of the weight tile records
 //    (16 rows x 128 channels each).
-//  * warpgroup 1 (expansion): unpacks each record's int4 codes to signed
+//  * warpgroup 1 (expansion): thread t unpacks row t's int4 codes to signed
 //    int8 (q - z) and writes them in the same swizzled K-major layout.
 //  * warp 1 (MMA): issues 4 tcgen05.mma (K = 32 each) per group into one of
 //    two 256-column TMEM buffers and commits completion to mbarriers.
@@ -19,8 +22,8 @@
 //    buffer is pre-seeded with the integer bit pattern of 1.5 * 2^23, so after
 //    the group's MMAs the int32 word reinterpreted as float32 is exactly
 //    1.5 * 2^23 + acc (|acc| < 2^22); one packed subtract and one packed FMA
-//    per two elements apply the group scale, then the buffer is re-seeded.
-//    After the last group: token scale, bias, convert, store.
+//    per two elements apply the row's group scale, then the buffer is
+//    re-seeded.  After the last group: token scale, bias, convert, store.
 //
 // All mbarrier waits are bounded (report kErrMbarTimeout and drop out), and
 // the tensor memory is freed on every path out of the kernel.
@@ -33,23 +36,22 @@ namespace paro {
 
 PARO_DEFINE_ERROR_ACCESSOR(tc)
 
-constexpr int kTcBM = 128;
-constexpr int kTcBN = 256;
+constexpr int kTcRows = 128;                              // output rows per tile (MMA M)
+constexpr int kTcTok = 256;                               // tokens per tile (MMA N)
 constexpr int kTcStages = 3;
 constexpr int kTcThreads = 512;
-constexpr int kTcRecs = kTcBN / kRecRows;                // 16 records per group
-constexpr int kTcABytes = kTcBM * kGroup;                 // 16 KB
-constexpr int kTcBBytes = kTcBN * kGroup;                 // 32 KB
-constexpr int kTcRawBytes = kTcRecs * kRecBytes;          // 17152
+constexpr int kTcRecs = kTcRows / kRecRows;               // 8 records per group
+constexpr int kTcWBytes = kTcRows * kGroup;               // 16 KB expanded weights
+constexpr int kTcXBytes = kTcTok * kGroup;                // 32 KB activations
+constexpr int kTcRawBytes = kTcRecs * kRecBytes;          // 8576
 constexpr uint32_t kMagic = 0x4B400000u;                  // bits of 12582912.0f = 1.5 * 2^23
 constexpr float kMagicF = 12582912.0f;
 
 // shared memory plan (offsets from a 1024-byte aligned base)
-constexpr int kOffA = 0;
-constexpr int kOffB = kOffA + kTcStages * kTcABytes;
-constexpr int kOffRaw = kOffB + kTcStages * kTcBBytes;
-constexpr int kOffScale = kOffRaw + kTcStages * kTcRawBytes;          // [3][256] float
-constexpr int kOffBar = kOffScale + 3 * kTcBN * 4;
+constexpr int kOffW = 0;
+constexpr int kOffX = kOffW + kTcStages * kTcWBytes;
+constexpr int kOffRaw = kOffX + kTcStages * kTcXBytes;
+constexpr int kOffBar = kOffRaw + kTcStages * kTcRawBytes;
 constexpr int kTcSmem = kOffBar + 256 + 1024;                         // + alignment slack
 
 struct TcParams {
@@ -71,8 +73,8 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
 }
 
 // instruction descriptor: s32 accumulate, A s8, B s8, both K-major, N = 256, M = 128
-constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTcBN >> 3) << 17) |
-                            ((uint32_t)(kTcBM >> 4) << 24);
+constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTcTok >> 3) << 17) |
+                            ((uint32_t)(kTcRows >> 4) << 24);
 
 __device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
   asm volatile(
@@ -151,27 +153,40 @@ __device__ __forceinline__ float tc_bias(const void* bias, int dtype, int n) {
   return static_cast<const float*>(bias)[n];
 }
 
-__global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap amap, TcParams p) {
+// Stores one output row's `valid` (<= 128) tokens: out[j * N] = y_j * xscale[j] + bias.
+template <typename T>
+__device__ __forceinline__ void store_row(const uint64_t (&y)[64], T* out, int N, const float* xscale, float bias,
+                                          int valid) {
+#pragma unroll
+  for (int j = 0; j < 64; ++j) {
+    if (2 * j < valid) {
+      const float2 f = unpack2(y[j]);
+      out[(size_t)(2 * j) * N] = from_f32<T>(f.x * __ldg(xscale + 2 * j) + bias);
+      if (2 * j + 1 < valid) out[(size_t)(2 * j + 1) * N] = from_f32<T>(f.y * __ldg(xscale + 2 * j + 1) + bias);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap xmap, TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  uint64_t* full_raw = reinterpret_cast<uint64_t*>(smem + kOffBar);     // [3] A + records landed
-  uint64_t* bexp_full = full_raw + kTcStages;                            // [3] expanded B written
-  uint64_t* smem_empty = bexp_full + kTcStages;                          // [3] MMA done with the stage
+  uint64_t* full_raw = reinterpret_cast<uint64_t*>(smem + kOffBar);     // [3] activations + records landed
+  uint64_t* wexp_full = full_raw + kTcStages;                            // [3] expanded weights written
+  uint64_t* smem_empty = wexp_full + kTcStages;                          // [3] MMA done with the stage
   uint64_t* acc_full = smem_empty + kTcStages;                           // [2] group's MMAs complete
   uint64_t* acc_empty = acc_full + 2;                                    // [2] epilogue read + re-seeded
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
-  float* scale_ring = reinterpret_cast<float*>(smem + kOffScale);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = p.K / kGroup;
-  const int n0 = blockIdx.x * kTcBN;
-  const int64_t m0 = (int64_t)blockIdx.y * kTcBM;
+  const int n0 = blockIdx.x * kTcRows;
+  const int64_t m0 = (int64_t)blockIdx.y * kTcTok;
   const int nrec = min(kTcRecs, (p.N - n0) / kRecRows);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTcStages; ++s) {
       mbar_init(&full_raw[s], 1);
-      mbar_init(&bexp_full[s], 128);
+      mbar_init(&wexp_full[s], 128);
       mbar_init(&smem_empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -201,104 +216,94 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
           failed = true;
           break;
         }
-        mbar_arrive_expect_tx(&full_raw[s], (uint32_t)(kTcABytes + nrec * kRecBytes));
-        tma_load_2d(smem + kOffA + s * kTcABytes, &amap, g * kGroup, (int)m0, &full_raw[s]);
+        mbar_arrive_expect_tx(&full_raw[s], (uint32_t)(kTcXBytes + nrec * kRecBytes));
+        tma_load_2d(smem + kOffX + s * kTcXBytes, &xmap, g * kGroup, (int)m0, &full_raw[s]);
         uint8_t* raw = smem + kOffRaw + s * kTcRawBytes;
         for (int i = 0; i < nrec; ++i)
           bulk_g2s(raw + i * kRecBytes, p.packed + rec_offset(n0 / kRecRows + i, g, G), kRecBytes, &full_raw[s]);
       }
     } else if (warp == 1 && lane == 0) {
       // MMA issuer
-      const uint32_t a_base = smem_u32(smem + kOffA), b_base = smem_u32(smem + kOffB);
+      const uint32_t w_base = smem_u32(smem + kOffW), x_base = smem_u32(smem + kOffX);
       for (int g = 0; g < G && !failed; ++g) {
         const int s = g % kTcStages, b = g & 1;
-        if (!mbar_wait(&full_raw[s], (g / kTcStages) & 1) || !mbar_wait(&bexp_full[s], (g / kTcStages) & 1) ||
+        if (!mbar_wait(&full_raw[s], (g / kTcStages) & 1) || !mbar_wait(&wexp_full[s], (g / kTcStages) & 1) ||
             !mbar_wait(&acc_empty[b], (g >> 1) & 1)) {
           failed = true;
           break;
         }
         tc_fence_after();
-        const uint64_t da = umma_desc_sw128(a_base + s * kTcABytes);
-        const uint64_t db = umma_desc_sw128(b_base + s * kTcBBytes);
+        const uint64_t da = umma_desc_sw128(w_base + s * kTcWBytes);
+        const uint64_t db = umma_desc_sw128(x_base + s * kTcXBytes);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) mma_i8(tmem + b * kTcBN, da + 2 * kk, db + 2 * kk, 1u);
+        for (int kk = 0; kk < 4; ++kk) mma_i8(tmem + b * kTcTok, da + 2 * kk, db + 2 * kk, 1u);
         umma_commit(&smem_empty[s]);
         umma_commit(&acc_full[b]);
       }
     }
   } else if (warp < 8) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 88;");
-    // expansion: thread t writes rows t and t + 128 of the 256-row B tile
+    // expansion: thread t writes weight row t of the tile
     const int t = threadIdx.x - 128;
+    const int i = t >> 4, r = t & 15;
+    const int sw = t & 7;
     for (int g = 0; g < G && !failed; ++g) {
       const int s = g % kTcStages;
       if (!mbar_wait(&full_raw[s], (g / kTcStages) & 1)) {
         failed = true;
         break;
       }
-      const uint8_t* raw = smem + kOffRaw + s * kTcRawBytes;
-      uint8_t* bt = smem + kOffB + s * kTcBBytes;
+      uint8_t* row = smem + kOffW + s * kTcWBytes + t * 128;
+      if (i < nrec) {
+        const uint8_t* rec = smem + kOffRaw + s * kTcRawBytes + i * kRecBytes;
+        const uint32_t zz = (uint32_t)rec[kRecZeroOff + r] * 0x01010101u;
+        uint32_t w[4][4];  // [t][j]
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int n = t + 128 * h;
-        const int i = n >> 4, r = n & 15;
-        uint8_t* row = bt + n * 128;
-        const int sw = n & 7;
-        if (i < nrec) {
-          const uint8_t* rec = raw + i * kRecBytes;
-          const uint32_t zz = (uint32_t)rec[kRecZeroOff + r] * 0x01010101u;
-          uint32_t w[4][4];  // [t][j]
+        for (int tt = 0; tt < 4; ++tt) {
+          const uint4 v = *reinterpret_cast<const uint4*>(rec + r * 64 + tt * 16);
+          w[tt][0] = v.x; w[tt][1] = v.y; w[tt][2] = v.z; w[tt][3] = v.w;
+        }
+        // 16-channel chunk c < 4 holds the low nibbles of words (t, c) for
+        // t = 0..3; chunk c + 4 holds their high nibbles
 #pragma unroll
-          for (int tt = 0; tt < 4; ++tt) {
-            const uint4 v = *reinterpret_cast<const uint4*>(rec + r * 64 + tt * 16);
-            w[tt][0] = v.x; w[tt][1] = v.y; w[tt][2] = v.z; w[tt][3] = v.w;
-          }
-          // 16-channel chunk c < 4 holds the low nibbles of words (t, c) for
-          // t = 0..3; chunk c + 4 holds their high nibbles
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            *reinterpret_cast<uint4*>(row + ((c ^ sw) << 4)) =
-                make_uint4(expand_signed(w[0][c] & 0x0F0F0F0Fu, zz), expand_signed(w[1][c] & 0x0F0F0F0Fu, zz),
-                           expand_signed(w[2][c] & 0x0F0F0F0Fu, zz), expand_signed(w[3][c] & 0x0F0F0F0Fu, zz));
-            *reinterpret_cast<uint4*>(row + (((c + 4) ^ sw) << 4)) =
-                make_uint4(expand_signed((w[0][c] >> 4) & 0x0F0F0F0Fu, zz),
-                           expand_signed((w[1][c] >> 4) & 0x0F0F0F0Fu, zz),
-                           expand_signed((w[2][c] >> 4) & 0x0F0F0F0Fu, zz),
-                           expand_signed((w[3][c] >> 4) & 0x0F0F0F0Fu, zz));
-          }
-        } else {
-#pragma unroll
-          for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(row + (c << 4)) = make_uint4(0, 0, 0, 0);
+        for (int c = 0; c < 4; ++c) {
+          *reinterpret_cast<uint4*>(row + ((c ^ sw) << 4)) =
+              make_uint4(expand_signed(w[0][c] & 0x0F0F0F0Fu, zz), expand_signed(w[1][c] & 0x0F0F0F0Fu, zz),
+                         expand_signed(w[2][c] & 0x0F0F0F0Fu, zz), expand_signed(w[3][c] & 0x0F0F0F0Fu, zz));
+          *reinterpret_cast<uint4*>(row + (((c + 4) ^ sw) << 4)) =
+              make_uint4(expand_signed((w[0][c] >> 4) & 0x0F0F0F0Fu, zz),
+                         expand_signed((w[1][c] >> 4) & 0x0F0F0F0Fu, zz),
+                         expand_signed((w[2][c] >> 4) & 0x0F0F0F0Fu, zz),
+                         expand_signed((w[3][c] >> 4) & 0x0F0F0F0Fu, zz));
         }
       }
+      // rows past the layer's end are left as they are: their outputs are
+      // never stored
       fence_proxy_async_smem();  // make the generic-proxy writes visible to the tensor core
-      mbar_arrive(&bexp_full[s]);
+      mbar_arrive(&wexp_full[s]);
     }
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 184;");
-    // epilogue: 8 warps; warp (w % 4) owns TMEM lanes 32*(w%4).., and
-    // column half (w - 8) / 4
-    const int ew = warp - 8;
-    const int q4 = warp & 3, half = ew >> 2;
-    const int et = threadIdx.x - 256;  // 0..255: the column this thread fetches scales for
+    // epilogue: warp w reads TMEM lanes 32*(w%4).. (output rows) and token
+    // columns 128*((w-8)/4)..
+    const int q4 = warp & 3, half = (warp - 8) >> 2;
+    const int row = q4 * 32 + lane;                       // output row within the tile
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
     const int col0 = half * 128;
-    // scale prefetch: column et's scale of a group, from its tile record
+    const bool row_ok = (row >> 4) < nrec;
+    const uint16_t* sp = reinterpret_cast<const uint16_t*>(
+        p.packed + rec_offset(n0 / kRecRows + (row_ok ? (row >> 4) : 0), 0, G) + kRecScaleOff) + (row & 15);
+    // this row's scale of group g is sp[g * kRecBytes / 2]; prefetched two
+    // groups ahead
     auto fetch_scale = [&](int g) -> float {
-      const int i = et >> 4, r = et & 15;
-      if (g >= G || i >= nrec) return 0.f;
-      const uint16_t* sp = reinterpret_cast<const uint16_t*>(p.packed + rec_offset(n0 / kRecRows + i, g, G) +
-                                                             kRecScaleOff);
-      return half_bits_to_f32(__ldg(sp + r));
+      return (row_ok && g < G) ? half_bits_to_f32(__ldg(sp + (size_t)g * (kRecBytes / 2))) : 0.f;
     };
-    scale_ring[0 * kTcBN + et] = fetch_scale(0);
-    scale_ring[1 * kTcBN + et] = fetch_scale(1);
-    float pending = fetch_scale(2);
+    float s_cur = fetch_scale(0), s_next = fetch_scale(1);
     // seed both accumulator buffers
 #pragma unroll
     for (int c = 0; c < 128; c += 8) {
       tmem_st8_magic(tmem + lane_base + col0 + c);
-      tmem_st8_magic(tmem + lane_base + kTcBN + col0 + c);
+      tmem_st8_magic(tmem + lane_base + kTcTok + col0 + c);
     }
     tmem_wait_st();
     tc_fence_before();
@@ -313,65 +318,46 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     const uint64_t negc = pack2(-kMagicF, -kMagicF);
     for (int g = 0; g < G && !failed; ++g) {
       const int b = g & 1;
-      if (g >= 1) scale_ring[((g + 1) % 3) * kTcBN + et] = pending;
-      pending = fetch_scale(g + 2);
-      named_barrier(2, 256);
+      const float s_after = fetch_scale(g + 2);
       if (!mbar_wait(&acc_full[b], (g >> 1) & 1)) {
         failed = true;
         break;
       }
       tc_fence_after();
-      const float* sc = scale_ring + (g % 3) * kTcBN + col0;
+      const uint64_t s2 = pack2(s_cur, s_cur);
 #pragma unroll
       for (int c = 0; c < 8; ++c) {
         uint32_t v[16];
-        tmem_ld16(tmem + lane_base + b * kTcBN + col0 + c * 16, v);
+        tmem_ld16(tmem + lane_base + b * kTcTok + col0 + c * 16, v);
         tmem_wait_ld();
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const float2 s2 = *reinterpret_cast<const float2*>(sc + c * 16 + 2 * j);
           const uint64_t t2 = add2(pack2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1])), negc);
-          y[c * 8 + j] = fma2(pack2(s2.x, s2.y), t2, y[c * 8 + j]);
+          y[c * 8 + j] = fma2(s2, t2, y[c * 8 + j]);
         }
       }
 #pragma unroll
-      for (int c = 0; c < 16; ++c) tmem_st8_magic(tmem + lane_base + b * kTcBN + col0 + c * 8);
+      for (int c = 0; c < 16; ++c) tmem_st8_magic(tmem + lane_base + b * kTcTok + col0 + c * 8);
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[b]);
+      s_cur = s_next;
+      s_next = s_after;
     }
-    // token scale, bias, convert, store: this thread holds row m0 + 32*q4 + lane
-    const int64_t m = m0 + q4 * 32 + lane;
-    if (!failed && m < p.M) {
-      const float a = p.xscale[m];
-#pragma unroll
-      for (int c8 = 0; c8 < 16; ++c8) {
-        const int nb = n0 + col0 + c8 * 8;
-        if (nb >= p.N) break;
-        float o[8];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = unpack2(y[c8 * 4 + e]);
-          o[2 * e] = f.x * a + tc_bias(p.bias, p.bias_dtype, nb + 2 * e);
-          o[2 * e + 1] = f.y * a + tc_bias(p.bias, p.bias_dtype, nb + 2 * e + 1);
-        }
-        if (p.out_dtype == PARO_BF16) {
-          __nv_bfloat162 h[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(o[2 * e], o[2 * e + 1]);
-          *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + m * p.N + nb) = *reinterpret_cast<uint4*>(h);
-        } else if (p.out_dtype == PARO_F16) {
-          __half2 h[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) h[e] = __floats2half2_rn(o[2 * e], o[2 * e + 1]);
-          *reinterpret_cast<uint4*>(static_cast<__half*>(p.out) + m * p.N + nb) = *reinterpret_cast<uint4*>(h);
-        } else {
-          float* dst = static_cast<float*>(p.out) + m * p.N + nb;
-          *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
-          *reinterpret_cast<float4*>(dst + 4) = make_float4(o[4], o[5], o[6], o[7]);
-        }
-      }
+    // token scale, bias, convert, store: this thread holds output row
+    // n0 + row for tokens m0 + col0 + (0..127)
+    const int n = n0 + row;
+    if (!failed && row_ok) {
+      const float bn = tc_bias(p.bias, p.bias_dtype, n);
+      const int64_t mbase = m0 + col0;
+      const int valid = (int)(p.M - mbase < 128 ? p.M - mbase : 128);   // tokens of this half that exist
+      if (p.out_dtype == PARO_BF16)
+        store_row(y, static_cast<__nv_bfloat16*>(p.out) + mbase * p.N + n, p.N, p.xscale + mbase, bn, valid);
+      else if (p.out_dtype == PARO_F16)
+        store_row(y, static_cast<__half*>(p.out) + mbase * p.N + n, p.N, p.xscale + mbase, bn, valid);
+      else
+        store_row(y, static_cast<float*>(p.out) + mbase * p.N + n, p.N, p.xscale + mbase, bn, valid);
     }
   }
 
@@ -409,12 +395,12 @@ cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int
   auto encode = get_encode();
   if (!encode) return cudaErrorNotSupported;
   if (M > 0x7FFFFFFF) return cudaErrorInvalidValue;
-  CUtensorMap amap;
+  CUtensorMap xmap;
   const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
   const cuuint64_t strides[1] = {(cuuint64_t)K};
-  const cuuint32_t box[2] = {(cuuint32_t)kGroup, (cuuint32_t)kTcBM};
+  const cuuint32_t box[2] = {(cuuint32_t)kGroup, (cuuint32_t)kTcTok};
   const cuuint32_t estr[2] = {1, 1};
-  CUresult r = encode(&amap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(xq), dims, strides, box, estr,
+  CUresult r = encode(&xmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(xq), dims, strides, box, estr,
                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
@@ -430,8 +416,8 @@ cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int
   p.out_dtype = out_dtype;
   cudaError_t e = ensure_smem_limit((const void*)gemm_tc_kernel, kTcSmem);
   if (e != cudaSuccess) return e;
-  dim3 grid((unsigned)((N + kTcBN - 1) / kTcBN), (unsigned)((M + kTcBM - 1) / kTcBM));
-  gemm_tc_kernel<<<grid, kTcThreads, kTcSmem, st>>>(amap, p);
+  dim3 grid((unsigned)((N + kTcRows - 1) / kTcRows), (unsigned)((M + kTcTok - 1) / kTcTok));
+  gemm_tc_kernel<<<grid, kTcThreads, kTcSmem, st>>>(xmap, p);
   return cudaGetLastError();
 }
 
