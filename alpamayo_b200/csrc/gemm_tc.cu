@@ -12,18 +12,20 @@
 //  * warp 0 (producer): per group, one tensor TMA of the activation tile
 //    (256 tokens x 128 int8 channels, 128-byte swizzle = the UMMA K-major
 //    canonical layout) and 8 bulk copies of the weight tile records
-//    (16 rows x 128 channels each).
-//  * warpgroup 1 (expansion): thread t unpacks row t's int4 codes to signed
-//    int8 (q - z) and writes them in the same swizzled K-major layout.
+//    (16 rows x 128 channels each), which land in the stage's weight area.
+//  * warpgroup 1 (expansion): thread t reads row t's int4 codes and zero
+//    point into registers, the warpgroup synchronises (the records and the
+//    expanded rows share the area), and thread t writes row t as signed int8
+//    (q - z) in the same swizzled K-major layout.
 //  * warp 1 (MMA): issues 4 tcgen05.mma (K = 32 each) per group into one of
-//    two 256-column TMEM buffers and commits completion to mbarriers.
+//    two 256-column TMEM buffers, the first one overwriting the buffer, and
+//    commits completion to mbarriers.
 //  * warpgroups 2-3 (epilogue): fold each finished group into float32
-//    registers while the tensor core works on the next group.  Each TMEM
-//    buffer is pre-seeded with the integer bit pattern of 1.5 * 2^23, so after
-//    the group's MMAs the int32 word reinterpreted as float32 is exactly
-//    1.5 * 2^23 + acc (|acc| < 2^22); one packed subtract and one packed FMA
-//    per two elements apply the row's group scale, then the buffer is
-//    re-seeded.  After the last group: token scale, bias, convert, store.
+//    registers while the tensor core works on the next group: each int32
+//    group sum (|acc| < 2^18, so the conversion is exact) is converted to
+//    float32 and one packed FMA per two elements applies the row's group
+//    scale.  After the last group: token scale, bias, convert, store.
+//    Nothing is written back to tensor memory.
 //
 // All mbarrier waits are bounded (report kErrMbarTimeout and drop out), and
 // the tensor memory is freed on every path out of the kernel.
@@ -38,20 +40,17 @@ PARO_DEFINE_ERROR_ACCESSOR(tc)
 
 constexpr int kTcRows = 128;                              // output rows per tile (MMA M)
 constexpr int kTcTok = 256;                               // tokens per tile (MMA N)
-constexpr int kTcStages = 3;
+constexpr int kTcStages = 4;
 constexpr int kTcThreads = 512;
 constexpr int kTcRecs = kTcRows / kRecRows;               // 8 records per group
 constexpr int kTcWBytes = kTcRows * kGroup;               // 16 KB expanded weights
 constexpr int kTcXBytes = kTcTok * kGroup;                // 32 KB activations
-constexpr int kTcRawBytes = kTcRecs * kRecBytes;          // 8576
-constexpr uint32_t kMagic = 0x4B400000u;                  // bits of 12582912.0f = 1.5 * 2^23
-constexpr float kMagicF = 12582912.0f;
+static_assert(kTcRecs * kRecBytes <= kTcWBytes, "records land in the expanded-weight area");
 
 // shared memory plan (offsets from a 1024-byte aligned base)
 constexpr int kOffW = 0;
 constexpr int kOffX = kOffW + kTcStages * kTcWBytes;
-constexpr int kOffRaw = kOffX + kTcStages * kTcXBytes;
-constexpr int kOffBar = kOffRaw + kTcStages * kTcRawBytes;
+constexpr int kOffBar = kOffX + kTcStages * kTcXBytes;
 constexpr int kTcSmem = kOffBar + 256 + 1024;                         // + alignment slack
 
 struct TcParams {
@@ -100,16 +99,7 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
       : "r"(taddr));
 }
 
-// Seeds 8 consecutive columns of this warp's 32 lanes with the magic value
-// (the .x8 shape keeps the source register block small).
-__device__ __forceinline__ void tmem_st8_magic(uint32_t taddr) {
-  const uint32_t m = kMagic;
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr), "r"(m)
-               : "memory");
-}
-
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
@@ -128,11 +118,6 @@ __device__ __forceinline__ uint64_t pack2(float a, float b) {
 __device__ __forceinline__ float2 unpack2(uint64_t v) {
   float2 r;
   asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
-  return r;
-}
-__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
 }
 __device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
@@ -218,7 +203,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
         }
         mbar_arrive_expect_tx(&full_raw[s], (uint32_t)(kTcXBytes + nrec * kRecBytes));
         tma_load_2d(smem + kOffX + s * kTcXBytes, &xmap, g * kGroup, (int)m0, &full_raw[s]);
-        uint8_t* raw = smem + kOffRaw + s * kTcRawBytes;
+        uint8_t* raw = smem + kOffW + s * kTcWBytes;
         for (int i = 0; i < nrec; ++i)
           bulk_g2s(raw + i * kRecBytes, p.packed + rec_offset(n0 / kRecRows + i, g, G), kRecBytes, &full_raw[s]);
       }
@@ -236,7 +221,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
         const uint64_t da = umma_desc_sw128(w_base + s * kTcWBytes);
         const uint64_t db = umma_desc_sw128(x_base + s * kTcXBytes);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) mma_i8(tmem + b * kTcTok, da + 2 * kk, db + 2 * kk, 1u);
+        for (int kk = 0; kk < 4; ++kk) mma_i8(tmem + b * kTcTok, da + 2 * kk, db + 2 * kk, kk > 0 ? 1u : 0u);
         umma_commit(&smem_empty[s]);
         umma_commit(&acc_full[b]);
       }
@@ -253,16 +238,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
         failed = true;
         break;
       }
-      uint8_t* row = smem + kOffW + s * kTcWBytes + t * 128;
+      uint8_t* area = smem + kOffW + s * kTcWBytes;
+      uint32_t w[4][4];  // [t][j] code words of row t
+      uint32_t zz = 0;
       if (i < nrec) {
-        const uint8_t* rec = smem + kOffRaw + s * kTcRawBytes + i * kRecBytes;
-        const uint32_t zz = (uint32_t)rec[kRecZeroOff + r] * 0x01010101u;
-        uint32_t w[4][4];  // [t][j]
+        const uint8_t* rec = area + i * kRecBytes;
+        zz = (uint32_t)rec[kRecZeroOff + r] * 0x01010101u;
 #pragma unroll
         for (int tt = 0; tt < 4; ++tt) {
           const uint4 v = *reinterpret_cast<const uint4*>(rec + r * 64 + tt * 16);
           w[tt][0] = v.x; w[tt][1] = v.y; w[tt][2] = v.z; w[tt][3] = v.w;
         }
+      }
+      named_barrier(1, 128);  // every record is read before any row is overwritten
+      if (i < nrec) {
+        uint8_t* row = area + t * 128;
         // 16-channel chunk c < 4 holds the low nibbles of words (t, c) for
         // t = 0..3; chunk c + 4 holds their high nibbles
 #pragma unroll
@@ -299,15 +289,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
       return (row_ok && g < G) ? half_bits_to_f32(__ldg(sp + (size_t)g * (kRecBytes / 2))) : 0.f;
     };
     float s_cur = fetch_scale(0), s_next = fetch_scale(1);
-    // seed both accumulator buffers
-#pragma unroll
-    for (int c = 0; c < 128; c += 8) {
-      tmem_st8_magic(tmem + lane_base + col0 + c);
-      tmem_st8_magic(tmem + lane_base + kTcTok + col0 + c);
-    }
-    tmem_wait_st();
-    tc_fence_before();
-    __syncwarp();
+    // both accumulator buffers start free
     if (lane == 0) {
       mbar_arrive(&acc_empty[0]);
       mbar_arrive(&acc_empty[1]);
@@ -315,7 +297,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     uint64_t y[64];
 #pragma unroll
     for (int j = 0; j < 64; ++j) y[j] = 0ull;  // (+0.0f, +0.0f)
-    const uint64_t negc = pack2(-kMagicF, -kMagicF);
     for (int g = 0; g < G && !failed; ++g) {
       const int b = g & 1;
       const float s_after = fetch_scale(g + 2);
@@ -332,13 +313,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
         tmem_wait_ld();
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          const uint64_t t2 = add2(pack2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1])), negc);
-          y[c * 8 + j] = fma2(s2, t2, y[c * 8 + j]);
+          y[c * 8 + j] = fma2(s2, pack2((float)(int)v[2 * j], (float)(int)v[2 * j + 1]), y[c * 8 + j]);
         }
       }
-#pragma unroll
-      for (int c = 0; c < 16; ++c) tmem_st8_magic(tmem + lane_base + b * kTcTok + col0 + c * 8);
-      tmem_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[b]);
