@@ -3,32 +3,43 @@
 //
 // y[m, n] = xscale[m] * sum_g s[g, n] * sum_{k in g} (q[n, k] - z[g, n]) x[m, k] (+ bias[n])
 //
-// One CTA computes a 128 (output rows n) x 256 (tokens m) tile of y^T: the
-// weights are the MMA's M operand and the tokens its N operand, so a TMEM
+// A cluster of two CTAs (one tcgen05 "CTA pair") computes a 256 (output
+// rows n) x 256 (tokens m) tile of y^T with cta_group::2 MMAs (M = 256,
+// N = 256, K = 32): each CTA holds 128 weight rows (half of the MMA's A
+// operand) and 128 tokens (half of its B operand) in shared memory, and its
+// tensor memory holds the int32 sums of its own 128 rows for all 256 tokens.
+// The weights are the MMA's M operand and the tokens its N operand, so a TMEM
 // lane is one output row and each epilogue thread owns one row (its group
 // scale is one scalar per group).  K is walked one 128-channel group per
-// pipeline stage:
+// pipeline stage (6 stages):
 //
-//  * warp 0 (producer): per group, one tensor TMA of the activation tile
-//    (256 tokens x 128 int8 channels, 128-byte swizzle = the UMMA K-major
-//    canonical layout) and 8 bulk copies of the weight tile records
-//    (16 rows x 128 channels each), which land in the stage's weight area.
-//  * warpgroup 1 (expansion): thread t reads row t's int4 codes and zero
-//    point into registers, the warpgroup synchronises (the records and the
-//    expanded rows share the area), and thread t writes row t as signed int8
-//    (q - z) in the same swizzled K-major layout.
-//  * warp 1 (MMA): issues 4 tcgen05.mma (K = 32 each) per group into one of
-//    two 256-column TMEM buffers, the first one overwriting the buffer, and
-//    commits completion to mbarriers.
-//  * warpgroups 2-3 (epilogue): fold each finished group into float32
-//    registers while the tensor core works on the next group: each int32
-//    group sum (|acc| < 2^18, so the conversion is exact) is converted to
-//    float32 and one packed FMA per two elements applies the row's group
-//    scale.  After the last group: token scale, bias, convert, store.
-//    Nothing is written back to tensor memory.
+//  * warp 0 (producer, each CTA): per group, one tensor TMA of the CTA's
+//    activation half (128 tokens x 128 int8 channels, 128-byte swizzle =
+//    the UMMA K-major canonical layout) and 8 bulk copies of its weight
+//    records (16 rows x 128 channels each), which land in the stage's
+//    weight area.
+//  * warpgroup 1 (expansion, each CTA): thread t reads row t's int4 codes
+//    and zero point into registers, the warpgroup synchronises (records and
+//    expanded rows share the area), thread t writes row t as signed int8
+//    (q - z) in the swizzled K-major layout, and each warp then arrives on
+//    the leader CTA's "stage ready" barrier.
+//  * warp 1 of the leader CTA (MMA): once both CTAs' stage is ready and the
+//    accumulator buffer has been drained by both epilogues, issues 4 MMAs
+//    into one of two 256-column TMEM buffers (the first overwriting it) and
+//    commits completion to the stage-free and accumulator-full barriers of
+//    both CTAs (tcgen05.commit multicast).
+//  * warpgroups 2-3 (epilogue, each CTA): fold each finished group into
+//    float32 registers while the tensor core works on the next group: each
+//    int32 group sum (|acc| < 2^18, so the conversion is exact) is converted
+//    to float32 and one packed FMA per two elements applies the row's group
+//    scale; then each warp arrives on the leader's "buffer drained" barrier.
+//    After the last group: token scale, bias, convert, store.
 //
-// All mbarrier waits are bounded (report kErrMbarTimeout and drop out), and
-// the tensor memory is freed on every path out of the kernel.
+// Per SM and group this moves 24.5 KB from L2 (16 KB activations + 8.5 KB
+// records) for 128 x 256 x 128 MACs.  No load uses cluster multicast.  All
+// mbarrier waits are bounded (report kErrMbarTimeout and drop out), and the
+// tensor memory is freed on every path out of the kernel, after both CTAs
+// have stopped using it.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -38,16 +49,18 @@ namespace paro {
 
 PARO_DEFINE_ERROR_ACCESSOR(tc)
 
-constexpr int kTcRows = 128;                              // output rows per tile (MMA M)
+constexpr int kTcRows = 128;                              // output rows per CTA (half the MMA's M)
 constexpr int kTcTok = 256;                               // tokens per tile (MMA N)
-constexpr int kTcStages = 4;
+constexpr int kTcTokHalf = kTcTok / 2;                    // tokens staged per CTA
+constexpr int kTcStages = 6;
 constexpr int kTcThreads = 512;
 constexpr int kTcRecs = kTcRows / kRecRows;               // 8 records per group
 constexpr int kTcWBytes = kTcRows * kGroup;               // 16 KB expanded weights
-constexpr int kTcXBytes = kTcTok * kGroup;                // 32 KB activations
+constexpr int kTcXBytes = kTcTokHalf * kGroup;            // 16 KB activations
 static_assert(kTcRecs * kRecBytes <= kTcWBytes, "records land in the expanded-weight area");
 
-// shared memory plan (offsets from a 1024-byte aligned base)
+// shared memory plan (offsets from a 1024-byte aligned base; identical in
+// both CTAs, which the pair MMA's descriptors rely on)
 constexpr int kOffW = 0;
 constexpr int kOffX = kOffW + kTcStages * kTcWBytes;
 constexpr int kOffBar = kOffX + kTcStages * kTcXBytes;
@@ -71,21 +84,70 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
-// instruction descriptor: s32 accumulate, A s8, B s8, both K-major, N = 256, M = 128
+// instruction descriptor: s32 accumulate, A s8, B s8, both K-major,
+// N = 256, M = 256 (the CTA pair)
 constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTcTok >> 3) << 17) |
-                            ((uint32_t)(kTcRows >> 4) << 24);
+                            ((uint32_t)((2 * kTcRows) >> 4) << 24);
 
-__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+__device__ __forceinline__ void mma_i8_pair(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      " tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
       "l"(da), "l"(db), "r"(kIdesc), "r"(accumulate)
       : "memory");
 }
 
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
+// Arrives on the barrier at this offset in both CTAs of the pair once every
+// MMA the calling thread issued before has completed.
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
+  const uint16_t both = 3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(both)
+      : "memory");
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Arrive on the barrier at the same offset in CTA `rank` of this cluster.
+__device__ __forceinline__ void mbar_arrive_cluster(uint64_t* bar, uint32_t rank) {
+  asm volatile(
+      "{\n .reg .b32 ra;\n mapa.shared::cluster.u32 ra, %0, %1;\n"
+      " mbarrier.arrive.shared::cluster.b64 _, [ra];\n}\n" ::"r"(smem_u32(bar)),
+      "r"(rank)
+      : "memory");
+}
+
+// Bounded wait on a barrier the peer CTA also arrives on.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity, long long limit_cycles = 1000000000LL) {
+  auto try_once = [&]() {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+  };
+  if (try_once()) return true;
+  const long long t0 = clock64();
+  while (!try_once()) {
+    if (clock64() - t0 > limit_cycles) {
+      report_error(kErrMbarTimeout);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -155,38 +217,42 @@ __device__ __forceinline__ void store_row(const uint64_t (&y)[64], T* out, int N
 __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap xmap, TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  uint64_t* full_raw = reinterpret_cast<uint64_t*>(smem + kOffBar);     // [3] activations + records landed
-  uint64_t* wexp_full = full_raw + kTcStages;                            // [3] expanded weights written
-  uint64_t* smem_empty = wexp_full + kTcStages;                          // [3] MMA done with the stage
-  uint64_t* acc_full = smem_empty + kTcStages;                           // [2] group's MMAs complete
-  uint64_t* acc_empty = acc_full + 2;                                    // [2] epilogue read + re-seeded
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBar);        // [6] this CTA's loads landed
+  uint64_t* ready = full + kTcStages;                                   // [6] leader: both CTAs' stage expanded
+  uint64_t* freed = ready + kTcStages;                                  // [6] MMAs done with the stage
+  uint64_t* acc_full = freed + kTcStages;                               // [2] group's MMAs complete
+  uint64_t* acc_empty = acc_full + 2;                                   // [2] leader: both epilogues drained
+  uint64_t* mma_done = acc_empty + 2;                                   // [1] leader: every MMA complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
   const int G = p.K / kGroup;
-  const int n0 = blockIdx.x * kTcRows;
-  const int64_t m0 = (int64_t)blockIdx.y * kTcTok;
-  const int nrec = min(kTcRecs, (p.N - n0) / kRecRows);
+  const int n0 = (blockIdx.x >> 1) * (2 * kTcRows) + (int)rank * kTcRows;   // this CTA's first output row
+  const int64_t m0 = (int64_t)blockIdx.y * kTcTok;                          // the pair's first token
+  const int nrec = max(0, min(kTcRecs, (p.N - n0) / kRecRows));
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTcStages; ++s) {
-      mbar_init(&full_raw[s], 1);
-      mbar_init(&wexp_full[s], 128);
-      mbar_init(&smem_empty[s], 1);
+      mbar_init(&full[s], 1);
+      mbar_init(&ready[s], 8);      // 4 expansion warps x 2 CTAs
+      mbar_init(&freed[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 8);
+      mbar_init(&acc_empty[b], 16); // 8 epilogue warps x 2 CTAs
     }
+    mbar_init(mma_done, 1);
     fence_mbar_init();
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot))
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot))
                  : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
   }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync_all();  // barriers initialised and tensor memory allocated in both CTAs
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   bool failed = false;
@@ -197,23 +263,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
       // producer
       for (int g = 0; g < G && !failed; ++g) {
         const int s = g % kTcStages;
-        if (g >= kTcStages && !mbar_wait(&smem_empty[s], ((g / kTcStages) - 1) & 1)) {
+        if (g >= kTcStages && !mbar_wait(&freed[s], ((g / kTcStages) - 1) & 1)) {
           failed = true;
           break;
         }
-        mbar_arrive_expect_tx(&full_raw[s], (uint32_t)(kTcXBytes + nrec * kRecBytes));
-        tma_load_2d(smem + kOffX + s * kTcXBytes, &xmap, g * kGroup, (int)m0, &full_raw[s]);
+        mbar_arrive_expect_tx(&full[s], (uint32_t)(kTcXBytes + nrec * kRecBytes));
+        tma_load_2d(smem + kOffX + s * kTcXBytes, &xmap, g * kGroup, (int)(m0 + rank * kTcTokHalf), &full[s]);
         uint8_t* raw = smem + kOffW + s * kTcWBytes;
         for (int i = 0; i < nrec; ++i)
-          bulk_g2s(raw + i * kRecBytes, p.packed + rec_offset(n0 / kRecRows + i, g, G), kRecBytes, &full_raw[s]);
+          bulk_g2s(raw + i * kRecBytes, p.packed + rec_offset(n0 / kRecRows + i, g, G), kRecBytes, &full[s]);
       }
-    } else if (warp == 1 && lane == 0) {
-      // MMA issuer
+    } else if (warp == 1 && lane == 0 && leader) {
+      // MMA issuer (leader CTA only)
       const uint32_t w_base = smem_u32(smem + kOffW), x_base = smem_u32(smem + kOffX);
       for (int g = 0; g < G && !failed; ++g) {
         const int s = g % kTcStages, b = g & 1;
-        if (!mbar_wait(&full_raw[s], (g / kTcStages) & 1) || !mbar_wait(&wexp_full[s], (g / kTcStages) & 1) ||
-            !mbar_wait(&acc_empty[b], (g >> 1) & 1)) {
+        if (!mbar_wait_cluster(&ready[s], (g / kTcStages) & 1) || !mbar_wait_cluster(&acc_empty[b], (g >> 1) & 1)) {
           failed = true;
           break;
         }
@@ -221,20 +286,23 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
         const uint64_t da = umma_desc_sw128(w_base + s * kTcWBytes);
         const uint64_t db = umma_desc_sw128(x_base + s * kTcXBytes);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) mma_i8(tmem + b * kTcTok, da + 2 * kk, db + 2 * kk, kk > 0 ? 1u : 0u);
-        umma_commit(&smem_empty[s]);
-        umma_commit(&acc_full[b]);
+        for (int kk = 0; kk < 4; ++kk) mma_i8_pair(tmem + b * kTcTok, da + 2 * kk, db + 2 * kk, kk > 0 ? 1u : 0u);
+        umma_commit_pair(&freed[s]);
+        umma_commit_pair(&acc_full[b]);
       }
+      // every MMA issued above completes before the pair frees its tensor memory
+      umma_commit_pair(mma_done);
+      mbar_wait(mma_done, 0);
     }
   } else if (warp < 8) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 88;");
-    // expansion: thread t writes weight row t of the tile
+    // expansion: thread t writes weight row t of this CTA's half
     const int t = threadIdx.x - 128;
     const int i = t >> 4, r = t & 15;
     const int sw = t & 7;
     for (int g = 0; g < G && !failed; ++g) {
       const int s = g % kTcStages;
-      if (!mbar_wait(&full_raw[s], (g / kTcStages) & 1)) {
+      if (!mbar_wait(&full[s], (g / kTcStages) & 1)) {
         failed = true;
         break;
       }
@@ -270,14 +338,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
       // rows past the layer's end are left as they are: their outputs are
       // never stored
       fence_proxy_async_smem();  // make the generic-proxy writes visible to the tensor core
-      mbar_arrive(&wexp_full[s]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(&ready[s], 0);
     }
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 184;");
     // epilogue: warp w reads TMEM lanes 32*(w%4).. (output rows) and token
     // columns 128*((w-8)/4)..
     const int q4 = warp & 3, half = (warp - 8) >> 2;
-    const int row = q4 * 32 + lane;                       // output row within the tile
+    const int row = q4 * 32 + lane;                       // output row within this CTA's half
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
     const int col0 = half * 128;
     const bool row_ok = (row >> 4) < nrec;
@@ -291,8 +360,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     float s_cur = fetch_scale(0), s_next = fetch_scale(1);
     // both accumulator buffers start free
     if (lane == 0) {
-      mbar_arrive(&acc_empty[0]);
-      mbar_arrive(&acc_empty[1]);
+      mbar_arrive_cluster(&acc_empty[0], 0);
+      mbar_arrive_cluster(&acc_empty[1], 0);
     }
     uint64_t y[64];
 #pragma unroll
@@ -312,13 +381,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
         tmem_ld16(tmem + lane_base + b * kTcTok + col0 + c * 16, v);
         tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (int j = 0; j < 8; ++j)
           y[c * 8 + j] = fma2(s2, pack2((float)(int)v[2 * j], (float)(int)v[2 * j + 1]), y[c * 8 + j]);
-        }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[b]);
+      if (lane == 0) mbar_arrive_cluster(&acc_empty[b], 0);
       s_cur = s_next;
       s_next = s_after;
     }
@@ -338,12 +406,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     }
   }
 
-  // every role reaches this point; the tensor memory is freed once nobody
-  // reads it any more
+  // every role of both CTAs reaches this point; the pair's tensor memory is
+  // freed once neither CTA reads it any more
   tc_fence_before();
-  __syncthreads();
+  cluster_sync_all();
   tc_fence_after();
-  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -375,7 +443,7 @@ cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int
   CUtensorMap xmap;
   const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
   const cuuint64_t strides[1] = {(cuuint64_t)K};
-  const cuuint32_t box[2] = {(cuuint32_t)kGroup, (cuuint32_t)kTcTok};
+  const cuuint32_t box[2] = {(cuuint32_t)kGroup, (cuuint32_t)kTcTokHalf};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = encode(&xmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(xq), dims, strides, box, estr,
                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -393,9 +461,19 @@ cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int
   p.out_dtype = out_dtype;
   cudaError_t e = ensure_smem_limit((const void*)gemm_tc_kernel, kTcSmem);
   if (e != cudaSuccess) return e;
-  dim3 grid((unsigned)((N + kTcRows - 1) / kTcRows), (unsigned)((M + kTcTok - 1) / kTcTok));
-  gemm_tc_kernel<<<grid, kTcThreads, kTcSmem, st>>>(xmap, p);
-  return cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(2 * ((N + 2 * kTcRows - 1) / (2 * kTcRows))), (unsigned)((M + kTcTok - 1) / kTcTok));
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = kTcSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel, xmap, p);
 }
 
 }  // namespace paro
