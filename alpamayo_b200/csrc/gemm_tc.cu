@@ -3,8 +3,10 @@
 //
 // y[m, n] = xscale[m] * sum_g s[g, n] * sum_{k in g} (q[n, k] - z[g, n]) x[m, k] (+ bias[n])
 //
-// A cluster of two CTAs (one tcgen05 "CTA pair") computes a 256 (output
-// rows n) x 256 (tokens m) tile of y^T with cta_group::2 MMAs (M = 256,
+// Persistent grid of CTA pairs (clusters of two): pair P walks the tiles
+// P, P + pairs, ... of the (N / 256) x (M / 256) tile grid, so one tile's
+// final stores overlap the next tile's loads and MMAs.  A pair computes a
+// 256 (output rows n) x 256 (tokens m) tile of y^T with cta_group::2 MMAs (M = 256,
 // N = 256, K = 32): each CTA holds 128 weight rows (half of the MMA's A
 // operand) and 128 tokens (half of its B operand) in shared memory, and its
 // tensor memory holds the int32 sums of its own 128 rows for all 256 tokens.
@@ -15,9 +17,9 @@
 //
 //  * warp 0 (producer, each CTA): per group, one tensor TMA of the CTA's
 //    activation half (128 tokens x 128 int8 channels, 128-byte swizzle =
-//    the UMMA K-major canonical layout) and 8 bulk copies of its weight
-//    records (16 rows x 128 channels each), which land in the stage's
-//    weight area.
+//    the UMMA K-major canonical layout) and one 3-D tensor TMA of its 8
+//    weight records (16 rows x 128 channels each; the packed buffer viewed
+//    as [N/16][G][1072 bytes]), which land in the stage's weight area.
 //  * warpgroup 1 (expansion, each CTA): thread t reads row t's int4 codes
 //    and zero point into registers, the warpgroup synchronises (records and
 //    expanded rows share the area), thread t writes row t as signed int8
@@ -63,13 +65,15 @@ static_assert(kTcRecs * kRecBytes <= kTcWBytes, "records land in the expanded-we
 // both CTAs, which the pair MMA's descriptors rely on)
 constexpr int kOffW = 0;
 constexpr int kOffX = kOffW + kTcStages * kTcWBytes;
-constexpr int kOffBar = kOffX + kTcStages * kTcXBytes;
+constexpr int kOffXs = kOffX + kTcStages * kTcXBytes;                // [8 warps][128] float token scales
+constexpr int kOffBar = kOffXs + 8 * 128 * 4;
 constexpr int kTcSmem = kOffBar + 256 + 1024;                         // + alignment slack
 
 struct TcParams {
   const float* xscale;
   int64_t M;
   int N, K;
+  int tiles_n, tiles;   // tiles along N (256 rows each) and in total
   const uint8_t* packed;
   const void* bias;
   int bias_dtype;
@@ -163,6 +167,15 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, int x, int y, int z,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
@@ -200,21 +213,24 @@ __device__ __forceinline__ float tc_bias(const void* bias, int dtype, int n) {
   return static_cast<const float*>(bias)[n];
 }
 
-// Stores one output row's `valid` (<= 128) tokens: out[j * N] = y_j * xscale[j] + bias.
+// Stores one output row's `valid` (<= 128) tokens: out[j * N] = y_j * xs[j] + bias,
+// with the token scales xs staged in shared memory.
 template <typename T>
-__device__ __forceinline__ void store_row(const uint64_t (&y)[64], T* out, int N, const float* xscale, float bias,
-                                          int valid) {
+__device__ __forceinline__ void store_row(const uint64_t (&y)[64], T* __restrict__ out, int N,
+                                          const float* __restrict__ xs, float bias, int valid) {
 #pragma unroll
   for (int j = 0; j < 64; ++j) {
     if (2 * j < valid) {
       const float2 f = unpack2(y[j]);
-      out[(size_t)(2 * j) * N] = from_f32<T>(f.x * __ldg(xscale + 2 * j) + bias);
-      if (2 * j + 1 < valid) out[(size_t)(2 * j + 1) * N] = from_f32<T>(f.y * __ldg(xscale + 2 * j + 1) + bias);
+      const float2 a = *reinterpret_cast<const float2*>(xs + 2 * j);
+      out[(size_t)(2 * j) * N] = from_f32<T>(f.x * a.x + bias);
+      if (2 * j + 1 < valid) out[(size_t)(2 * j + 1) * N] = from_f32<T>(f.y * a.y + bias);
     }
   }
 }
 
-__global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap xmap, TcParams p) {
+__global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap xmap,
+                                                                const __grid_constant__ CUtensorMap wmap, TcParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBar);        // [6] this CTA's loads landed
@@ -229,9 +245,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
   const uint32_t rank = cluster_rank();
   const bool leader = rank == 0;
   const int G = p.K / kGroup;
-  const int n0 = (blockIdx.x >> 1) * (2 * kTcRows) + (int)rank * kTcRows;   // this CTA's first output row
-  const int64_t m0 = (int64_t)blockIdx.y * kTcTok;                          // the pair's first token
-  const int nrec = max(0, min(kTcRecs, (p.N - n0) / kRecRows));
+  const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+  // tile t: output rows (t % tiles_n) * 256 + rank * 128 .. (this CTA's
+  // half), tokens (t / tiles_n) * 256 ..
+  auto tile_n0 = [&](int t) { return (t % p.tiles_n) * (2 * kTcRows) + (int)rank * kTcRows; };
+  auto tile_m0 = [&](int t) { return (int64_t)(t / p.tiles_n) * kTcTok; };
+  auto tile_nrec = [&](int n0) { return max(0, min(kTcRecs, (p.N - n0) / kRecRows)); };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTcStages; ++s) {
@@ -261,24 +280,30 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     asm volatile("setmaxnreg.dec.sync.aligned.u32 56;");
     if (warp == 0 && lane == 0) {
       // producer
-      for (int g = 0; g < G && !failed; ++g) {
-        const int s = g % kTcStages;
-        if (g >= kTcStages && !mbar_wait(&freed[s], ((g / kTcStages) - 1) & 1)) {
-          failed = true;
-          break;
+      uint32_t it = 0;  // groups issued by this CTA so far
+      for (int t = pair; t < p.tiles && !failed; t += pairs) {
+        const int n0 = tile_n0(t);
+        const int ty = (int)(tile_m0(t) + rank * kTcTokHalf);
+        for (int g = 0; g < G; ++g, ++it) {
+          const uint32_t s = it % kTcStages;
+          if (it >= kTcStages && !mbar_wait(&freed[s], ((it / kTcStages) - 1) & 1)) {
+            failed = true;
+            break;
+          }
+          // a box always delivers all its bytes (rows past the layer's end
+          // read as zeros)
+          mbar_arrive_expect_tx(&full[s], (uint32_t)(kTcXBytes + kTcRecs * kRecBytes));
+          tma_load_2d(smem + kOffX + s * kTcXBytes, &xmap, g * kGroup, ty, &full[s]);
+          tma_load_3d(smem + kOffW + s * kTcWBytes, &wmap, 0, g, n0 / kRecRows, &full[s]);
         }
-        mbar_arrive_expect_tx(&full[s], (uint32_t)(kTcXBytes + nrec * kRecBytes));
-        tma_load_2d(smem + kOffX + s * kTcXBytes, &xmap, g * kGroup, (int)(m0 + rank * kTcTokHalf), &full[s]);
-        uint8_t* raw = smem + kOffW + s * kTcWBytes;
-        for (int i = 0; i < nrec; ++i)
-          bulk_g2s(raw + i * kRecBytes, p.packed + rec_offset(n0 / kRecRows + i, g, G), kRecBytes, &full[s]);
       }
     } else if (warp == 1 && lane == 0 && leader) {
       // MMA issuer (leader CTA only)
       const uint32_t w_base = smem_u32(smem + kOffW), x_base = smem_u32(smem + kOffX);
-      for (int g = 0; g < G && !failed; ++g) {
-        const int s = g % kTcStages, b = g & 1;
-        if (!mbar_wait_cluster(&ready[s], (g / kTcStages) & 1) || !mbar_wait_cluster(&acc_empty[b], (g >> 1) & 1)) {
+      const uint32_t total = (uint32_t)((p.tiles - pair + pairs - 1) / pairs) * (uint32_t)G;
+      for (uint32_t it = 0; it < total && !failed; ++it) {
+        const uint32_t s = it % kTcStages, b = it & 1;
+        if (!mbar_wait_cluster(&ready[s], (it / kTcStages) & 1) || !mbar_wait_cluster(&acc_empty[b], (it >> 1) & 1)) {
           failed = true;
           break;
         }
@@ -300,9 +325,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     const int t = threadIdx.x - 128;
     const int i = t >> 4, r = t & 15;
     const int sw = t & 7;
-    for (int g = 0; g < G && !failed; ++g) {
-      const int s = g % kTcStages;
-      if (!mbar_wait(&full[s], (g / kTcStages) & 1)) {
+    uint32_t it = 0;
+    for (int tile = pair; tile < p.tiles && !failed; tile += pairs) {
+    const int nrec = tile_nrec(tile_n0(tile));
+    for (int g = 0; g < G; ++g, ++it) {
+      const uint32_t s = it % kTcStages;
+      if (!mbar_wait(&full[s], (it / kTcStages) & 1)) {
         failed = true;
         break;
       }
@@ -341,6 +369,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(&ready[s], 0);
     }
+    }
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 184;");
     // epilogue: warp w reads TMEM lanes 32*(w%4).. (output rows) and token
@@ -349,60 +378,75 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     const int row = q4 * 32 + lane;                       // output row within this CTA's half
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
     const int col0 = half * 128;
-    const bool row_ok = (row >> 4) < nrec;
-    const uint16_t* sp = reinterpret_cast<const uint16_t*>(
-        p.packed + rec_offset(n0 / kRecRows + (row_ok ? (row >> 4) : 0), 0, G) + kRecScaleOff) + (row & 15);
-    // this row's scale of group g is sp[g * kRecBytes / 2]; prefetched two
-    // groups ahead
-    auto fetch_scale = [&](int g) -> float {
-      return (row_ok && g < G) ? half_bits_to_f32(__ldg(sp + (size_t)g * (kRecBytes / 2))) : 0.f;
-    };
-    float s_cur = fetch_scale(0), s_next = fetch_scale(1);
     // both accumulator buffers start free
     if (lane == 0) {
       mbar_arrive_cluster(&acc_empty[0], 0);
       mbar_arrive_cluster(&acc_empty[1], 0);
     }
-    uint64_t y[64];
+    uint32_t it = 0;
+    for (int tile = pair; tile < p.tiles && !failed; tile += pairs) {
+      const int n0 = tile_n0(tile);
+      const int64_t m0 = tile_m0(tile);
+      const bool row_ok = (row >> 4) < tile_nrec(n0);
+      const uint16_t* sp = reinterpret_cast<const uint16_t*>(
+          p.packed + rec_offset(n0 / kRecRows + (row_ok ? (row >> 4) : 0), 0, G) + kRecScaleOff) + (row & 15);
+      // this row's scale of group g is sp[g * kRecBytes / 2]; prefetched two
+      // groups ahead
+      auto fetch_scale = [&](int g) -> float {
+        return (row_ok && g < G) ? half_bits_to_f32(__ldg(sp + (size_t)g * (kRecBytes / 2))) : 0.f;
+      };
+      float s_cur = fetch_scale(0), s_next = fetch_scale(1);
+      uint64_t y[64];
 #pragma unroll
-    for (int j = 0; j < 64; ++j) y[j] = 0ull;  // (+0.0f, +0.0f)
-    for (int g = 0; g < G && !failed; ++g) {
-      const int b = g & 1;
-      const float s_after = fetch_scale(g + 2);
-      if (!mbar_wait(&acc_full[b], (g >> 1) & 1)) {
-        failed = true;
-        break;
+      for (int j = 0; j < 64; ++j) y[j] = 0ull;  // (+0.0f, +0.0f)
+      for (int g = 0; g < G; ++g, ++it) {
+        const uint32_t b = it & 1;
+        const float s_after = fetch_scale(g + 2);
+        if (!mbar_wait(&acc_full[b], (it >> 1) & 1)) {
+          failed = true;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t s2 = pack2(s_cur, s_cur);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint32_t v[16];
+          tmem_ld16(tmem + lane_base + b * kTcTok + col0 + c * 16, v);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            y[c * 8 + j] = fma2(s2, pack2((float)(int)v[2 * j], (float)(int)v[2 * j + 1]), y[c * 8 + j]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(&acc_empty[b], 0);
+        s_cur = s_next;
+        s_next = s_after;
       }
-      tc_fence_after();
-      const uint64_t s2 = pack2(s_cur, s_cur);
+      // token scale, bias, convert, store: this thread holds output row
+      // n0 + row for tokens m0 + col0 + (0..127); the tensor core is already
+      // on the next tile.  The warp first stages its 128 token scales in its
+      // own slice of shared memory (4 per lane).
+      float* xs = reinterpret_cast<float*>(smem + kOffXs) + (warp - 8) * 128;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint32_t v[16];
-        tmem_ld16(tmem + lane_base + b * kTcTok + col0 + c * 16, v);
-        tmem_wait_ld();
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          y[c * 8 + j] = fma2(s2, pack2((float)(int)v[2 * j], (float)(int)v[2 * j + 1]), y[c * 8 + j]);
+      for (int q = 0; q < 4; ++q) {
+        const int64_t m = m0 + col0 + lane * 4 + q;
+        xs[lane * 4 + q] = m < p.M ? __ldg(p.xscale + m) : 0.f;
       }
-      tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(&acc_empty[b], 0);
-      s_cur = s_next;
-      s_next = s_after;
-    }
-    // token scale, bias, convert, store: this thread holds output row
-    // n0 + row for tokens m0 + col0 + (0..127)
-    const int n = n0 + row;
-    if (!failed && row_ok) {
-      const float bn = tc_bias(p.bias, p.bias_dtype, n);
-      const int64_t mbase = m0 + col0;
-      const int valid = (int)(p.M - mbase < 128 ? p.M - mbase : 128);   // tokens of this half that exist
-      if (p.out_dtype == PARO_BF16)
-        store_row(y, static_cast<__nv_bfloat16*>(p.out) + mbase * p.N + n, p.N, p.xscale + mbase, bn, valid);
-      else if (p.out_dtype == PARO_F16)
-        store_row(y, static_cast<__half*>(p.out) + mbase * p.N + n, p.N, p.xscale + mbase, bn, valid);
-      else
-        store_row(y, static_cast<float*>(p.out) + mbase * p.N + n, p.N, p.xscale + mbase, bn, valid);
+      const int n = n0 + row;
+      if (!failed && row_ok) {
+        const float bn = tc_bias(p.bias, p.bias_dtype, n);
+        const int64_t mbase = m0 + col0;
+        const int valid = (int)(p.M - mbase < 128 ? (p.M - mbase > 0 ? p.M - mbase : 0) : 128);
+        if (p.out_dtype == PARO_BF16)
+          store_row(y, static_cast<__nv_bfloat16*>(p.out) + mbase * p.N + n, p.N, xs, bn, valid);
+        else if (p.out_dtype == PARO_F16)
+          store_row(y, static_cast<__half*>(p.out) + mbase * p.N + n, p.N, xs, bn, valid);
+        else
+          store_row(y, static_cast<float*>(p.out) + mbase * p.N + n, p.N, xs, bn, valid);
+      }
+      __syncwarp();  // the slice is rewritten for the next tile
     }
   }
 
@@ -429,6 +473,8 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   return fn;
 }
 
+static int g_tc_sms = 0;
+
 // The tensor-core kernel handles token counts above the decode range.
 int gemm_tc_supported(int64_t M, int N, int K) { return M > 64 && N % kRecRows == 0 && K % kGroup == 0; }
 
@@ -449,6 +495,18 @@ cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int
                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  // tile records as a [N/16][G][134 x 8 bytes] tensor; one box = the 8
+  // records of one group for 8 consecutive 16-row blocks
+  CUtensorMap wmap;
+  const int G = K / kGroup;
+  const cuuint64_t wdims[3] = {(cuuint64_t)(kRecBytes / 8), (cuuint64_t)G, (cuuint64_t)(N / kRecRows)};
+  const cuuint64_t wstrides[2] = {(cuuint64_t)kRecBytes, (cuuint64_t)G * kRecBytes};
+  const cuuint32_t wbox[3] = {(cuuint32_t)(kRecBytes / 8), 1, (cuuint32_t)kTcRecs};
+  const cuuint32_t westr[3] = {1, 1, 1};
+  r = encode(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<void*>(packed), wdims, wstrides, wbox, westr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
   TcParams p;
   p.xscale = xscale;
   p.M = M;
@@ -461,8 +519,19 @@ cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int
   p.out_dtype = out_dtype;
   cudaError_t e = ensure_smem_limit((const void*)gemm_tc_kernel, kTcSmem);
   if (e != cudaSuccess) return e;
+  p.tiles_n = (N + 2 * kTcRows - 1) / (2 * kTcRows);
+  const int64_t tiles = (int64_t)p.tiles_n * ((M + kTcTok - 1) / kTcTok);
+  if (tiles > 0x7FFFFFFF) return cudaErrorInvalidValue;
+  p.tiles = (int)tiles;
+  if (g_tc_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_tc_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (g_tc_sms <= 1) g_tc_sms = 148;
+  }
+  const int pairs = (int)(tiles < g_tc_sms / 2 ? tiles : g_tc_sms / 2);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(2 * ((N + 2 * kTcRows - 1) / (2 * kTcRows))), (unsigned)((M + kTcTok - 1) / kTcTok));
+  cfg.gridDim = dim3((unsigned)(2 * pairs));
   cfg.blockDim = dim3(kTcThreads);
   cfg.dynamicSmemBytes = kTcSmem;
   cfg.stream = st;
@@ -473,7 +542,7 @@ cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel, xmap, p);
+  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel, xmap, wmap, p);
 }
 
 }  // namespace paro
