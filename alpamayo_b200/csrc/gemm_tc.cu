@@ -201,6 +201,12 @@ __device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
   return r;
 }
 
+__device__ __forceinline__ uint32_t ldg_nc_u16(const uint16_t* p) {
+  uint16_t r;
+  asm volatile("ld.global.nc.u16 %0, [%1];" : "=h"(r) : "l"(p));
+  return r;
+}
+
 __device__ __forceinline__ uint32_t expand_signed(uint32_t nib4, uint32_t zz) {
   // bytes 0x80 + q - z (no borrows: q, z <= 15), then flip the bias bit
   return ((nib4 | 0x80808080u) - zz) ^ 0x80808080u;
@@ -390,38 +396,50 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
       const bool row_ok = (row >> 4) < tile_nrec(n0);
       const uint16_t* sp = reinterpret_cast<const uint16_t*>(
           p.packed + rec_offset(n0 / kRecRows + (row_ok ? (row >> 4) : 0), 0, G) + kRecScaleOff) + (row & 15);
-      // this row's scale of group g is sp[g * kRecBytes / 2]; prefetched two
-      // groups ahead
-      auto fetch_scale = [&](int g) -> float {
-        return (row_ok && g < G) ? half_bits_to_f32(__ldg(sp + (size_t)g * (kRecBytes / 2))) : 0.f;
+      // this row's scale of group g is sp[g * kRecBytes / 2]: its fp16 bits
+      // are loaded three groups ahead and converted only where used, so the
+      // load's latency never stalls the fold
+      auto fetch_bits = [&](int g) -> uint32_t {
+        return (row_ok && g < G) ? ldg_nc_u16(sp + (size_t)g * (kRecBytes / 2)) : 0u;
       };
-      float s_cur = fetch_scale(0), s_next = fetch_scale(1);
+      uint32_t r0 = fetch_bits(0), r1 = fetch_bits(1), r2 = fetch_bits(2);
       uint64_t y[64];
 #pragma unroll
       for (int j = 0; j < 64; ++j) y[j] = 0ull;  // (+0.0f, +0.0f)
       for (int g = 0; g < G; ++g, ++it) {
         const uint32_t b = it & 1;
-        const float s_after = fetch_scale(g + 2);
+        const uint32_t r_after = fetch_bits(g + 3);
         if (!mbar_wait(&acc_full[b], (it >> 1) & 1)) {
           failed = true;
           break;
         }
         tc_fence_after();
-        const uint64_t s2 = pack2(s_cur, s_cur);
+        const float sc = half_bits_to_f32((uint16_t)r0);
+        const uint64_t s2 = pack2(sc, sc);
+        // chunk c + 1 is read from tensor memory while chunk c is folded
+        const uint32_t tb = tmem + lane_base + b * kTcTok + col0;
+        uint32_t va[16], vb[16];
+        tmem_ld16(tb, va);
+        tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint32_t v[16];
-          tmem_ld16(tmem + lane_base + b * kTcTok + col0 + c * 16, v);
-          tmem_wait_ld();
+        for (int c = 0; c < 8; c += 2) {
+          tmem_ld16(tb + (c + 1) * 16, vb);
 #pragma unroll
           for (int j = 0; j < 8; ++j)
-            y[c * 8 + j] = fma2(s2, pack2((float)(int)v[2 * j], (float)(int)v[2 * j + 1]), y[c * 8 + j]);
+            y[c * 8 + j] = fma2(s2, pack2((float)(int)va[2 * j], (float)(int)va[2 * j + 1]), y[c * 8 + j]);
+          tmem_wait_ld();
+          if (c + 2 < 8) tmem_ld16(tb + (c + 2) * 16, va);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            y[c * 8 + 8 + j] = fma2(s2, pack2((float)(int)vb[2 * j], (float)(int)vb[2 * j + 1]), y[c * 8 + 8 + j]);
+          if (c + 2 < 8) tmem_wait_ld();
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(&acc_empty[b], 0);
-        s_cur = s_next;
-        s_next = s_after;
+        r0 = r1;
+        r1 = r2;
+        r2 = r_after;
       }
       // token scale, bias, convert, store: this thread holds output row
       // n0 + row for tokens m0 + col0 + (0..127); the tensor core is already
