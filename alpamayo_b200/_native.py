@@ -57,6 +57,8 @@ def capi() -> ctypes.CDLL:
         "paro_prepare_rotation": (i32, [vp, vp, i32, i32, i32, vp, vp, vp]),
         "paro_rotate": (i32, [vp, i32, i64, i32, vp, vp, i32, vp, i32, i32, vp, vp]),
         "paro_rotq_int8": (i32, [vp, i32, i64, i32, vp, vp, i32, i32, i32, vp, vp, vp]),
+        "paro_rotq_int8_workspace_size": (sz, [i64, i32, i32]),
+        "paro_rotq_int8_ws": (i32, [vp, i32, i64, i32, vp, vp, i32, i32, i32, vp, vp, vp, sz, vp]),
         "paro_quant_int8": (i32, [vp, i32, i64, i32, vp, vp, vp]),
         "paro_packed_weight_bytes": (sz, [i32, i32]),
         "paro_prepare_weights": (i32, [vp, vp, vp, i32, i32, i32, vp, vp]),

@@ -24,7 +24,7 @@ OBJ = os.path.join(PKG, "_build")
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 
-CU_SOURCES = ["capi.cu", "rotq.cu", "rotq_fused.cu", "prepare.cu", "gemm_decode.cu", "gemm_tc.cu"]
+CU_SOURCES = ["capi.cu", "rotq.cu", "rotq_fused.cu", "rotq_rows.cu", "prepare.cu", "gemm_decode.cu", "gemm_tc.cu"]
 HEADERS = ["paro_common.cuh", "tc_ptx.cuh"]
 GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",

@@ -16,6 +16,10 @@ cudaError_t launch_rotate(int x_dtype, int krot, int group, const void* x, int64
 cudaError_t launch_rotq(int x_dtype, const void* x, int64_t M, int K, const uint16_t* scales, const uint32_t* rtab,
                         int fp16_round, int8_t* q, float* s, cudaStream_t st);
 int rotq_max_k();
+size_t rotq_rows_workspace(int64_t M, int K);
+int rotq_rows_min_m();
+cudaError_t launch_rotq_rows(int x_dtype, const void* x, int64_t M, int K, const uint16_t* scales,
+                             const uint32_t* rtab, int8_t* q, float* s, void* ws, cudaStream_t st);
 cudaError_t launch_quant(int x_dtype, const void* x, int64_t M, int K, int8_t* q, float* s, cudaStream_t st);
 cudaError_t launch_prepare_rotation(const int16_t* pairs, const uint16_t* theta, int krot, int K, int group,
                                     uint32_t* out, int32_t* bad, cudaStream_t st);
@@ -139,6 +143,29 @@ int paro_rotq_int8(const void* x, int x_dtype, int64_t M, int K, const uint16_t*
   if (int d = device_check()) return d;
   return cuda_status(
       launch_rotq(x_dtype, x, M, K, scales, rot_table, fp16_round ? 1 : 0, out_q, out_scale, (cudaStream_t)stream));
+}
+
+size_t paro_rotq_int8_workspace_size(int64_t M, int K, int fp16_round) {
+  if (M < rotq_rows_min_m() || K <= 0 || K % kGroup || !fp16_round) return 0;
+  return rotq_rows_workspace(M, K);
+}
+
+int paro_rotq_int8_ws(const void* x, int x_dtype, int64_t M, int K, const uint16_t* scales,
+                      const uint32_t* rot_table, int krot, int group, int fp16_round, int8_t* out_q,
+                      float* out_scale, void* workspace, size_t workspace_bytes, paro_stream_t stream) {
+  const size_t need = paro_rotq_int8_workspace_size(M, K, fp16_round);
+  if (need == 0)
+    return paro_rotq_int8(x, x_dtype, M, K, scales, rot_table, krot, group, fp16_round, out_q, out_scale, stream);
+  if (!x || !rot_table || !out_q || !out_scale) return PARO_ERR_INVALID_ARGUMENT;
+  if (!valid_dtype(x_dtype)) return PARO_ERR_UNSUPPORTED;
+  if (krot != 8 || group != 128) return PARO_ERR_UNSUPPORTED;
+  if (!aligned(x, x_dtype == PARO_F32 ? 4 : 2) || (scales && !aligned(scales, 2)) || !aligned(rot_table, 4))
+    return PARO_ERR_MISALIGNED;
+  if (!workspace || workspace_bytes < need) return PARO_ERR_WORKSPACE;
+  if (!aligned(workspace, 256)) return PARO_ERR_MISALIGNED;
+  if (int d = device_check()) return d;
+  return cuda_status(launch_rotq_rows(x_dtype, x, M, K, scales, rot_table, out_q, out_scale, workspace,
+                                      (cudaStream_t)stream));
 }
 
 int paro_quant_int8(const void* x, int x_dtype, int64_t M, int K, int8_t* out_q, float* out_scale,

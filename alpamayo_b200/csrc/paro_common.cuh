@@ -60,6 +60,29 @@ __device__ __forceinline__ float round_fp16(float v) {
 // reference's Triton quantiser); calls the CUDA math library's roundf.
 __device__ __forceinline__ float round_half_away(float v) { return roundf(v); }
 
+// One Givens update of a channel: x' = x * p + partner * q, both products and
+// the sum rounded separately (the reference evaluates c*a + s*b as two
+// multiplies and an add), so the result does not depend on which operand
+// comes first.
+__device__ __forceinline__ float givens(float x, float partner, float p, float q) {
+  return __fadd_rn(__fmul_rn(x, p), __fmul_rn(partner, q));
+}
+
+// The same on two rows at once (packed float32 pairs, sm_100).
+__device__ __forceinline__ float2 givens2(float2 x, float2 partner, float p, float q) {
+  uint64_t xv, wv, pv, qv, a, b, r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(xv) : "f"(x.x), "f"(x.y));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(wv) : "f"(partner.x), "f"(partner.y));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(pv) : "f"(p));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(qv) : "f"(q));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(a) : "l"(xv), "l"(pv));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(b) : "l"(wv), "l"(qv));
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  float2 o;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(o.x), "=f"(o.y) : "l"(r));
+  return o;
+}
+
 // Raise a kernel's dynamic shared-memory limit to `bytes` once per (kernel,
 // device); later calls are a map lookup instead of a driver call.
 cudaError_t ensure_smem_limit(const void* kernel, int bytes);

@@ -13,12 +13,12 @@
 //   2. one barrier,
 //   3. reads its partner's R values and computes its own half of the
 //      rotation:  i' = c*i + s*j  (role i),  j' = -s*i + c*j  (role j),
-//      evaluated as a*ca + b*cb exactly as the reference writes the two
-//      halves.
+//      with both products and the sum rounded separately, as the
+//      reference's c*a + s*b is evaluated.
 // Shared buffers alternate between layers, so one barrier per layer is
 // enough.  The per-channel table (partner, role, fp16 angle; built at load
-// time by paro_prepare_rotation) makes this one 32-bit load per channel per
-// layer, prefetched a layer ahead.
+// time by paro_prepare_rotation) is one 32-bit word per channel per layer;
+// all layers' words are staged into shared memory with cp.async at start.
 //
 // The row's absolute maximum spans all K channels: a thread-block cluster of
 // C <= 8 CTAs covers a row block's groups, each CTA reduces its rows' maxima,
@@ -154,13 +154,10 @@ rotq_fused_kernel(const InT* __restrict__ x, int64_t M, int K, const uint16_t* _
         __sincosf(half_bits_to_f32((uint16_t)(tab >> 16)), &s_, &c_);
         float w[R];
         ld_vec<R>(buf + ((size_t)(p * GB + gs) * 128 + partner) * R, w);
-        const float ca = role_j ? -s_ : c_, cb = role_j ? c_ : s_;
+        // first element of the pair: c*i + s*j; second: -s*i + c*j
+        const float cp = role_j ? -s_ : s_;
 #pragma unroll
-        for (int r = 0; r < R; ++r) {
-          const float a = role_j ? w[r] : v[p][r];
-          const float b = role_j ? v[p][r] : w[r];
-          v[p][r] = a * ca + b * cb;
-        }
+        for (int r = 0; r < R; ++r) v[p][r] = givens(v[p][r], w[r], c_, cp);
       }
     }
   }

@@ -137,10 +137,17 @@ std::tuple<at::Tensor, at::Tensor> rotq_int8(const at::Tensor& x_in, const at::T
   auto ssz = x.sizes().vec();
   ssz.back() = 1;
   at::Tensor s = at::empty(ssz, x.options().dtype(at::kFloat));
-  check_status(paro_rotq_int8(x.data_ptr(), to_paro_dtype(x.scalar_type()), M, (int)K, sp,
-                              reinterpret_cast<const uint32_t*>(rot_table.data_ptr<int32_t>()),
-                              (int)rot_table.size(0), (int)group_size, fp16_round ? 1 : 0, q.data_ptr<int8_t>(),
-                              s.data_ptr<float>(), cur_stream()),
+  // prefill sizes take the two-pass path; its workspace comes from the
+  // caching allocator and is released when this call returns
+  const size_t wsb = paro_rotq_int8_workspace_size(M, (int)K, fp16_round ? 1 : 0);
+  at::Tensor ws;
+  if (wsb) ws = at::empty({(int64_t)wsb + 256}, x.options().dtype(at::kByte));
+  void* wsp = wsb ? reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(ws.data_ptr()) + 255) & ~(uintptr_t)255)
+                  : nullptr;
+  check_status(paro_rotq_int8_ws(x.data_ptr(), to_paro_dtype(x.scalar_type()), M, (int)K, sp,
+                                 reinterpret_cast<const uint32_t*>(rot_table.data_ptr<int32_t>()),
+                                 (int)rot_table.size(0), (int)group_size, fp16_round ? 1 : 0, q.data_ptr<int8_t>(),
+                                 s.data_ptr<float>(), wsp, wsb, cur_stream()),
                "rotq_int8");
   return {q, s};
 }

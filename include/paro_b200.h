@@ -122,6 +122,25 @@ int paro_rotq_int8(const void* x, int x_dtype, int64_t M, int K,
                    paro_stream_t stream);
 
 /*
+ * paro_rotq_int8 for many tokens: from paro_rotq_int8_workspace_size(M, K,
+ * fp16_round) > 0 tokens on (prefill sizes, fp16_round = 1), a two-pass path
+ * (rotation into an fp16 workspace with per-row maxima, then quantisation)
+ * that keeps the GPU busy where the single-pass cluster kernel cannot; the
+ * codes match paro_rotq_int8's within the code tolerance (rare 1-step
+ * differences from packed float arithmetic).  Below that size, or
+ * with a size of 0, it is paro_rotq_int8.
+ *   workspace : at least paro_rotq_int8_workspace_size(...) bytes (about
+ *               2 * M * K), 256-byte aligned; no initial contents required.
+ *               Calls that may run concurrently need separate workspaces.
+ */
+size_t paro_rotq_int8_workspace_size(int64_t M, int K, int fp16_round);
+
+int paro_rotq_int8_ws(const void* x, int x_dtype, int64_t M, int K,
+                      const uint16_t* scales, const uint32_t* rot_table, int krot,
+                      int group, int fp16_round, int8_t* out_q, float* out_scale,
+                      void* workspace, size_t workspace_bytes, paro_stream_t stream);
+
+/*
  * per_token_quant_int8 (int8_utils.py:131-156): absmax = max(max|x|, 1e-10),
  * scale = absmax / 127, q = round_half_away(x * (127 / absmax)).
  *   x : [M, K] of x_dtype;  out_q : int8 [M, K];  out_scale : float32 [M].

@@ -184,3 +184,36 @@ def test_rotq_ragged_rows_and_large_k(ops, M):
     q_ref, s_ref, _ = O.rot_quant_reference(xt.float().numpy(), pairs, theta.astype(np.float32),
                                             cs.astype(np.float32))
     check_codes(q.cpu().numpy(), q_ref, s.cpu().numpy().reshape(-1), s_ref)
+
+
+@pytest.mark.parametrize("M,K,xdt", [(512, 1024, torch.bfloat16), (700, 3584, torch.bfloat16),
+                                     (1030, 18944, torch.bfloat16), (600, 640, torch.float16),
+                                     (520, 256, torch.float32)])
+def test_rotq_two_pass_path_matches_fused_kernel_and_oracle(ops, M, K, xdt):
+    """Prefill sizes run the two-pass path (rotation into an fp16 workspace,
+    then quantisation).  It does the cluster kernel's arithmetic on packed
+    row pairs, so its codes match the single-pass kernel's (C ABI without
+    workspace) up to the code tolerance (a handful of 1-LSB flips per
+    million), and the oracle's on sampled rows within the same tolerance."""
+    from alpamayo_b200 import _native
+    L = _native.capi()
+    assert L.paro_rotq_int8_workspace_size(M, K, 1) > 0
+    pairs, theta, cs = make_rotation(K, seed=M + K)
+    x = make_activations(M, K, seed=M)
+    xt = torch.from_numpy(x).to(xdt).cuda()
+    table = ops.prepare_rotation(dev(pairs), dev(theta), 128)
+    csd = dev(cs.reshape(-1))
+    q, s = ops.rotq_int8(xt, table, csd, 128, True)          # two-pass path
+    q1 = torch.empty_like(q)
+    s1 = torch.empty_like(s)
+    code = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}[xdt]
+    st = L.paro_rotq_int8(xt.data_ptr(), code, M, K, csd.data_ptr(), table.data_ptr(), 8, 128, 1,
+                          q1.data_ptr(), s1.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert st == 0
+    torch.cuda.synchronize()
+    check_codes(q.cpu().numpy(), q1.cpu().numpy(), s.cpu().numpy().reshape(-1), s1.cpu().numpy().reshape(-1))
+    assert (q.int() - q1.int()).abs().gt(0).float().mean().item() <= 1e-5
+    rows = np.sort(np.random.default_rng(M).choice(M, size=24, replace=False))
+    q_ref, s_ref, _ = O.rot_quant_reference(xt.float().cpu().numpy()[rows], pairs, theta.astype(np.float32),
+                                            cs.astype(np.float32))
+    check_codes(q.cpu().numpy()[rows], q_ref, s.cpu().numpy().reshape(-1)[rows], s_ref)

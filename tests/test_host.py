@@ -37,6 +37,10 @@ def test_status_strings_and_version():
     assert L.paro_status_string(6) == b"workspace too small"
     assert L.paro_packed_weight_bytes(3584, 3584) == (3584 // 16) * 28 * 1072
     assert L.paro_packed_weight_bytes(3585, 3584) == 0
+    # the two-pass activation path: prefill sizes only, about 2 * M * K bytes
+    assert L.paro_rotq_int8_workspace_size(8, 3584, 1) == 0
+    assert L.paro_rotq_int8_workspace_size(4096, 3584, 0) == 0
+    assert L.paro_rotq_int8_workspace_size(4096, 3584, 1) >= 2 * 4096 * 3584
 
 
 def test_argument_validation_before_launch():
