@@ -5,6 +5,7 @@
 // mirroring the reference's TORCH_CHECKs in rotation.cu:117-124,456-493),
 // then launches asynchronously on the caller's stream.  Nothing here
 // allocates device memory or synchronises.
+#include <algorithm>
 #include <cstring>
 #include <string>
 
@@ -31,6 +32,10 @@ cudaError_t launch_gemm_decode(const int8_t* xq, const float* xscale, int64_t M,
                                const void* bias, int bias_dtype, void* out, int out_dtype, void* ws,
                                cudaStream_t st);
 size_t gemm_decode_workspace(int64_t M, int N);
+size_t linear_decode_workspace(int64_t M, int N);
+cudaError_t launch_linear_decode(const void* x, int x_dtype, const uint16_t* cscale, const uint32_t* rtab, int64_t M,
+                                 int N, int K, const void* packed, const void* bias, int bias_dtype, void* out,
+                                 int out_dtype, void* ws, void* scratch, cudaStream_t st);
 int gemm_tc_supported(int64_t M, int N, int K);
 size_t gemm_tc_workspace(int64_t M, int N, int K);
 cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
@@ -207,6 +212,76 @@ size_t paro_w4a8_gemm_workspace_size(int64_t M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0 || N % kRecRows || K % kGroup) return 0;
   return gemm_tc_supported(M, N, K) ? gemm_tc_workspace(M, N, K) : gemm_decode_workspace(M, N);
 }
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// one rotated W4A8 linear (activation + GEMM)
+// ---------------------------------------------------------------------------
+namespace {
+constexpr int64_t kLinearFusedMaxM = 64;
+size_t al256(size_t b) { return (b + 255) & ~(size_t)255; }
+// scratch of the two-kernel route: int8 rows, token scales, activation workspace
+size_t linear_unfused_scratch(int64_t M, int K, int fp16_round) {
+  return al256((size_t)M * K) + al256((size_t)M * sizeof(float)) + paro_rotq_int8_workspace_size(M, K, fp16_round);
+}
+}  // namespace
+
+extern "C" {
+
+size_t paro_w4a8_linear_workspace_size(int64_t M, int N, int K) {
+  if (M <= 0 || N <= 0 || K <= 0 || N % kRecRows || K % kGroup) return 0;
+  size_t ws = paro_w4a8_gemm_workspace_size(M, N, K);
+  if (M <= kLinearFusedMaxM) ws = std::max(ws, linear_decode_workspace(M, N));
+  return ws;
+}
+
+size_t paro_w4a8_linear_scratch_size(int64_t M, int N, int K, int fp16_round) {
+  if (M <= 0 || N <= 0 || K <= 0 || N % kRecRows || K % kGroup) return 0;
+  size_t sc = linear_unfused_scratch(M, K, fp16_round);
+  if (M <= kLinearFusedMaxM) sc = std::max(sc, al256((size_t)M * K * sizeof(uint16_t)));
+  return sc;
+}
+
+int paro_w4a8_linear(const void* x, int x_dtype, int64_t M, int K, int N, const uint16_t* channel_scales,
+                     const uint32_t* rot_table, int fp16_round, const void* packed, const void* bias, int bias_dtype,
+                     void* out, int out_dtype, void* workspace, size_t workspace_bytes, void* scratch,
+                     size_t scratch_bytes, paro_stream_t stream) {
+  if (M == 0 && N > 0 && K > 0) return PARO_OK;
+  if (!x || !rot_table || !packed || !out || M < 0 || N <= 0 || K <= 0) return PARO_ERR_INVALID_ARGUMENT;
+  if (!valid_dtype(x_dtype) || !valid_dtype(out_dtype) || (bias && !valid_dtype(bias_dtype)))
+    return PARO_ERR_UNSUPPORTED;
+  if (N % kRecRows || K % kGroup) return PARO_ERR_SHAPE;
+  if (!aligned(x, x_dtype == PARO_F32 ? 4 : 2) || (channel_scales && !aligned(channel_scales, 2)) ||
+      !aligned(rot_table, 4) || !aligned(packed, 16))
+    return PARO_ERR_MISALIGNED;
+  if (workspace_bytes < paro_w4a8_linear_workspace_size(M, N, K) ||
+      scratch_bytes < paro_w4a8_linear_scratch_size(M, N, K, fp16_round) || !workspace || !scratch)
+    return PARO_ERR_WORKSPACE;
+  if (!aligned(workspace, 256) || !aligned(scratch, 256)) return PARO_ERR_MISALIGNED;
+  if (int d = device_check()) return d;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (M <= kLinearFusedMaxM && fp16_round) {
+    const cudaError_t e = launch_linear_decode(x, x_dtype, channel_scales, rot_table, M, N, K, packed, bias,
+                                               bias_dtype, out, out_dtype, workspace, scratch, st);
+    if (e != cudaErrorNotSupported) return cuda_status(e);
+  }
+  // two kernels: activation into the scratch, then the GEMM
+  uint8_t* sp = static_cast<uint8_t*>(scratch);
+  int8_t* xq = reinterpret_cast<int8_t*>(sp);
+  float* xs = reinterpret_cast<float*>(sp + al256((size_t)M * K));
+  void* aws = sp + al256((size_t)M * K) + al256((size_t)M * sizeof(float));
+  const size_t aws_bytes = paro_rotq_int8_workspace_size(M, K, fp16_round);
+  int rc = paro_rotq_int8_ws(x, x_dtype, M, K, channel_scales, rot_table, 8, kGroup, fp16_round, xq, xs,
+                             aws_bytes ? aws : nullptr, aws_bytes, stream);
+  if (rc != PARO_OK) return rc;
+  return paro_w4a8_gemm(xq, xs, M, N, K, packed, bias, bias_dtype, out, out_dtype, workspace, workspace_bytes,
+                        stream);
+}
+
+}  // extern "C"
+
+extern "C" {
 
 int paro_device_error_word(int clear) {
   const uint32_t a = error_word_decode(clear), b = error_word_tc(clear);

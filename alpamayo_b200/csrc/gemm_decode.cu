@@ -58,6 +58,13 @@ struct DecParams {
   int out_dtype;
   float* ws;        // [N][M] float32 partial sums, zero between calls
   uint32_t* cnt;    // [token slices][N/16] unit counters, zero between calls
+  // fused activation (linear entry point): x -> rotation -> int8 in-kernel
+  const void* x;            // [M, K] activations
+  const uint16_t* cscale;   // [K] fp16 channel scales or null
+  const uint32_t* rtab;     // [8, K] rotation table
+  __half* rot16;            // [M, K] scratch: rotated rows, fp16
+  uint32_t* amax;           // [M] row |max| bits, zero between calls
+  uint32_t* gsync;          // [2] grid barrier and exit counters, zero between calls
   int64_t units;    // (N/16) * G
   int ctas;
   int stages;
@@ -86,6 +93,71 @@ __device__ __forceinline__ int frag_sum(const uint32_t (&b)[8]) {
 }
 
 __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <int XIN>
+__device__ __forceinline__ float load_x(const void* x, size_t i) {
+  if constexpr (XIN == PARO_F16) return __half2float(static_cast<const __half*>(x)[i]);
+  else if constexpr (XIN == PARO_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(x)[i]);
+  else return static_cast<const float*>(x)[i];
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Fused activation, phase A (the CTA's consumer threads, two halves of 128):
+// half h rotates groups g = blockIdx.x + h * gridDim.x, ... for all M rows,
+// 8 rows at a time, exactly as the activation kernels do (channel scale, 8
+// Givens layers with separately rounded products, fp16 rounding); the rows go
+// to the fp16 scratch and each row's |max| to amax (atomicMax on the bits).
+template <int XIN>
+__device__ __forceinline__ void fused_rotate(const DecParams& p, int ctid, float* xb) {
+  const int half = ctid >> 7, ch = ctid & 127, lane = ctid & 31;
+  const int G = p.K / kGroup;
+  float* buf = xb + half * (2 * 8 * 128);
+  for (int g = blockIdx.x + half * gridDim.x; g < G; g += 2 * gridDim.x) {
+    const int c = g * kGroup + ch;
+    int part[8];
+    float cc[8], cp[8];
+#pragma unroll
+    for (int l = 0; l < 8; ++l) {
+      const uint32_t tab = __ldg(p.rtab + (size_t)l * p.K + c);
+      part[l] = (int)(tab & 0x7F);
+      float s_, c_;
+      __sincosf(half_bits_to_f32((uint16_t)(tab >> 16)), &s_, &c_);
+      cc[l] = c_;
+      cp[l] = ((tab >> 7) & 1) ? -s_ : s_;
+    }
+    const float sc = p.cscale ? half_bits_to_f32(p.cscale[c]) : 1.f;
+    for (int64_t r0 = 0; r0 < p.M; r0 += 8) {
+      float v[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) v[r] = (r0 + r < p.M) ? load_x<XIN>(p.x, (size_t)(r0 + r) * p.K + c) * sc : 0.f;
+#pragma unroll
+      for (int l = 0; l < 8; ++l) {
+        float* b = buf + (l & 1) * (8 * 128);
+#pragma unroll
+        for (int r = 0; r < 8; ++r) b[r * 128 + ch] = v[r];
+        named_barrier(2 + half, 128);
+#pragma unroll
+        for (int r = 0; r < 8; ++r) v[r] = givens(v[r], b[r * 128 + part[l]], cc[l], cp[l]);
+      }
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const __half h = __float2half_rn(v[r]);
+        uint32_t a = 0u;
+        if (r0 + r < p.M) {
+          p.rot16[(size_t)(r0 + r) * p.K + c] = h;
+          a = __float_as_uint(fabsf(__half2float(h)));
+        }
+        a = __reduce_max_sync(0xffffffffu, a);
+        if (lane == 0 && a) atomicMax(p.amax + r0 + r, a);
+      }
+    }
+  }
+}
 
 __device__ __forceinline__ float bias_at(const void* bias, int dtype, int n) {
   if (!bias) return 0.f;
@@ -185,8 +257,16 @@ struct ChunkIter {
 // padded by 16 bytes so the B-fragment reads of a warp hit 32 distinct
 // banks) and the per-group sums computed there; otherwise fragments are read
 // from global memory per record.
-template <int MT, bool XS>
+// XIN < 0: the int8 activations and token scales come from paro_rotq_int8;
+// XIN = a paro dtype: the kernel computes them itself from x (fused linear,
+// cooperative launch, M <= 64, XS only).
+template <int MT, bool XS, int XIN>
 __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p) {
+  constexpr bool FUSE = XIN >= 0;
+  static_assert(!FUSE || XS, "the fused activation stages its int8 rows in shared memory");
+  __shared__ float tok_scale_s[FUSE ? kDecMaxTokens : 1];
+  __shared__ float tok_inv_s[FUSE ? kDecMaxTokens : 1];
+  __shared__ int fuse_fail;
   extern __shared__ __align__(128) uint8_t smem[];
   const int S = p.stages;
   const int G = p.K / kGroup;
@@ -234,7 +314,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p
         mbar_arrive_expect_tx(&full[s], bytes);
         bulk_g2s(smem + (size_t)s * kDecStageBytes, p.packed + it.u * kRecBytes, bytes, &full[s]);
         it.advance(n);
-        if (XS && (k == S - 1 || (!it.more() && k < S - 1))) {
+        if (XS && !FUSE && (k == S - 1 || (!it.more() && k < S - 1))) {
           // the ring is full of weights: now fetch the activations, which
           // the previous kernel may still be writing
           grid_dependency_wait();
@@ -243,7 +323,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p
             bulk_g2s(xrows + (size_t)r * xstride, p.xq + (tok0 + r) * (int64_t)p.K, (uint32_t)p.K, xbar);
         }
       }
-      if (XS && u1 <= u0) {  // no weights to stream: still complete xbar
+      if (XS && !FUSE && u1 <= u0) {  // no weights to stream: still complete xbar
         grid_dependency_wait();
         mbar_arrive_expect_tx(xbar, (uint32_t)ntok_slice * p.K);
         for (int r = 0; r < ntok_slice; ++r)
@@ -283,7 +363,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p
         if (t < p.M) {
           if (whole)
             store_out(p.out, p.out_dtype, (size_t)t * p.N + n,
-                      v[sl] * p.xscale[t] + bias_at(p.bias, p.bias_dtype, n));
+                      v[sl] * (FUSE ? tok_scale_s[t - tok0] : p.xscale[t]) + bias_at(p.bias, p.bias_dtype, n));
           else
             red_add_f32(p.ws + (size_t)n * p.M + t, v[sl]);
         }
@@ -308,7 +388,8 @@ __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p
             float* wp = p.ws + (size_t)n * p.M + t;
             const float a = __ldcg(wp);
             __stcg(wp, 0.f);
-            store_out(p.out, p.out_dtype, (size_t)t * p.N + n, a * p.xscale[t] + bias_at(p.bias, p.bias_dtype, n));
+            store_out(p.out, p.out_dtype, (size_t)t * p.N + n,
+                      a * (FUSE ? tok_scale_s[t - tok0] : p.xscale[t]) + bias_at(p.bias, p.bias_dtype, n));
           }
           __syncwarp();
           if (lane == 0) cnt[nb] = 0u;
@@ -329,10 +410,66 @@ __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p
     xvalid[mt] = t < p.M;
     xrow[mt] = p.xq + (xvalid[mt] ? t : 0) * (int64_t)p.K + 4 * tig;
   }
+  if constexpr (FUSE) {
+    // phase A: rotate this CTA's groups (the shared activation area is the
+    // exchange buffer until phase B fills it)
+    fused_rotate<XIN>(p, ctid, reinterpret_cast<float*>(xrows));
+    __threadfence();
+    named_barrier(1, kDecConsumers * 32);
+    // grid barrier: every CTA's rows and maxima are in place (cooperative
+    // launch: all CTAs are resident; the wait is bounded)
+    if (ctid == 0) {
+      fuse_fail = 0;
+      atomicAdd(p.gsync, 1u);
+      const long long t0 = clock64();
+      while (ld_acquire_gpu(p.gsync) < gridDim.x) {
+        if (clock64() - t0 > 400000000LL) {
+          report_error(kErrMbarTimeout);
+          fuse_fail = 1;
+          break;
+        }
+      }
+    }
+    named_barrier(1, kDecConsumers * 32);
+    if (fuse_fail) return;
+    // phase B: token scales, then the int8 rows into shared memory
+    if (ctid < ntok_slice) {
+      const float a = fmaxf(__uint_as_float(__ldcg(p.amax + tok0 + ctid)), 1e-10f);
+      tok_inv_s[ctid] = __fdiv_rn(127.0f, a);
+      tok_scale_s[ctid] = __fdiv_rn(a, 127.0f);
+    }
+    named_barrier(1, kDecConsumers * 32);
+    const int k8n = p.K / 8;
+    for (int e = ctid; e < ntok_slice * k8n; e += kDecConsumers * 32) {
+      const int r = e / k8n, k8 = e - r * k8n;
+      const uint4 u = __ldcg(reinterpret_cast<const uint4*>(p.rot16 + (size_t)(tok0 + r) * p.K) + k8);
+      const __half* h = reinterpret_cast<const __half*>(&u);
+      const float inv = tok_inv_s[r];
+      uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        w0 |= ((uint32_t)(uint8_t)(int8_t)(int)round_half_away(__half2float(h[q]) * inv)) << (8 * q);
+        w1 |= ((uint32_t)(uint8_t)(int8_t)(int)round_half_away(__half2float(h[q + 4]) * inv)) << (8 * q);
+      }
+      *reinterpret_cast<uint2*>(xrows + (size_t)r * xstride + (size_t)k8 * 8) = make_uint2(w0, w1);
+    }
+    named_barrier(1, kDecConsumers * 32);
+    // the last CTA past this point returns the barrier state to zero
+    if (ctid == 0) {
+      __threadfence();
+      const uint32_t old = atomicAdd(p.gsync + 1, 1u);
+      if (old == gridDim.x - 1) {
+        __threadfence();
+        for (int64_t r = 0; r < p.M; ++r) p.amax[r] = 0u;
+        p.gsync[0] = 0u;
+        p.gsync[1] = 0u;
+      }
+    }
+  }
   if constexpr (XS) {
     // rows beyond the slice's tokens hold stale bytes; they only feed output
     // columns that are never stored
-    if (!mbar_wait(xbar, 0)) return;
+    if (!FUSE && !mbar_wait(xbar, 0)) return;
     for (int e = ctid; e < G * MP; e += kDecConsumers * 32) {
       const int g = e / MP, r = e - g * MP;
       int sum = 0;
@@ -437,10 +574,10 @@ static size_t fixed_smem(int MT) {
   return (2 * kDecMaxStages + 6) * sizeof(uint64_t) + 2 * (size_t)kDecConsumers * MT * 4 * 32 * sizeof(float);
 }
 
-template <int MT, bool XS>
+template <int MT, bool XS, int XIN = -1>
 static cudaError_t launch_mt(DecParams p, size_t xs_bytes, cudaStream_t st) {
   const size_t smem = (size_t)p.stages * kDecStageBytes + fixed_smem(MT) + (XS ? xs_bytes : 0);
-  auto kern = gemm_stream_kernel<MT, XS>;
+  auto kern = gemm_stream_kernel<MT, XS, XIN>;
   cudaError_t e = ensure_smem_limit((const void*)kern, kDecSmemBudget + 4096);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
@@ -449,8 +586,14 @@ static cudaError_t launch_mt(DecParams p, size_t xs_bytes, cudaStream_t st) {
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  if (XIN >= 0) {
+    // the fused activation's grid barrier needs every CTA resident
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+  } else {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+  }
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, p);
@@ -479,7 +622,7 @@ cudaError_t launch_gemm_decode(const int8_t* xq, const float* xscale, int64_t M,
     cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
     if (g_num_sms <= 0) g_num_sms = 148;
   }
-  DecParams p;
+  DecParams p = {};
   p.xq = xq;
   p.xscale = xscale;
   p.M = M;
@@ -500,6 +643,74 @@ cudaError_t launch_gemm_decode(const int8_t* xq, const float* xscale, int64_t M,
   if (M <= 16) return launch_pick<2>(p, st);
   if (M <= 32) return launch_pick<4>(p, st);
   return launch_pick<8>(p, st);
+}
+
+// ---------------------------------------------------------------------------
+// fused linear for decode sizes: activation rotation + quantisation inside
+// the GEMM kernel (see fused_rotate and the consumers' phase B)
+// ---------------------------------------------------------------------------
+size_t linear_decode_workspace(int64_t M, int N) {
+  return gemm_decode_workspace(M, N) + (((size_t)M * sizeof(uint32_t) + 255) & ~(size_t)255) + 256;
+}
+
+template <int MT>
+static cudaError_t launch_pick_fused(DecParams p, int x_dtype, cudaStream_t st) {
+  const int G = p.K / kGroup;
+  size_t xs_bytes = (size_t)8 * MT * (p.K + 16) + (size_t)G * 8 * MT * sizeof(int);
+  const size_t xch = (size_t)2 * 2 * 8 * 128 * sizeof(float);  // phase A exchange buffers
+  if (xs_bytes < xch) xs_bytes = xch;
+  const size_t base = fixed_smem(MT);
+  if (base + xs_bytes + 3 * (size_t)kDecStageBytes > (size_t)kDecSmemBudget) return cudaErrorNotSupported;
+  int stages = (int)((kDecSmemBudget - base - xs_bytes) / kDecStageBytes);
+  p.stages = stages > kDecMaxStages ? kDecMaxStages : stages;
+  switch (x_dtype) {
+    case PARO_F32: return launch_mt<MT, true, PARO_F32>(p, xs_bytes, st);
+    case PARO_F16: return launch_mt<MT, true, PARO_F16>(p, xs_bytes, st);
+    case PARO_BF16: return launch_mt<MT, true, PARO_BF16>(p, xs_bytes, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
+// Returns cudaErrorNotSupported (nothing launched) for shapes whose int8
+// rows do not fit in shared memory; callers then run the two kernels.
+cudaError_t launch_linear_decode(const void* x, int x_dtype, const uint16_t* cscale, const uint32_t* rtab, int64_t M,
+                                 int N, int K, const void* packed, const void* bias, int bias_dtype, void* out,
+                                 int out_dtype, void* ws, void* scratch, cudaStream_t st) {
+  if (M > kDecMaxTokens) return cudaErrorNotSupported;
+  if (g_num_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (g_num_sms <= 0) g_num_sms = 148;
+  }
+  DecParams p = {};
+  p.xq = nullptr;
+  p.xscale = nullptr;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.packed = static_cast<const uint8_t*>(packed);
+  p.bias = bias;
+  p.bias_dtype = bias_dtype;
+  p.out = out;
+  p.out_dtype = out_dtype;
+  const size_t wsf = ((size_t)N * (size_t)M * sizeof(float) + 255) & ~(size_t)255;
+  p.ws = static_cast<float*>(ws);
+  p.cnt = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(ws) + wsf);
+  uint8_t* tail = static_cast<uint8_t*>(ws) + gemm_decode_workspace(M, N);
+  p.amax = reinterpret_cast<uint32_t*>(tail);
+  p.gsync = reinterpret_cast<uint32_t*>(tail + (((size_t)M * sizeof(uint32_t) + 255) & ~(size_t)255));
+  p.x = x;
+  p.cscale = cscale;
+  p.rtab = rtab;
+  p.rot16 = static_cast<__half*>(scratch);
+  p.units = (int64_t)(N / kRecRows) * (K / kGroup);
+  p.ctas = (int)min64(g_num_sms, p.units);
+  p.stages = 0;
+  if (M <= 8) return launch_pick_fused<1>(p, x_dtype, st);
+  if (M <= 16) return launch_pick_fused<2>(p, x_dtype, st);
+  if (M <= 32) return launch_pick_fused<4>(p, x_dtype, st);
+  return launch_pick_fused<8>(p, x_dtype, st);
 }
 
 }  // namespace paro

@@ -244,12 +244,53 @@ at::Tensor w4a8_gemm(const at::Tensor& xq_in, const at::Tensor& xscale_in, const
   return out;
 }
 
-// One W4A8 rotated linear: fused activation kernel + GEMM (two launches).
-at::Tensor linear_w4a8(const at::Tensor& x, const at::Tensor& rot_table, const c10::optional<at::Tensor>& channel_scales,
-                       const at::Tensor& packed, int64_t N, const c10::optional<at::Tensor>& bias, bool fp16_round,
-                       at::ScalarType out_dtype) {
-  auto qs = rotq_int8(x, rot_table, channel_scales, 128, fp16_round);
-  return w4a8_gemm(std::get<0>(qs), std::get<1>(qs), packed, N, bias, out_dtype);
+// One W4A8 rotated linear (paro_w4a8_linear: one kernel at decode sizes).
+at::Tensor linear_w4a8(const at::Tensor& x_in, const at::Tensor& rot_table,
+                       const c10::optional<at::Tensor>& channel_scales, const at::Tensor& packed, int64_t N,
+                       const c10::optional<at::Tensor>& bias_opt, bool fp16_round, at::ScalarType out_dtype) {
+  at::Tensor x = x_in.contiguous();
+  check_cuda(x, "x");
+  check_cuda(rot_table, "rot_table");
+  check_cuda(packed, "packed");
+  TORCH_CHECK(rot_table.scalar_type() == at::kInt, "rot_table must be the int32 tensor from prepare_rotation");
+  const int64_t K = x.size(-1);
+  TORCH_CHECK(rot_table.size(-1) == K && rot_table.size(0) == 8, "rot_table must be [8, K]");
+  TORCH_CHECK((size_t)packed.numel() == paro_packed_weight_bytes((int)N, (int)K), "packed weight size mismatch");
+  const int64_t M = x.numel() / K;
+  const uint16_t* csp = nullptr;
+  at::Tensor cs;
+  if (channel_scales.has_value() && channel_scales->defined() && channel_scales->numel() > 0) {
+    cs = channel_scales->to(at::kHalf).contiguous();
+    check_cuda(cs, "channel_scales");
+    csp = reinterpret_cast<const uint16_t*>(cs.data_ptr());
+  }
+  const void* bp = nullptr;
+  int bdt = PARO_F32;
+  at::Tensor bias;
+  if (bias_opt.has_value() && bias_opt->defined()) {
+    bias = bias_opt->contiguous();
+    check_cuda(bias, "bias");
+    TORCH_CHECK(bias.numel() == N, "bias must have N elements");
+    bp = bias.data_ptr();
+    bdt = to_paro_dtype(bias.scalar_type());
+  }
+  c10::cuda::CUDAGuard guard(x.device());
+  auto osz = x.sizes().vec();
+  osz.back() = N;
+  at::Tensor out = at::empty(osz, x.options().dtype(out_dtype));
+  if (M == 0) return out;
+  const size_t wsb = paro_w4a8_linear_workspace_size(M, (int)N, (int)K);
+  void* wsp = workspace_for(x.device(), wsb);
+  // the scratch needs no initial contents: take it from the caching allocator
+  const size_t scb = paro_w4a8_linear_scratch_size(M, (int)N, (int)K, fp16_round ? 1 : 0);
+  at::Tensor sct = at::empty({(int64_t)scb + 256}, x.options().dtype(at::kByte));
+  void* scp = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(sct.data_ptr()) + 255) & ~(uintptr_t)255);
+  check_status(paro_w4a8_linear(x.data_ptr(), to_paro_dtype(x.scalar_type()), M, (int)K, (int)N, csp,
+                                reinterpret_cast<const uint32_t*>(rot_table.data_ptr<int32_t>()), fp16_round ? 1 : 0,
+                                packed.data_ptr(), bp, bdt, out.data_ptr(), to_paro_dtype(out_dtype), wsp, wsb, scp,
+                                scb, cur_stream()),
+               "linear_w4a8");
+  return out;
 }
 
 }  // namespace

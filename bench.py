@@ -4,8 +4,9 @@
 Headline workload ("decode sweep"): the four
 projection shapes of one 7B-class decoder layer (qkv 3584->4608, o 3584->3584,
 gate_up 3584->37888, down 18944->3584) at M = 1, 4 and 8 tokens; each linear
-is the fused rotation + int8 activation kernel followed by the int4 x int8
-GEMM.  One step = STEP_SWEEPS passes over the 12 (shape, M) cases.  Three
+runs through torch.ops.paro_b200.linear_w4a8, which at these sizes is one
+kernel (channel scale, 8 Givens layers and per-token int8 quantisation of the
+activations inside the persistent W4A8 GEMM).  One step = STEP_SWEEPS passes over the 12 (shape, M) cases.  Three
 weight replicas (one per M) make the per-pass weight working set 363 MB
 (> 126 MB L2), so every GEMM streams its weights from HBM.  The metric value
 is weight-stream GB/s (algorithmic int4 code + fp16 scale + int4 zero bytes
@@ -13,9 +14,14 @@ per second), whole job.
 
 Timing: CUDA graph of one step, replayed; CUDA events around the timed
 replays, barrier + synchronize on both sides, max over ranks.  Per-kernel
-launch durations for the roofline come from an eager pass in which the host
-runs ahead of the device (a device sleep is queued first), with events
-between launches.
+launch durations for the roofline: each case's linear (one fused kernel at
+these sizes) runs after a 512 MiB write that flushes the L2, with CUDA
+events on the launching stream around it.
+
+Prefill (configs[2], the "prefill" object): the same four projections at
+M = 2048, 4096, 8192 through the tcgen05 GEMM, TOPS against the dense int8
+peak measured in the same run (torch._int_mm on 8192^3), plus the
+activation kernel's share of each linear's time.
 
 --impl reference: the reference's CPU fake-quant path (oracle/cpu_baseline.py,
 a port, since the reference's own Python cannot run here) on the host cores,
@@ -50,6 +56,7 @@ def args_():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--no-prefill", action="store_true")
     return p.parse_args()
 
 
@@ -64,10 +71,108 @@ def gemm_alg_bytes(M, N, K):
     return weight_bytes(N, K) + M * K + 4 * M + 2 * M * N
 
 
+def linear_alg_bytes(M, N, K):
+    """Algorithmic bytes of one fused decode linear: int4 weights + fp16
+    scales + int4 zeros, bf16 activations, the reference's rotation tables,
+    bf16 output."""
+    L = 8
+    return weight_bytes(N, K) + 2 * M * K + 2 * L * K + L * K + 2 * K + 2 * M * N
+
+
 def act_alg_bytes(M, K):
-    """Activation kernel: bf16 in, int8 + fp32 scale out, fp16 angles,
-    uint8 pairs and fp16 channel scales."""
-    return 2 * M * K + M * K + 4 * M + 8 * (K // 2) * 2 + 8 * K + 2 * K
+    """Activation kernel: bf16 in, int8 + fp32 scale out, and the reference's
+    rotation tables (int16 pairs, fp16 angles, fp16 channel scales)."""
+    L = 8
+    return 2 * M * K + M * K + 4 * M + 2 * L * K + L * K + 2 * K
+
+
+FLUSH_BYTES = 512 * 2 ** 20
+PAIR_REPS = 5
+PREFILL_M = [2048, 4096, 8192]
+
+
+def kernel_pair_times(torch, flush, act_fn, gemm_fn, reps):
+    """Device time of the activation kernel and of the GEMM that consumes its
+    output, each bracketed by CUDA events on the current stream, with the L2
+    flushed (a 512 MiB write) before every pair."""
+    ta, tg = [], []
+    for _ in range(reps):
+        flush.zero_()
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record()
+        q = act_fn()
+        e1.record()
+        gemm_fn(q)
+        e2.record()
+        torch.cuda.synchronize()
+        ta.append(e0.elapsed_time(e1) * 1e-3)
+        tg.append(e1.elapsed_time(e2) * 1e-3)
+    return ta, tg
+
+
+def kernel_times(torch, flush, fn, reps):
+    """Device time of one launch of fn, with the L2 flushed (a 512 MiB write)
+    before every launch, CUDA events on the current stream."""
+    ts = []
+    for _ in range(reps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ts.append(e0.elapsed_time(e1) * 1e-3)
+    return ts
+
+
+def int8_peak_tops(torch):
+    """Dense int8 tensor throughput of this GPU, measured as torch._int_mm
+    (cuBLASLt) on 8192^3, best of 5 after warm-up."""
+    n = 8192
+    a = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda")
+    b = torch.randint(-127, 128, (n, n), dtype=torch.int8, device="cuda").t()
+    for _ in range(3):
+        torch._int_mm(a, b)
+    best = None
+    for _ in range(5):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch._int_mm(a, b)
+        e1.record()
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) * 1e-3
+        best = t if best is None or t < best else best
+    del a, b
+    return 2 * n ** 3 / best / 1e12
+
+
+def prefill_section(torch, ops, syn, layers, flush, rank):
+    """the four projections at M = 2048, 4096, 8192, activation
+    kernel + tcgen05 GEMM per linear, L2 flushed before each pair."""
+    peak = int8_peak_tops(torch)
+    out, ops_sum, t_sum, act_sum = {}, 0.0, 0.0, 0.0
+    for M in PREFILL_M:
+        xk = {K: syn.make_activations(M, K, seed=31 * M + K + rank) for K in {3584, 18944}}
+        for (name, N, K) in SHAPES:
+            L = layers[name]
+            ta_l, tg_l = kernel_pair_times(
+                torch, flush, lambda: ops.rotq_int8(xk[K], L["rot_table"], L["cs_vec"], 128, True),
+                lambda q: ops.w4a8_gemm(q[0], q[1], L["packed"], N, None, torch.bfloat16), 3)
+            tg, ta = statistics.median(tg_l), statistics.median(ta_l)
+            tops = 2 * M * N * K / tg / 1e12
+            ops_sum += 2 * M * N * K
+            t_sum += tg
+            act_sum += ta
+            out[f"{name}_m{M}"] = {"gemm_us": round(tg * 1e6, 1), "tops": round(tops, 1),
+                                   "frac": round(tops / peak, 4), "act_us": round(ta * 1e6, 1),
+                                   "act_share": round(ta / (ta + tg), 4),
+                                   "act_GBps": round(act_alg_bytes(M, K) / ta / 1e9, 1)}
+        del xk
+    agg = ops_sum / t_sum / 1e12
+    return {"workload": "configs[2]: qkv/o/gate_up/down at M=2048,4096,8192, bf16 activations",
+            "kernel": "gemm_tc (tcgen05 kind::i8, TMEM accumulators)", "tops": round(agg, 1),
+            "int8_peak_tops": round(peak, 1), "peak_kind": "measured in this run: torch._int_mm 8192^3",
+            "frac": round(agg / peak, 4), "act_share": round(act_sum / (act_sum + t_sum), 4), "cases": out}
 
 
 def peaks():
@@ -243,8 +348,9 @@ def main():
     wset = sum(weight_bytes(N, K) for (_, N, K) in SHAPES) * len(DECODE_M)
 
     def linear(L, x, M):
-        q, s = ops.rotq_int8(x, L["rot_table"], L["cs_vec"], 128, True)
-        return ops.w4a8_gemm(q, s, L["packed"], L["N"], None, torch.bfloat16)
+        # the whole rotated linear: at decode sizes one kernel (activation
+        # rotation + int8 quantisation inside the GEMM)
+        return ops.linear_w4a8(x, L["rot_table"], L["cs_vec"], L["packed"], L["N"], None, True, torch.bfloat16)
 
     def sweep():
         for ri, M in enumerate(DECODE_M):
@@ -256,7 +362,7 @@ def main():
             sweep()
 
     bytes_per_step = STEP_SWEEPS * wset
-    launches_per_step = STEP_SWEEPS * len(DECODE_M) * len(SHAPES) * 2
+    launches_per_step = STEP_SWEEPS * len(DECODE_M) * len(SHAPES)
 
     # --- capture one step as a CUDA graph
     s = torch.cuda.Stream()
@@ -289,41 +395,29 @@ def main():
     ms = max_over_ranks(ms, world)
     value = world * bytes_per_step / (ms * 1e-3) / 1e9
 
-    # --- per-kernel launch durations (eager, host ahead of the device)
-    gemm_t, gemm_b, act_t, act_b, cases = 0.0, 0, 0.0, 0, {}
-    for _ in range(3):
-        torch.cuda._sleep(int(2e7))
-        evs = []
-        for ri, M in enumerate(DECODE_M):
-            for (name, N, K) in SHAPES:
-                L = reps[ri][name]
-                ea, eb, ec = (torch.cuda.Event(enable_timing=True) for _ in range(3))
-                ea.record()
-                q, sc = ops.rotq_int8(xs[(M, K)], L["rot_table"], L["cs_vec"], 128, True)
-                eb.record()
-                ops.w4a8_gemm(q, sc, L["packed"], N, None, torch.bfloat16)
-                ec.record()
-                evs.append((name, M, N, K, ea, eb, ec))
-        torch.cuda.synchronize()
-        for (name, M, N, K, ea, eb, ec) in evs:
-            ta, tg = ea.elapsed_time(eb) * 1e-3, eb.elapsed_time(ec) * 1e-3
-            act_t += ta
-            act_b += act_alg_bytes(M, K)
-            gemm_t += tg
-            gemm_b += gemm_alg_bytes(M, N, K)
-            c = cases.setdefault(f"{name}_m{M}", {"gemm_us": [], "act_us": []})
-            c["gemm_us"].append(tg * 1e6)
-            c["act_us"].append(ta * 1e6)
+    # --- per-kernel launch durations: the fused linear kernel of each case,
+    # L2 flushed before every launch, CUDA events on the launching stream
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    lin_t, lin_b, cases = 0.0, 0, {}
+    for ri, M in enumerate(DECODE_M):
+        for (name, N, K) in SHAPES:
+            L = reps[ri][name]
+            tl = kernel_times(torch, flush, lambda: linear(L, xs[(M, K)], M), PAIR_REPS)
+            lin_t += sum(tl)
+            lin_b += linear_alg_bytes(M, N, K) * len(tl)
+            tm = statistics.median(tl)
+            cases[f"{name}_m{M}"] = {"linear_us": round(1e6 * tm, 2),
+                                     "weight_GBps": round(weight_bytes(N, K) / tm / 1e9, 1)}
     hbm, peak_kind = peaks()
-    gemm_gbs = gemm_b / gemm_t / 1e9
-    case_out = {}
-    for (name, N, K) in SHAPES:
-        for M in DECODE_M:
-            c = cases[f"{name}_m{M}"]
-            gu = statistics.median(c["gemm_us"])
-            case_out[f"{name}_m{M}"] = {"gemm_us": round(gu, 2), "act_us": round(statistics.median(c["act_us"]), 2),
-                                       "weight_GBps": round(weight_bytes(N, K) / gu / 1e3, 1)}
-    traffic = profile_traffic("gemm_decode_gate_up_m8.md")
+    lin_gbs = lin_b / lin_t / 1e9
+    case_out = cases
+    traffic = profile_traffic("linear_decode_gate_up_m8.md")
+
+    # --- prefill: tcgen05 GEMM and activation kernel per shape
+    prefill = None
+    if not a.no_prefill:
+        prefill = prefill_section(torch, ops, syn, reps[0], flush, rank)
+    del flush
 
     # --- end to end through the public op with host buffers (graph of the step)
     e2e = None
@@ -378,19 +472,21 @@ def main():
             "warmup": a.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int4xint8->int32 (bf16 act/out)", "data": "synthetic",
             "config": {"workload": "decode sweep, BASELINE configs[1]: qkv 3584->4608, o 3584->3584, "
-                                   "gate_up 3584->37888, down 18944->3584 at M=1,4,8; rotation+int8 quant kernel "
-                                   "+ W4A8 GEMM per linear",
+                                   "gate_up 3584->37888, down 18944->3584 at M=1,4,8; per linear one fused "
+                                   "kernel (channel scale + 8 Givens layers + per-token int8 + W4A8 GEMM)",
                        "step": f"{STEP_SWEEPS} sweeps of the 12 (shape, M) linears, CUDA graph",
                        "l2": f"weight working set {wset / 2**20:.0f} MiB per sweep > L2 {L2_BYTES / 2**20:.0f} MiB "
                              "(3 replicas, one per M); inputs not flushed",
                        "parallelism": f"dp{world} (independent replicas, no collective)"},
-            "roofline": {"kernel": "gemm_decode (int4 x int8 mma.sync streaming)", "bound": "hbm",
-                         "achieved": round(gemm_gbs, 1), "peak": hbm, "unit": "GB/s",
-                         "frac": round(gemm_gbs / hbm, 4), "peak_kind": peak_kind,
+            "roofline": {"kernel": "linear_decode (gemm_stream_kernel with in-kernel activation rotation + "
+                                   "int8 quantisation; persistent, cooperative)", "bound": "hbm",
+                         "achieved": round(lin_gbs, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(lin_gbs / hbm, 4), "peak_kind": peak_kind,
                          "traffic": traffic,
-                         "alg_bytes": "N*K/2 + G*N*2 + G*N/2 + M*K + 4M + 2*M*N per launch"},
-            "activation_kernel": {"achieved_GBps": round(act_b / act_t / 1e9, 1),
-                                  "frac": round(act_b / act_t / 1e9 / hbm, 4)},
+                         "alg_bytes": "weights N*K/2 + G*N*2 + G*N/2, activations 2*M*K (bf16), rotation tables "
+                                      "2LK + LK + 2K (L = 8), output 2*M*N, per launch",
+                         "timing": "per launch, L2 flushed (512 MiB write) before each, CUDA events"},
+            "prefill": prefill,
             "cases": case_out,
             "gpu_launches": launches_per_step * a.steps,
             "clocks": clk,

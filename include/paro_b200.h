@@ -219,6 +219,33 @@ int paro_w4a8_gemm(const int8_t* xq, const float* xscale, int64_t M, int N, int 
  * read them.  clear != 0 resets the word.  Returns -1 if it cannot be read. */
 int paro_device_error_word(int clear);
 
+/*
+ * One rotated W4A8 linear: y = paro_w4a8_gemm(paro_rotq_int8(x)), the whole
+ * forward of RotateLinearInt4 / BF16RotateLinearWrapper
+ * (src/alpamayo_r1/utils/quantization/paroquant_marlin_w4a8.py:47-71 with
+ * rotation_linear.py:53-139).  Up to 64 tokens with fp16_round = 1 this is
+ * ONE cooperative kernel: the GEMM's CTAs rotate and quantise the
+ * activations themselves (a grid-wide barrier between the rotation and the
+ * quantisation) while their weight streams are already running; otherwise
+ * it is the activation kernel(s) followed by the GEMM.
+ *   x             : [M, K] of x_dtype;  channel_scales : fp16 [K] or NULL.
+ *   rot_table     : uint32 [8, K] from paro_prepare_rotation (group 128).
+ *   workspace     : paro_w4a8_linear_workspace_size(M, N, K) bytes, 256-byte
+ *                   aligned, ZERO-FILLED before first use and left zero-filled
+ *                   by every call (as paro_w4a8_gemm's).
+ *   scratch       : paro_w4a8_linear_scratch_size(M, N, K, fp16_round) bytes,
+ *                   256-byte aligned, no initial contents required.
+ * Calls that may run concurrently need separate workspaces and scratches.
+ */
+size_t paro_w4a8_linear_workspace_size(int64_t M, int N, int K);
+size_t paro_w4a8_linear_scratch_size(int64_t M, int N, int K, int fp16_round);
+
+int paro_w4a8_linear(const void* x, int x_dtype, int64_t M, int K, int N,
+                     const uint16_t* channel_scales, const uint32_t* rot_table, int fp16_round,
+                     const void* packed, const void* bias, int bias_dtype,
+                     void* out, int out_dtype, void* workspace, size_t workspace_bytes,
+                     void* scratch, size_t scratch_bytes, paro_stream_t stream);
+
 /* Which GEMM kernel paro_w4a8_gemm would launch for this shape
  * (0 = streaming decode kernel, 1 = tcgen05 tensor-core kernel). */
 int paro_w4a8_gemm_path(int64_t M, int N, int K);
