@@ -302,6 +302,9 @@ __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p
     fence_mbar_init();
   }
   __syncthreads();
+  // the next kernel on the stream may launch as soon as SMs free up (it
+  // waits for this grid's completion before reading its output)
+  asm volatile("griddepcontrol.launch_dependents;");
 
   if (warp == 0) {  // producer: weights do not depend on the previous kernel
     if (lane == 0) {

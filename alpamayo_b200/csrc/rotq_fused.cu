@@ -127,6 +127,9 @@ rotq_fused_kernel(const InT* __restrict__ x, int64_t M, int K, const uint16_t* _
       }
   asm volatile("cp.async.commit_group;" ::: "memory");
 
+  // x is the previous kernel's output: wait for that grid (a no-op when this
+  // launch has no programmatic dependency)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   float v[PM][R];
 #pragma unroll
   for (int p = 0; p < PM; ++p) {
@@ -223,13 +226,16 @@ static cudaError_t launch_fused(const FusedGeom& f, const void* x, int64_t M, in
   cfg.blockDim = dim3((unsigned)(128 * f.GB), 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = (unsigned)f.C;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // overlap the table staging with the previous kernel's tail
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, kern, static_cast<const InT*>(x), M, K, scales, rtab, fp16_round, f.gpc, f.GB, f.P,
                             q, s);
 }
