@@ -4,9 +4,11 @@
 Headline workload ("decode sweep"): the four
 projection shapes of one 7B-class decoder layer (qkv 3584->4608, o 3584->3584,
 gate_up 3584->37888, down 18944->3584) at M = 1, 4 and 8 tokens; each linear
-runs through torch.ops.paro_b200.linear_w4a8, which at these sizes is one
-kernel (channel scale, 8 Givens layers and per-token int8 quantisation of the
-activations inside the persistent W4A8 GEMM).  One step = STEP_SWEEPS passes over the 12 (shape, M) cases.  Three
+runs through torch.ops.paro_b200.linear_w4a8: the activation kernel (channel
+scale, 8 Givens layers, per-token int8) and the persistent W4A8 GEMM,
+chained by programmatic dependent launch (for down_proj at M <= 2, one kernel
+that does both).  One step = STEP_SWEEPS passes over the 12 (shape, M)
+cases.  Three
 weight replicas (one per M) make the per-pass weight working set 363 MB
 (> 126 MB L2), so every GEMM streams its weights from HBM.  The metric value
 is weight-stream GB/s (algorithmic int4 code + fp16 scale + int4 zero bytes
@@ -348,8 +350,9 @@ def main():
     wset = sum(weight_bytes(N, K) for (_, N, K) in SHAPES) * len(DECODE_M)
 
     def linear(L, x, M):
-        # the whole rotated linear: at decode sizes one kernel (activation
-        # rotation + int8 quantisation inside the GEMM)
+        # the whole rotated linear through the public op: the activation
+        # kernel and the decode GEMM chained with programmatic dependent
+        # launch (one fused kernel for down_proj at M <= 2)
         return ops.linear_w4a8(x, L["rot_table"], L["cs_vec"], L["packed"], L["N"], None, True, torch.bfloat16)
 
     def sweep():
@@ -362,7 +365,8 @@ def main():
             sweep()
 
     bytes_per_step = STEP_SWEEPS * wset
-    launches_per_step = STEP_SWEEPS * len(DECODE_M) * len(SHAPES)
+    launches_per_step = STEP_SWEEPS * sum(1 if (K >= 8192 and M <= 2) else 2
+                                          for M in DECODE_M for (_, N, K) in SHAPES)
 
     # --- capture one step as a CUDA graph
     s = torch.cuda.Stream()
@@ -395,23 +399,31 @@ def main():
     ms = max_over_ranks(ms, world)
     value = world * bytes_per_step / (ms * 1e-3) / 1e9
 
-    # --- per-kernel launch durations: the fused linear kernel of each case,
-    # L2 flushed before every launch, CUDA events on the launching stream
+    # --- per-kernel launch durations for the roofline: the decode GEMM (the
+    # dominant kernel) and the activation kernel of each case, L2 flushed
+    # before every pair, CUDA events on the launching stream around each
+    # kernel; and the whole linear through the op, timed the same way
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
-    lin_t, lin_b, cases = 0.0, 0, {}
+    gemm_t, gemm_b, act_t, act_b, cases = 0.0, 0, 0.0, 0, {}
     for ri, M in enumerate(DECODE_M):
         for (name, N, K) in SHAPES:
             L = reps[ri][name]
+            ta_l, tg_l = kernel_pair_times(
+                torch, flush, lambda: ops.rotq_int8(xs[(M, K)], L["rot_table"], L["cs_vec"], 128, True),
+                lambda q: ops.w4a8_gemm(q[0], q[1], L["packed"], N, None, torch.bfloat16), PAIR_REPS)
             tl = kernel_times(torch, flush, lambda: linear(L, xs[(M, K)], M), PAIR_REPS)
-            lin_t += sum(tl)
-            lin_b += linear_alg_bytes(M, N, K) * len(tl)
-            tm = statistics.median(tl)
-            cases[f"{name}_m{M}"] = {"linear_us": round(1e6 * tm, 2),
-                                     "weight_GBps": round(weight_bytes(N, K) / tm / 1e9, 1)}
+            act_t += sum(ta_l)
+            act_b += act_alg_bytes(M, K) * len(ta_l)
+            gemm_t += sum(tg_l)
+            gemm_b += gemm_alg_bytes(M, N, K) * len(tg_l)
+            cases[f"{name}_m{M}"] = {"gemm_us": round(1e6 * statistics.median(tg_l), 2),
+                                     "act_us": round(1e6 * statistics.median(ta_l), 2),
+                                     "linear_us": round(1e6 * statistics.median(tl), 2),
+                                     "weight_GBps": round(weight_bytes(N, K) / statistics.median(tg_l) / 1e9, 1)}
     hbm, peak_kind = peaks()
-    lin_gbs = lin_b / lin_t / 1e9
+    gemm_gbs = gemm_b / gemm_t / 1e9
     case_out = cases
-    traffic = profile_traffic("linear_decode_gate_up_m8.md")
+    traffic = profile_traffic("gemm_decode_gate_up_m8.md")
 
     # --- prefill: tcgen05 GEMM and activation kernel per shape
     prefill = None
@@ -472,20 +484,23 @@ def main():
             "warmup": a.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int4xint8->int32 (bf16 act/out)", "data": "synthetic",
             "config": {"workload": "decode sweep, BASELINE configs[1]: qkv 3584->4608, o 3584->3584, "
-                                   "gate_up 3584->37888, down 18944->3584 at M=1,4,8; per linear one fused "
-                                   "kernel (channel scale + 8 Givens layers + per-token int8 + W4A8 GEMM)",
+                                   "gate_up 3584->37888, down 18944->3584 at M=1,4,8; per linear the op "
+                                   "linear_w4a8: activation kernel (channel scale + 8 Givens layers + per-token "
+                                   "int8) and W4A8 GEMM chained by programmatic dependent launch",
                        "step": f"{STEP_SWEEPS} sweeps of the 12 (shape, M) linears, CUDA graph",
                        "l2": f"weight working set {wset / 2**20:.0f} MiB per sweep > L2 {L2_BYTES / 2**20:.0f} MiB "
                              "(3 replicas, one per M); inputs not flushed",
                        "parallelism": f"dp{world} (independent replicas, no collective)"},
-            "roofline": {"kernel": "linear_decode (gemm_stream_kernel with in-kernel activation rotation + "
-                                   "int8 quantisation; persistent, cooperative)", "bound": "hbm",
-                         "achieved": round(lin_gbs, 1), "peak": hbm, "unit": "GB/s",
-                         "frac": round(lin_gbs / hbm, 4), "peak_kind": peak_kind,
+            "roofline": {"kernel": "gemm_stream_kernel (decode W4A8 GEMM: TMA weight stream, mma.sync "
+                                   "int4 x int8, stream-K)", "bound": "hbm",
+                         "achieved": round(gemm_gbs, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(gemm_gbs / hbm, 4), "peak_kind": peak_kind,
                          "traffic": traffic,
-                         "alg_bytes": "weights N*K/2 + G*N*2 + G*N/2, activations 2*M*K (bf16), rotation tables "
-                                      "2LK + LK + 2K (L = 8), output 2*M*N, per launch",
-                         "timing": "per launch, L2 flushed (512 MiB write) before each, CUDA events"},
+                         "alg_bytes": "N*K/2 + G*N*2 + G*N/2 + M*K + 4M + 2*M*N per launch",
+                         "timing": "per launch, L2 flushed (512 MiB write) before each pair, CUDA events"},
+            "activation_kernel": {"achieved_GBps": round(act_b / act_t / 1e9, 1),
+                                  "frac": round(act_b / act_t / 1e9 / hbm, 4),
+                                  "alg_bytes": "2MK + MK + 4M + tables 2LK + LK + 2K (L = 8) per launch"},
             "prefill": prefill,
             "cases": case_out,
             "gpu_launches": launches_per_step * a.steps,
