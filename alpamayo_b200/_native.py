@@ -24,7 +24,7 @@ _ops_loaded = False
 def _missing(path):
     raise ImportError(
         f"alpamayo_b200 native library not found: {path}\n"
-        "build it with:  python -m alpamayo_b200.csrc.build")
+        "build it with:  python alpamayo_b200/csrc/build.py")
 
 
 def load_ops() -> None:
@@ -70,6 +70,8 @@ def capi() -> ctypes.CDLL:
         "paro_w4a8_linear_scratch_size": (sz, [i64, i32, i32, i32]),
         "paro_w4a8_linear": (i32, [vp, i32, i64, i32, i32, vp, vp, i32, vp, vp, i32, vp, i32, vp, sz, vp, sz, vp]),
         "paro_device_error_word": (i32, [i32]),
+        "paro_add_rmsnorm": (i32, [vp, vp, vp, i64, i32, ctypes.c_float, vp, vp]),
+        "paro_silu_mul": (i32, [vp, i64, i32, vp, vp]),
     }
     for name, (res, args) in sigs.items():
         f = getattr(L, name)

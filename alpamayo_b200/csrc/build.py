@@ -4,7 +4,8 @@
                                        (nvcc, -gencode arch=compute_100a,code=sm_100a)
   alpamayo_b200/lib/libparo_torch.so — the TORCH_LIBRARY(paro_b200) shim
 
-Usage: python -m alpamayo_b200.csrc.build [--force]
+Usage: python alpamayo_b200/csrc/build.py [--force]   (run by path: importing the
+package would load the libraries before they are rebuilt)
 Objects go to alpamayo_b200/_build/.  Only sources newer than their outputs
 are recompiled.  Works without a GPU (nvcc cross-compiles).
 """
@@ -24,7 +25,7 @@ OBJ = os.path.join(PKG, "_build")
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 
-CU_SOURCES = ["capi.cu", "rotq.cu", "rotq_fused.cu", "rotq_rows.cu", "prepare.cu", "gemm_decode.cu", "gemm_tc.cu"]
+CU_SOURCES = ["capi.cu", "rotq.cu", "rotq_fused.cu", "rotq_rows.cu", "prepare.cu", "gemm_decode.cu", "gemm_tc.cu", "elementwise.cu"]
 HEADERS = ["paro_common.cuh", "tc_ptx.cuh"]
 GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",

@@ -32,6 +32,9 @@ cudaError_t launch_gemm_decode(const int8_t* xq, const float* xscale, int64_t M,
                                const void* bias, int bias_dtype, void* out, int out_dtype, void* ws,
                                cudaStream_t st);
 size_t gemm_decode_workspace(int64_t M, int N);
+cudaError_t launch_add_rmsnorm(const void* x, void* residual, const void* weight, int64_t M, int K, float eps,
+                               void* out, cudaStream_t st);
+cudaError_t launch_silu_mul(const void* x, int64_t M, int I, void* out, cudaStream_t st);
 size_t linear_decode_workspace(int64_t M, int N);
 cudaError_t launch_linear_decode(const void* x, int x_dtype, const uint16_t* cscale, const uint32_t* rtab, int64_t M,
                                  int N, int K, const void* packed, const void* bias, int bias_dtype, void* out,
@@ -286,6 +289,26 @@ int paro_w4a8_linear(const void* x, int x_dtype, int64_t M, int K, int N, const 
 }  // extern "C"
 
 extern "C" {
+
+int paro_add_rmsnorm(const void* x, void* residual, const void* weight, int64_t M, int K, float eps, void* out,
+                     paro_stream_t stream) {
+  if (M == 0 && K > 0) return PARO_OK;
+  if (!x || !weight || !out || M < 0 || K <= 0) return PARO_ERR_INVALID_ARGUMENT;
+  if (K % 8) return PARO_ERR_SHAPE;
+  if (!aligned(x, 16) || !aligned(weight, 16) || !aligned(out, 16) || (residual && !aligned(residual, 16)))
+    return PARO_ERR_MISALIGNED;
+  if (int d = device_check()) return d;
+  return cuda_status(launch_add_rmsnorm(x, residual, weight, M, K, eps, out, (cudaStream_t)stream));
+}
+
+int paro_silu_mul(const void* x, int64_t M, int I, void* out, paro_stream_t stream) {
+  if (M == 0 && I > 0) return PARO_OK;
+  if (!x || !out || M < 0 || I <= 0) return PARO_ERR_INVALID_ARGUMENT;
+  if (I % 8) return PARO_ERR_SHAPE;
+  if (!aligned(x, 16) || !aligned(out, 16)) return PARO_ERR_MISALIGNED;
+  if (int d = device_check()) return d;
+  return cuda_status(launch_silu_mul(x, M, I, out, (cudaStream_t)stream));
+}
 
 int paro_device_error_word(int clear) {
   const uint32_t a = error_word_decode(clear), b = error_word_tc(clear);

@@ -293,6 +293,48 @@ at::Tensor linear_w4a8(const at::Tensor& x_in, const at::Tensor& rot_table,
   return out;
 }
 
+// residual add + RMSNorm: returns (normalised, new residual); residual may be
+// None (then the new residual is x itself)
+std::tuple<at::Tensor, at::Tensor> add_rmsnorm(const at::Tensor& x_in, const c10::optional<at::Tensor>& residual_opt,
+                                               const at::Tensor& weight, double eps) {
+  at::Tensor x = x_in.contiguous();
+  check_cuda(x, "x");
+  check_cuda(weight, "weight");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && weight.scalar_type() == at::kBFloat16,
+              "add_rmsnorm: bf16 tensors expected");
+  const int64_t K = x.size(-1);
+  TORCH_CHECK(weight.numel() == K, "weight must have K elements");
+  const int64_t M = x.numel() / K;
+  c10::cuda::CUDAGuard guard(x.device());
+  at::Tensor res;
+  void* rp = nullptr;
+  if (residual_opt.has_value() && residual_opt->defined()) {
+    res = residual_opt->contiguous().clone();
+    TORCH_CHECK(res.sizes() == x.sizes() && res.scalar_type() == at::kBFloat16, "residual must match x");
+    rp = res.data_ptr();
+  }
+  at::Tensor out = at::empty_like(x);
+  check_status(paro_add_rmsnorm(x.data_ptr(), rp, weight.data_ptr(), M, (int)K, (float)eps, out.data_ptr(),
+                                cur_stream()),
+               "add_rmsnorm");
+  return {out, rp ? res : x};
+}
+
+at::Tensor silu_mul(const at::Tensor& x_in) {
+  at::Tensor x = x_in.contiguous();
+  check_cuda(x, "x");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16, "silu_mul: bf16 expected");
+  const int64_t I2 = x.size(-1);
+  TORCH_CHECK(I2 % 16 == 0, "silu_mul: last dimension must be 2*I with I % 8 == 0");
+  const int64_t M = x.numel() / I2;
+  c10::cuda::CUDAGuard guard(x.device());
+  auto osz = x.sizes().vec();
+  osz.back() = I2 / 2;
+  at::Tensor out = at::empty(osz, x.options());
+  check_status(paro_silu_mul(x.data_ptr(), M, (int)(I2 / 2), out.data_ptr(), cur_stream()), "silu_mul");
+  return out;
+}
+
 }  // namespace
 
 TORCH_LIBRARY(paro_b200, m) {
@@ -305,6 +347,8 @@ TORCH_LIBRARY(paro_b200, m) {
   m.def("w4a8_gemm(Tensor xq, Tensor xscale, Tensor packed, int N, Tensor? bias, ScalarType out_dtype) -> Tensor");
   m.def("linear_w4a8(Tensor x, Tensor rot_table, Tensor? channel_scales, Tensor packed, int N, Tensor? bias, "
         "bool fp16_round, ScalarType out_dtype) -> Tensor");
+  m.def("add_rmsnorm(Tensor x, Tensor? residual, Tensor weight, float eps) -> (Tensor, Tensor)");
+  m.def("silu_mul(Tensor x) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(paro_b200, CUDA, m) {
@@ -316,4 +360,6 @@ TORCH_LIBRARY_IMPL(paro_b200, CUDA, m) {
   m.impl("prepare_weights_awq", &prepare_weights_awq);
   m.impl("w4a8_gemm", &w4a8_gemm);
   m.impl("linear_w4a8", &linear_w4a8);
+  m.impl("add_rmsnorm", &add_rmsnorm);
+  m.impl("silu_mul", &silu_mul);
 }

@@ -107,3 +107,24 @@ def linear_w4a8(x, rot_table, channel_scales, packed, N, bias=None, fp16_round=T
     """One W4A8 rotated linear: fused activation kernel + GEMM."""
     return _ops.linear_w4a8(x, rot_table, channel_scales, packed, N, bias, fp16_round,
                             out_dtype if out_dtype is not None else x.dtype)
+
+
+@torch.library.register_fake("paro_b200::add_rmsnorm")
+def _add_rmsnorm_fake(x, residual, weight, eps):
+    return torch.empty_like(x), torch.empty_like(x)
+
+
+@torch.library.register_fake("paro_b200::silu_mul")
+def _silu_mul_fake(x):
+    return x.new_empty((*x.shape[:-1], x.shape[-1] // 2))
+
+
+def add_rmsnorm(x, residual, weight, eps=1e-6):
+    """Residual add + Qwen3VLTextRMSNorm (bf16): returns (normalised, new
+    residual stream)."""
+    return _ops.add_rmsnorm(x, residual, weight, eps)
+
+
+def silu_mul(x):
+    """SiLU(gate) * up of a fused gate_up output [..., 2I] -> [..., I] (bf16)."""
+    return _ops.silu_mul(x)

@@ -59,6 +59,8 @@ def args_():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-prefill", action="store_true")
+    p.add_argument("--no-stack", action="store_true")
+    p.add_argument("--no-sharded", action="store_true")
     return p.parse_args()
 
 
@@ -177,6 +179,92 @@ def prefill_section(torch, ops, syn, layers, flush, rank):
             "frac": round(agg / peak, 4), "act_share": round(act_sum / (act_sum + t_sum), 4), "cases": out}
 
 
+STACK_CLIPS = 64
+STACK_LAYERS = 28
+SHARD_M, SHARD_N, SHARD_K = 16384, 37888, 3584
+
+
+def stack_section(torch, world, rank):
+    """28 rotated W4A8 decoder layers at decode, 64 independent
+    clips x 1 token split across the ranks (no collective); tokens/s of the
+    whole job and weight-stream GB/s per GPU, CUDA-graph timed, max over
+    ranks."""
+    from alpamayo_b200 import synthetic as syn
+    from alpamayo_b200.stack import DecoderStack
+    if STACK_CLIPS % world:
+        return {"skipped": f"{STACK_CLIPS} clips do not split over {world} ranks"}
+    M = STACK_CLIPS // world
+    st = DecoderStack(layers=STACK_LAYERS, seed=0)
+    x = syn.make_activations(M, 3584, seed=500 + rank)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        st.forward(x)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        y = st.forward(x)
+    for _ in range(3):
+        g.replay()
+    reps = 10
+    barrier_sync(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    barrier_sync(world)
+    t = max_over_ranks(e0.elapsed_time(e1) * 1e-3 / reps, world)
+    finite = bool(torch.isfinite(y).all().item())
+    wb = st.weight_bytes()
+    del g, st
+    torch.cuda.empty_cache()
+    return {"workload": "configs[3]: 28-layer decode stack (RMSNorm -> qkv, identity attention -> o, RMSNorm -> "
+                        "gate_up -> SiLU*up -> down), 64 clips x 1 token split over the ranks, no collective",
+            "tokens_per_rank": M, "ms_per_forward": round(t * 1e3, 3),
+            "tokens_per_s": round(STACK_CLIPS / t, 1),
+            "weight_GBps_per_gpu": round(wb / t / 1e9, 1), "weight_bytes_per_forward": wb,
+            "outputs_finite": finite}
+
+
+def sharded_section(torch, world, rank):
+    """gate_up (K=3584, N=37888) at M=16384, output columns split
+    over the ranks, NCCL all-gather of the bf16 blocks; end-to-end time, the
+    exposed all-gather time and int8 TOPS of the whole job, max over ranks."""
+    from alpamayo_b200 import synthetic as syn
+    from alpamayo_b200.stack import ColumnShardedLinear, column_shard, linear, serving_layer
+    c0, c1 = column_shard(SHARD_N, rank, world)
+    L = serving_layer(c1 - c0, SHARD_K, seed=700 + rank)
+    x = syn.make_activations(SHARD_M, SHARD_K, seed=701)
+    csl = ColumnShardedLinear(lambda v: linear(L, v))
+    for _ in range(2):
+        csl(x)
+    reps = 5
+    tl, tt = [], []
+    for _ in range(reps):
+        barrier_sync(world)
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record()
+        y = csl.local_fn(x)
+        e1.record()
+        blocks = csl.gather(y)
+        e2.record()
+        torch.cuda.synchronize()
+        tl.append(e0.elapsed_time(e1) * 1e-3)
+        tt.append(e0.elapsed_time(e2) * 1e-3)
+    t_lin = max_over_ranks(min(tl), world)
+    t_tot = max_over_ranks(min(tt), world)
+    ops_total = 2.0 * SHARD_M * SHARD_N * SHARD_K
+    shape = list(blocks.shape)
+    del L, x, y, blocks
+    torch.cuda.empty_cache()
+    return {"workload": "configs[4]: gate_up K=3584 N=37888 at M=16384, N split over the ranks, NCCL all-gather "
+                        "of the bf16 output blocks", "world": world, "block_columns": c1 - c0,
+            "gathered_shape": shape, "ms_end_to_end": round(t_tot * 1e3, 3),
+            "ms_linear": round(t_lin * 1e3, 3), "ms_exposed_all_gather": round((t_tot - t_lin) * 1e3, 3),
+            "int8_tops_end_to_end": round(ops_total / t_tot / 1e12, 1)}
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -251,7 +339,7 @@ def dist_setup(n):
     if world > 1:
         from datetime import timedelta
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     elif torch.cuda.is_available():
         torch.cuda.set_device(0)
@@ -426,6 +514,8 @@ def main():
     traffic = profile_traffic("gemm_decode_gate_up_m8.md")
 
     # --- prefill: tcgen05 GEMM and activation kernel per shape
+    stack = None if a.no_stack else stack_section(torch, world, rank)
+    sharded = None if a.no_sharded else sharded_section(torch, world, rank)
     prefill = None
     if not a.no_prefill:
         prefill = prefill_section(torch, ops, syn, reps[0], flush, rank)
@@ -502,6 +592,8 @@ def main():
                                   "frac": round(act_b / act_t / 1e9 / hbm, 4),
                                   "alg_bytes": "2MK + MK + 4M + tables 2LK + LK + 2K (L = 8) per launch"},
             "prefill": prefill,
+            "stack": stack,
+            "sharded_prefill": sharded,
             "cases": case_out,
             "gpu_launches": launches_per_step * a.steps,
             "clocks": clk,

@@ -214,6 +214,24 @@ int paro_w4a8_gemm(const int8_t* xq, const float* xscale, int64_t M, int N, int 
                    void* out, int out_dtype, void* workspace, size_t workspace_bytes,
                    paro_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Decoder-layer glue (bf16), used by the decoder-stack benchmark
+ * ------------------------------------------------------------------------ */
+
+/*
+ * Residual add + Qwen3VLTextRMSNorm (src/alpamayo_r1/models/qwen3_vl/
+ * modeling_qwen3_vl.py:340-357): if residual is not NULL it becomes
+ * bf16(x + residual) and is normalised; otherwise x is.  out = bf16(weight *
+ * bf16(s * rsqrt(mean(s^2) + eps))), float32 math.  All bf16 [M, K] / [K],
+ * K % 8 == 0, 16-byte aligned.
+ */
+int paro_add_rmsnorm(const void* x, void* residual, const void* weight, int64_t M, int K,
+                     float eps, void* out, paro_stream_t stream);
+
+/* SiLU(gate) * up on a fused gate_up output: x bf16 [M, 2I] (gate columns
+ * first), out bf16 [M, I] = bf16(bf16(silu(gate)) * up).  I % 8 == 0. */
+int paro_silu_mul(const void* x, int64_t M, int I, void* out, paro_stream_t stream);
+
 /* Error bits kernels raise instead of hanging (1 = a pipeline wait timed
  * out, 2 = tensor-memory allocation failed); synchronises with the device to
  * read them.  clear != 0 resets the word.  Returns -1 if it cannot be read. */

@@ -360,6 +360,24 @@ def rmsnorm(x, weight, eps=1e-6):
     return round_to_bf16(f32(weight) * h)
 
 
+def silu_mul(x, eps_unused=None):
+    """act_fn(gate_proj(x)) * up_proj(x) of the decoder MLP on a fused
+    gate_up output [..., 2I] (gate first): SiLU in float32 rounded to bf16,
+    times up, rounded to bf16 (bf16 torch semantics)."""
+    x32 = f32(x)
+    I = x32.shape[-1] // 2
+    g, u = x32[..., :I], x32[..., I:]
+    s = round_to_bf16(g / (np.float32(1.0) + np.exp(-g, dtype=np.float32)))
+    return round_to_bf16(s * u)
+
+
+def add_rmsnorm(x, residual, weight, eps=1e-6):
+    """Residual add in bf16 (s = bf16(x + residual)) followed by rmsnorm;
+    returns (normalised, s)."""
+    s = round_to_bf16(f32(x) + f32(residual)) if residual is not None else round_to_bf16(x)
+    return rmsnorm(s, weight, eps), s
+
+
 def rot_quant_reference(x, pairs, theta, channel_scales, group_size=GROUP,
                         fp16_intermediate=True):
     """The reference activation chain of one W4A8 linear: x (already fp16

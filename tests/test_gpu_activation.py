@@ -217,3 +217,27 @@ def test_rotq_two_pass_path_matches_fused_kernel_and_oracle(ops, M, K, xdt):
     q_ref, s_ref, _ = O.rot_quant_reference(xt.float().cpu().numpy()[rows], pairs, theta.astype(np.float32),
                                             cs.astype(np.float32))
     check_codes(q.cpu().numpy()[rows], q_ref, s.cpu().numpy().reshape(-1)[rows], s_ref)
+
+
+@pytest.mark.parametrize("M,K,with_res", [(1, 3584, True), (64, 3584, False), (7, 18944, True)])
+def test_add_rmsnorm_against_oracle(ops, M, K, with_res):
+    rng = np.random.default_rng(M + K)
+    x = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).to(torch.bfloat16)
+    r = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).to(torch.bfloat16) if with_res else None
+    w = torch.from_numpy((0.9 + 0.2 * rng.random(K)).astype(np.float32)).to(torch.bfloat16)
+    y, s = ops.add_rmsnorm(x.cuda(), None if r is None else r.cuda(), w.cuda(), 1e-6)
+    y_ref, s_ref = O.add_rmsnorm(x.float().numpy(), None if r is None else r.float().numpy(), w.float().numpy())
+    assert np.array_equal(s.float().cpu().numpy(), s_ref)
+    d = np.abs(y.float().cpu().numpy() - y_ref)
+    # summation order and rsqrt may move a value across a bf16 rounding boundary
+    assert (d > 0).mean() <= 1e-2 and d.max() <= 2 ** -6 * np.abs(y_ref).max()
+
+
+@pytest.mark.parametrize("M,I", [(1, 18944), (37, 1024)])
+def test_silu_mul_against_oracle(ops, M, I):
+    rng = np.random.default_rng(M)
+    x = torch.from_numpy((3 * rng.standard_normal((M, 2 * I))).astype(np.float32)).to(torch.bfloat16)
+    y = ops.silu_mul(x.cuda()).float().cpu().numpy()
+    ref = O.silu_mul(x.float().numpy())
+    d = np.abs(y - ref)
+    assert (d > 0).mean() <= 1e-3 and d.max() <= 2 ** -7 * np.abs(ref).max()
