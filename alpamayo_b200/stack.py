@@ -109,8 +109,34 @@ class ColumnShardedLinear:
     def __call__(self, x):
         return self.gather(self.local_fn(x))
 
+    def overlapped(self, x, chunks=4):
+        """The same result computed in `chunks` row blocks: the all-gather
+        of block i (asynchronous, on the collective's own stream) runs while
+        block i + 1 is computed.  Returns [chunks, world, M / chunks, N /
+        world] (see assemble_chunks)."""
+        import torch.distributed as dist
+        M = x.shape[0]
+        if self.world == 1 or chunks <= 1 or M % chunks:
+            return self(x).unsqueeze(0)
+        mc = M // chunks
+        outs, works = [], []
+        for c in range(chunks):
+            y = self.local_fn(x[c * mc:(c + 1) * mc].contiguous()).contiguous()
+            out = y.new_empty((self.world * mc, *y.shape[1:]))
+            works.append(dist.all_gather_into_tensor(out, y, group=self.group, async_op=True))
+            outs.append(out.view(self.world, mc, *y.shape[1:]))
+        for w in works:
+            w.wait()
+        return torch.stack(outs)
+
     @staticmethod
     def assemble(blocks):
         """[world, M, N / world] -> [M, N] (columns in rank order)."""
         w, M, n = blocks.shape
         return blocks.permute(1, 0, 2).reshape(M, w * n)
+
+    @staticmethod
+    def assemble_chunks(blocks):
+        """[chunks, world, M / chunks, N / world] -> [M, N]."""
+        c, w, mc, n = blocks.shape
+        return blocks.permute(0, 2, 1, 3).reshape(c * mc, w * n)

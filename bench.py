@@ -254,6 +254,22 @@ def sharded_section(torch, world, rank):
         tt.append(e0.elapsed_time(e2) * 1e-3)
     t_lin = max_over_ranks(min(tl), world)
     t_tot = max_over_ranks(min(tt), world)
+    # the same with the all-gather overlapped: 4 row blocks, block i gathered
+    # while block i + 1 is computed
+    CH = 4
+    for _ in range(2):
+        csl.overlapped(x, CH)
+    to = []
+    for _ in range(reps):
+        barrier_sync(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        ob = csl.overlapped(x, CH)
+        e1.record()
+        torch.cuda.synchronize()
+        to.append(e0.elapsed_time(e1) * 1e-3)
+    del ob
+    t_ov = max_over_ranks(min(to), world)
     ops_total = 2.0 * SHARD_M * SHARD_N * SHARD_K
     shape = list(blocks.shape)
     del L, x, y, blocks
@@ -262,7 +278,10 @@ def sharded_section(torch, world, rank):
                         "of the bf16 output blocks", "world": world, "block_columns": c1 - c0,
             "gathered_shape": shape, "ms_end_to_end": round(t_tot * 1e3, 3),
             "ms_linear": round(t_lin * 1e3, 3), "ms_exposed_all_gather": round((t_tot - t_lin) * 1e3, 3),
-            "int8_tops_end_to_end": round(ops_total / t_tot / 1e12, 1)}
+            "int8_tops_end_to_end": round(ops_total / t_tot / 1e12, 1),
+            "overlapped": {"row_blocks": CH, "ms_end_to_end": round(t_ov * 1e3, 3),
+                           "ms_exposed_all_gather": round((t_ov - t_lin) * 1e3, 3),
+                           "int8_tops_end_to_end": round(ops_total / t_ov / 1e12, 1)}}
 
 
 def peaks():
