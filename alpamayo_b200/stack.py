@@ -10,8 +10,10 @@
   stack and runs its share of the tokens.
 * ColumnShardedLinear — the sharded-prefill workload:
   one rotated linear whose output columns are split across the ranks of a
-  process group; each rank computes its [M, N / world] block and an
-  all-gather assembles [world, M, N / world] (rank-major blocks).
+  process group; each rank computes its [M, N / world] block and a gather
+  assembles [world, M, N / world] (rank-major blocks) on every rank: an
+  NCCL all-gather, or copy-engine copies into buffers every peer has mapped
+  (peer_gathered), which overlap the GEMM because they use no SM.
 """
 from __future__ import annotations
 
@@ -32,6 +34,34 @@ def serving_layer(N, K, seed, device="cuda"):
 
 def linear(L, x, out_dtype=torch.bfloat16):
     return ops.linear_w4a8(x, L["rot_table"], L["cs_vec"], L["packed"], L["N"], None, True, out_dtype)
+
+
+_ws_cache = {}
+
+
+def linear_into(L, x, out):
+    """linear() writing into a given bf16 [M, N] tensor (through the C ABI's
+    paro_w4a8_linear, whose output is any device pointer)."""
+    import ctypes
+    from ._native import capi
+    Lc = capi()
+    M, K = x.shape
+    N = L["N"]
+    wsb = Lc.paro_w4a8_linear_workspace_size(M, N, K)
+    scb = Lc.paro_w4a8_linear_scratch_size(M, N, K, 1)
+    key = (x.device, torch.cuda.current_stream().cuda_stream)
+    ws = _ws_cache.get(key)
+    if ws is None or ws.numel() < wsb + 256:
+        ws = torch.zeros(max(wsb, 16 << 20) + 256, dtype=torch.uint8, device=x.device)
+        _ws_cache[key] = ws
+    sc = torch.empty(scb + 256, dtype=torch.uint8, device=x.device)
+    al = lambda t: (t.data_ptr() + 255) & ~255
+    st = Lc.paro_w4a8_linear(x.data_ptr(), 2, M, K, N, L["cs_vec"].data_ptr(), L["rot_table"].data_ptr(), 1,
+                             L["packed"].data_ptr(), None, 0, out.data_ptr(), 2, al(ws), wsb, al(sc), scb,
+                             ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    if st:
+        raise RuntimeError(f"paro_w4a8_linear: {Lc.paro_status_string(st).decode()}")
+    return out
 
 
 class DecoderStack:
@@ -91,11 +121,12 @@ class ColumnShardedLinear:
     on the GPU; any callable in tests).  `gather(y_local)` all-gathers the
     blocks over the process group into a [world, M, N / world] tensor."""
 
-    def __init__(self, local_fn, group=None):
+    def __init__(self, local_fn, group=None, block_columns=None):
         import torch.distributed as dist
         self.local_fn = local_fn
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self._n = block_columns
 
     def gather(self, y_local):
         import torch.distributed as dist
@@ -129,6 +160,68 @@ class ColumnShardedLinear:
             w.wait()
         return torch.stack(outs)
 
+    def peer_gathered(self, x, into_fn, chunks=4):
+        """The gather done by the copy engines over NVLink instead of a
+        collective kernel, so that it overlaps the GEMM (which holds every
+        SM).  The result lives in one of two [world, M, N / world] buffers
+        that every peer has mapped (CUDA IPC, plain peer mappings).  For each
+        of `chunks` row blocks, `into_fn(x_rows, dst)` writes this rank's
+        block straight into its own slot; a side stream then copies the slot
+        into every peer's buffer with cudaMemcpyAsync (DMA; no kernel reads
+        or writes peer memory) while the next block is computed (one stream
+        for all peers measured faster at 4 ranks than one per peer).  A
+        one-word
+        all-reduce after the copies tells every rank that all blocks have
+        landed.  The two buffers alternate, so the result of a call stays
+        valid until the call after next; the closing all-reduce of the next
+        call also orders a peer's writes after this rank's use of the
+        buffer.  Returns [world, M, N / world]; close_peer_buffers() frees
+        the buffers (collective)."""
+        import torch.distributed as dist
+        from cuda.bindings import runtime as cudart
+        M = x.shape[0]
+        if self.world == 1:
+            out = torch.empty((1, M, self._n), dtype=torch.bfloat16, device=x.device)
+            into_fn(x, out[0])
+            return out
+        key = (M, self._n, x.device)
+        if getattr(self, "_peer", None) is None or self._peer.key != key:
+            self.close_peer_buffers()
+            self._peer = _PeerBuffers(self.world, (self.world, M, self._n), x.device, self.group, key)
+            self._comm = torch.cuda.Stream(device=x.device)
+            self._flag = torch.zeros(1, dtype=torch.int32, device=x.device)
+        pb = self._peer
+        b = pb.flip()
+        out = pb.tensor(b)
+        rank = pb.rank
+        mc = M // chunks if chunks > 1 and M % chunks == 0 else M
+        blk = mc * self._n * 2
+        cur = torch.cuda.current_stream()
+        for r0 in range(0, M, mc):
+            mine = out[rank, r0:r0 + mc]
+            into_fn(x[r0:r0 + mc], mine)
+            ev = torch.cuda.Event()
+            ev.record(cur)
+            self._comm.wait_event(ev)
+            off = (rank * M + r0) * self._n * 2
+            for j in range(self.world):
+                if j != rank:
+                    err, = cudart.cudaMemcpyAsync(pb.ptrs[b][j] + off, pb.ptrs[b][rank] + off, blk,
+                                                  cudart.cudaMemcpyKind.cudaMemcpyDeviceToDevice,
+                                                  self._comm.cuda_stream)
+                    if err != cudart.cudaError_t.cudaSuccess:
+                        raise RuntimeError(f"peer copy failed: {err}")
+        cur.wait_stream(self._comm)
+        dist.all_reduce(self._flag, group=self.group)
+        return out
+
+    def close_peer_buffers(self):
+        """Unmap and free the peer_gathered buffers (every rank calls it)."""
+        pb = getattr(self, "_peer", None)
+        if pb is not None:
+            pb.close()
+            self._peer = None
+
     @staticmethod
     def assemble(blocks):
         """[world, M, N / world] -> [M, N] (columns in rank order)."""
@@ -140,3 +233,83 @@ class ColumnShardedLinear:
         """[chunks, world, M / chunks, N / world] -> [M, N]."""
         c, w, mc, n = blocks.shape
         return blocks.permute(0, 2, 1, 3).reshape(c * mc, w * n)
+
+
+class _PeerBuffers:
+    """Two bf16 buffers of `shape` on every rank, each from its own
+    cudaMalloc, exported with cudaIpcGetMemHandle and opened by every peer
+    (cudaIpcOpenMemHandle with lazy peer access): ptrs[b][j] is rank j's
+    buffer b as this rank addresses it.  Setup and close are collective; a
+    failure on any rank raises on every rank."""
+
+    def __init__(self, world, shape, device, group, key):
+        import torch.distributed as dist
+        from cuda.bindings import runtime as cudart
+        self.world, self.shape, self.device, self.group, self.key = world, shape, device, group, key
+        self.rank = dist.get_rank(group)
+        self.nbytes = 2
+        for d in shape:
+            self.nbytes *= d
+        self.own, self.opened, self.ptrs, self._b = [], [], [], 1
+        ok = True
+        cudart.cudaSetDevice(device.index)
+        for _ in range(2):
+            h = b""
+            if ok:
+                err, p = cudart.cudaMalloc(self.nbytes)
+                ok = err == cudart.cudaError_t.cudaSuccess
+                if ok:
+                    self.own.append(p)
+                    err, hd = cudart.cudaIpcGetMemHandle(p)
+                    ok = err == cudart.cudaError_t.cudaSuccess
+                    h = bytes(hd.reserved) if ok else b""
+            handles = [None] * world
+            dist.all_gather_object(handles, h, group=group)
+            row = []
+            for j in range(world):
+                if j == self.rank:
+                    row.append(self.own[-1] if ok else 0)
+                elif ok and handles[j]:
+                    hh = cudart.cudaIpcMemHandle_t()
+                    hh.reserved = handles[j]
+                    err, q = cudart.cudaIpcOpenMemHandle(hh, cudart.cudaIpcMemLazyEnablePeerAccess)
+                    ok = err == cudart.cudaError_t.cudaSuccess
+                    if ok:
+                        self.opened.append(q)
+                    row.append(q if ok else 0)
+                else:
+                    ok = False
+                    row.append(0)
+            self.ptrs.append(row)
+        flag = torch.tensor([0 if ok else 1], dtype=torch.int32, device=device)
+        dist.all_reduce(flag, group=group)
+        if flag.item():
+            self.close()
+            raise RuntimeError("peer buffer setup failed on at least one rank")
+        self._views = [self._wrap(self.own[b]) for b in range(2)]
+
+    def _wrap(self, ptr):
+        class _Mem:
+            __cuda_array_interface__ = {"shape": tuple(self.shape), "typestr": "<i2", "data": (ptr, False),
+                                        "version": 3, "strides": None}
+        return torch.as_tensor(_Mem(), device=self.device).view(torch.bfloat16)
+
+    def flip(self):
+        self._b ^= 1
+        return self._b
+
+    def tensor(self, b):
+        return self._views[b]
+
+    def close(self):
+        import torch.distributed as dist
+        from cuda.bindings import runtime as cudart
+        torch.cuda.synchronize(self.device)
+        for q in self.opened:
+            cudart.cudaIpcCloseMemHandle(q)
+        self.opened = []
+        dist.barrier(group=self.group)
+        for p in self.own:
+            cudart.cudaFree(p)
+        self.own = []
+        self._views = []
