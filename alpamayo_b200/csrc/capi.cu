@@ -264,11 +264,10 @@ int paro_w4a8_linear(const void* x, int x_dtype, int64_t M, int K, int N, const 
   if (!aligned(workspace, 256) || !aligned(scratch, 256)) return PARO_ERR_MISALIGNED;
   if (int d = device_check()) return d;
   cudaStream_t st = (cudaStream_t)stream;
-  // The single-kernel route pays for its grid barrier with the overlap of
-  // the activation work and the weight prefetch; measured on B200 that wins
-  // only for long rows and one or two tokens, elsewhere the two chained
-  // kernels (programmatic dependent launch) are faster.
-  if (M <= 2 && K >= 8192 && fp16_round) {
+  // decode sizes: rotation kernel + GEMM that quantises in its prologue
+  // (measured on B200 faster than the activation kernel + GEMM pair, whose
+  // single-pass activation kernel spreads a row over one 8-CTA cluster)
+  if (M <= kLinearFusedMaxM && fp16_round) {
     const cudaError_t e = launch_linear_decode(x, x_dtype, channel_scales, rot_table, M, N, K, packed, bias,
                                                bias_dtype, out, out_dtype, workspace, scratch, st);
     if (e != cudaErrorNotSupported) return cuda_status(e);

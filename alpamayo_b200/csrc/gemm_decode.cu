@@ -2,34 +2,41 @@
 //
 // Memory-bound regime: the weight stream (N*K/2 bytes of codes plus group
 // scales and zero points) dominates, so the kernel is built to keep every SM
-// pulling weights at its share of HBM bandwidth:
+// pulling weights at its share of HBM bandwidth and to spend as few issue
+// slots per weight byte as possible:
 //
 //  * Persistent, load-balanced grid ("stream-K"): the layer's tile records —
 //    one per (16-row block nb, 128-channel group g), stored nb-major so each
 //    row block's K strip is contiguous — are split into one contiguous range
 //    per CTA.  A CTA's range covers parts of a few row blocks (segments).
+//    The two end segments, which a CTA shares with its neighbours, are
+//    visited first, so their fix-up through the workspace overlaps the rest
+//    of the stream; the whole row blocks in between come last.
 //  * TMA bulk copies: one producer thread streams the range through a shared
 //    memory ring (cp.async.bulk + mbarrier complete_tx).  A chunk holds the
 //    records of up to 16 consecutive groups of one row block, aligned to
 //    16-group boundaries.
-//  * 8 consumer warps; warp w owns the groups g = w (mod 8), so each chunk
-//    gives every warp up to two independent records, and the activation
-//    fragments a warp needs are the same for every row block.  The token
-//    activations are staged once per CTA in shared memory in mma fragment
-//    order (falls back to L1-cached global loads when they do not fit).
-//  * Each record's int4 codes are expanded to int8 (q - z) in registers and
-//    fed to int8 mma.sync m16n8k32 (A = 16 weight rows x 32 channels, B = 8
+//  * Consumer warps (16 for up to 16 tokens, 8 beyond); warp w owns the
+//    groups g = w (mod warps), so a chunk gives each warp one or two
+//    independent records.  The token slice's int8 rows are staged once per
+//    CTA in shared memory and rearranged there into mma fragment order (a
+//    lane's eight B words of a group are 32 contiguous bytes: two 16-byte
+//    loads per record); rows that do not fit are read from global memory.
+//  * Each record's int4 codes are expanded to int8 in registers and fed to
+//    int8 mma.sync m16n8k32 (A = 16 weight rows x 32 channels, B = 8
 //    tokens); each group's int32 sum is exact and is scaled into float32.
-//  * Segment end: partial sums of the 8 warps are reduced in shared memory.
-//    A segment covering a whole row block is finished in place (token scale,
-//    bias, store).  A boundary segment shared with a neighbouring CTA adds
-//    its partial into a float32 workspace (red.global.add) and bumps the row
-//    block's unit counter; the CTA that completes the count applies the
-//    epilogue and returns the workspace slice and counter to zero, so the
-//    workspace is zero again after every call.
+//  * Segment end: partial sums of the warps are reduced in shared memory by
+//    an epilogue warp.  A segment covering a whole row block is finished in
+//    place (token scale, bias, store).  A boundary segment shared with a
+//    neighbouring CTA adds its partial into a float32 workspace
+//    (red.global.add) and bumps the row block's unit counter; the CTA that
+//    completes the count applies the epilogue and returns the workspace
+//    slice and counter to zero, so the workspace is zero again after every
+//    call.
 //  * Programmatic dependent launch: the weight stream starts before the
 //    activation kernel that produces this GEMM's input has finished; only
-//    the reads of the activations wait (griddepcontrol.wait).
+//    the reads of the activations wait (griddepcontrol.wait), and the
+//    epilogue warp fetches them as soon as they are ready.
 //
 // Record layout: for lane (gid = lane/4, tig = lane%4), the A fragment words
 // of rows gid and gid+8 for the four 32-channel steps of a group are one
@@ -38,13 +45,19 @@
 
 namespace paro {
 
-constexpr int kDecConsumers = 8;
-constexpr int kDecThreads = 32 * (kDecConsumers + 2);  // producer + consumers + epilogue
+// consumer warps: 16 for up to 16 tokens (more warps hide the latency of
+// each record's load -> mma -> scale chain), 8 for more tokens (more work
+// per record, and the reduction slices would not fit)
+__host__ __device__ constexpr int dec_consumers(int MT) { return MT <= 2 ? 16 : 8; }
+// warps: producer, consumers, two epilogue warps (alternate segments, so two
+// workspace fix-ups can be in flight at once)
+__host__ __device__ constexpr int dec_threads(int MT) { return 32 * (dec_consumers(MT) + 3); }
 constexpr int kDecChunkGroups = 16;
 constexpr int kDecStageBytes = kDecChunkGroups * kRecBytes;  // 17152
 constexpr int kDecMaxStages = 8;
 constexpr int kDecMaxTokens = 64;   // tokens per CTA slice (8 tiles of 8)
 constexpr int kDecSmemBudget = 220 * 1024;
+constexpr int kXinRot16 = 16;       // gemm_stream_kernel's XIN for pre-rotated fp16 rows
 
 struct DecParams {
   const int8_t* xq;
@@ -58,16 +71,15 @@ struct DecParams {
   int out_dtype;
   float* ws;        // [N][M] float32 partial sums, zero between calls
   uint32_t* cnt;    // [token slices][N/16] unit counters, zero between calls
-  // fused activation (linear entry point): x -> rotation -> int8 in-kernel
-  const void* x;            // [M, K] activations
-  const uint16_t* cscale;   // [K] fp16 channel scales or null
-  const uint32_t* rtab;     // [8, K] rotation table
-  __half* rot16;            // [M, K] scratch: rotated rows, fp16
+  // linear entry point: rotated fp16 rows from rot16_decode_kernel,
+  // quantised in the kernel's prologue
+  const __half* rot16;      // [M, K] rotated rows, fp16
   uint32_t* amax;           // [M] row |max| bits, zero between calls
-  uint32_t* gsync;          // [2] grid barrier and exit counters, zero between calls
+  uint32_t* gsync;          // [2] exit counter (word 1), zero between calls
   int64_t units;    // (N/16) * G
   int ctas;
   int stages;
+  int xrows_n;      // token rows staged in shared memory (XS)
 };
 
 __host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
@@ -93,71 +105,6 @@ __device__ __forceinline__ int frag_sum(const uint32_t (&b)[8]) {
 }
 
 __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-
-template <int XIN>
-__device__ __forceinline__ float load_x(const void* x, size_t i) {
-  if constexpr (XIN == PARO_F16) return __half2float(static_cast<const __half*>(x)[i]);
-  else if constexpr (XIN == PARO_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(x)[i]);
-  else return static_cast<const float*>(x)[i];
-}
-
-__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-// Fused activation, phase A (the CTA's consumer threads, two halves of 128):
-// half h rotates groups g = blockIdx.x + h * gridDim.x, ... for all M rows,
-// 8 rows at a time, exactly as the activation kernels do (channel scale, 8
-// Givens layers with separately rounded products, fp16 rounding); the rows go
-// to the fp16 scratch and each row's |max| to amax (atomicMax on the bits).
-template <int XIN>
-__device__ __forceinline__ void fused_rotate(const DecParams& p, int ctid, float* xb) {
-  const int half = ctid >> 7, ch = ctid & 127, lane = ctid & 31;
-  const int G = p.K / kGroup;
-  float* buf = xb + half * (2 * 8 * 128);
-  for (int g = blockIdx.x + half * gridDim.x; g < G; g += 2 * gridDim.x) {
-    const int c = g * kGroup + ch;
-    int part[8];
-    float cc[8], cp[8];
-#pragma unroll
-    for (int l = 0; l < 8; ++l) {
-      const uint32_t tab = __ldg(p.rtab + (size_t)l * p.K + c);
-      part[l] = (int)(tab & 0x7F);
-      float s_, c_;
-      __sincosf(half_bits_to_f32((uint16_t)(tab >> 16)), &s_, &c_);
-      cc[l] = c_;
-      cp[l] = ((tab >> 7) & 1) ? -s_ : s_;
-    }
-    const float sc = p.cscale ? half_bits_to_f32(p.cscale[c]) : 1.f;
-    for (int64_t r0 = 0; r0 < p.M; r0 += 8) {
-      float v[8];
-#pragma unroll
-      for (int r = 0; r < 8; ++r) v[r] = (r0 + r < p.M) ? load_x<XIN>(p.x, (size_t)(r0 + r) * p.K + c) * sc : 0.f;
-#pragma unroll
-      for (int l = 0; l < 8; ++l) {
-        float* b = buf + (l & 1) * (8 * 128);
-#pragma unroll
-        for (int r = 0; r < 8; ++r) b[r * 128 + ch] = v[r];
-        named_barrier(2 + half, 128);
-#pragma unroll
-        for (int r = 0; r < 8; ++r) v[r] = givens(v[r], b[r * 128 + part[l]], cc[l], cp[l]);
-      }
-#pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        const __half h = __float2half_rn(v[r]);
-        uint32_t a = 0u;
-        if (r0 + r < p.M) {
-          p.rot16[(size_t)(r0 + r) * p.K + c] = h;
-          a = __float_as_uint(fabsf(__half2float(h)));
-        }
-        a = __reduce_max_sync(0xffffffffu, a);
-        if (lane == 0 && a) atomicMax(p.amax + r0 + r, a);
-      }
-    }
-  }
-}
 
 __device__ __forceinline__ float bias_at(const void* bias, int dtype, int n) {
   if (!bias) return 0.f;
@@ -226,47 +173,64 @@ __device__ __forceinline__ void process_record(const uint8_t* rec, const uint32_
   }
 }
 
-// Walks a CTA's unit range in chunks: a chunk is the records of up to 16
-// consecutive groups of one row block, aligned to 16-group boundaries.
-struct ChunkIter {
-  int64_t u, u1;
-  int nb, g, G;
-  __device__ __forceinline__ ChunkIter(int64_t u0, int64_t u1_, int G_) : u(u0), u1(u1_), G(G_) {
-    nb = (int)(u0 / G_);
-    g = (int)(u0 - (int64_t)nb * G_);
-  }
-  __device__ __forceinline__ bool more() const { return u < u1; }
-  __device__ __forceinline__ int count() const {
-    const int gend = min(G, ((g >> 4) + 1) << 4);
-    return (int)min64(gend - g, u1 - u);
-  }
-  // advance past a chunk of n records; true if that ended a segment
-  __device__ __forceinline__ bool advance(int n) {
-    u += n;
-    g += n;
-    if (g == G) {
-      g = 0;
-      ++nb;
-      return true;
+// The order in which a CTA visits its unit range [u0, u1), one row-block
+// segment at a time: the head of the last row block, the tail of the first
+// (the two segments shared with neighbouring CTAs), then the whole row blocks
+// in between.  Two divisions at set-up; a segment is then a few integer
+// operations (the producer's loop must stay short: it shares its SM
+// sub-partition with consumer warps).
+struct Segs {
+  int nb0, g0, nbL, gL1, G, n;
+  __device__ __forceinline__ Segs(int64_t u0, int64_t u1, int G_) : G(G_) {
+    if (u1 <= u0) {
+      n = nb0 = g0 = nbL = gL1 = 0;
+      return;
     }
-    return u == u1;
+    nb0 = (int)(u0 / G);
+    g0 = (int)(u0 - (int64_t)nb0 * G);
+    nbL = (int)((u1 - 1) / G);
+    gL1 = (int)(u1 - (int64_t)nbL * G);
+    n = nbL == nb0 ? 1 : nbL - nb0 + 1;
+  }
+  // segment i (0 <= i < n): row block nb, groups [gb, ge)
+  __device__ __forceinline__ void get(int i, int& nb, int& gb, int& ge) const {
+    if (nbL == nb0) {
+      nb = nb0;
+      gb = g0;
+      ge = gL1;
+    } else if (i == 0) {
+      nb = nbL;
+      gb = 0;
+      ge = gL1;
+    } else if (i == 1) {
+      nb = nb0;
+      gb = g0;
+      ge = G;
+    } else {
+      nb = nb0 + i - 1;
+      gb = 0;
+      ge = G;
+    }
   }
 };
 
 // XS: the token slice's int8 rows are bulk-copied into shared memory (rows
-// padded by 16 bytes so the B-fragment reads of a warp hit 32 distinct
-// banks) and the per-group sums computed there; otherwise fragments are read
-// from global memory per record.
+// padded by 16 bytes so that the fragment reads of a warp hit 32 distinct
+// banks), rearranged into fragment order, and their per-group sums computed
+// there; otherwise fragments are read from global memory per record.
 // XIN < 0: the int8 activations and token scales come from paro_rotq_int8;
-// XIN = a paro dtype: the kernel computes them itself from x (fused linear,
-// cooperative launch, M <= 64, XS only).
+// XIN = kXinRot16: the previous kernel (rot16_decode_kernel) left the
+// rotated fp16 rows and row maxima, and the consumers quantise them in the
+// prologue (phase B; M <= 64, XS only).
 template <int MT, bool XS, int XIN>
-__global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p) {
-  constexpr bool FUSE = XIN >= 0;
-  static_assert(!FUSE || XS, "the fused activation stages its int8 rows in shared memory");
-  __shared__ float tok_scale_s[FUSE ? kDecMaxTokens : 1];
+__global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecParams p) {
+  constexpr bool FUSE = XIN == kXinRot16;
+  constexpr int NC = dec_consumers(MT);
+  constexpr int NCT = NC * 32;
+  constexpr int SLOTS = kDecChunkGroups / NC;   // records per warp per chunk
+  static_assert(!FUSE || XS, "phase B stages the int8 rows in shared memory");
+  __shared__ float tok_scale_s[kDecMaxTokens];
   __shared__ float tok_inv_s[FUSE ? kDecMaxTokens : 1];
-  __shared__ int fuse_fail;
   extern __shared__ __align__(128) uint8_t smem[];
   const int S = p.stages;
   const int G = p.K / kGroup;
@@ -277,9 +241,9 @@ __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p
   uint64_t* seg_full = empty + kDecMaxStages;   // [2]: all consumer slices written
   uint64_t* seg_free = seg_full + 2;             // [2]: epilogue has read them
   uint64_t* xbar = seg_free + 2;                 // activation rows landed
-  float* red = reinterpret_cast<float*>(xbar + 2);                                    // [2][8][MT*4][32]
-  uint8_t* xrows = reinterpret_cast<uint8_t*>(red + 2 * kDecConsumers * MT * 4 * 32);  // [MP][K + 16]
-  int* sxs = reinterpret_cast<int*>(xrows + (XS ? (size_t)MP * xstride : 0));          // [G][MP] group sums
+  float* red = reinterpret_cast<float*>(xbar + 2);                           // [2][NC][MT*4][32]
+  uint8_t* xrows = reinterpret_cast<uint8_t*>(red + 2 * NC * MT * 4 * 32);    // [xrows_n][K + 16]
+  int* sxs = reinterpret_cast<int*>(xrows + (XS ? (size_t)p.xrows_n * xstride : 0));  // [G][MP] group sums
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t u0 = (int64_t)blockIdx.x * p.units / p.ctas;
@@ -292,10 +256,10 @@ __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kDecConsumers);
+      mbar_init(&empty[s], NC);
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&seg_full[b], kDecConsumers);
+      mbar_init(&seg_full[b], NC);
       mbar_init(&seg_free[b], 1);
     }
     mbar_init(xbar, 1);
@@ -308,51 +272,66 @@ __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p
 
   if (warp == 0) {  // producer: weights do not depend on the previous kernel
     if (lane == 0) {
-      ChunkIter it(u0, u1, G);
-      for (int k = 0; it.more(); ++k) {
-        const int n = it.count();
-        const int s = k % S;
-        if (k >= S && !mbar_wait(&empty[s], ((k / S) - 1) & 1)) break;
-        const uint32_t bytes = (uint32_t)n * kRecBytes;
-        mbar_arrive_expect_tx(&full[s], bytes);
-        bulk_g2s(smem + (size_t)s * kDecStageBytes, p.packed + it.u * kRecBytes, bytes, &full[s]);
-        it.advance(n);
-        if (XS && !FUSE && (k == S - 1 || (!it.more() && k < S - 1))) {
-          // the ring is full of weights: now fetch the activations, which
-          // the previous kernel may still be writing
-          grid_dependency_wait();
-          mbar_arrive_expect_tx(xbar, (uint32_t)ntok_slice * p.K);
-          for (int r = 0; r < ntok_slice; ++r)
-            bulk_g2s(xrows + (size_t)r * xstride, p.xq + (tok0 + r) * (int64_t)p.K, (uint32_t)p.K, xbar);
+      const Segs sg(u0, u1, G);
+      int s = 0;
+      uint32_t rnd = 0;   // passes over the ring so far
+      bool ok = true;
+      for (int i = 0; ok && i < sg.n; ++i) {
+        int nb, g, ge;
+        sg.get(i, nb, g, ge);
+        const uint8_t* src = p.packed + ((int64_t)nb * G + g) * kRecBytes;
+        while (g < ge) {
+          const int n = min((g | 15) + 1, ge) - g;
+          if (rnd > 0 && !mbar_wait_sleep(&empty[s], (rnd - 1) & 1)) {
+            ok = false;
+            break;
+          }
+          const uint32_t bytes = (uint32_t)n * kRecBytes;
+          mbar_arrive_expect_tx(&full[s], bytes);
+          bulk_g2s(smem + (size_t)s * kDecStageBytes, src, bytes, &full[s]);
+          src += bytes;
+          g += n;
+          if (++s == S) {
+            s = 0;
+            ++rnd;
+          }
         }
-      }
-      if (XS && !FUSE && u1 <= u0) {  // no weights to stream: still complete xbar
-        grid_dependency_wait();
-        mbar_arrive_expect_tx(xbar, (uint32_t)ntok_slice * p.K);
-        for (int r = 0; r < ntok_slice; ++r)
-          bulk_g2s(xrows + (size_t)r * xstride, p.xq + (tok0 + r) * (int64_t)p.K, (uint32_t)p.K, xbar);
       }
     }
     return;
   }
 
-  if (warp == kDecConsumers + 1) {  // epilogue warp
-    grid_dependency_wait();         // token scales come from the previous kernel
+  if (warp > NC) {  // epilogue warps: warp NC + 1 + e takes the segments q = e (mod 2)
+    const int ew = warp - (NC + 1);
+    grid_dependency_wait();  // token scales (and rows) come from the previous kernel
+    if constexpr (!FUSE) {
+      // both warps write the same token scales; each reads back its own
+      for (int t = lane; t < ntok_slice; t += 32) tok_scale_s[t] = p.xscale[tok0 + t];
+      __syncwarp();
+    }
+    if constexpr (XS && !FUSE) {
+      // the activation rows: fetched as soon as the previous kernel is done
+      if (ew == 0 && lane == 0) {
+        mbar_arrive_expect_tx(xbar, (uint32_t)ntok_slice * p.K);
+        for (int r = 0; r < ntok_slice; ++r)
+          bulk_g2s(xrows + (size_t)r * xstride, p.xq + (tok0 + r) * (int64_t)p.K, (uint32_t)p.K, xbar);
+      }
+    }
     uint32_t* cnt = p.cnt + (size_t)blockIdx.y * (p.N / kRecRows);
-    const int nb0 = (int)(u0 / G);
-    const int nseg = u1 > u0 ? (int)((u1 - 1) / G) - nb0 + 1 : 0;
     const int ntok = (int)min64(kDecMaxTokens, p.M - tok0);
-    for (int q = 0; q < nseg; ++q) {
-      const int par = q & 1, nb = nb0 + q;
-      const int64_t seg_b = max64(u0, (int64_t)nb * G), seg_e = min64(u1, (int64_t)(nb + 1) * G);
-      const int seg_units = (int)(seg_e - seg_b);
-      if (!mbar_wait(&seg_full[par], (q >> 1) & 1)) return;
+    const Segs sg(u0, u1, G);
+    for (int q = ew; q < sg.n; q += 2) {
+      const int par = ew;
+      int nb, gb, ge;
+      sg.get(q, nb, gb, ge);
+      const int seg_units = ge - gb;
+      if (!mbar_wait_sleep(&seg_full[par], (q >> 1) & 1)) return;
       float v[MT * 4];
 #pragma unroll
       for (int sl = 0; sl < MT * 4; ++sl) {
         float a = 0.f;
 #pragma unroll
-        for (int w = 0; w < kDecConsumers; ++w) a += red[(size_t)(par * kDecConsumers + w) * kSlice + sl * 32 + lane];
+        for (int w2 = 0; w2 < NC; ++w2) a += red[(size_t)(par * NC + w2) * kSlice + sl * 32 + lane];
         v[sl] = a;
       }
       __syncwarp();
@@ -366,7 +345,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p
         if (t < p.M) {
           if (whole)
             store_out(p.out, p.out_dtype, (size_t)t * p.N + n,
-                      v[sl] * (FUSE ? tok_scale_s[t - tok0] : p.xscale[t]) + bias_at(p.bias, p.bias_dtype, n));
+                      v[sl] * tok_scale_s[t - tok0] + bias_at(p.bias, p.bias_dtype, n));
           else
             red_add_f32(p.ws + (size_t)n * p.M + t, v[sl]);
         }
@@ -389,10 +368,10 @@ __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p
             const int n = nb * kRecRows + r;
             const int64_t t = tok0 + tt;
             float* wp = p.ws + (size_t)n * p.M + t;
-            const float a = __ldcg(wp);
-            __stcg(wp, 0.f);
+            const float a = ld_cg_f32(wp);
+            st_cg_f32(wp, 0.f);
             store_out(p.out, p.out_dtype, (size_t)t * p.N + n,
-                      a * (FUSE ? tok_scale_s[t - tok0] : p.xscale[t]) + bias_at(p.bias, p.bias_dtype, n));
+                      a * tok_scale_s[t - tok0] + bias_at(p.bias, p.bias_dtype, n));
           }
           __syncwarp();
           if (lane == 0) cnt[nb] = 0u;
@@ -407,45 +386,28 @@ __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p
   const int ctid = threadIdx.x - 32;
   const int8_t* xrow[MT];
   bool xvalid[MT];
+  int xr[MT];   // staged row of this lane's token (clamped: rows past the tokens feed unused columns)
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt) {
     const int64_t t = tok0 + mt * 8 + gid;
     xvalid[mt] = t < p.M;
     xrow[mt] = p.xq + (xvalid[mt] ? t : 0) * (int64_t)p.K + 4 * tig;
+    xr[mt] = min(mt * 8 + gid, p.xrows_n - 1);
   }
   if constexpr (FUSE) {
-    // phase A: rotate this CTA's groups (the shared activation area is the
-    // exchange buffer until phase B fills it)
-    fused_rotate<XIN>(p, ctid, reinterpret_cast<float*>(xrows));
-    __threadfence();
-    named_barrier(1, kDecConsumers * 32);
-    // grid barrier: every CTA's rows and maxima are in place (cooperative
-    // launch: all CTAs are resident; the wait is bounded)
-    if (ctid == 0) {
-      fuse_fail = 0;
-      atomicAdd(p.gsync, 1u);
-      const long long t0 = clock64();
-      while (ld_acquire_gpu(p.gsync) < gridDim.x) {
-        if (clock64() - t0 > 400000000LL) {
-          report_error(kErrMbarTimeout);
-          fuse_fail = 1;
-          break;
-        }
-      }
-    }
-    named_barrier(1, kDecConsumers * 32);
-    if (fuse_fail) return;
-    // phase B: token scales, then the int8 rows into shared memory
+    // phase B: token scales from the row maxima, then the int8 rows into
+    // shared memory (round half away from zero, as vLLM's quantiser)
+    grid_dependency_wait();
     if (ctid < ntok_slice) {
-      const float a = fmaxf(__uint_as_float(__ldcg(p.amax + tok0 + ctid)), 1e-10f);
+      const float a = fmaxf(__uint_as_float(ld_cg_u32(p.amax + tok0 + ctid)), 1e-10f);
       tok_inv_s[ctid] = __fdiv_rn(127.0f, a);
       tok_scale_s[ctid] = __fdiv_rn(a, 127.0f);
     }
-    named_barrier(1, kDecConsumers * 32);
+    named_barrier(1, NCT);
     const int k8n = p.K / 8;
-    for (int e = ctid; e < ntok_slice * k8n; e += kDecConsumers * 32) {
+    for (int e = ctid; e < ntok_slice * k8n; e += NCT) {
       const int r = e / k8n, k8 = e - r * k8n;
-      const uint4 u = __ldcg(reinterpret_cast<const uint4*>(p.rot16 + (size_t)(tok0 + r) * p.K) + k8);
+      const uint4 u = ld_cg_v4(reinterpret_cast<const uint4*>(p.rot16 + (size_t)(tok0 + r) * p.K) + k8);
       const __half* h = reinterpret_cast<const __half*>(&u);
       const float inv = tok_inv_s[r];
       uint32_t w0 = 0, w1 = 0;
@@ -456,40 +418,52 @@ __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p
       }
       *reinterpret_cast<uint2*>(xrows + (size_t)r * xstride + (size_t)k8 * 8) = make_uint2(w0, w1);
     }
-    named_barrier(1, kDecConsumers * 32);
-    // the last CTA past this point returns the barrier state to zero
+    named_barrier(1, NCT);
+    // the last CTA past this point returns the maxima and the exit counter
+    // to zero
     if (ctid == 0) {
       __threadfence();
       const uint32_t old = atomicAdd(p.gsync + 1, 1u);
       if (old == gridDim.x - 1) {
         __threadfence();
         for (int64_t r = 0; r < p.M; ++r) p.amax[r] = 0u;
-        p.gsync[0] = 0u;
         p.gsync[1] = 0u;
       }
     }
   }
   if constexpr (XS) {
-    // rows beyond the slice's tokens hold stale bytes; they only feed output
-    // columns that are never stored
+    // staged rows past the slice's tokens (when a later slice is short) hold
+    // stale bytes, and lanes of tokens past the staged rows read the last
+    // one; both only feed output columns that are never stored
     if (!FUSE && !mbar_wait(xbar, 0)) return;
-    for (int e = ctid; e < G * MP; e += kDecConsumers * 32) {
+    // per (group, row): the group's sum, and its 32 words rearranged into
+    // fragment order: word j*4 + t (bytes 16j + 4t) moves to t*8 + j, so
+    // lane tig's eight B words are the 32 bytes at tig*32
+    for (int e = ctid; e < G * MP; e += NCT) {
       const int g = e / MP, r = e - g * MP;
       int sum = 0;
       if (r < ntok_slice) {
-        const uint4* src = reinterpret_cast<const uint4*>(xrows + (size_t)r * xstride + (size_t)g * kGroup);
+        uint4* blk = reinterpret_cast<uint4*>(xrows + (size_t)r * xstride + (size_t)g * kGroup);
+        uint32_t o[32];
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-          const uint4 v = src[c];
-          sum = __dp4a((int)v.x, 0x01010101, sum);
-          sum = __dp4a((int)v.y, 0x01010101, sum);
-          sum = __dp4a((int)v.z, 0x01010101, sum);
-          sum = __dp4a((int)v.w, 0x01010101, sum);
+          const uint4 v = blk[c];
+          o[4 * c] = v.x;
+          o[4 * c + 1] = v.y;
+          o[4 * c + 2] = v.z;
+          o[4 * c + 3] = v.w;
+        }
+#pragma unroll
+        for (int c = 0; c < 32; ++c) sum = __dp4a((int)o[c], 0x01010101, sum);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          blk[2 * t] = make_uint4(o[t], o[4 + t], o[8 + t], o[12 + t]);
+          blk[2 * t + 1] = make_uint4(o[16 + t], o[20 + t], o[24 + t], o[28 + t]);
         }
       }
       sxs[e] = sum;
     }
-    named_barrier(1, kDecConsumers * 32);
+    named_barrier(1, NCT);
   } else {
     grid_dependency_wait();  // the activations come from the previous kernel
   }
@@ -500,81 +474,95 @@ __global__ void __launch_bounds__(kDecThreads, 1) gemm_stream_kernel(DecParams p
 #pragma unroll
     for (int i = 0; i < 4; ++i) y[mt][i] = 0.f;
 
-  ChunkIter it(u0, u1, G);
-  int q = 0;
-  for (int k = 0; it.more(); ++k) {
-    const int n = it.count();
-    const int s = k % S;
-    const int gfirst = it.g, gbase = (it.g >> 4) << 4;
-    if (!mbar_wait(&full[s], (k / S) & 1)) return;
+  const Segs sg(u0, u1, G);
+  int s = 0;
+  uint32_t rnd = 0;
+  for (int q = 0; q < sg.n; ++q) {
+    int nb, g, ge;
+    sg.get(q, nb, g, ge);
+    while (g < ge) {
+      const int n = min((g | 15) + 1, ge) - g;
+      const int gbase = g & ~15;
+      if (!mbar_wait(&full[s], rnd & 1)) return;
 #pragma unroll
-    for (int slot = 0; slot < 2; ++slot) {
-      const int g = gbase + slot * 8 + cw;
-      if (g >= gfirst && g < gfirst + n) {
-        uint32_t bf[MT][8];
-        int sx[MT][2];
+      for (int slot = 0; slot < SLOTS; ++slot) {
+        const int gg = gbase + slot * NC + cw;
+        if (gg >= g && gg < g + n) {
+          uint32_t bf[MT][8];
+          int sx[MT][2];
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-          if constexpr (XS) {
-            const uint8_t* xb = xrows + (size_t)(mt * 8 + gid) * xstride + (size_t)g * kGroup + 4 * tig;
-#pragma unroll
-            for (int s4 = 0; s4 < 4; ++s4) {
-              bf[mt][2 * s4] = *reinterpret_cast<const uint32_t*>(xb + 32 * s4);
-              bf[mt][2 * s4 + 1] = *reinterpret_cast<const uint32_t*>(xb + 32 * s4 + 16);
+          for (int mt = 0; mt < MT; ++mt) {
+            if constexpr (XS) {
+              const uint4* xb = reinterpret_cast<const uint4*>(xrows + (size_t)xr[mt] * xstride +
+                                                               (size_t)gg * kGroup + 32 * tig);
+              const uint4 b0 = xb[0], b1 = xb[1];
+              bf[mt][0] = b0.x;
+              bf[mt][1] = b0.y;
+              bf[mt][2] = b0.z;
+              bf[mt][3] = b0.w;
+              bf[mt][4] = b1.x;
+              bf[mt][5] = b1.y;
+              bf[mt][6] = b1.z;
+              bf[mt][7] = b1.w;
+              const int2 s2 = *reinterpret_cast<const int2*>(sxs + (size_t)gg * MP + mt * 8 + 2 * tig);
+              sx[mt][0] = s2.x;
+              sx[mt][1] = s2.y;
+            } else {
+              load_bfrag_global(xrow[mt], xvalid[mt], gg, bf[mt]);
+              // token row gid's sum, then the sums of this lane's C columns
+              int part = frag_sum(bf[mt]);
+              part += __shfl_xor_sync(0xffffffffu, part, 1);
+              part += __shfl_xor_sync(0xffffffffu, part, 2);
+              sx[mt][0] = __shfl_sync(0xffffffffu, part, 8 * tig);
+              sx[mt][1] = __shfl_sync(0xffffffffu, part, 8 * tig + 4);
             }
-            const int2 s2 = *reinterpret_cast<const int2*>(sxs + (size_t)g * MP + mt * 8 + 2 * tig);
-            sx[mt][0] = s2.x;
-            sx[mt][1] = s2.y;
-          } else {
-            load_bfrag_global(xrow[mt], xvalid[mt], g, bf[mt]);
-            // token row gid's sum, then the sums of this lane's C columns
-            int part = frag_sum(bf[mt]);
-            part += __shfl_xor_sync(0xffffffffu, part, 1);
-            part += __shfl_xor_sync(0xffffffffu, part, 2);
-            sx[mt][0] = __shfl_sync(0xffffffffu, part, 8 * tig);
-            sx[mt][1] = __shfl_sync(0xffffffffu, part, 8 * tig + 4);
           }
+          process_record<MT>(smem + (size_t)s * kDecStageBytes + (size_t)(gg - g) * kRecBytes, bf, sx, gid, tig,
+                             y);
         }
-        process_record<MT>(smem + (size_t)s * kDecStageBytes + (size_t)(g - gfirst) * kRecBytes, bf, sx, gid, tig,
-                           y);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      g += n;
+      if (++s == S) {
+        s = 0;
+        ++rnd;
       }
     }
+    // segment end: hand this warp's partial to the epilogue warp
+    const int par = q & 1;
+    if (q >= 2 && !mbar_wait(&seg_free[par], ((q >> 1) - 1) & 1)) return;
+    float* sl = red + (size_t)(par * NC + cw) * kSlice;
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        sl[(mt * 4 + i) * 32 + lane] = y[mt][i];
+        y[mt][i] = 0.f;
+      }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-
-    if (it.advance(n)) {  // segment end: hand this warp's partial to the epilogue warp
-      const int par = q & 1;
-      if (q >= 2 && !mbar_wait(&seg_free[par], ((q >> 1) - 1) & 1)) return;
-      float* sl = red + (size_t)(par * kDecConsumers + cw) * kSlice;
-#pragma unroll
-      for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          sl[(mt * 4 + i) * 32 + lane] = y[mt][i];
-          y[mt][i] = 0.f;
-        }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&seg_full[par]);
-      ++q;
-    }
+    if (lane == 0) mbar_arrive(&seg_full[par]);
   }
 }
 
 PARO_DEFINE_ERROR_ACCESSOR(decode)
 
-static int g_num_sms = 0;
-
-size_t gemm_decode_workspace(int64_t M, int N) {
-  const int64_t slices = (M + kDecMaxTokens - 1) / kDecMaxTokens;
-  size_t ws = (size_t)N * (size_t)M * sizeof(float);
-  ws = (ws + 255) & ~(size_t)255;
-  return ws + (size_t)slices * (N / kRecRows) * sizeof(uint32_t);
-}
-
 static size_t fixed_smem(int MT) {
   // full/empty rings, seg_full/seg_free pairs, xbar (+1 slot keeps 16-byte
-  // alignment), then the epilogue slices
-  return (2 * kDecMaxStages + 6) * sizeof(uint64_t) + 2 * (size_t)kDecConsumers * MT * 4 * 32 * sizeof(float);
+  // alignment), then the reduction slices
+  return (2 * kDecMaxStages + 6) * sizeof(uint64_t) +
+         2 * (size_t)dec_consumers(MT) * MT * 4 * 32 * sizeof(float);
+}
+
+// Token rows staged per CTA: the slice's tokens (all of them below 64).
+static int xrows_for(int MT, int64_t M) { return (int)(M < 8 * MT ? M : 8 * MT); }
+
+// Shared memory of the staged int8 rows and their group sums for MT token
+// tiles, or 0 if they do not fit beside three ring stages.
+static size_t xs_bytes_for(int MT, int K, int64_t M) {
+  const int G = K / kGroup;
+  const size_t xs = (size_t)xrows_for(MT, M) * (K + 16) + (size_t)G * 8 * MT * sizeof(int);
+  return fixed_smem(MT) + xs + 3 * (size_t)kDecStageBytes <= (size_t)kDecSmemBudget ? xs : 0;
 }
 
 template <int MT, bool XS, int XIN = -1>
@@ -585,49 +573,53 @@ static cudaError_t launch_mt(DecParams p, size_t xs_bytes, cudaStream_t st) {
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)p.ctas, (unsigned)((p.M + kDecMaxTokens - 1) / kDecMaxTokens), 1);
-  cfg.blockDim = dim3(kDecThreads, 1, 1);
+  cfg.blockDim = dim3(dec_threads(MT), 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
-  if (XIN >= 0) {
-    // the fused activation's grid barrier needs every CTA resident
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-  } else {
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-  }
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
-template <int MT>
-static cudaError_t launch_pick(DecParams p, cudaStream_t st) {
-  const int G = p.K / kGroup;
-  const size_t xs_bytes = (size_t)8 * MT * (p.K + 16) + (size_t)G * 8 * MT * sizeof(int);
-  const size_t base = fixed_smem(MT);
-  const bool xs = base + xs_bytes + 3 * (size_t)kDecStageBytes <= (size_t)kDecSmemBudget;
-  const size_t avail = kDecSmemBudget - base - (xs ? xs_bytes : 0);
-  int stages = (int)(avail / kDecStageBytes);
-  stages = stages > kDecMaxStages ? kDecMaxStages : stages;
-  if (stages < 2) return cudaErrorInvalidValue;
-  p.stages = stages;
-  return xs ? launch_mt<MT, true>(p, xs_bytes, st) : launch_mt<MT, false>(p, xs_bytes, st);
+static void stages_for(DecParams& p, int MT, size_t xs_bytes) {
+  const int stages = (int)((kDecSmemBudget - fixed_smem(MT) - xs_bytes) / kDecStageBytes);
+  p.stages = stages > kDecMaxStages ? kDecMaxStages : stages;
 }
 
-cudaError_t launch_gemm_decode(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
-                               const void* bias, int bias_dtype, void* out, int out_dtype, void* ws,
-                               cudaStream_t st) {
+template <int MT>
+static cudaError_t launch_pick(DecParams p, cudaStream_t st) {
+  const size_t xs_bytes = xs_bytes_for(MT, p.K, p.M);
+  p.xrows_n = xrows_for(MT, p.M);
+  stages_for(p, MT, xs_bytes);
+  if (p.stages < 2) return cudaErrorInvalidValue;
+  return xs_bytes ? launch_mt<MT, true>(p, xs_bytes, st) : launch_mt<MT, false>(p, 0, st);
+}
+
+static int g_num_sms = 0;
+
+static void init_sms() {
   if (g_num_sms == 0) {
     int dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
     if (g_num_sms <= 0) g_num_sms = 148;
   }
+}
+
+size_t gemm_decode_workspace(int64_t M, int N) {
+  const int64_t slices = (M + kDecMaxTokens - 1) / kDecMaxTokens;
+  size_t ws = (size_t)N * (size_t)M * sizeof(float);
+  ws = (ws + 255) & ~(size_t)255;
+  return ws + (size_t)slices * (N / kRecRows) * sizeof(uint32_t);
+}
+
+static DecParams dec_params(int64_t M, int N, int K, const void* packed, const void* bias, int bias_dtype, void* out,
+                            int out_dtype, void* ws) {
+  init_sms();
   DecParams p = {};
-  p.xq = xq;
-  p.xscale = xscale;
   p.M = M;
   p.N = N;
   p.K = K;
@@ -642,6 +634,15 @@ cudaError_t launch_gemm_decode(const int8_t* xq, const float* xscale, int64_t M,
   p.units = (int64_t)(N / kRecRows) * (K / kGroup);
   p.ctas = (int)min64(g_num_sms, p.units);
   p.stages = 0;
+  return p;
+}
+
+cudaError_t launch_gemm_decode(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
+                               const void* bias, int bias_dtype, void* out, int out_dtype, void* ws,
+                               cudaStream_t st) {
+  DecParams p = dec_params(M, N, K, packed, bias, bias_dtype, out, out_dtype, ws);
+  p.xq = xq;
+  p.xscale = xscale;
   if (M <= 8) return launch_pick<1>(p, st);
   if (M <= 16) return launch_pick<2>(p, st);
   if (M <= 32) return launch_pick<4>(p, st);
@@ -649,29 +650,26 @@ cudaError_t launch_gemm_decode(const int8_t* xq, const float* xscale, int64_t M,
 }
 
 // ---------------------------------------------------------------------------
-// fused linear for decode sizes: activation rotation + quantisation inside
-// the GEMM kernel (see fused_rotate and the consumers' phase B)
+// decode linear: rot16_decode_kernel rotates the activations into an fp16
+// scratch and records each row's |max|; the GEMM quantises them in its
+// prologue (phase B) and streams the weights meanwhile
 // ---------------------------------------------------------------------------
+cudaError_t launch_rot16_decode(int x_dtype, const void* x, int64_t M, int K, const uint16_t* scales,
+                                const uint32_t* rtab, __half* y, uint32_t* amax, cudaStream_t st);
+
 size_t linear_decode_workspace(int64_t M, int N) {
   return gemm_decode_workspace(M, N) + (((size_t)M * sizeof(uint32_t) + 255) & ~(size_t)255) + 256;
 }
 
+static int fused_mt(int64_t M) { return M <= 8 ? 1 : M <= 16 ? 2 : M <= 32 ? 4 : 8; }
+
 template <int MT>
-static cudaError_t launch_pick_fused(DecParams p, int x_dtype, cudaStream_t st) {
-  const int G = p.K / kGroup;
-  size_t xs_bytes = (size_t)8 * MT * (p.K + 16) + (size_t)G * 8 * MT * sizeof(int);
-  const size_t xch = (size_t)2 * 2 * 8 * 128 * sizeof(float);  // phase A exchange buffers
-  if (xs_bytes < xch) xs_bytes = xch;
-  const size_t base = fixed_smem(MT);
-  if (base + xs_bytes + 3 * (size_t)kDecStageBytes > (size_t)kDecSmemBudget) return cudaErrorNotSupported;
-  int stages = (int)((kDecSmemBudget - base - xs_bytes) / kDecStageBytes);
-  p.stages = stages > kDecMaxStages ? kDecMaxStages : stages;
-  switch (x_dtype) {
-    case PARO_F32: return launch_mt<MT, true, PARO_F32>(p, xs_bytes, st);
-    case PARO_F16: return launch_mt<MT, true, PARO_F16>(p, xs_bytes, st);
-    case PARO_BF16: return launch_mt<MT, true, PARO_BF16>(p, xs_bytes, st);
-  }
-  return cudaErrorInvalidValue;
+static cudaError_t launch_pick_fused(DecParams p, cudaStream_t st) {
+  const size_t xs_bytes = xs_bytes_for(MT, p.K, p.M);
+  p.xrows_n = xrows_for(MT, p.M);
+  if (!xs_bytes) return cudaErrorNotSupported;
+  stages_for(p, MT, xs_bytes);
+  return launch_mt<MT, true, kXinRot16>(p, xs_bytes, st);
 }
 
 // Returns cudaErrorNotSupported (nothing launched) for shapes whose int8
@@ -679,41 +677,22 @@ static cudaError_t launch_pick_fused(DecParams p, int x_dtype, cudaStream_t st) 
 cudaError_t launch_linear_decode(const void* x, int x_dtype, const uint16_t* cscale, const uint32_t* rtab, int64_t M,
                                  int N, int K, const void* packed, const void* bias, int bias_dtype, void* out,
                                  int out_dtype, void* ws, void* scratch, cudaStream_t st) {
-  if (M > kDecMaxTokens) return cudaErrorNotSupported;
-  if (g_num_sms == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-    if (g_num_sms <= 0) g_num_sms = 148;
-  }
-  DecParams p = {};
-  p.xq = nullptr;
-  p.xscale = nullptr;
-  p.M = M;
-  p.N = N;
-  p.K = K;
-  p.packed = static_cast<const uint8_t*>(packed);
-  p.bias = bias;
-  p.bias_dtype = bias_dtype;
-  p.out = out;
-  p.out_dtype = out_dtype;
-  const size_t wsf = ((size_t)N * (size_t)M * sizeof(float) + 255) & ~(size_t)255;
-  p.ws = static_cast<float*>(ws);
-  p.cnt = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(ws) + wsf);
+  if (M > kDecMaxTokens || M <= 0) return cudaErrorNotSupported;
+  if (!xs_bytes_for(fused_mt(M), K, M)) return cudaErrorNotSupported;
+  DecParams p = dec_params(M, N, K, packed, bias, bias_dtype, out, out_dtype, ws);
   uint8_t* tail = static_cast<uint8_t*>(ws) + gemm_decode_workspace(M, N);
   p.amax = reinterpret_cast<uint32_t*>(tail);
   p.gsync = reinterpret_cast<uint32_t*>(tail + (((size_t)M * sizeof(uint32_t) + 255) & ~(size_t)255));
-  p.x = x;
-  p.cscale = cscale;
-  p.rtab = rtab;
-  p.rot16 = static_cast<__half*>(scratch);
-  p.units = (int64_t)(N / kRecRows) * (K / kGroup);
-  p.ctas = (int)min64(g_num_sms, p.units);
-  p.stages = 0;
-  if (M <= 8) return launch_pick_fused<1>(p, x_dtype, st);
-  if (M <= 16) return launch_pick_fused<2>(p, x_dtype, st);
-  if (M <= 32) return launch_pick_fused<4>(p, x_dtype, st);
-  return launch_pick_fused<8>(p, x_dtype, st);
+  __half* rot16 = static_cast<__half*>(scratch);
+  p.rot16 = rot16;
+  const cudaError_t e = launch_rot16_decode(x_dtype, x, M, K, cscale, rtab, rot16, p.amax, st);
+  if (e != cudaSuccess) return e;
+  switch (fused_mt(M)) {
+    case 1: return launch_pick_fused<1>(p, st);
+    case 2: return launch_pick_fused<2>(p, st);
+    case 4: return launch_pick_fused<4>(p, st);
+  }
+  return launch_pick_fused<8>(p, st);
 }
 
 }  // namespace paro

@@ -83,6 +83,51 @@ __device__ __forceinline__ float2 givens2(float2 x, float2 partner, float p, flo
   return o;
 }
 
+// Loads of data that the previous kernel on the stream writes, in a kernel
+// launched with programmatic dependent launch: it may start before that
+// kernel ends, so these loads must stay after its griddepcontrol.wait.
+// Plain loads through const __restrict__ pointers may be compiled as
+// invariant (read-only path) loads, which the compiler is free to move above
+// the wait; volatile asm with a memory clobber keeps them in place.
+__device__ __forceinline__ float ld_dep(const float* p) {
+  float v;
+  asm volatile("ld.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ float ld_dep(const __half* p) {
+  unsigned short b;
+  asm volatile("ld.global.u16 %0, [%1];" : "=h"(b) : "l"(p) : "memory");
+  return __half2float(__ushort_as_half(b));
+}
+__device__ __forceinline__ float ld_dep(const __nv_bfloat16* p) {
+  unsigned short b;
+  asm volatile("ld.global.u16 %0, [%1];" : "=h"(b) : "l"(p) : "memory");
+  return __uint_as_float((uint32_t)b << 16);  // bf16 is the high half of a float32
+}
+
+// L2 (.cg) accesses to data shared between CTAs or grids, as volatile asm
+// with a memory clobber so that they keep their place relative to the
+// fences, barriers and dependency waits that order them.
+__device__ __forceinline__ float ld_cg_f32(const float* p) {
+  float v;
+  asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint32_t ld_cg_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.global.cg.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint4 ld_cg_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_cg_f32(float* p, float v) {
+  asm volatile("st.global.cg.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+}
+
 // Raise a kernel's dynamic shared-memory limit to `bytes` once per (kernel,
 // device); later calls are a map lookup instead of a driver call.
 cudaError_t ensure_smem_limit(const void* kernel, int bytes);

@@ -1,0 +1,122 @@
+// rotq_decode.cu — the rotation half of a decode-size rotated linear
+// (sm_100a): channel scale + 8 Givens layers per 128-channel group, rounded
+// to fp16, plus each token row's |max|.  The int8 quantisation that needs
+// the whole row's maximum is done by the GEMM that consumes these rows, in
+// its prologue (gemm_decode.cu, phase B), so no kernel here waits for
+// another CTA.
+//
+// Geometry for a handful of tokens: one CTA per (group, block of R rows),
+// 128 threads, thread ch owning channel ch of the group for the R rows.  A
+// 7B-class layer has 28 (K = 3584) or 148 (K = 18944) groups, so the work
+// spreads over that many SMs instead of the 8-CTA cluster of the
+// single-pass kernel, and a CTA's critical path is one table load, one
+// activation load and 8 exchange rounds.  Per layer each thread publishes
+// its R values to shared memory, the CTA synchronises once, and each thread
+// reads its partner's values and applies its own half of the pair with both
+// products and the sum rounded separately (the arithmetic of the reference's
+// rotate kernel, kernels/paroquant_kernels/src/rotation.cuh:248-337, and of
+// rotq_fused.cu, operation for operation).  Row maxima: a warp reduction
+// of the fp16 values' bit patterns (non-negative floats order like their
+// bits), then one shared-memory atomic per warp and one global atomicMax per
+// row and CTA.
+#include "tc_ptx.cuh"
+
+namespace paro {
+
+template <typename InT, int R>
+__global__ void __launch_bounds__(128)
+rot16_decode_kernel(const InT* x, int64_t M, int K, const uint16_t* __restrict__ scales,
+                    const uint32_t* __restrict__ rtab, __half* __restrict__ y, uint32_t* __restrict__ amax) {
+  // the GEMM that consumes these rows may launch now and start its weight
+  // stream; it waits for this grid before reading y and amax
+  asm volatile("griddepcontrol.launch_dependents;");
+  __shared__ float buf[2][R][128];
+  __shared__ uint32_t cmax[R];
+  const int ch = threadIdx.x, lane = ch & 31;
+  const int c = blockIdx.x * 128 + ch;
+  const int64_t r0 = (int64_t)blockIdx.y * R;
+  const int nrows = M - r0 < R ? (int)(M - r0) : R;
+
+  int part[8];
+  float cc[8], cp[8];
+#pragma unroll
+  for (int l = 0; l < 8; ++l) {
+    const uint32_t tab = __ldg(rtab + (size_t)l * K + c);
+    part[l] = (int)(tab & 0x7F);
+    float s_, c_;
+    __sincosf(half_bits_to_f32((uint16_t)(tab >> 16)), &s_, &c_);
+    cc[l] = c_;
+    cp[l] = ((tab >> 7) & 1) ? -s_ : s_;
+  }
+  const float sc = scales ? half_bits_to_f32(scales[c]) : 1.f;
+  if (ch < R) cmax[ch] = 0u;
+
+  // x (and the zero state of amax) belong to the previous kernels on the
+  // stream: wait for them before touching either
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  float v[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) v[r] = r < nrows ? ld_dep(x + (r0 + r) * (int64_t)K + c) * sc : 0.f;
+#pragma unroll
+  for (int l = 0; l < 8; ++l) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) buf[l & 1][r][ch] = v[r];
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < R; ++r) v[r] = givens(v[r], buf[l & 1][r][part[l]], cc[l], cp[l]);
+  }
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const __half h = __float2half_rn(v[r]);
+    uint32_t a = 0u;
+    if (r < nrows) {
+      y[(r0 + r) * (int64_t)K + c] = h;
+      a = __float_as_uint(fabsf(__half2float(h)));
+    }
+    a = __reduce_max_sync(0xffffffffu, a);
+    if (lane == 0 && a) atomicMax(&cmax[r], a);
+  }
+  __syncthreads();
+  if (ch < nrows && cmax[ch]) atomicMax(amax + r0 + ch, cmax[ch]);
+}
+
+template <typename InT, int R>
+static cudaError_t launch_r(const void* x, int64_t M, int K, const uint16_t* scales, const uint32_t* rtab, __half* y,
+                            uint32_t* amax, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(K / kGroup), (unsigned)((M + R - 1) / R), 1);
+  cfg.blockDim = dim3(128, 1, 1);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, rot16_decode_kernel<InT, R>, static_cast<const InT*>(x), M, K, scales, rtab, y,
+                            amax);
+}
+
+template <typename InT>
+static cudaError_t launch_t(const void* x, int64_t M, int K, const uint16_t* scales, const uint32_t* rtab, __half* y,
+                            uint32_t* amax, cudaStream_t st) {
+  if (M <= 1) return launch_r<InT, 1>(x, M, K, scales, rtab, y, amax, st);
+  if (M <= 2) return launch_r<InT, 2>(x, M, K, scales, rtab, y, amax, st);
+  if (M <= 4) return launch_r<InT, 4>(x, M, K, scales, rtab, y, amax, st);
+  return launch_r<InT, 8>(x, M, K, scales, rtab, y, amax, st);
+}
+
+// amax must hold zeros for the M rows (the consuming GEMM returns it to
+// zero); y receives M x K fp16 values.
+cudaError_t launch_rot16_decode(int x_dtype, const void* x, int64_t M, int K, const uint16_t* scales,
+                                const uint32_t* rtab, __half* y, uint32_t* amax, cudaStream_t st) {
+  if (M <= 0 || M > 65535 * 8) return cudaErrorInvalidValue;
+  switch (x_dtype) {
+    case PARO_F32: return launch_t<float>(x, M, K, scales, rtab, y, amax, st);
+    case PARO_F16: return launch_t<__half>(x, M, K, scales, rtab, y, amax, st);
+    case PARO_BF16: return launch_t<__nv_bfloat16>(x, M, K, scales, rtab, y, amax, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace paro

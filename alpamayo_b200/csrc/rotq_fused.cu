@@ -81,7 +81,7 @@ __device__ __forceinline__ void ld_vec(const float* p, float (&v)[R]) {
 
 template <typename InT, int R, int PM>
 __global__ void __launch_bounds__(512)
-rotq_fused_kernel(const InT* __restrict__ x, int64_t M, int K, const uint16_t* __restrict__ scales,
+rotq_fused_kernel(const InT* x, int64_t M, int K, const uint16_t* __restrict__ scales,
                   const uint32_t* __restrict__ rtab, int fp16_round, int gpc, int GB, int P,
                   int8_t* __restrict__ out_q, float* __restrict__ out_scale) {
   namespace cg = cooperative_groups;
@@ -136,7 +136,7 @@ rotq_fused_kernel(const InT* __restrict__ x, int64_t M, int K, const uint16_t* _
     const float sc = (goff[p] >= 0 && scales) ? half_bits_to_f32(scales[goff[p]]) : 1.f;
 #pragma unroll
     for (int r = 0; r < R; ++r)
-      v[p][r] = (goff[p] >= 0 && r < nrows) ? to_f32(x[(row0 + r) * (int64_t)K + goff[p]]) * sc : 0.f;
+      v[p][r] = (goff[p] >= 0 && r < nrows) ? ld_dep(x + (row0 + r) * (int64_t)K + goff[p]) * sc : 0.f;
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
 

@@ -244,7 +244,8 @@ at::Tensor w4a8_gemm(const at::Tensor& xq_in, const at::Tensor& xscale_in, const
   return out;
 }
 
-// One W4A8 rotated linear (paro_w4a8_linear: one kernel at decode sizes).
+// One W4A8 rotated linear (paro_w4a8_linear: rotation kernel + GEMM with
+// in-prologue quantisation at decode sizes).
 at::Tensor linear_w4a8(const at::Tensor& x_in, const at::Tensor& rot_table,
                        const c10::optional<at::Tensor>& channel_scales, const at::Tensor& packed, int64_t N,
                        const c10::optional<at::Tensor>& bias_opt, bool fp16_round, at::ScalarType out_dtype) {

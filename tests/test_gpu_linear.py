@@ -1,7 +1,8 @@
 """paro_w4a8_linear (torch.ops.paro_b200.linear_w4a8): the whole rotated
-linear.  Up to 64 tokens it is one cooperative kernel that rotates and
-quantises the activations inside the GEMM; the tests hold it to the
-two-kernel route (paro_rotq_int8 + paro_w4a8_gemm) and to the oracle.
+linear.  Up to 64 tokens it is a rotation kernel (fp16 rows + row maxima)
+chained to the decode GEMM, which quantises the rows in its prologue; the
+tests hold it to the activation-kernel route (paro_rotq_int8 +
+paro_w4a8_gemm) and to the oracle.
 
 Tolerances: the two routes compute the same int8 codes and int32 group sums;
 only the order of float32 additions across CTAs may differ, so float32
@@ -52,8 +53,8 @@ def test_linear_matches_two_kernel_route(ops, M, N, K):
 
 @pytest.mark.parametrize("M,N,K", [(1, 3584, 18944), (8, 3584, 18944), (4, 37888, 3584), (64, 256, 18944)])
 def test_linear_large_shapes(ops, M, N, K):
-    """down_proj / gate_up decode shapes (fused), and a shape whose int8 rows
-    do not fit in shared memory (M = 64, K = 18944: two-kernel fallback)."""
+    """down_proj / gate_up decode shapes, and a shape whose int8 rows do not
+    fit in shared memory (M = 64, K = 18944: activation-kernel route)."""
     L = synthetic_layer(N, K, seed=K + M)
     from alpamayo_b200 import synthetic as syn
     x = syn.make_activations(M, K, seed=M + 1)
@@ -76,8 +77,9 @@ def test_linear_against_oracle(ops, M):
     m = m.cuda()
     x = torch.from_numpy(make_activations(M, K, seed=M + 5)).to(torch.bfloat16)
     y = m(x.cuda()).float().cpu().numpy()
-    # the activation codes the kernels compute (the fused kernel's arithmetic
-    # is the activation kernel's) against the oracle's: the code tolerance
+    # the activation codes the kernels compute (the linear's rotation and
+    # quantisation are the activation kernel's, operation for operation)
+    # against the oracle's: the code tolerance
     qk, sk = ops.rotq_int8(x.cuda(), m.rotation.rot_table(), m.rotation.channel_scales.reshape(-1).cuda(), 128, True)
     qk, sk = qk.cpu().numpy(), sk.cpu().numpy().reshape(-1)
     q, s, _ = O.rot_quant_reference(x.float().numpy(), d["pairs"], d["theta"].astype(np.float32),
