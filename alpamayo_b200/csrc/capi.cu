@@ -36,6 +36,7 @@ cudaError_t launch_add_rmsnorm(const void* x, void* residual, const void* weight
                                void* out, cudaStream_t st);
 cudaError_t launch_silu_mul(const void* x, int64_t M, int I, void* out, cudaStream_t st);
 size_t linear_decode_workspace(int64_t M, int N);
+size_t linear_decode_scratch(int64_t M, int K);
 cudaError_t launch_linear_decode(const void* x, int x_dtype, const uint16_t* cscale, const uint32_t* rtab, int64_t M,
                                  int N, int K, const void* packed, const void* bias, int bias_dtype, void* out,
                                  int out_dtype, void* ws, void* scratch, cudaStream_t st);
@@ -242,7 +243,7 @@ size_t paro_w4a8_linear_workspace_size(int64_t M, int N, int K) {
 size_t paro_w4a8_linear_scratch_size(int64_t M, int N, int K, int fp16_round) {
   if (M <= 0 || N <= 0 || K <= 0 || N % kRecRows || K % kGroup) return 0;
   size_t sc = linear_unfused_scratch(M, K, fp16_round);
-  if (M <= kLinearFusedMaxM) sc = std::max(sc, al256((size_t)M * K * sizeof(uint16_t)));
+  if (M <= kLinearFusedMaxM) sc = std::max(sc, linear_decode_scratch(M, K));
   return sc;
 }
 

@@ -58,6 +58,8 @@ constexpr int kDecMaxStages = 8;
 constexpr int kDecMaxTokens = 64;   // tokens per CTA slice (8 tiles of 8)
 constexpr int kDecSmemBudget = 220 * 1024;
 constexpr int kXinRot16 = 16;       // gemm_stream_kernel's XIN for pre-rotated fp16 rows
+constexpr int kXinPreQ = 17;        // ... for int8 rows in fragment order with code sums
+constexpr int kDecBulkXBytes = 32 * 1024;  // activation blocks above this are bulk-copied
 
 struct DecParams {
   const int8_t* xq;
@@ -80,6 +82,8 @@ struct DecParams {
   int ctas;
   int stages;
   int xrows_n;      // token rows staged in shared memory (XS)
+  const int* gsum;  // kXinPreQ: per (group, token) code sums, [G][gsum_mp]
+  int gsum_mp;
 };
 
 __host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
@@ -225,6 +229,8 @@ struct Segs {
 template <int MT, bool XS, int XIN>
 __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecParams p) {
   constexpr bool FUSE = XIN == kXinRot16;
+  constexpr bool PREQ = XIN == kXinPreQ;
+  static_assert(!PREQ || !XS, "pre-quantised rows are read from global memory");
   constexpr int NC = dec_consumers(MT);
   constexpr int NCT = NC * 32;
   constexpr int SLOTS = kDecChunkGroups / NC;   // records per warp per chunk
@@ -240,7 +246,7 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
   uint64_t* empty = full + kDecMaxStages;
   uint64_t* seg_full = empty + kDecMaxStages;   // [2]: all consumer slices written
   uint64_t* seg_free = seg_full + 2;             // [2]: epilogue has read them
-  uint64_t* xbar = seg_free + 2;                 // activation rows landed
+  uint64_t* xbar = seg_free + 2;                 // activation rows landed (bulk path)
   float* red = reinterpret_cast<float*>(xbar + 2);                           // [2][NC][MT*4][32]
   uint8_t* xrows = reinterpret_cast<uint8_t*>(red + 2 * NC * MT * 4 * 32);    // [xrows_n][K + 16]
   int* sxs = reinterpret_cast<int*>(xrows + (XS ? (size_t)p.xrows_n * xstride : 0));  // [G][MP] group sums
@@ -309,15 +315,16 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
       for (int t = lane; t < ntok_slice; t += 32) tok_scale_s[t] = p.xscale[tok0 + t];
       __syncwarp();
     }
+    uint32_t* cnt = p.cnt + (size_t)blockIdx.y * (p.N / kRecRows);
     if constexpr (XS && !FUSE) {
-      // the activation rows: fetched as soon as the previous kernel is done
-      if (ew == 0 && lane == 0) {
+      // large activation blocks: bulk copies of the rows (behind the weight
+      // chunks already queued, but one copy per row)
+      if (ew == 0 && lane == 0 && (int64_t)ntok_slice * p.K > kDecBulkXBytes) {
         mbar_arrive_expect_tx(xbar, (uint32_t)ntok_slice * p.K);
         for (int r = 0; r < ntok_slice; ++r)
           bulk_g2s(xrows + (size_t)r * xstride, p.xq + (tok0 + r) * (int64_t)p.K, (uint32_t)p.K, xbar);
       }
     }
-    uint32_t* cnt = p.cnt + (size_t)blockIdx.y * (p.N / kRecRows);
     const int ntok = (int)min64(kDecMaxTokens, p.M - tok0);
     const Segs sg(u0, u1, G);
     for (int q = ew; q < sg.n; q += 2) {
@@ -386,6 +393,7 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
   const int ctid = threadIdx.x - 32;
   const int8_t* xrow[MT];
   bool xvalid[MT];
+  const uint8_t* xrowf[MT];   // kXinPreQ: this lane's 32 bytes of group 0
   int xr[MT];   // staged row of this lane's token (clamped: rows past the tokens feed unused columns)
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt) {
@@ -393,30 +401,57 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
     xvalid[mt] = t < p.M;
     xrow[mt] = p.xq + (xvalid[mt] ? t : 0) * (int64_t)p.K + 4 * tig;
     xr[mt] = min(mt * 8 + gid, p.xrows_n - 1);
+    xrowf[mt] = reinterpret_cast<const uint8_t*>(p.xq) + (xvalid[mt] ? t : 0) * (int64_t)p.K + 32 * tig;
   }
   if constexpr (FUSE) {
     // phase B: token scales from the row maxima, then the int8 rows into
-    // shared memory (round half away from zero, as vLLM's quantiser)
+    // shared memory (round half away from zero, as vLLM's quantiser).  The
+    // rotation kernel stores each group's 4-channel quads already in
+    // fragment order, so the codes land where the fragment loads want them;
+    // each group's code sum is reduced over the 16 lanes that quantise it.
     grid_dependency_wait();
     if (ctid < ntok_slice) {
       const float a = fmaxf(__uint_as_float(ld_cg_u32(p.amax + tok0 + ctid)), 1e-10f);
       tok_inv_s[ctid] = __fdiv_rn(127.0f, a);
       tok_scale_s[ctid] = __fdiv_rn(a, 127.0f);
     }
+    for (int e = ctid; e < G * MP; e += NCT)
+      if (e % MP >= ntok_slice) sxs[e] = 0;
     named_barrier(1, NCT);
     const int k8n = p.K / 8;
-    for (int e = ctid; e < ntok_slice * k8n; e += NCT) {
-      const int r = e / k8n, k8 = e - r * k8n;
-      const uint4 u = ld_cg_v4(reinterpret_cast<const uint4*>(p.rot16 + (size_t)(tok0 + r) * p.K) + k8);
-      const __half* h = reinterpret_cast<const __half*>(&u);
-      const float inv = tok_inv_s[r];
-      uint32_t w0 = 0, w1 = 0;
+    const int total = ntok_slice * k8n;   // a multiple of 16: a group is 16 items
+    constexpr int kBatch = 8;              // loads in flight per thread
+    for (int e0 = ctid; e0 < total; e0 += kBatch * NCT) {
+      uint4 u[kBatch];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        w0 |= ((uint32_t)(uint8_t)(int8_t)(int)round_half_away(__half2float(h[q]) * inv)) << (8 * q);
-        w1 |= ((uint32_t)(uint8_t)(int8_t)(int)round_half_away(__half2float(h[q + 4]) * inv)) << (8 * q);
+      for (int j = 0; j < kBatch; ++j) {
+        const int e = e0 + j * NCT;
+        if (e < total) {
+          const int r = e / k8n, k8 = e - r * k8n;
+          u[j] = ld_cg_v4(reinterpret_cast<const uint4*>(p.rot16 + (size_t)(tok0 + r) * p.K) + k8);
+        }
       }
-      *reinterpret_cast<uint2*>(xrows + (size_t)r * xstride + (size_t)k8 * 8) = make_uint2(w0, w1);
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        const int e = e0 + j * NCT;
+        const bool ok = e < total;   // uniform over each 16-lane group
+        const int r = ok ? e / k8n : 0, k8 = ok ? e - r * k8n : 0;
+        uint32_t w0 = 0, w1 = 0;
+        if (ok) {
+          const __half* h = reinterpret_cast<const __half*>(&u[j]);
+          const float inv = tok_inv_s[r];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            w0 |= ((uint32_t)(uint8_t)(int8_t)(int)round_half_away(__half2float(h[q]) * inv)) << (8 * q);
+            w1 |= ((uint32_t)(uint8_t)(int8_t)(int)round_half_away(__half2float(h[q + 4]) * inv)) << (8 * q);
+          }
+          *reinterpret_cast<uint2*>(xrows + (size_t)r * xstride + (size_t)k8 * 8) = make_uint2(w0, w1);
+        }
+        int sum = __dp4a((int)w0, 0x01010101, __dp4a((int)w1, 0x01010101, 0));
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (ok && (k8 & 15) == 0) sxs[(k8 >> 4) * MP + r] = sum;
+      }
     }
     named_barrier(1, NCT);
     // the last CTA past this point returns the maxima and the exit counter
@@ -430,19 +465,21 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
         p.gsync[1] = 0u;
       }
     }
-  }
-  if constexpr (XS) {
-    // staged rows past the slice's tokens (when a later slice is short) hold
+  } else if constexpr (XS) {
+    // Staged rows past the slice's tokens (when a later slice is short) hold
     // stale bytes, and lanes of tokens past the staged rows read the last
-    // one; both only feed output columns that are never stored
-    if (!FUSE && !mbar_wait(xbar, 0)) return;
-    // per (group, row): the group's sum, and its 32 words rearranged into
-    // fragment order: word j*4 + t (bytes 16j + 4t) moves to t*8 + j, so
-    // lane tig's eight B words are the 32 bytes at tig*32
-    for (int e = ctid; e < G * MP; e += NCT) {
-      const int g = e / MP, r = e - g * MP;
-      int sum = 0;
-      if (r < ntok_slice) {
+    // one; both only feed output columns that are never stored.  Each
+    // (row, group) block's 32 words go to fragment order (word j*4 + t,
+    // bytes 16j + 4t, to t*8 + j: lane tig's eight B words are then the 32
+    // bytes at tig*32), and its code sum to sxs.
+    grid_dependency_wait();
+    for (int e = ctid; e < G * MP; e += NCT)
+      if (e % MP >= ntok_slice) sxs[e] = 0;
+    if ((int64_t)ntok_slice * p.K > kDecBulkXBytes) {
+      // rows bulk-copied by the epilogue warp; a thread per block
+      if (!mbar_wait(xbar, 0)) return;
+      for (int e = ctid; e < ntok_slice * G; e += NCT) {
+        const int r = e / G, g = e - r * G;
         uint4* blk = reinterpret_cast<uint4*>(xrows + (size_t)r * xstride + (size_t)g * kGroup);
         uint32_t o[32];
 #pragma unroll
@@ -453,6 +490,7 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
           o[4 * c + 2] = v.z;
           o[4 * c + 3] = v.w;
         }
+        int sum = 0;
 #pragma unroll
         for (int c = 0; c < 32; ++c) sum = __dp4a((int)o[c], 0x01010101, sum);
 #pragma unroll
@@ -460,8 +498,37 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
           blk[2 * t] = make_uint4(o[t], o[4 + t], o[8 + t], o[12 + t]);
           blk[2 * t + 1] = make_uint4(o[16 + t], o[20 + t], o[24 + t], o[28 + t]);
         }
+        sxs[g * MP + r] = sum;
       }
-      sxs[e] = sum;
+    } else {
+      // small blocks: loaded straight from global memory (L2: the previous
+      // kernel just wrote them), a warp per block and a lane per word, so
+      // they do not queue behind the weight stream's bulk copies
+      const int nblk = ntok_slice * G;
+      constexpr int kBatch = 8;   // loads in flight per lane
+      for (int b0 = cw; b0 < nblk; b0 += kBatch * NC) {
+        uint32_t v[kBatch];
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+          const int blk = b0 + j * NC;
+          if (blk < nblk) {
+            const int r = blk / G, g = blk - r * G;
+            v[j] = ld_dep_u32(
+                reinterpret_cast<const uint32_t*>(p.xq + (tok0 + r) * (int64_t)p.K + (size_t)g * kGroup) + lane);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+          const int blk = b0 + j * NC;
+          if (blk < nblk) {   // uniform over the warp
+            const int r = blk / G, g = blk - r * G;
+            const int sum = __reduce_add_sync(0xffffffffu, __dp4a((int)v[j], 0x01010101, 0));
+            reinterpret_cast<uint32_t*>(xrows + (size_t)r * xstride + (size_t)g * kGroup)[(lane & 3) * 8 + (lane >> 2)] =
+                v[j];
+            if (lane == 0) sxs[g * MP + r] = sum;
+          }
+        }
+      }
     }
     named_barrier(1, NCT);
   } else {
@@ -483,7 +550,7 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
     while (g < ge) {
       const int n = min((g | 15) + 1, ge) - g;
       const int gbase = g & ~15;
-      if (!mbar_wait(&full[s], rnd & 1)) return;
+      if (!mbar_wait_sleep(&full[s], rnd & 1)) return;
 #pragma unroll
       for (int slot = 0; slot < SLOTS; ++slot) {
         const int gg = gbase + slot * NC + cw;
@@ -505,6 +572,27 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
               bf[mt][6] = b1.z;
               bf[mt][7] = b1.w;
               const int2 s2 = *reinterpret_cast<const int2*>(sxs + (size_t)gg * MP + mt * 8 + 2 * tig);
+              sx[mt][0] = s2.x;
+              sx[mt][1] = s2.y;
+            } else if constexpr (PREQ) {
+              // fragment-order rows and code sums in global memory (L2; .cg:
+              // a previous call's lines in this SM's L1 could be stale)
+              if (xvalid[mt]) {
+                const uint4 b0 = ld_l2_v4(xrowf[mt] + (size_t)gg * kGroup);
+                const uint4 b1 = ld_l2_v4(xrowf[mt] + (size_t)gg * kGroup + 16);
+                bf[mt][0] = b0.x;
+                bf[mt][1] = b0.y;
+                bf[mt][2] = b0.z;
+                bf[mt][3] = b0.w;
+                bf[mt][4] = b1.x;
+                bf[mt][5] = b1.y;
+                bf[mt][6] = b1.z;
+                bf[mt][7] = b1.w;
+              } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) bf[mt][i] = 0u;
+              }
+              const int2 s2 = ld_l2_v2(p.gsum + (size_t)gg * p.gsum_mp + tok0 + mt * 8 + 2 * tig);
               sx[mt][0] = s2.x;
               sx[mt][1] = s2.y;
             } else {
@@ -531,7 +619,7 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
     }
     // segment end: hand this warp's partial to the epilogue warp
     const int par = q & 1;
-    if (q >= 2 && !mbar_wait(&seg_free[par], ((q >> 1) - 1) & 1)) return;
+    if (q >= 2 && !mbar_wait_sleep(&seg_free[par], ((q >> 1) - 1) & 1)) return;
     float* sl = red + (size_t)(par * NC + cw) * kSlice;
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
@@ -616,6 +704,21 @@ size_t gemm_decode_workspace(int64_t M, int N) {
   return ws + (size_t)slices * (N / kRecRows) * sizeof(uint32_t);
 }
 
+// CTAs for nbk row blocks of G groups.  When the row blocks split evenly
+// into at least 3/4 as many CTAs as SMs and a CTA's share is small (at most
+// 64 records: the layer streams in a couple of microseconds), each CTA takes
+// whole row blocks: no segment is shared, so no partial sums go through the
+// workspace, whose fix-up latency would end the kernel; otherwise stream-K
+// over all SMs keeps the per-CTA byte counts equal.
+static int dec_ctas(int nbk, int G) {
+  for (int k = 1; k <= 4; ++k) {
+    if (nbk % k) continue;
+    const int c = nbk / k;
+    if (c <= g_num_sms && 4 * c >= 3 * g_num_sms && k * G <= 64) return c;
+  }
+  return (int)min64(g_num_sms, (int64_t)nbk * G);
+}
+
 static DecParams dec_params(int64_t M, int N, int K, const void* packed, const void* bias, int bias_dtype, void* out,
                             int out_dtype, void* ws) {
   init_sms();
@@ -632,7 +735,7 @@ static DecParams dec_params(int64_t M, int N, int K, const void* packed, const v
   p.ws = static_cast<float*>(ws);
   p.cnt = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(ws) + wsf);
   p.units = (int64_t)(N / kRecRows) * (K / kGroup);
-  p.ctas = (int)min64(g_num_sms, p.units);
+  p.ctas = dec_ctas(N / kRecRows, K / kGroup);
   p.stages = 0;
   return p;
 }
@@ -672,21 +775,69 @@ static cudaError_t launch_pick_fused(DecParams p, cudaStream_t st) {
   return launch_mt<MT, true, kXinRot16>(p, xs_bytes, st);
 }
 
+cudaError_t launch_quant16_decode(const __half* y, uint32_t* amax, int64_t M, int K, int Mp, int8_t* xq, float* xscale,
+                                  int* gsum, uint32_t* exit_count, cudaStream_t st);
+
+// When the rows are quantised by their own kernel instead of the GEMM's
+// prologue (measured on B200): always for large row blocks (the prologue
+// would read all of them into every CTA), and for medium ones when each CTA
+// streams few records (its prologue is then most of its time).
+static bool use_quant_kernel(int64_t M, int K, const DecParams& p) {
+  const int64_t bytes = M * (int64_t)K * 2;
+  return bytes > 64 * 1024 || (bytes > 16 * 1024 && p.units <= 64 * (int64_t)p.ctas);
+}
+
+static size_t al256(size_t b) { return (b + 255) & ~(size_t)255; }
+
+size_t linear_decode_scratch(int64_t M, int K) {
+  const size_t Mp = (size_t)8 * (M <= 8 ? 1 : M <= 16 ? 2 : M <= 32 ? 4 : 8);
+  return al256((size_t)M * K * 2) + al256((size_t)M * K) + al256((size_t)M * 4) + al256((size_t)(K / kGroup) * Mp * 4);
+}
+
+template <int MT>
+static cudaError_t launch_pick_preq(DecParams p, cudaStream_t st) {
+  p.xrows_n = 0;
+  stages_for(p, MT, 0);
+  return launch_mt<MT, false, kXinPreQ>(p, 0, st);
+}
+
 // Returns cudaErrorNotSupported (nothing launched) for shapes whose int8
 // rows do not fit in shared memory; callers then run the two kernels.
 cudaError_t launch_linear_decode(const void* x, int x_dtype, const uint16_t* cscale, const uint32_t* rtab, int64_t M,
                                  int N, int K, const void* packed, const void* bias, int bias_dtype, void* out,
                                  int out_dtype, void* ws, void* scratch, cudaStream_t st) {
   if (M > kDecMaxTokens || M <= 0) return cudaErrorNotSupported;
-  if (!xs_bytes_for(fused_mt(M), K, M)) return cudaErrorNotSupported;
   DecParams p = dec_params(M, N, K, packed, bias, bias_dtype, out, out_dtype, ws);
+  const bool preq = use_quant_kernel(M, K, p);
+  if (!preq && !xs_bytes_for(fused_mt(M), K, M)) return cudaErrorNotSupported;
   uint8_t* tail = static_cast<uint8_t*>(ws) + gemm_decode_workspace(M, N);
   p.amax = reinterpret_cast<uint32_t*>(tail);
   p.gsync = reinterpret_cast<uint32_t*>(tail + (((size_t)M * sizeof(uint32_t) + 255) & ~(size_t)255));
   __half* rot16 = static_cast<__half*>(scratch);
   p.rot16 = rot16;
-  const cudaError_t e = launch_rot16_decode(x_dtype, x, M, K, cscale, rtab, rot16, p.amax, st);
+  cudaError_t e = launch_rot16_decode(x_dtype, x, M, K, cscale, rtab, rot16, p.amax, st);
   if (e != cudaSuccess) return e;
+  if (preq) {
+    // rotation, quantisation (fragment order + code sums), then the GEMM
+    // reading its fragments from global memory
+    uint8_t* sp = static_cast<uint8_t*>(scratch) + al256((size_t)M * K * 2);
+    int8_t* xq = reinterpret_cast<int8_t*>(sp);
+    float* xs = reinterpret_cast<float*>(sp + al256((size_t)M * K));
+    int* gsum = reinterpret_cast<int*>(sp + al256((size_t)M * K) + al256((size_t)M * 4));
+    const int Mp = 8 * fused_mt(M);
+    e = launch_quant16_decode(rot16, p.amax, M, K, Mp, xq, xs, gsum, p.gsync + 1, st);
+    if (e != cudaSuccess) return e;
+    p.xq = xq;
+    p.xscale = xs;
+    p.gsum = gsum;
+    p.gsum_mp = Mp;
+    switch (fused_mt(M)) {
+      case 1: return launch_pick_preq<1>(p, st);
+      case 2: return launch_pick_preq<2>(p, st);
+      case 4: return launch_pick_preq<4>(p, st);
+    }
+    return launch_pick_preq<8>(p, st);
+  }
   switch (fused_mt(M)) {
     case 1: return launch_pick_fused<1>(p, st);
     case 2: return launch_pick_fused<2>(p, st);

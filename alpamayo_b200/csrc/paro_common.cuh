@@ -89,6 +89,11 @@ __device__ __forceinline__ float2 givens2(float2 x, float2 partner, float p, flo
 // Plain loads through const __restrict__ pointers may be compiled as
 // invariant (read-only path) loads, which the compiler is free to move above
 // the wait; volatile asm with a memory clobber keeps them in place.
+__device__ __forceinline__ uint32_t ld_dep_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 __device__ __forceinline__ float ld_dep(const float* p) {
   float v;
   asm volatile("ld.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
@@ -122,6 +127,19 @@ __device__ __forceinline__ uint4 ld_cg_v4(const void* p) {
   uint4 v;
   asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p)
                : "memory");
+  return v;
+}
+// The same without the memory clobber, for loads issued in bulk whose order
+// against other memory operations does not matter (they follow the
+// dependency wait in program order: volatile asm keeps that order).
+__device__ __forceinline__ uint4 ld_l2_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ int2 ld_l2_v2(const int* p) {
+  int2 v;
+  asm volatile("ld.global.cg.v2.s32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
   return v;
 }
 __device__ __forceinline__ void st_cg_f32(float* p, float v) {

@@ -19,6 +19,11 @@
 // of the fp16 values' bit patterns (non-negative floats order like their
 // bits), then one shared-memory atomic per warp and one global atomicMax per
 // row and CTA.
+//
+// Output order: within each group the 32 quads of 4 channels are stored in
+// the order the GEMM's mma fragments read them (quad j*4 + t at position
+// t*8 + j), so the GEMM's quantising prologue writes its int8 codes straight
+// into fragment order.  The scratch is private to the linear.
 #include "tc_ptx.cuh"
 
 namespace paro {
@@ -34,6 +39,8 @@ rot16_decode_kernel(const InT* x, int64_t M, int K, const uint16_t* __restrict__
   __shared__ uint32_t cmax[R];
   const int ch = threadIdx.x, lane = ch & 31;
   const int c = blockIdx.x * 128 + ch;
+  // where this channel's value goes: quad w = ch / 4 to position (w % 4) * 8 + w / 4
+  const int cpos = blockIdx.x * 128 + ((((ch >> 2) & 3) << 3) + (ch >> 4)) * 4 + (ch & 3);
   const int64_t r0 = (int64_t)blockIdx.y * R;
   const int nrows = M - r0 < R ? (int)(M - r0) : R;
 
@@ -70,7 +77,7 @@ rot16_decode_kernel(const InT* x, int64_t M, int K, const uint16_t* __restrict__
     const __half h = __float2half_rn(v[r]);
     uint32_t a = 0u;
     if (r < nrows) {
-      y[(r0 + r) * (int64_t)K + c] = h;
+      y[(r0 + r) * (int64_t)K + cpos] = h;
       a = __float_as_uint(fabsf(__half2float(h)));
     }
     a = __reduce_max_sync(0xffffffffu, a);
@@ -107,7 +114,7 @@ static cudaError_t launch_t(const void* x, int64_t M, int K, const uint16_t* sca
 }
 
 // amax must hold zeros for the M rows (the consuming GEMM returns it to
-// zero); y receives M x K fp16 values.
+// zero); y receives M x K fp16 values, quads in fragment order.
 cudaError_t launch_rot16_decode(int x_dtype, const void* x, int64_t M, int K, const uint16_t* scales,
                                 const uint32_t* rtab, __half* y, uint32_t* amax, cudaStream_t st) {
   if (M <= 0 || M > 65535 * 8) return cudaErrorInvalidValue;
@@ -117,6 +124,72 @@ cudaError_t launch_rot16_decode(int x_dtype, const void* x, int64_t M, int K, co
     case PARO_BF16: return launch_t<__nv_bfloat16>(x, M, K, scales, rtab, y, amax, st);
   }
   return cudaErrorInvalidValue;
+}
+
+// Quantisation of the rotated rows for long rows (the GEMM's prologue would
+// read every row from every CTA): per (group, block of 8 rows) a CTA of 128
+// threads, 16 per row, each turning 8 fp16 values into int8 with the row's
+// scale (round half away from zero, vLLM's per_token_quant_int8,
+// int8_utils.py:106-128).  The codes keep the scratch's fragment order; each
+// (row, group) code sum goes to gsum[g][row] (rows padded to a multiple of
+// 8), the token scales to xscale, and the last CTA returns amax and its exit
+// counter to zero.
+__global__ void __launch_bounds__(128)
+quant16_decode_kernel(const __half* y, uint32_t* amax, int64_t M, int K, int Mp, int8_t* __restrict__ xq,
+                      float* __restrict__ xscale, int* __restrict__ gsum, uint32_t* exit_count) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  const int t = threadIdx.x, part = t & 15;
+  const int g = blockIdx.x;
+  const int64_t r = (int64_t)blockIdx.y * 8 + (t >> 4);
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  int sum = 0;
+  if (r < M) {
+    const float a = fmaxf(__uint_as_float(ld_cg_u32(amax + r)), 1e-10f);
+    const float inv = __fdiv_rn(127.0f, a);
+    if (g == 0 && part == 0) xscale[r] = __fdiv_rn(a, 127.0f);
+    const size_t off = (size_t)r * K + (size_t)g * kGroup + part * 8;
+    const uint4 u = ld_cg_v4(y + off);
+    const __half* h = reinterpret_cast<const __half*>(&u);
+    uint32_t w0 = 0, w1 = 0;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      w0 |= ((uint32_t)(uint8_t)(int8_t)(int)round_half_away(__half2float(h[q]) * inv)) << (8 * q);
+      w1 |= ((uint32_t)(uint8_t)(int8_t)(int)round_half_away(__half2float(h[q + 4]) * inv)) << (8 * q);
+    }
+    *reinterpret_cast<uint2*>(xq + off) = make_uint2(w0, w1);
+    sum = __dp4a((int)w0, 0x01010101, __dp4a((int)w1, 0x01010101, 0));
+  }
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  if (part == 0 && r < Mp) gsum[(size_t)g * Mp + r] = sum;   // zero for padding rows
+  // every thread of the grid has read its row's maximum once all CTAs are
+  // past this point; the last one clears the maxima for the next call
+  __syncthreads();
+  if (t == 0) {
+    __threadfence();
+    const uint32_t n = gridDim.x * gridDim.y;
+    if (atomicAdd(exit_count, 1u) == n - 1) {
+      __threadfence();
+      for (int64_t i = 0; i < M; ++i) amax[i] = 0u;
+      *exit_count = 0u;
+    }
+  }
+}
+
+// Mp: rows of gsum per group (a multiple of 8, at least M; rows past M get
+// zero sums).
+cudaError_t launch_quant16_decode(const __half* y, uint32_t* amax, int64_t M, int K, int Mp, int8_t* xq,
+                                  float* xscale, int* gsum, uint32_t* exit_count, cudaStream_t st) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(K / kGroup), (unsigned)(Mp / 8), 1);
+  cfg.blockDim = dim3(128, 1, 1);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, quant16_decode_kernel, y, amax, M, K, Mp, xq, xscale, gsum, exit_count);
 }
 
 }  // namespace paro
