@@ -288,7 +288,7 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
         const uint8_t* src = p.packed + ((int64_t)nb * G + g) * kRecBytes;
         while (g < ge) {
           const int n = min((g | 15) + 1, ge) - g;
-          if (rnd > 0 && !mbar_wait_sleep(&empty[s], (rnd - 1) & 1)) {
+          if (rnd > 0 && !mbar_wait(&empty[s], (rnd - 1) & 1)) {
             ok = false;
             break;
           }
@@ -332,7 +332,7 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
       int nb, gb, ge;
       sg.get(q, nb, gb, ge);
       const int seg_units = ge - gb;
-      if (!mbar_wait_sleep(&seg_full[par], (q >> 1) & 1)) return;
+      if (!mbar_wait(&seg_full[par], (q >> 1) & 1)) return;
       float v[MT * 4];
 #pragma unroll
       for (int sl = 0; sl < MT * 4; ++sl) {
@@ -421,21 +421,28 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
     const int k8n = p.K / 8;
     const int total = ntok_slice * k8n;   // a multiple of 16: a group is 16 items
     constexpr int kBatch = 8;              // loads in flight per thread
+    // item e = (row r, 8-value column k8), walked with a running pair
+    int pr = ctid / k8n, pk = ctid - pr * k8n;
     for (int e0 = ctid; e0 < total; e0 += kBatch * NCT) {
       uint4 u[kBatch];
+      int rr[kBatch], kk[kBatch];
 #pragma unroll
       for (int j = 0; j < kBatch; ++j) {
-        const int e = e0 + j * NCT;
-        if (e < total) {
-          const int r = e / k8n, k8 = e - r * k8n;
-          u[j] = ld_cg_v4(reinterpret_cast<const uint4*>(p.rot16 + (size_t)(tok0 + r) * p.K) + k8);
+        rr[j] = pr;
+        kk[j] = pk;
+        if (e0 + j * NCT < total)
+          u[j] = ld_cg_v4(reinterpret_cast<const uint4*>(p.rot16 + (size_t)(tok0 + pr) * p.K) + pk);
+        pk += NCT;
+        while (pk >= k8n) {
+          pk -= k8n;
+          ++pr;
         }
       }
 #pragma unroll
       for (int j = 0; j < kBatch; ++j) {
         const int e = e0 + j * NCT;
         const bool ok = e < total;   // uniform over each 16-lane group
-        const int r = ok ? e / k8n : 0, k8 = ok ? e - r * k8n : 0;
+        const int r = rr[j], k8 = kk[j];
         uint32_t w0 = 0, w1 = 0;
         if (ok) {
           const __half* h = reinterpret_cast<const __half*>(&u[j]);
@@ -504,28 +511,37 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
       // small blocks: loaded straight from global memory (L2: the previous
       // kernel just wrote them), a warp per block and a lane per word, so
       // they do not queue behind the weight stream's bulk copies
-      const int nblk = ntok_slice * G;
+      // warp cw takes blocks cw, cw + NC, ... of the row-major (row, group)
+      // order, walked with a running (row, group) pair
       constexpr int kBatch = 8;   // loads in flight per lane
-      for (int b0 = cw; b0 < nblk; b0 += kBatch * NC) {
+      int r = 0, g = cw;
+      while (g >= G) {
+        g -= G;
+        ++r;
+      }
+      while (r < ntok_slice) {
         uint32_t v[kBatch];
+        int rr[kBatch], gg[kBatch];
 #pragma unroll
         for (int j = 0; j < kBatch; ++j) {
-          const int blk = b0 + j * NC;
-          if (blk < nblk) {
-            const int r = blk / G, g = blk - r * G;
+          rr[j] = r;
+          gg[j] = g;
+          if (r < ntok_slice)
             v[j] = ld_dep_u32(
                 reinterpret_cast<const uint32_t*>(p.xq + (tok0 + r) * (int64_t)p.K + (size_t)g * kGroup) + lane);
+          g += NC;
+          while (g >= G) {
+            g -= G;
+            ++r;
           }
         }
 #pragma unroll
         for (int j = 0; j < kBatch; ++j) {
-          const int blk = b0 + j * NC;
-          if (blk < nblk) {   // uniform over the warp
-            const int r = blk / G, g = blk - r * G;
+          if (rr[j] < ntok_slice) {   // uniform over the warp
             const int sum = __reduce_add_sync(0xffffffffu, __dp4a((int)v[j], 0x01010101, 0));
-            reinterpret_cast<uint32_t*>(xrows + (size_t)r * xstride + (size_t)g * kGroup)[(lane & 3) * 8 + (lane >> 2)] =
-                v[j];
-            if (lane == 0) sxs[g * MP + r] = sum;
+            reinterpret_cast<uint32_t*>(xrows + (size_t)rr[j] * xstride + (size_t)gg[j] * kGroup)
+                [(lane & 3) * 8 + (lane >> 2)] = v[j];
+            if (lane == 0) sxs[gg[j] * MP + rr[j]] = sum;
           }
         }
       }
@@ -550,7 +566,7 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
     while (g < ge) {
       const int n = min((g | 15) + 1, ge) - g;
       const int gbase = g & ~15;
-      if (!mbar_wait_sleep(&full[s], rnd & 1)) return;
+      if (!mbar_wait(&full[s], rnd & 1)) return;
 #pragma unroll
       for (int slot = 0; slot < SLOTS; ++slot) {
         const int gg = gbase + slot * NC + cw;
@@ -619,7 +635,7 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
     }
     // segment end: hand this warp's partial to the epilogue warp
     const int par = q & 1;
-    if (q >= 2 && !mbar_wait_sleep(&seg_free[par], ((q >> 1) - 1) & 1)) return;
+    if (q >= 2 && !mbar_wait(&seg_free[par], ((q >> 1) - 1) & 1)) return;
     float* sl = red + (size_t)(par * NC + cw) * kSlice;
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
