@@ -58,34 +58,6 @@ __device__ __forceinline__ uint32_t mbar_try_wait(uint64_t* bar, uint32_t parity
   return ok;
 }
 
-// try_wait with a suspend-time hint: the thread sleeps (without issuing)
-// until the phase completes or about `ns` nanoseconds pass.
-__device__ __forceinline__ uint32_t mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t ns) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
-      : "memory");
-  return ok;
-}
-
-// mbar_wait for a thread that usually waits (a producer whose ring is full,
-// an epilogue warp between segments): it suspends instead of spinning, so
-// the warps that do the work keep the issue slots.  Bounded like mbar_wait.
-__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity,
-                                                long long limit_cycles = 1000000000LL) {
-  if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
-  const long long t0 = clock64();
-  while (!mbar_try_wait_sleep(bar, parity, 20000u)) {
-    if (clock64() - t0 > limit_cycles) {
-      report_error(kErrMbarTimeout);
-      return false;
-    }
-  }
-  return true;
-}
-
 // Wait for the phase with the given parity to complete.  Gives up after
 // ~`limit_cycles` SM clocks (about half a second at the default), reports
 // kErrMbarTimeout and returns false, so a broken pipeline ends the kernel
