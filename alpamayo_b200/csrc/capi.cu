@@ -53,6 +53,7 @@ cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int
 namespace paro {
 uint32_t error_word_decode(int clear);
 uint32_t error_word_tc(int clear);
+uint32_t error_word_rtc(int clear);
 
 cudaError_t ensure_smem_limit(const void* kernel, int bytes) {
   static std::mutex mu;
@@ -311,9 +312,9 @@ int paro_silu_mul(const void* x, int64_t M, int I, void* out, paro_stream_t stre
 }
 
 int paro_device_error_word(int clear) {
-  const uint32_t a = error_word_decode(clear), b = error_word_tc(clear);
-  if (a == ~0u || b == ~0u) return -1;
-  return (int)(a | b);
+  const uint32_t a = error_word_decode(clear), b = error_word_tc(clear), c = error_word_rtc(clear);
+  if (a == ~0u || b == ~0u || c == ~0u) return -1;
+  return (int)(a | b | c);
 }
 
 int paro_w4a8_gemm(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,

@@ -24,6 +24,8 @@
 // and sums rounded separately); the packed pair instructions give the same
 // values except, very rarely, in the last bit, so a code may differ from the
 // single-pass kernel's by one step about once per million.
+#include <type_traits>
+
 #include "tc_ptx.cuh"
 
 namespace paro {
@@ -143,6 +145,9 @@ quant_rows_kernel(const __half* __restrict__ y, const uint32_t* __restrict__ ama
   }
 }
 
+cudaError_t launch_rot_tc(const void* x, int64_t M, int K, const uint16_t* scales, const uint32_t* rtab, __half* y,
+                          uint32_t* amax, cudaStream_t st);
+
 template <typename InT>
 static cudaError_t launch_rows_t(const void* x, int64_t M, int K, const uint16_t* scales, const uint32_t* rtab,
                                  int8_t* q, float* s, void* ws, cudaStream_t st) {
@@ -152,9 +157,14 @@ static cudaError_t launch_rows_t(const void* x, int64_t M, int K, const uint16_t
   cudaError_t e = cudaMemsetAsync(amax, 0, (size_t)M * sizeof(uint32_t), st);
   if (e != cudaSuccess) return e;
   const int G = K / kGroup;
-  dim3 grid1((unsigned)((G + kRowsGB - 1) / kRowsGB), (unsigned)((M + kRowsRB - 1) / kRowsRB));
-  rot_rows_kernel<InT><<<grid1, 128 * kRowsGB, 0, st>>>(static_cast<const InT*>(x), M, K, scales, rtab, y, amax);
-  e = cudaGetLastError();
+  if constexpr (std::is_same<InT, __nv_bfloat16>::value) {
+    // bf16 rows: the rotation on the tensor cores (rotq_tc.cu)
+    e = launch_rot_tc(x, M, K, scales, rtab, y, amax, st);
+  } else {
+    dim3 grid1((unsigned)((G + kRowsGB - 1) / kRowsGB), (unsigned)((M + kRowsRB - 1) / kRowsRB));
+    rot_rows_kernel<InT><<<grid1, 128 * kRowsGB, 0, st>>>(static_cast<const InT*>(x), M, K, scales, rtab, y, amax);
+    e = cudaGetLastError();
+  }
   if (e != cudaSuccess) return e;
   const int vec_ok = (reinterpret_cast<uintptr_t>(q) & 7) == 0;
   quant_rows_kernel<<<(unsigned)M, 256, 0, st>>>(y, amax, K, vec_ok, q, s);

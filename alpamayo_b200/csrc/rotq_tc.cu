@@ -1,0 +1,372 @@
+// rotq_tc.cu — the rotation pass of the prefill activation path on the
+// tensor cores (tcgen05 kind::f16, fp32 accumulators in tensor memory),
+// sm_100a, for bf16 activations.
+//
+// The eight Givens layers of a 128-channel group, with the channel scales in
+// front, are one linear map: y_g = R_g (s_g ⊙ x_g), R_g a 128 x 128
+// orthogonal matrix.  Applied layer by layer (rotq_rows.cu) every layer moves
+// every value through shared memory, and that exchange bounds the pass; here
+// each CTA builds R'_g = R_g diag(s_g) once, and the tensor core applies it to
+// 128-row tiles: Y[rows, 128] = X[rows, 128] R'_g^T.
+//
+//  * Build (all 256 threads, once per group): thread (half h, row n) carries
+//    component n of the 64 unit vectors e_k, k in half h, through the eight
+//    layers (the activation kernels' arithmetic: both products and the sum
+//    rounded separately, angles from __sincosf), exchanging with the
+//    partner's thread through shared memory once per layer; column k is
+//    then scaled by s_k.  R' is split into bf16 hi + lo (hi = bf16(R'), lo =
+//    bf16(R' - hi)) and written in the UMMA K-major 128-byte-swizzle layout.
+//  * Producer thread: tensor TMA of the 128-row x 128-channel bf16 tile
+//    (two 64-channel boxes, 128-byte swizzle), 3 stages.
+//  * MMA thread: 8 MMAs (M = 128 rows, N = 128 channels, K = 16) with R'_hi,
+//    then 8 with R'_lo, into one of two 128-column TMEM buffers.  x is exact
+//    in bf16, so Y = X hi^T + X lo^T carries R' to about 2^-16 relative:
+//    far below the fp16 spacing the result is rounded to.
+//  * Epilogue (4 warps, TMEM lanes = rows): each thread reads its row's 128
+//    outputs, rounds them to fp16 — the value the reference's rotate kernel
+//    stores (rotation.cuh:333-334) — stores them, and folds their |max| into
+//    the row's maximum (atomicMax on the bit pattern).  quant_rows_kernel
+//    then quantises per token (rotq_rows.cu).
+//
+// A CTA owns one group and a contiguous range of its row tiles (groups are
+// spread over the grid first).  Waits are bounded (kErrMbarTimeout), tensor
+// memory is freed on every exit.  No load uses cluster multicast.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "tc_ptx.cuh"
+
+namespace paro {
+
+PARO_DEFINE_ERROR_ACCESSOR(rtc)
+
+namespace {
+
+constexpr int kRtThreads = 256;
+constexpr int kRtStages = 3;
+constexpr int kRtRows = 128;                     // rows per tile (MMA M)
+constexpr int kRtTileBytes = kRtRows * 128 * 2;  // 32 KB bf16 tile
+constexpr int kRtRBytes = 128 * 128 * 2;         // one bf16 128 x 128 matrix
+// shared memory plan (from a 1024-byte aligned base)
+constexpr int kOffRhi = 0;
+constexpr int kOffRlo = kOffRhi + kRtRBytes;
+constexpr int kOffX = kOffRlo + kRtRBytes;
+constexpr int kOffEx = kOffX + kRtStages * kRtTileBytes;   // [2 halves][32 cols][128 rows] f32 exchange
+constexpr int kOffTab = kOffEx + 2 * 32 * 128 * 4;          // [8 layers][128] table words
+constexpr int kOffBar = kOffTab + 8 * 128 * 4;
+constexpr int kRtSmem = kOffBar + 256 + 1024;
+
+// kind::f16 instruction descriptor: f32 accumulate, A and B bf16, both
+// K-major, N = 128, M = 128
+constexpr uint32_t kRtIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(128 >> 3) << 17) |
+                              ((uint32_t)(128 >> 4) << 24);
+
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(da), "l"(db), "r"(kRtIdesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+        "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+        "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+        "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// byte offset of element (row n, column k) of a 128 x 128 bf16 K-major
+// matrix in the 128-byte-swizzle layout: two 16 KB halves along k, 8-row
+// atoms of 1024 bytes, 16-byte chunks XOR-swizzled by the row within the atom
+__device__ __forceinline__ uint32_t sw128_off(int n, int k) {
+  const int h = k >> 6, c = (k >> 3) & 7, e = k & 7;
+  return (uint32_t)(h * 16384 + (n >> 3) * 1024 + (n & 7) * 128 + ((c ^ (n & 7)) << 4) + e * 2);
+}
+
+}  // namespace
+
+struct RtParams {
+  int64_t M;
+  int K, G;
+  int tiles;        // row tiles of 128
+  int splits;       // CTAs per group
+  const uint16_t* scales;  // fp16 [K] or null
+  const uint32_t* rtab;    // [8, K]
+  __half* y;               // [M, K] fp16 out
+  uint32_t* amax;          // [M] row |max| bits (zero on entry)
+};
+
+__global__ void __launch_bounds__(kRtThreads, 1) rot_tc_kernel(const __grid_constant__ CUtensorMap xmap, RtParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBar);   // [3] tile landed
+  uint64_t* freed = full + kRtStages;                               // [3] MMAs done with the tile
+  uint64_t* acc_full = freed + kRtStages;                           // [2]
+  uint64_t* acc_empty = acc_full + 2;                               // [2] 4 epilogue warps
+  uint64_t* mma_done = acc_empty + 2;                               // [1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = threadIdx.x;
+  // this CTA's group and row tiles
+  const int part = blockIdx.x / p.G;
+  const int g = blockIdx.x - part * p.G;
+  const int tb = (int)((int64_t)part * p.tiles / p.splits);
+  const int te = (int)((int64_t)(part + 1) * p.tiles / p.splits);
+  const int ntile = te - tb;
+
+  if (t == 0) {
+    for (int s = 0; s < kRtStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&freed[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    mbar_init(mma_done, 1);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_u32(tmem_slot))
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  // the group's table words, for the build
+  uint32_t* tab = reinterpret_cast<uint32_t*>(smem + kOffTab);
+  for (int i = t; i < 8 * 128; i += kRtThreads) tab[i] = __ldg(p.rtab + (size_t)(i >> 7) * p.K + g * 128 + (i & 127));
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // the first tiles' loads go out before the build
+  if (t == 0) {
+    for (int i = 0; i < kRtStages && i < ntile; ++i) {
+      mbar_arrive_expect_tx(&full[i], kRtTileBytes);
+      const int y0 = (tb + i) * kRtRows;
+      tma_load_2d(smem + kOffX + i * kRtTileBytes, &xmap, g * 128, y0, &full[i]);
+      tma_load_2d(smem + kOffX + i * kRtTileBytes + 16384, &xmap, g * 128 + 64, y0, &full[i]);
+    }
+  }
+
+  // ---- build R'_g = R_g diag(s_g), split into bf16 hi + lo -------------
+  {
+    const int h = t >> 7, n = t & 127;   // half h: columns k = 64h .. 64h + 63
+    float* ex = reinterpret_cast<float*>(smem + kOffEx) + h * (32 * 128);   // [32 cols][128 rows]
+    for (int c0 = 0; c0 < 64; c0 += 32) {
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = (n == 64 * h + c0 + j) ? 1.f : 0.f;
+#pragma unroll 1
+      for (int l = 0; l < 8; ++l) {
+        const uint32_t w = tab[l * 128 + n];
+        const int partner = (int)(w & 0x7F);
+        float s_, c_;
+        __sincosf(half_bits_to_f32((uint16_t)(w >> 16)), &s_, &c_);
+        const float cp = ((w >> 7) & 1) ? -s_ : s_;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) ex[j * 128 + n] = v[j];
+        named_barrier(1 + h, 128);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = givens(v[j], ex[j * 128 + partner], c_, cp);
+        named_barrier(1 + h, 128);
+      }
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          float a[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int k = 64 * h + c0 + j + 2 * q + e;
+            a[e] = v[j + 2 * q + e] * (p.scales ? half_bits_to_f32(p.scales[g * 128 + k]) : 1.f);
+          }
+          const __nv_bfloat162 bh = __floats2bfloat162_rn(a[0], a[1]);
+          const float2 fh = __bfloat1622float2(bh);
+          const __nv_bfloat162 bl = __floats2bfloat162_rn(a[0] - fh.x, a[1] - fh.y);
+          hi[q] = *reinterpret_cast<const uint32_t*>(&bh);
+          lo[q] = *reinterpret_cast<const uint32_t*>(&bl);
+        }
+        const uint32_t off = sw128_off(n, 64 * h + c0 + j);
+        *reinterpret_cast<uint4*>(smem + kOffRhi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4*>(smem + kOffRlo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+      }
+    }
+  }
+  fence_proxy_async_smem();   // generic-proxy writes of R' -> visible to the tensor core
+  __syncthreads();
+
+  bool failed = false;
+  if (warp == 0) {
+    if (lane == 0) {
+      // producer: tiles kRtStages.. of this CTA's range
+      for (int i = kRtStages; i < ntile; ++i) {
+        const int s = i % kRtStages;
+        if (!mbar_wait(&freed[s], ((i / kRtStages) - 1) & 1)) break;
+        mbar_arrive_expect_tx(&full[s], kRtTileBytes);
+        const int y0 = (tb + i) * kRtRows;
+        tma_load_2d(smem + kOffX + s * kRtTileBytes, &xmap, g * 128, y0, &full[s]);
+        tma_load_2d(smem + kOffX + s * kRtTileBytes + 16384, &xmap, g * 128 + 64, y0, &full[s]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t x_base = smem_u32(smem + kOffX);
+      const uint32_t rh = smem_u32(smem + kOffRhi), rl = smem_u32(smem + kOffRlo);
+      for (int i = 0; i < ntile; ++i) {
+        const int s = i % kRtStages, b = i & 1;
+        if (!mbar_wait(&full[s], (i / kRtStages) & 1) || !mbar_wait(&acc_empty[b], ((i >> 1) & 1) ^ 1)) break;
+        fence_after();
+        const uint32_t d = tmem + (uint32_t)(b * 128);
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint32_t koff = (uint32_t)((ks >> 2) * 16384 + (ks & 3) * 32);
+          mma_bf16(d, desc_sw128(x_base + s * kRtTileBytes + koff), desc_sw128(rh + koff), ks > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const uint32_t koff = (uint32_t)((ks >> 2) * 16384 + (ks & 3) * 32);
+          mma_bf16(d, desc_sw128(x_base + s * kRtTileBytes + koff), desc_sw128(rl + koff), 1u);
+        }
+        umma_commit(&freed[s]);
+        umma_commit(&acc_full[b]);
+      }
+      umma_commit(mma_done);
+      mbar_wait(mma_done, 0);
+    }
+  } else if (warp >= 4) {
+    // epilogue: thread = row within the tile (TMEM lane)
+    const int q4 = warp & 3;
+    const int r = q4 * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
+    for (int i = 0; i < ntile && !failed; ++i) {
+      const int b = i & 1;
+      if (!mbar_wait(&acc_full[b], (i >> 1) & 1)) {
+        failed = true;
+        break;
+      }
+      fence_after();
+      const int64_t row = (int64_t)(tb + i) * kRtRows + r;
+      __half* yr = p.y + row * p.K + g * 128;
+      uint32_t mx = 0u;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_base + (uint32_t)(b * 128 + c * 32), v);
+        tmem_wait_ld();
+        uint32_t hv[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const __half2 hh = __floats2half2_rn(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
+          hv[j] = *reinterpret_cast<const uint32_t*>(&hh);
+          const float2 f = __half22float2(hh);
+          mx = max(mx, max(__float_as_uint(fabsf(f.x)), __float_as_uint(fabsf(f.y))));
+        }
+        if (row < p.M) {
+          uint4* dst = reinterpret_cast<uint4*>(yr + c * 32);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) dst[j] = make_uint4(hv[4 * j], hv[4 * j + 1], hv[4 * j + 2], hv[4 * j + 3]);
+        }
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);
+      if (row < p.M && mx) atomicMax(p.amax + row, mx);
+    }
+  }
+
+  fence_before();
+  __syncthreads();
+  fence_after();
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 rt_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }
+  return fn;
+}
+
+static int g_rt_sms = 0;
+
+// The rotation pass for bf16 x [M, K] (K % 128 == 0, 16-byte aligned rows):
+// y fp16 [M, K] and row maxima (amax zeroed by the caller).
+cudaError_t launch_rot_tc(const void* x, int64_t M, int K, const uint16_t* scales, const uint32_t* rtab, __half* y,
+                          uint32_t* amax, cudaStream_t st) {
+  if (M <= 0 || M > 0x7FFFFFFF) return cudaErrorInvalidValue;
+  auto encode = rt_encode();
+  if (!encode) return cudaErrorNotSupported;
+  if (g_rt_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_rt_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (g_rt_sms <= 0) g_rt_sms = 148;
+  }
+  CUtensorMap xmap;
+  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+  const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)kRtRows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode(&xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  RtParams p;
+  p.M = M;
+  p.K = K;
+  p.G = K / kGroup;
+  p.tiles = (int)((M + kRtRows - 1) / kRtRows);
+  int splits = g_rt_sms / p.G;
+  if (splits < 1) splits = 1;
+  if (splits > p.tiles) splits = p.tiles;
+  p.splits = splits;
+  p.scales = scales;
+  p.rtab = rtab;
+  p.y = y;
+  p.amax = amax;
+  cudaError_t e = ensure_smem_limit((const void*)rot_tc_kernel, kRtSmem);
+  if (e != cudaSuccess) return e;
+  rot_tc_kernel<<<(unsigned)(p.G * splits), kRtThreads, kRtSmem, st>>>(xmap, p);
+  return cudaGetLastError();
+}
+
+}  // namespace paro

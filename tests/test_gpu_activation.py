@@ -191,10 +191,14 @@ def test_rotq_ragged_rows_and_large_k(ops, M):
                                      (520, 256, torch.float32)])
 def test_rotq_two_pass_path_matches_fused_kernel_and_oracle(ops, M, K, xdt):
     """Prefill sizes run the two-pass path (rotation into an fp16 workspace,
-    then quantisation).  It does the cluster kernel's arithmetic on packed
-    row pairs, so its codes match the single-pass kernel's (C ABI without
-    workspace) up to the code tolerance (a handful of 1-LSB flips per
-    million), and the oracle's on sampled rows within the same tolerance."""
+    then quantisation).  For fp16 / fp32 rows the rotation does the cluster
+    kernel's arithmetic on packed row pairs, so its codes match the
+    single-pass kernel's (C ABI without workspace) up to a handful of 1-LSB
+    flips per million.  bf16 rows are rotated on the tensor cores as one
+    matrix per group (bf16 hi + lo split of the composed rotation), whose
+    rounding differs from the layer-by-layer chain by about 2^-16 relative:
+    their codes are held to the code tolerance.  Both are checked against
+    the oracle on sampled rows within the code tolerance."""
     from alpamayo_b200 import _native
     L = _native.capi()
     assert L.paro_rotq_int8_workspace_size(M, K, 1) > 0
@@ -212,8 +216,9 @@ def test_rotq_two_pass_path_matches_fused_kernel_and_oracle(ops, M, K, xdt):
     assert st == 0
     torch.cuda.synchronize()
     check_codes(q.cpu().numpy(), q1.cpu().numpy(), s.cpu().numpy().reshape(-1), s1.cpu().numpy().reshape(-1))
-    assert (q.int() - q1.int()).abs().gt(0).float().mean().item() <= 1e-5
-    rows = np.sort(np.random.default_rng(M).choice(M, size=24, replace=False))
+    if xdt != torch.bfloat16:
+        assert (q.int() - q1.int()).abs().gt(0).float().mean().item() <= 1e-5
+    rows = np.sort(np.random.default_rng(M).choice(M, size=48, replace=False))
     q_ref, s_ref, _ = O.rot_quant_reference(xt.float().cpu().numpy()[rows], pairs, theta.astype(np.float32),
                                             cs.astype(np.float32))
     check_codes(q.cpu().numpy()[rows], q_ref, s.cpu().numpy().reshape(-1)[rows], s_ref)
