@@ -121,26 +121,43 @@ rot_rows_kernel(const InT* __restrict__ x, int64_t M, int K, const uint16_t* __r
   }
 }
 
+// A warp per row (8 rows per CTA): the lanes request their share of the
+// row, 8 loads in flight each, together with the row's maximum.
 __global__ void __launch_bounds__(256)
-quant_rows_kernel(const __half* __restrict__ y, const uint32_t* __restrict__ amax, int K, int vec_ok,
+quant_rows_kernel(const __half* __restrict__ y, const uint32_t* __restrict__ amax, int64_t M, int K, int vec_ok,
                   int8_t* __restrict__ out_q, float* __restrict__ out_scale) {
-  const int64_t row = blockIdx.x;
-  const float a = fmaxf(__uint_as_float(amax[row]), 1e-10f);
-  const float inv = __fdiv_rn(127.0f, a);
-  if (threadIdx.x == 0) out_scale[row] = __fdiv_rn(a, 127.0f);
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (row >= M) return;
   const __half* yr = y + row * (int64_t)K;
   int8_t* qr = out_q + row * (int64_t)K;
-  for (int k = threadIdx.x * 8; k < K; k += blockDim.x * 8) {
-    const uint4 u = *reinterpret_cast<const uint4*>(yr + k);
-    const __half* h = reinterpret_cast<const __half*>(&u);
-    int8_t q[8];
+  const int n8 = K / 8;
+  constexpr int kBatch = 8;
+  for (int i0 = lane; i0 < n8; i0 += kBatch * 32) {
+    uint4 u[kBatch];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) q[e] = (int8_t)(int)round_half_away(__half2float(h[e]) * inv);
-    if (vec_ok) {
-      *reinterpret_cast<uint2*>(qr + k) = *reinterpret_cast<const uint2*>(q);
-    } else {
+    for (int j = 0; j < kBatch; ++j) {
+      const int i = i0 + j * 32;
+      if (i < n8) u[j] = *reinterpret_cast<const uint4*>(yr + (size_t)i * 8);
+    }
+    const float a = fmaxf(__uint_as_float(amax[row]), 1e-10f);
+    const float inv = __fdiv_rn(127.0f, a);
+    if (i0 == 0) out_scale[row] = __fdiv_rn(a, 127.0f);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) qr[k + e] = q[e];
+    for (int j = 0; j < kBatch; ++j) {
+      const int i = i0 + j * 32;
+      if (i < n8) {
+        const __half* h = reinterpret_cast<const __half*>(&u[j]);
+        int8_t q[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) q[e] = (int8_t)(int)round_half_away(__half2float(h[e]) * inv);
+        if (vec_ok) {
+          *reinterpret_cast<uint2*>(qr + (size_t)i * 8) = *reinterpret_cast<const uint2*>(q);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) qr[(size_t)i * 8 + e] = q[e];
+        }
+      }
     }
   }
 }
@@ -167,7 +184,7 @@ static cudaError_t launch_rows_t(const void* x, int64_t M, int K, const uint16_t
   }
   if (e != cudaSuccess) return e;
   const int vec_ok = (reinterpret_cast<uintptr_t>(q) & 7) == 0;
-  quant_rows_kernel<<<(unsigned)M, 256, 0, st>>>(y, amax, K, vec_ok, q, s);
+  quant_rows_kernel<<<(unsigned)((M + 7) / 8), 256, 0, st>>>(y, amax, M, K, vec_ok, q, s);
   return cudaGetLastError();
 }
 

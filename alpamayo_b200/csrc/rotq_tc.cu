@@ -9,23 +9,25 @@
 // each CTA builds R'_g = R_g diag(s_g) once, and the tensor core applies it to
 // 128-row tiles: Y[rows, 128] = X[rows, 128] R'_g^T.
 //
-//  * Build (all 256 threads, once per group): thread (half h, row n) carries
+//  * Build (256 threads, once per group): thread (half h, row n) carries
 //    component n of the 64 unit vectors e_k, k in half h, through the eight
 //    layers (the activation kernels' arithmetic: both products and the sum
 //    rounded separately, angles from __sincosf), exchanging with the
 //    partner's thread through shared memory once per layer; column k is
 //    then scaled by s_k.  R' is split into bf16 hi + lo (hi = bf16(R'), lo =
 //    bf16(R' - hi)) and written in the UMMA K-major 128-byte-swizzle layout.
+//    The first tiles' loads are issued before it.
 //  * Producer thread: tensor TMA of the 128-row x 128-channel bf16 tile
 //    (two 64-channel boxes, 128-byte swizzle), 3 stages.
 //  * MMA thread: 8 MMAs (M = 128 rows, N = 128 channels, K = 16) with R'_hi,
 //    then 8 with R'_lo, into one of two 128-column TMEM buffers.  x is exact
 //    in bf16, so Y = X hi^T + X lo^T carries R' to about 2^-16 relative:
 //    far below the fp16 spacing the result is rounded to.
-//  * Epilogue (4 warps, TMEM lanes = rows): each thread reads its row's 128
-//    outputs, rounds them to fp16 — the value the reference's rotate kernel
-//    stores (rotation.cuh:333-334) — stores them, and folds their |max| into
-//    the row's maximum (atomicMax on the bit pattern).  quant_rows_kernel
+//  * Epilogue (8 warps, TMEM lanes = rows, two warps per lane quarter): each
+//    thread reads 64 of its row's 128 outputs, rounds them to fp16 — the
+//    value the reference's rotate kernel stores (rotation.cuh:333-334) —
+//    stores them, and folds their |max| into the row's maximum (atomicMax
+//    on the bit pattern).  quant_rows_kernel
 //    then quantises per token (rotq_rows.cu).
 //
 // A CTA owns one group and a contiguous range of its row tiles (groups are
@@ -42,7 +44,7 @@ PARO_DEFINE_ERROR_ACCESSOR(rtc)
 
 namespace {
 
-constexpr int kRtThreads = 256;
+constexpr int kRtThreads = 384;   // producer, MMA, 2 idle, 8 epilogue warps
 constexpr int kRtStages = 3;
 constexpr int kRtRows = 128;                     // rows per tile (MMA M)
 constexpr int kRtTileBytes = kRtRows * 128 * 2;  // 32 KB bf16 tile
@@ -51,7 +53,8 @@ constexpr int kRtRBytes = 128 * 128 * 2;         // one bf16 128 x 128 matrix
 constexpr int kOffRhi = 0;
 constexpr int kOffRlo = kOffRhi + kRtRBytes;
 constexpr int kOffX = kOffRlo + kRtRBytes;
-constexpr int kOffEx = kOffX + kRtStages * kRtTileBytes;   // [2 halves][32 cols][128 rows] f32 exchange
+constexpr int kOffEx = kOffX + kRtStages * kRtTileBytes;   // build: [2 halves][32 cols][128 rows] f32 exchange;
+                                                            // epilogue: the fp16 output tile (32 KB)
 constexpr int kOffTab = kOffEx + 2 * 32 * 128 * 4;          // [8 layers][128] table words
 constexpr int kOffBar = kOffTab + 8 * 128 * 4;
 constexpr int kRtSmem = kOffBar + 256 + 1024;
@@ -124,13 +127,14 @@ struct RtParams {
   uint32_t* amax;          // [M] row |max| bits (zero on entry)
 };
 
-__global__ void __launch_bounds__(kRtThreads, 1) rot_tc_kernel(const __grid_constant__ CUtensorMap xmap, RtParams p) {
+__global__ void __launch_bounds__(kRtThreads, 1) rot_tc_kernel(const __grid_constant__ CUtensorMap xmap,
+                                                               const __grid_constant__ CUtensorMap ymap, RtParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBar);   // [3] tile landed
   uint64_t* freed = full + kRtStages;                               // [3] MMAs done with the tile
   uint64_t* acc_full = freed + kRtStages;                           // [2]
-  uint64_t* acc_empty = acc_full + 2;                               // [2] 4 epilogue warps
+  uint64_t* acc_empty = acc_full + 2;                               // [2] 8 epilogue warps
   uint64_t* mma_done = acc_empty + 2;                               // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
 
@@ -150,7 +154,7 @@ __global__ void __launch_bounds__(kRtThreads, 1) rot_tc_kernel(const __grid_cons
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);
+      mbar_init(&acc_empty[b], 8);
     }
     mbar_init(mma_done, 1);
     fence_mbar_init();
@@ -179,7 +183,7 @@ __global__ void __launch_bounds__(kRtThreads, 1) rot_tc_kernel(const __grid_cons
   }
 
   // ---- build R'_g = R_g diag(s_g), split into bf16 hi + lo -------------
-  {
+  if (t < 256) {
     const int h = t >> 7, n = t & 127;   // half h: columns k = 64h .. 64h + 63
     float* ex = reinterpret_cast<float*>(smem + kOffEx) + h * (32 * 128);   // [32 cols][128 rows]
     for (int c0 = 0; c0 < 64; c0 += 32) {
@@ -265,44 +269,65 @@ __global__ void __launch_bounds__(kRtThreads, 1) rot_tc_kernel(const __grid_cons
       mbar_wait(mma_done, 0);
     }
   } else if (warp >= 4) {
-    // epilogue: thread = row within the tile (TMEM lane)
-    const int q4 = warp & 3;
+    // epilogue: thread = row within the tile (TMEM lane), warps 4-7 take
+    // channels 0-63, warps 8-11 channels 64-127.  The fp16 tile is staged in
+    // shared memory (the build's exchange area, 128-byte swizzle) and written
+    // by two tensor TMA stores, so each row's 256 bytes leave as whole lines.
+    const int q4 = warp & 3, chh = (warp - 4) >> 2;
     const int r = q4 * 32 + lane;
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
-    for (int i = 0; i < ntile && !failed; ++i) {
+    const bool issuer = warp == 4 && lane == 0;
+    uint8_t* stage_out = smem + kOffEx;
+    // every epilogue thread passes both named barriers of every tile, also
+    // after a timed-out wait (then it only skips the work)
+    for (int i = 0; i < ntile; ++i) {
       const int b = i & 1;
-      if (!mbar_wait(&acc_full[b], (i >> 1) & 1)) {
-        failed = true;
-        break;
+      if (!failed && !mbar_wait(&acc_full[b], (i >> 1) & 1)) failed = true;
+      uint32_t v[64];
+      if (!failed) {
+        fence_after();
+        tmem_ld32(tmem + lane_base + (uint32_t)(b * 128 + chh * 64), *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        tmem_ld32(tmem + lane_base + (uint32_t)(b * 128 + chh * 64 + 32),
+                  *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        tmem_wait_ld();
+        fence_before();
       }
-      fence_after();
-      const int64_t row = (int64_t)(tb + i) * kRtRows + r;
-      __half* yr = p.y + row * p.K + g * 128;
+      __syncwarp();
+      if (!failed && lane == 0) mbar_arrive(&acc_empty[b]);   // the MMA may reuse the buffer
+      // the previous tile's stores have read the staging area
+      if (issuer) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+      named_barrier(3, 256);
       uint32_t mx = 0u;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tmem + lane_base + (uint32_t)(b * 128 + c * 32), v);
-        tmem_wait_ld();
-        uint32_t hv[16];
+      for (int q = 0; q < 8 && !failed; ++q) {
+        uint32_t hv[4];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const __half2 hh = __floats2half2_rn(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1]));
-          hv[j] = *reinterpret_cast<const uint32_t*>(&hh);
+        for (int j2 = 0; j2 < 4; ++j2) {
+          const int e = q * 8 + 2 * j2;
+          const __half2 hh = __floats2half2_rn(__uint_as_float(v[e]), __uint_as_float(v[e + 1]));
+          hv[j2] = *reinterpret_cast<const uint32_t*>(&hh);
           const float2 f = __half22float2(hh);
           mx = max(mx, max(__float_as_uint(fabsf(f.x)), __float_as_uint(fabsf(f.y))));
         }
-        if (row < p.M) {
-          uint4* dst = reinterpret_cast<uint4*>(yr + c * 32);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) dst[j] = make_uint4(hv[4 * j], hv[4 * j + 1], hv[4 * j + 2], hv[4 * j + 3]);
-        }
+        *reinterpret_cast<uint4*>(stage_out + sw128_off(r, chh * 64 + q * 8)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
       }
-      fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[b]);
-      if (row < p.M && mx) atomicMax(p.amax + row, mx);
+      fence_proxy_async_smem();
+      named_barrier(3, 256);
+      const int y0 = (tb + i) * kRtRows;
+      if (issuer && !failed) {
+        // rows past M are clipped by the tensor map
+        asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(&ymap),
+                     "r"(g * 128), "r"(y0), "r"(smem_u32(stage_out))
+                     : "memory");
+        asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(&ymap),
+                     "r"(g * 128 + 64), "r"(y0), "r"(smem_u32(stage_out + 16384))
+                     : "memory");
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      }
+      const int64_t row = (int64_t)y0 + r;
+      if (!failed && row < p.M && mx) atomicMax(p.amax + row, mx);
     }
+    if (issuer) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   }
 
   fence_before();
@@ -350,6 +375,10 @@ cudaError_t launch_rot_tc(const void* x, int64_t M, int K, const uint16_t* scale
                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  CUtensorMap ymap;
+  r = encode(&ymap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
   RtParams p;
   p.M = M;
   p.K = K;
@@ -365,7 +394,7 @@ cudaError_t launch_rot_tc(const void* x, int64_t M, int K, const uint16_t* scale
   p.amax = amax;
   cudaError_t e = ensure_smem_limit((const void*)rot_tc_kernel, kRtSmem);
   if (e != cudaSuccess) return e;
-  rot_tc_kernel<<<(unsigned)(p.G * splits), kRtThreads, kRtSmem, st>>>(xmap, p);
+  rot_tc_kernel<<<(unsigned)(p.G * splits), kRtThreads, kRtSmem, st>>>(xmap, ymap, p);
   return cudaGetLastError();
 }
 
