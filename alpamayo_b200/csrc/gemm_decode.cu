@@ -14,8 +14,8 @@
 //    of the stream; the whole row blocks in between come last.
 //  * TMA bulk copies: one producer thread streams the range through a shared
 //    memory ring (cp.async.bulk + mbarrier complete_tx).  A chunk holds the
-//    records of up to 16 consecutive groups of one row block, aligned to
-//    16-group boundaries.
+//    records of up to 32 consecutive groups of one row block, aligned to
+//    32-group boundaries (a whole row block when K = 3584).
 //  * Consumer warps (16 for up to 16 tokens, 8 beyond); warp w owns the
 //    groups g = w (mod warps), so a chunk gives each warp one or two
 //    independent records.  The token slice's int8 rows are staged once per
@@ -52,8 +52,8 @@ __host__ __device__ constexpr int dec_consumers(int MT) { return MT <= 2 ? 16 : 
 // warps: producer, consumers, two epilogue warps (alternate segments, so two
 // workspace fix-ups can be in flight at once)
 __host__ __device__ constexpr int dec_threads(int MT) { return 32 * (dec_consumers(MT) + 3); }
-constexpr int kDecChunkGroups = 16;
-constexpr int kDecStageBytes = kDecChunkGroups * kRecBytes;  // 17152
+constexpr int kDecChunkGroups = 32;
+constexpr int kDecStageBytes = kDecChunkGroups * kRecBytes;  // 34304
 constexpr int kDecMaxStages = 8;
 constexpr int kDecMaxTokens = 64;   // tokens per CTA slice (8 tiles of 8)
 constexpr int kDecSmemBudget = 220 * 1024;
@@ -287,7 +287,7 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
         sg.get(i, nb, g, ge);
         const uint8_t* src = p.packed + ((int64_t)nb * G + g) * kRecBytes;
         while (g < ge) {
-          const int n = min((g | 15) + 1, ge) - g;
+          const int n = min((g | (kDecChunkGroups - 1)) + 1, ge) - g;
           if (rnd > 0 && !mbar_wait(&empty[s], (rnd - 1) & 1)) {
             ok = false;
             break;
@@ -564,8 +564,8 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
     int nb, g, ge;
     sg.get(q, nb, g, ge);
     while (g < ge) {
-      const int n = min((g | 15) + 1, ge) - g;
-      const int gbase = g & ~15;
+      const int n = min((g | (kDecChunkGroups - 1)) + 1, ge) - g;
+      const int gbase = g & ~(kDecChunkGroups - 1);
       if (!mbar_wait(&full[s], rnd & 1)) return;
 #pragma unroll
       for (int slot = 0; slot < SLOTS; ++slot) {
