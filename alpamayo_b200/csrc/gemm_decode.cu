@@ -17,8 +17,8 @@
 //    records of up to 32 consecutive groups of one row block, aligned to
 //    32-group boundaries (a whole row block when K = 3584).
 //  * Consumer warps (16 for up to 16 tokens, 8 beyond); warp w owns the
-//    groups g = w (mod warps), so a chunk gives each warp one or two
-//    independent records.  The token slice's int8 rows are staged once per
+//    groups g = w (mod warps), so a chunk gives each warp up to two (16
+//    warps) or four (8 warps) independent records.  The token slice's int8 rows are staged once per
 //    CTA in shared memory and rearranged there into mma fragment order (a
 //    lane's eight B words of a group are 32 contiguous bytes: two 16-byte
 //    loads per record); rows that do not fit are read from global memory.
