@@ -410,22 +410,14 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
     // fragment order, so the codes land where the fragment loads want them;
     // each group's code sum is reduced over the 16 lanes that quantise it.
     grid_dependency_wait();
-    if (ctid < ntok_slice) {
-      const float a = fmaxf(__uint_as_float(ld_cg_u32(p.amax + tok0 + ctid)), 1e-10f);
-      tok_inv_s[ctid] = __fdiv_rn(127.0f, a);
-      tok_scale_s[ctid] = __fdiv_rn(a, 127.0f);
-    }
-    for (int e = ctid; e < G * MP; e += NCT)
-      if (e % MP >= ntok_slice) sxs[e] = 0;
-    named_barrier(1, NCT);
     const int k8n = p.K / 8;
     const int total = ntok_slice * k8n;   // a multiple of 16: a group is 16 items
     constexpr int kBatch = 8;              // loads in flight per thread
     // item e = (row r, 8-value column k8), walked with a running pair
     int pr = ctid / k8n, pk = ctid - pr * k8n;
-    for (int e0 = ctid; e0 < total; e0 += kBatch * NCT) {
-      uint4 u[kBatch];
-      int rr[kBatch], kk[kBatch];
+    uint4 u[kBatch];
+    int rr[kBatch], kk[kBatch];
+    auto load_batch = [&](int e0) {
 #pragma unroll
       for (int j = 0; j < kBatch; ++j) {
         rr[j] = pr;
@@ -438,6 +430,19 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
           ++pr;
         }
       }
+    };
+    // the first rows are requested before the maxima: one round trip for both
+    load_batch(ctid);
+    if (ctid < ntok_slice) {
+      const float a = fmaxf(__uint_as_float(ld_cg_u32(p.amax + tok0 + ctid)), 1e-10f);
+      tok_inv_s[ctid] = __fdiv_rn(127.0f, a);
+      tok_scale_s[ctid] = __fdiv_rn(a, 127.0f);
+    }
+    for (int e = ctid; e < G * MP; e += NCT)
+      if (e % MP >= ntok_slice) sxs[e] = 0;
+    named_barrier(1, NCT);
+    for (int e0 = ctid; e0 < total; e0 += kBatch * NCT) {
+      if (e0 != ctid) load_batch(e0);
 #pragma unroll
       for (int j = 0; j < kBatch; ++j) {
         const int e = e0 + j * NCT;
