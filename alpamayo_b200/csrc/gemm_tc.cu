@@ -494,7 +494,26 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
 static int g_tc_sms = 0;
 
 // The tensor-core kernel handles token counts above the decode range.
-int gemm_tc_supported(int64_t M, int N, int K) { return M > 64 && N % kRecRows == 0 && K % kGroup == 0; }
+static int tc_sms() {
+  if (g_tc_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_tc_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (g_tc_sms <= 1) g_tc_sms = 148;
+  }
+  return g_tc_sms;
+}
+
+// The tensor-core kernel from 65 tokens; from 25 tokens too when the layer
+// alone has enough 256-row tiles to occupy most SMs (gate_up: 148), where the
+// streaming kernel's mma.sync throughput bounds it (measured on B200, the
+// whole gate_up linear: 126 us streaming vs 59 us here at 64 tokens, 61 vs
+// 58 us at 32; at 16 tokens streaming wins, 38 vs 57 us).
+int gemm_tc_supported(int64_t M, int N, int K) {
+  if (N % kRecRows || K % kGroup) return 0;
+  if (M > 64) return 1;
+  return M > 24 && (int64_t)((N + 2 * kTcRows - 1) / (2 * kTcRows)) * 5 >= (int64_t)tc_sms() * 4;
+}
 
 size_t gemm_tc_workspace(int64_t, int, int) { return 0; }
 
@@ -541,12 +560,7 @@ cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int
   const int64_t tiles = (int64_t)p.tiles_n * ((M + kTcTok - 1) / kTcTok);
   if (tiles > 0x7FFFFFFF) return cudaErrorInvalidValue;
   p.tiles = (int)tiles;
-  if (g_tc_sms == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&g_tc_sms, cudaDevAttrMultiProcessorCount, dev);
-    if (g_tc_sms <= 1) g_tc_sms = 148;
-  }
+  tc_sms();
   const int pairs = (int)(tiles < g_tc_sms / 2 ? tiles : g_tc_sms / 2);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(2 * pairs));

@@ -5,8 +5,8 @@
 Builds one seeded synthetic layer of the named projection shape (the
 7B-class decoder shapes the benchmark uses), then runs the fused activation
 kernel and the GEMM ``--iters`` times on the current GPU and prints the
-CUDA-event time of the last pair.  M <= 64 runs the streaming decode GEMM,
-larger M the tcgen05 kernel.  Meant to be launched under ``ncu -k <kernel>``
+CUDA-event time of the last pair.  M <= 64 runs the streaming decode GEMM
+(except gate_up above 24 tokens), larger M the tcgen05 kernel.  Meant to be launched under ``ncu -k <kernel>``
 with a small launch count; it holds at most a few hundred MB on the device.
 """
 from __future__ import annotations

@@ -203,8 +203,9 @@ int paro_prepare_weights_awq(const int32_t* awq_qweight, const uint16_t* awq_sca
  *               call leaves it zero-filled again (the kernels clear what they
  *               use), so one buffer serves all calls on one stream; calls that
  *               may run concurrently need separate workspaces.
- * Requires N % 16 == 0, K % 128 == 0, M >= 1.  Above 64 tokens the
- * tensor-core kernel runs (paro_w4a8_gemm_path); it needs no workspace and
+ * Requires N % 16 == 0, K % 128 == 0, M >= 1.  Above 64 tokens (above 24
+ * for layers with at least 0.8 x SMs 256-row tiles) the tensor-core kernel
+ * runs (paro_w4a8_gemm_path); it needs no workspace and
  * writes `out` with 16-byte stores, so `out` must then be 16-byte aligned.
  */
 size_t paro_w4a8_gemm_workspace_size(int64_t M, int N, int K);

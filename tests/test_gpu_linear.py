@@ -51,10 +51,12 @@ def test_linear_matches_two_kernel_route(ops, M, N, K):
     assert rel_l2(y.cpu().numpy(), y2.cpu().numpy()) <= 1e-6
 
 
-@pytest.mark.parametrize("M,N,K", [(1, 3584, 18944), (8, 3584, 18944), (4, 37888, 3584), (64, 256, 18944)])
+@pytest.mark.parametrize("M,N,K", [(1, 3584, 18944), (8, 3584, 18944), (4, 37888, 3584), (64, 256, 18944),
+                                   (40, 37888, 3584)])
 def test_linear_large_shapes(ops, M, N, K):
-    """down_proj / gate_up decode shapes, and a shape whose int8 rows do not
-    fit in shared memory (M = 64, K = 18944: activation-kernel route)."""
+    """down_proj / gate_up decode shapes, a shape whose int8 rows do not fit
+    in shared memory (M = 64, K = 18944: long-row route), and gate_up at 40
+    tokens (tensor-core GEMM below 65 tokens)."""
     L = synthetic_layer(N, K, seed=K + M)
     from alpamayo_b200 import synthetic as syn
     x = syn.make_activations(M, K, seed=M + 1)
