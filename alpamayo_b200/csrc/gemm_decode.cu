@@ -41,6 +41,7 @@
 // Record layout: for lane (gid = lane/4, tig = lane%4), the A fragment words
 // of rows gid and gid+8 for the four 32-channel steps of a group are one
 // 16-byte chunk each: low nibbles give a0/a1, high nibbles a2/a3.
+#include "stream_segs.cuh"
 #include "tc_ptx.cuh"
 
 namespace paro {
@@ -86,8 +87,6 @@ struct DecParams {
   int gsum_mp;
 };
 
-__host__ __device__ __forceinline__ int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
-__host__ __device__ __forceinline__ int64_t max64(int64_t a, int64_t b) { return a > b ? a : b; }
 
 // A = unsigned 8-bit codes (q, or 16*q from a high nibble), B = signed int8
 // activations, int32 accumulate.
@@ -177,46 +176,6 @@ __device__ __forceinline__ void process_record(const uint8_t* rec, const uint32_
   }
 }
 
-// The order in which a CTA visits its unit range [u0, u1), one row-block
-// segment at a time: the head of the last row block, the tail of the first
-// (the two segments shared with neighbouring CTAs), then the whole row blocks
-// in between.  Two divisions at set-up; a segment is then a few integer
-// operations (the producer's loop must stay short: it shares its SM
-// sub-partition with consumer warps).
-struct Segs {
-  int nb0, g0, nbL, gL1, G, n;
-  __device__ __forceinline__ Segs(int64_t u0, int64_t u1, int G_) : G(G_) {
-    if (u1 <= u0) {
-      n = nb0 = g0 = nbL = gL1 = 0;
-      return;
-    }
-    nb0 = (int)(u0 / G);
-    g0 = (int)(u0 - (int64_t)nb0 * G);
-    nbL = (int)((u1 - 1) / G);
-    gL1 = (int)(u1 - (int64_t)nbL * G);
-    n = nbL == nb0 ? 1 : nbL - nb0 + 1;
-  }
-  // segment i (0 <= i < n): row block nb, groups [gb, ge)
-  __device__ __forceinline__ void get(int i, int& nb, int& gb, int& ge) const {
-    if (nbL == nb0) {
-      nb = nb0;
-      gb = g0;
-      ge = gL1;
-    } else if (i == 0) {
-      nb = nbL;
-      gb = 0;
-      ge = gL1;
-    } else if (i == 1) {
-      nb = nb0;
-      gb = g0;
-      ge = G;
-    } else {
-      nb = nb0 + i - 1;
-      gb = 0;
-      ge = G;
-    }
-  }
-};
 
 // XS: the token slice's int8 rows are bulk-copied into shared memory (rows
 // padded by 16 bytes so that the fragment reads of a warp hit 32 distinct
@@ -370,15 +329,31 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
         }
         last = __shfl_sync(0xffffffffu, last, 0);
         if (last) {
-          for (int idx = lane; idx < kRecRows * ntok; idx += 32) {
-            const int r = idx / ntok, tt = idx - r * ntok;
-            const int n = nb * kRecRows + r;
-            const int64_t t = tok0 + tt;
-            float* wp = p.ws + (size_t)n * p.M + t;
-            const float a = ld_cg_f32(wp);
-            st_cg_f32(wp, 0.f);
-            store_out(p.out, p.out_dtype, (size_t)t * p.N + n,
-                      a * tok_scale_s[t - tok0] + bias_at(p.bias, p.bias_dtype, n));
+          // up to 8 loads per lane in flight before the first store (each
+          // load would otherwise wait out an L2 round trip on its own)
+          const int nidx = kRecRows * ntok;
+          for (int base = 0; base < nidx; base += 8 * 32) {
+            float a[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int idx = base + j * 32 + lane;
+              if (idx < nidx) {
+                const int r = idx / ntok, tt = idx - r * ntok;
+                a[j] = ld_cg_f32(p.ws + (size_t)(nb * kRecRows + r) * p.M + tok0 + tt);
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int idx = base + j * 32 + lane;
+              if (idx < nidx) {
+                const int r = idx / ntok, tt = idx - r * ntok;
+                const int n = nb * kRecRows + r;
+                const int64_t t = tok0 + tt;
+                st_cg_f32(p.ws + (size_t)n * p.M + t, 0.f);
+                store_out(p.out, p.out_dtype, (size_t)t * p.N + n,
+                          a[j] * tok_scale_s[tt] + bias_at(p.bias, p.bias_dtype, n));
+              }
+            }
           }
           __syncwarp();
           if (lane == 0) cnt[nb] = 0u;

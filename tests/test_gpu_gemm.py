@@ -69,11 +69,11 @@ def test_single_group_int32_exact(ops, M):
     assert np.array_equal(y, P)
 
 
-@pytest.mark.parametrize("M", [8, 256])
+@pytest.mark.parametrize("M", [3, 8, 12, 256])
 def test_multi_group_int32_exact_with_power_of_two_scales(ops, M):
     """Scales 2^-g keep every product and sum exact in fp32, so the output
-    must equal the exact per-group partials combined (M = 8: decode kernel,
-    M = 256: tensor-core kernel)."""
+    must equal the exact per-group partials combined (M <= 16: decode
+    kernels, M = 256: prefill tensor-core kernel)."""
     N, K = 128, 512   # 18-bit partials x 2^-3 stay within fp32's 24 bits
     G = K // 128
     rng = np.random.default_rng(1)
