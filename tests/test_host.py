@@ -73,6 +73,24 @@ def test_argument_validation_before_launch():
     assert L.paro_quant_int8(dummy, 2, 0, 256, dummy, dummy, None) == 0
 
 
+def test_gemm_kernel_choice_by_shape():
+    """The GEMM route is a pure function of the shape (host logic, no device
+    work): the streaming kernel up to 64 tokens, the tensor-core kernel
+    above, and from 25 tokens on layers with at least 0.8 x SMs 256-row
+    tiles (gate_up: N = 37888; the SM count falls back to 148 without a GPU)."""
+    from alpamayo_b200._native import capi
+    import torch
+    L = capi()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count if torch.cuda.is_available() else 148
+    assert L.paro_w4a8_gemm_path(8, 37888, 3584) == 0
+    assert L.paro_w4a8_gemm_path(24, 37888, 3584) == 0
+    assert L.paro_w4a8_gemm_path(25, 37888, 3584) == (1 if 37888 // 256 * 5 >= sms * 4 else 0)
+    assert L.paro_w4a8_gemm_path(64, 4608, 3584) == 0
+    assert L.paro_w4a8_gemm_path(64, 3584, 18944) == 0
+    assert L.paro_w4a8_gemm_path(65, 4608, 3584) == 1
+    assert L.paro_w4a8_gemm_path(65, 100, 3584) == 0   # not a whole number of 16-row records
+
+
 def test_header_has_reference_citations():
     src = open(os.path.join(ROOT, "include", "paro_b200.h")).read()
     for cite in ["rotation.cu:456-493", "int8_utils.py", "_custom_ops.py:1277-1318", "paroquant_marlin_w4a8.py"]:
