@@ -5,12 +5,13 @@
 // its prologue (gemm_decode.cu, phase B), so no kernel here waits for
 // another CTA.
 //
-// Geometry for a handful of tokens: one CTA per (group, block of R rows),
-// 128 threads, thread ch owning channel ch of the group for the R rows.  A
-// 7B-class layer has 28 (K = 3584) or 148 (K = 18944) groups, so the work
-// spreads over that many SMs instead of the 8-CTA cluster of the
-// single-pass kernel, and a CTA's critical path is one table load, one
-// activation load and 8 exchange rounds.  Per layer each thread publishes
+// Geometry for a handful of tokens: one CTA per (group, token row) (the
+// kernel is written for blocks of R rows; R = 1 is launched), 128 threads,
+// thread ch owning channel ch of the group.  A 7B-class layer has 28
+// (K = 3584) or 148 (K = 18944) groups per row, so the work spreads over
+// many SMs instead of the 8-CTA cluster of the single-pass kernel, and a
+// CTA's critical path is one table load, one activation load and 8
+// exchange rounds.  Per layer each thread publishes
 // its R values to shared memory, the CTA synchronises once, and each thread
 // reads its partner's values and applies its own half of the pair with both
 // products and the sum rounded separately (the arithmetic of the reference's
@@ -107,17 +108,18 @@ static cudaError_t launch_r(const void* x, int64_t M, int K, const uint16_t* sca
 template <typename InT>
 static cudaError_t launch_t(const void* x, int64_t M, int K, const uint16_t* scales, const uint32_t* rtab, __half* y,
                             uint32_t* amax, cudaStream_t st) {
-  if (M <= 1) return launch_r<InT, 1>(x, M, K, scales, rtab, y, amax, st);
-  if (M <= 2) return launch_r<InT, 2>(x, M, K, scales, rtab, y, amax, st);
-  if (M <= 4) return launch_r<InT, 4>(x, M, K, scales, rtab, y, amax, st);
-  return launch_r<InT, 8>(x, M, K, scales, rtab, y, amax, st);
+  // one row per CTA: a CTA with R rows runs its eight exchange rounds R
+  // times longer, and at decode sizes the kernel's latency is what the
+  // linear waits for (measured on B200, 8 tokens: R = 8 cost 2.3 us more per
+  // qkv / o linear than R = 1, 16 tokens on down 7 us more)
+  return launch_r<InT, 1>(x, M, K, scales, rtab, y, amax, st);
 }
 
 // amax must hold zeros for the M rows (the consuming GEMM returns it to
 // zero); y receives M x K fp16 values, quads in fragment order.
 cudaError_t launch_rot16_decode(int x_dtype, const void* x, int64_t M, int K, const uint16_t* scales,
                                 const uint32_t* rtab, __half* y, uint32_t* amax, cudaStream_t st) {
-  if (M <= 0 || M > 65535 * 8) return cudaErrorInvalidValue;
+  if (M <= 0 || M > 65535) return cudaErrorInvalidValue;
   switch (x_dtype) {
     case PARO_F32: return launch_t<float>(x, M, K, scales, rtab, y, amax, st);
     case PARO_F16: return launch_t<__half>(x, M, K, scales, rtab, y, amax, st);
