@@ -146,11 +146,12 @@ quant16_decode_kernel(const __half* y, uint32_t* amax, int64_t M, int K, int Mp,
   asm volatile("griddepcontrol.wait;" ::: "memory");
   int sum = 0;
   if (r < M) {
+    // both loads in flight before either value is used: one L2 round trip
+    const size_t off = (size_t)r * K + (size_t)g * kGroup + part * 8;
+    const uint4 u = ld_cg_v4(y + off);
     const float a = fmaxf(__uint_as_float(ld_cg_u32(amax + r)), 1e-10f);
     const float inv = __fdiv_rn(127.0f, a);
     if (g == 0 && part == 0) xscale[r] = __fdiv_rn(a, 127.0f);
-    const size_t off = (size_t)r * K + (size_t)g * kGroup + part * 8;
-    const uint4 u = ld_cg_v4(y + off);
     const __half* h = reinterpret_cast<const __half*>(&u);
     uint32_t w0 = 0, w1 = 0;
 #pragma unroll
