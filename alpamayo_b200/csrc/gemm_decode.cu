@@ -77,7 +77,8 @@ struct DecParams {
   // linear entry point: rotated fp16 rows from rot16_decode_kernel,
   // quantised in the kernel's prologue
   const __half* rot16;      // [M, K] rotated rows, fp16
-  uint32_t* amax;           // [M] row |max| bits, zero between calls
+  uint32_t* amax;           // [M] row |max| bits, zero between calls (kXinRot16 and
+                            // kXinPreQ: this kernel returns them to zero)
   uint32_t* gsync;          // [2] exit counter (word 1), zero between calls
   int64_t units;    // (N/16) * G
   int ctas;
@@ -273,6 +274,12 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
       // both warps write the same token scales; each reads back its own
       for (int t = lane; t < ntok_slice; t += 32) tok_scale_s[t] = p.xscale[tok0 + t];
       __syncwarp();
+    }
+    if constexpr (PREQ) {
+      // the quantiser that read the row maxima has finished: return them to
+      // zero for the next call's rotation kernel
+      if (blockIdx.x == 0 && blockIdx.y == 0 && ew == 0)
+        for (int64_t t = lane; t < p.M; t += 32) p.amax[t] = 0u;
     }
     uint32_t* cnt = p.cnt + (size_t)blockIdx.y * (p.N / kRecRows);
     if constexpr (XS && !FUSE) {
@@ -772,7 +779,7 @@ static cudaError_t launch_pick_fused(DecParams p, cudaStream_t st) {
 }
 
 cudaError_t launch_quant16_decode(const __half* y, uint32_t* amax, int64_t M, int K, int Mp, int8_t* xq, float* xscale,
-                                  int* gsum, uint32_t* exit_count, cudaStream_t st);
+                                  int* gsum, cudaStream_t st);
 
 // When the rows are quantised by their own kernel instead of the GEMM's
 // prologue (measured on B200): always for large row blocks (the prologue
@@ -821,7 +828,7 @@ cudaError_t launch_linear_decode(const void* x, int x_dtype, const uint16_t* csc
     float* xs = reinterpret_cast<float*>(sp + al256((size_t)M * K));
     int* gsum = reinterpret_cast<int*>(sp + al256((size_t)M * K) + al256((size_t)M * 4));
     const int Mp = 8 * fused_mt(M);
-    e = launch_quant16_decode(rot16, p.amax, M, K, Mp, xq, xs, gsum, p.gsync + 1, st);
+    e = launch_quant16_decode(rot16, p.amax, M, K, Mp, xq, xs, gsum, st);
     if (e != cudaSuccess) return e;
     p.xq = xq;
     p.xscale = xs;

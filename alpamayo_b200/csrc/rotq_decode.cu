@@ -134,11 +134,11 @@ cudaError_t launch_rot16_decode(int x_dtype, const void* x, int64_t M, int K, co
 // scale (round half away from zero, vLLM's per_token_quant_int8,
 // int8_utils.py:106-128).  The codes keep the scratch's fragment order; each
 // (row, group) code sum goes to gsum[g][row] (rows padded to a multiple of
-// 8), the token scales to xscale, and the last CTA returns amax and its exit
-// counter to zero.
+// 8) and the token scales to xscale.  The maxima stay as they are: the GEMM
+// that reads these codes returns them to zero once this grid has finished.
 __global__ void __launch_bounds__(128)
 quant16_decode_kernel(const __half* y, uint32_t* amax, int64_t M, int K, int Mp, int8_t* __restrict__ xq,
-                      float* __restrict__ xscale, int* __restrict__ gsum, uint32_t* exit_count) {
+                      float* __restrict__ xscale, int* __restrict__ gsum) {
   asm volatile("griddepcontrol.launch_dependents;");
   const int t = threadIdx.x, part = t & 15;
   const int g = blockIdx.x;
@@ -165,24 +165,12 @@ quant16_decode_kernel(const __half* y, uint32_t* amax, int64_t M, int K, int Mp,
 #pragma unroll
   for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
   if (part == 0 && r < Mp) gsum[(size_t)g * Mp + r] = sum;   // zero for padding rows
-  // every thread of the grid has read its row's maximum once all CTAs are
-  // past this point; the last one clears the maxima for the next call
-  __syncthreads();
-  if (t == 0) {
-    __threadfence();
-    const uint32_t n = gridDim.x * gridDim.y;
-    if (atomicAdd(exit_count, 1u) == n - 1) {
-      __threadfence();
-      for (int64_t i = 0; i < M; ++i) amax[i] = 0u;
-      *exit_count = 0u;
-    }
-  }
 }
 
 // Mp: rows of gsum per group (a multiple of 8, at least M; rows past M get
 // zero sums).
 cudaError_t launch_quant16_decode(const __half* y, uint32_t* amax, int64_t M, int K, int Mp, int8_t* xq,
-                                  float* xscale, int* gsum, uint32_t* exit_count, cudaStream_t st) {
+                                  float* xscale, int* gsum, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(K / kGroup), (unsigned)(Mp / 8), 1);
   cfg.blockDim = dim3(128, 1, 1);
@@ -192,7 +180,7 @@ cudaError_t launch_quant16_decode(const __half* y, uint32_t* amax, int64_t M, in
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, quant16_decode_kernel, y, amax, M, K, Mp, xq, xscale, gsum, exit_count);
+  return cudaLaunchKernelEx(&cfg, quant16_decode_kernel, y, amax, M, K, Mp, xq, xscale, gsum);
 }
 
 }  // namespace paro
