@@ -23,18 +23,34 @@ namespace paro {
 // One CTA per (layer, group) block.  Entry t of the block is element (t & 1)
 // of pair t / 2.  Output, indexed by channel c: the partner channel
 // (bits 0-6, group-local), the role (bit 7: 0 = first element i of the pair,
-// 1 = second element j) and the pair's fp16 angle (bits 16-31), so the thread
+// 1 = second element j), an exchange slot (bits 8-14, 128-channel groups
+// only; see below) and the pair's fp16 angle (bits 16-31), so the thread
 // owning channel c applies its half of the Givens update
 //   i' = c*i + s*j,  j' = -s*i + c*j
 // with one 32-bit load.
+//
+// Exchange slots: a kernel whose thread c (warp c / 32) publishes channel c's
+// value in shared memory and reads its partner's would see bank conflicts
+// from the pairing's arbitrary permutation.  Publishing at slot(c) instead,
+// with slot(c) % 32 a colour such that every warp's 32 writes and every
+// warp's 32 reads hit 32 different banks, avoids them.  The colouring always
+// exists: channel c is an edge from writer warp c / 32 to reader warp
+// partner(c) / 32 in a 32-regular bipartite multigraph on 4 + 4 nodes, which
+// splits into 32 perfect matchings (Konig's edge-colouring theorem); colour
+// = matching index, slot = colour + 32 * (c / 32).
 __global__ void prepare_rotation_kernel(const int16_t* __restrict__ pairs, const uint16_t* __restrict__ theta,
                                         int K, int group, uint32_t* __restrict__ out, int32_t* __restrict__ bad) {
   __shared__ int cnt[128];
+  __shared__ uint32_t word[128];
+  __shared__ uint8_t slot[128];
   const int blk = blockIdx.x;  // = layer * (K / group) + g
   const int layer = blk / (K / group), g = blk - layer * (K / group);
   const size_t base = (size_t)blk * group;
   const int t = threadIdx.x;
-  if (t < group) cnt[t] = 0;
+  if (t < group) {
+    cnt[t] = 0;
+    slot[t] = 0;
+  }
   __syncthreads();
   if (t < group) {
     const int v = pairs[base + t];
@@ -42,12 +58,58 @@ __global__ void prepare_rotation_kernel(const int16_t* __restrict__ pairs, const
     if (v >= 0 && v < group) {
       atomicAdd(&cnt[v], 1);
       const uint32_t th = theta[(size_t)layer * (K / 2) + (size_t)g * (group / 2) + (t >> 1)];
-      out[base + v] = (uint32_t)(w & 0x7F) | ((uint32_t)(t & 1) << 7) | (th << 16);
+      word[v] = (uint32_t)(w & 0x7F) | ((uint32_t)(t & 1) << 7) | (th << 16);
     }
   }
   __syncthreads();
   const int ok = (t >= group) || (cnt[t] == 1);
-  if (!__syncthreads_and(ok) && t == 0) atomicAdd(bad, 1);
+  const bool valid = __syncthreads_and(ok);
+  if (!valid) {
+    if (t == 0) atomicAdd(bad, 1);
+    return;
+  }
+  if (group == 128 && t == 0) {
+    // channels by (writer warp, reader warp)
+    uint8_t lst[4][4][32];
+    int n[4][4];
+    for (int a = 0; a < 4; ++a)
+      for (int b = 0; b < 4; ++b) n[a][b] = 0;
+    for (int c = 0; c < 128; ++c) {
+      const int a = c >> 5, b = (int)(word[c] & 0x7F) >> 5;
+      lst[a][b][n[a][b]++] = (uint8_t)c;
+    }
+    // peel 32 perfect matchings (writer a -> reader pi[a]); the multigraph
+    // stays regular after each, so one of the 24 permutations always fits
+    for (int colour = 0; colour < 32; ++colour) {
+      int pi[4] = {-1, -1, -1, -1};
+      bool found = false;
+      for (int p0 = 0; p0 < 4 && !found; ++p0)
+        for (int p1 = 0; p1 < 4 && !found; ++p1)
+          for (int p2 = 0; p2 < 4 && !found; ++p2) {
+            const int p3 = 6 - p0 - p1 - p2;
+            if (p0 == p1 || p0 == p2 || p1 == p2 || p3 < 0 || p3 > 3 || p3 == p0 || p3 == p1 || p3 == p2) continue;
+            if (n[0][p0] && n[1][p1] && n[2][p2] && n[3][p3]) {
+              pi[0] = p0;
+              pi[1] = p1;
+              pi[2] = p2;
+              pi[3] = p3;
+              found = true;
+            }
+          }
+      if (!found) {
+        // cannot happen for a valid pairing; the identity slots are correct
+        // too (each channel its own slot), only not conflict-free
+        for (int c = 0; c < 128; ++c) slot[c] = (uint8_t)c;
+        break;
+      }
+      for (int a = 0; a < 4; ++a) {
+        const int c = lst[a][pi[a]][--n[a][pi[a]]];
+        slot[c] = (uint8_t)(colour + 32 * a);
+      }
+    }
+  }
+  __syncthreads();
+  if (t < group) out[base + t] = word[t] | ((uint32_t)slot[t] << 8);
 }
 
 // Position of code (n, k) inside WQLinear.qweight, inverse of pack_intweight

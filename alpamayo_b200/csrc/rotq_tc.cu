@@ -194,14 +194,17 @@ __global__ void __launch_bounds__(kRtThreads, 1) rot_tc_kernel(const __grid_cons
       for (int l = 0; l < 8; ++l) {
         const uint32_t w = tab[l * 128 + n];
         const int partner = (int)(w & 0x7F);
+        // exchange slots from the table (bits 8-14): every warp's 32 writes
+        // and 32 reads fall in 32 different banks
+        const int s_me = (int)((w >> 8) & 0x7F), s_pt = (int)((tab[l * 128 + partner] >> 8) & 0x7F);
         float s_, c_;
         __sincosf(half_bits_to_f32((uint16_t)(w >> 16)), &s_, &c_);
         const float cp = ((w >> 7) & 1) ? -s_ : s_;
 #pragma unroll
-        for (int j = 0; j < 32; ++j) ex[j * 128 + n] = v[j];
+        for (int j = 0; j < 32; ++j) ex[j * 128 + s_me] = v[j];
         named_barrier(1 + h, 128);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = givens(v[j], ex[j * 128 + partner], c_, cp);
+        for (int j = 0; j < 32; ++j) v[j] = givens(v[j], ex[j * 128 + s_pt], c_, cp);
         named_barrier(1 + h, 128);
       }
 #pragma unroll

@@ -72,7 +72,10 @@ const char* paro_last_cuda_error(void);
  *   theta     : fp16 [krot, K/2] angle of each pair.
  *   out_table : uint32 [krot, K] indexed by channel: partner channel (bits
  *               0-6, group-local), role (bit 7: 0 = first element of its
- *               pair, 1 = second) and the pair's fp16 angle bits (16-31).
+ *               pair, 1 = second), a shared-memory exchange slot (bits 8-14:
+ *               a permutation of the group's channels under which each
+ *               32-channel warp's writes and its partners' reads fall in 32
+ *               different banks) and the pair's fp16 angle bits (16-31).
  *   bad       : device int32, set to the number of (layer, group) blocks that
  *               are not a permutation of 0..group-1 (must be zero before the
  *               table is trusted: overlapping pairs make a layer

@@ -144,13 +144,49 @@ def expected_rot_table(pairs, theta):
     return out.view(np.int32)
 
 
+def check_exchange_slots(table):
+    """Bits 8-14 of each (layer, group) block: a permutation of the 128 slots
+    in which warp w's channels (32w .. 32w+31) write 32 different banks
+    (slot % 32) and the partners of warp w's channels, which warp w reads,
+    also sit in 32 different banks."""
+    u = table.view(np.uint32)
+    L, K = u.shape
+    for l in range(L):
+        for g in range(K // 128):
+            blk = u[l, g * 128:(g + 1) * 128]
+            slot = ((blk >> 8) & 0x7F).astype(np.int64)
+            partner = (blk & 0x7F).astype(np.int64)
+            assert sorted(slot) == list(range(128)), (l, g)
+            for w in range(4):
+                chans = np.arange(32 * w, 32 * w + 32)
+                assert len(set(slot[chans] % 32)) == 32, (l, g, w)
+                assert len(set(slot[partner[chans]] % 32)) == 32, (l, g, w)
+
+
 def test_prepare_rotation_table_and_rejects_overlapping_pairs(ops):
     pairs, theta, _ = make_rotation(256, seed=1)
-    ok = ops.prepare_rotation(dev(pairs), dev(theta), 128)
-    assert np.array_equal(ok.cpu().numpy(), expected_rot_table(pairs, theta))
+    ok = ops.prepare_rotation(dev(pairs), dev(theta), 128).cpu().numpy()
+    # partner, role and angle bits as restated from the pair list; the
+    # exchange slots (bits 8-14) by their defining property
+    assert np.array_equal(ok.view(np.uint32) & 0xFFFF80FF, expected_rot_table(pairs, theta).view(np.uint32))
+    check_exchange_slots(ok)
     pairs[2, 130] = pairs[2, 131]
     with pytest.raises(RuntimeError, match="not permutations"):
         ops.prepare_rotation(dev(pairs), dev(theta), 128)
+
+
+def test_exchange_slots_for_checkpoint_like_pairings(ops):
+    """Slots for several random pairings, including ones that pair channels
+    only within a warp and only across warps."""
+    for seed in range(4):
+        pairs, theta, _ = make_rotation(512, seed=10 + seed)
+        check_exchange_slots(ops.prepare_rotation(dev(pairs), dev(theta), 128).cpu().numpy())
+    pairs, theta, _ = make_rotation(128, seed=3)
+    ident = np.tile(np.arange(128, dtype=pairs.dtype), (pairs.shape[0], 1))   # pairs (2i, 2i+1): same warp
+    check_exchange_slots(ops.prepare_rotation(dev(ident), dev(theta), 128).cpu().numpy())
+    cross = np.tile(np.stack([np.arange(64), np.arange(64) + 64], 1).reshape(-1).astype(pairs.dtype),
+                    (pairs.shape[0], 1))   # pairs (i, i + 64): always another warp
+    check_exchange_slots(ops.prepare_rotation(dev(cross), dev(theta), 128).cpu().numpy())
 
 
 def test_empty_batch(ops):
