@@ -266,9 +266,10 @@ int paro_w4a8_linear(const void* x, int x_dtype, int64_t M, int K, int N, const 
   if (!aligned(workspace, 256) || !aligned(scratch, 256)) return PARO_ERR_MISALIGNED;
   if (int d = device_check()) return d;
   cudaStream_t st = (cudaStream_t)stream;
-  // decode sizes: rotation kernel + GEMM that quantises in its prologue
-  // (measured on B200 faster than the activation kernel + GEMM pair, whose
-  // single-pass activation kernel spreads a row over one 8-CTA cluster)
+  // decode sizes: rotation kernel + quantiser + GEMM, chained by
+  // programmatic dependent launch (measured on B200 faster than the
+  // activation kernel + GEMM pair, whose single-pass activation kernel
+  // spreads a row over one 8-CTA cluster)
   if (M <= kLinearFusedMaxM && fp16_round && !gemm_tc_supported(M, N, K)) {
     const cudaError_t e = launch_linear_decode(x, x_dtype, channel_scales, rot_table, M, N, K, packed, bias,
                                                bias_dtype, out, out_dtype, workspace, scratch, st);

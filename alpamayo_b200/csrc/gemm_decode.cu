@@ -58,8 +58,8 @@ constexpr int kDecStageBytes = kDecChunkGroups * kRecBytes;  // 34304
 constexpr int kDecMaxStages = 8;
 constexpr int kDecMaxTokens = 64;   // tokens per CTA slice (8 tiles of 8)
 constexpr int kDecSmemBudget = 220 * 1024;
-constexpr int kXinRot16 = 16;       // gemm_stream_kernel's XIN for pre-rotated fp16 rows
-constexpr int kXinPreQ = 17;        // ... for int8 rows in fragment order with code sums
+constexpr int kXinPreQ = 17;        // gemm_stream_kernel's XIN for int8 rows in fragment order with code sums
+constexpr int kXinPreQS = 18;       // ... the same rows and sums bulk-copied into shared memory
 constexpr int kDecBulkXBytes = 32 * 1024;  // activation blocks above this are bulk-copied
 
 struct DecParams {
@@ -74,12 +74,10 @@ struct DecParams {
   int out_dtype;
   float* ws;        // [N][M] float32 partial sums, zero between calls
   uint32_t* cnt;    // [token slices][N/16] unit counters, zero between calls
-  // linear entry point: rotated fp16 rows from rot16_decode_kernel,
-  // quantised in the kernel's prologue
-  const __half* rot16;      // [M, K] rotated rows, fp16
-  uint32_t* amax;           // [M] row |max| bits, zero between calls (kXinRot16 and
-                            // kXinPreQ: this kernel returns them to zero)
-  uint32_t* gsync;          // [2] exit counter (word 1), zero between calls
+  // linear entry point (kXinPreQ, kXinPreQS): the row maxima the
+  // rotation kernel accumulated and the quantiser read; this kernel
+  // returns them to zero once the quantiser has finished
+  uint32_t* amax;           // [M] row |max| bits, zero between calls
   int64_t units;    // (N/16) * G
   int ctas;
   int stages;
@@ -183,20 +181,19 @@ __device__ __forceinline__ void process_record(const uint8_t* rec, const uint32_
 // banks), rearranged into fragment order, and their per-group sums computed
 // there; otherwise fragments are read from global memory per record.
 // XIN < 0: the int8 activations and token scales come from paro_rotq_int8;
-// XIN = kXinRot16: the previous kernel (rot16_decode_kernel) left the
-// rotated fp16 rows and row maxima, and the consumers quantise them in the
-// prologue (phase B; M <= 64, XS only).
+// XIN = kXinPreQ: quant16_decode_kernel left the int8 rows in fragment order
+// with their code sums, read per record from L2 (!XS); XIN = kXinPreQS: the
+// same, bulk-copied into shared memory once (XS, no rearrangement).
 template <int MT, bool XS, int XIN>
 __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecParams p) {
-  constexpr bool FUSE = XIN == kXinRot16;
   constexpr bool PREQ = XIN == kXinPreQ;
+  constexpr bool PREQS = XIN == kXinPreQS;
   static_assert(!PREQ || !XS, "pre-quantised rows are read from global memory");
+  static_assert(!PREQS || XS, "staged pre-quantised rows live in shared memory");
   constexpr int NC = dec_consumers(MT);
   constexpr int NCT = NC * 32;
   constexpr int SLOTS = kDecChunkGroups / NC;   // records per warp per chunk
-  static_assert(!FUSE || XS, "phase B stages the int8 rows in shared memory");
   __shared__ float tok_scale_s[kDecMaxTokens];
-  __shared__ float tok_inv_s[FUSE ? kDecMaxTokens : 1];
   extern __shared__ __align__(128) uint8_t smem[];
   const int S = p.stages;
   const int G = p.K / kGroup;
@@ -270,19 +267,26 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
   if (warp > NC) {  // epilogue warps: warp NC + 1 + e takes the segments q = e (mod 2)
     const int ew = warp - (NC + 1);
     grid_dependency_wait();  // token scales (and rows) come from the previous kernel
-    if constexpr (!FUSE) {
-      // both warps write the same token scales; each reads back its own
-      for (int t = lane; t < ntok_slice; t += 32) tok_scale_s[t] = p.xscale[tok0 + t];
-      __syncwarp();
-    }
-    if constexpr (PREQ) {
+    // both warps write the same token scales; each reads back its own
+    for (int t = lane; t < ntok_slice; t += 32) tok_scale_s[t] = p.xscale[tok0 + t];
+    __syncwarp();
+    if constexpr (PREQ || PREQS) {
       // the quantiser that read the row maxima has finished: return them to
       // zero for the next call's rotation kernel
       if (blockIdx.x == 0 && blockIdx.y == 0 && ew == 0)
         for (int64_t t = lane; t < p.M; t += 32) p.amax[t] = 0u;
     }
     uint32_t* cnt = p.cnt + (size_t)blockIdx.y * (p.N / kRecRows);
-    if constexpr (XS && !FUSE) {
+    if constexpr (PREQS) {
+      // rows already in fragment order and their code sums ([G][MP], padding
+      // tokens zero): bulk copies straight into place
+      if (ew == 0 && lane == 0) {
+        mbar_arrive_expect_tx(xbar, (uint32_t)ntok_slice * p.K + (uint32_t)(G * MP * 4));
+        for (int r = 0; r < ntok_slice; ++r)
+          bulk_g2s(xrows + (size_t)r * xstride, p.xq + (tok0 + r) * (int64_t)p.K, (uint32_t)p.K, xbar);
+        bulk_g2s(sxs, p.gsum, (uint32_t)(G * MP * 4), xbar);
+      }
+    } else if constexpr (XS) {
       // large activation blocks: bulk copies of the rows (behind the weight
       // chunks already queued, but one copy per row)
       if (ew == 0 && lane == 0 && (int64_t)ntok_slice * p.K > kDecBulkXBytes) {
@@ -385,80 +389,9 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
     xr[mt] = min(mt * 8 + gid, p.xrows_n - 1);
     xrowf[mt] = reinterpret_cast<const uint8_t*>(p.xq) + (xvalid[mt] ? t : 0) * (int64_t)p.K + 32 * tig;
   }
-  if constexpr (FUSE) {
-    // phase B: token scales from the row maxima, then the int8 rows into
-    // shared memory (round half away from zero, as vLLM's quantiser).  The
-    // rotation kernel stores each group's 4-channel quads already in
-    // fragment order, so the codes land where the fragment loads want them;
-    // each group's code sum is reduced over the 16 lanes that quantise it.
+  if constexpr (PREQS) {
     grid_dependency_wait();
-    const int k8n = p.K / 8;
-    const int total = ntok_slice * k8n;   // a multiple of 16: a group is 16 items
-    constexpr int kBatch = 8;              // loads in flight per thread
-    // item e = (row r, 8-value column k8), walked with a running pair
-    int pr = ctid / k8n, pk = ctid - pr * k8n;
-    uint4 u[kBatch];
-    int rr[kBatch], kk[kBatch];
-    auto load_batch = [&](int e0) {
-#pragma unroll
-      for (int j = 0; j < kBatch; ++j) {
-        rr[j] = pr;
-        kk[j] = pk;
-        if (e0 + j * NCT < total)
-          u[j] = ld_cg_v4(reinterpret_cast<const uint4*>(p.rot16 + (size_t)(tok0 + pr) * p.K) + pk);
-        pk += NCT;
-        while (pk >= k8n) {
-          pk -= k8n;
-          ++pr;
-        }
-      }
-    };
-    // the first rows are requested before the maxima: one round trip for both
-    load_batch(ctid);
-    if (ctid < ntok_slice) {
-      const float a = fmaxf(__uint_as_float(ld_cg_u32(p.amax + tok0 + ctid)), 1e-10f);
-      tok_inv_s[ctid] = __fdiv_rn(127.0f, a);
-      tok_scale_s[ctid] = __fdiv_rn(a, 127.0f);
-    }
-    for (int e = ctid; e < G * MP; e += NCT)
-      if (e % MP >= ntok_slice) sxs[e] = 0;
-    named_barrier(1, NCT);
-    for (int e0 = ctid; e0 < total; e0 += kBatch * NCT) {
-      if (e0 != ctid) load_batch(e0);
-#pragma unroll
-      for (int j = 0; j < kBatch; ++j) {
-        const int e = e0 + j * NCT;
-        const bool ok = e < total;   // uniform over each 16-lane group
-        const int r = rr[j], k8 = kk[j];
-        uint32_t w0 = 0, w1 = 0;
-        if (ok) {
-          const __half* h = reinterpret_cast<const __half*>(&u[j]);
-          const float inv = tok_inv_s[r];
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            w0 |= ((uint32_t)(uint8_t)(int8_t)(int)round_half_away(__half2float(h[q]) * inv)) << (8 * q);
-            w1 |= ((uint32_t)(uint8_t)(int8_t)(int)round_half_away(__half2float(h[q + 4]) * inv)) << (8 * q);
-          }
-          *reinterpret_cast<uint2*>(xrows + (size_t)r * xstride + (size_t)k8 * 8) = make_uint2(w0, w1);
-        }
-        int sum = __dp4a((int)w0, 0x01010101, __dp4a((int)w1, 0x01010101, 0));
-#pragma unroll
-        for (int o = 8; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if (ok && (k8 & 15) == 0) sxs[(k8 >> 4) * MP + r] = sum;
-      }
-    }
-    named_barrier(1, NCT);
-    // the last CTA past this point returns the maxima and the exit counter
-    // to zero
-    if (ctid == 0) {
-      __threadfence();
-      const uint32_t old = atomicAdd(p.gsync + 1, 1u);
-      if (old == gridDim.x - 1) {
-        __threadfence();
-        for (int64_t r = 0; r < p.M; ++r) p.amax[r] = 0u;
-        p.gsync[1] = 0u;
-      }
-    }
+    if (!mbar_wait(xbar, 0)) return;   // rows and code sums landed (epilogue warp's copies)
   } else if constexpr (XS) {
     // Staged rows past the slice's tokens (when a later slice is short) hold
     // stale bytes, and lanes of tokens past the staged rows read the last
@@ -757,98 +690,83 @@ cudaError_t launch_gemm_decode(const int8_t* xq, const float* xscale, int64_t M,
 
 // ---------------------------------------------------------------------------
 // decode linear: rot16_decode_kernel rotates the activations into an fp16
-// scratch and records each row's |max|; the GEMM quantises them in its
-// prologue (phase B) and streams the weights meanwhile
+// scratch and records each row's |max|, quant16_decode_kernel writes the
+// int8 codes in fragment order with their group sums, and the GEMM, whose
+// weight stream started during both, consumes them
 // ---------------------------------------------------------------------------
 cudaError_t launch_rot16_decode(int x_dtype, const void* x, int64_t M, int K, const uint16_t* scales,
                                 const uint32_t* rtab, __half* y, uint32_t* amax, cudaStream_t st);
 
 size_t linear_decode_workspace(int64_t M, int N) {
-  return gemm_decode_workspace(M, N) + (((size_t)M * sizeof(uint32_t) + 255) & ~(size_t)255) + 256;
+  return gemm_decode_workspace(M, N) + (((size_t)M * sizeof(uint32_t) + 255) & ~(size_t)255);
 }
 
-static int fused_mt(int64_t M) { return M <= 8 ? 1 : M <= 16 ? 2 : M <= 32 ? 4 : 8; }
-
-template <int MT>
-static cudaError_t launch_pick_fused(DecParams p, cudaStream_t st) {
-  const size_t xs_bytes = xs_bytes_for(MT, p.K, p.M);
-  p.xrows_n = xrows_for(MT, p.M);
-  if (!xs_bytes) return cudaErrorNotSupported;
-  stages_for(p, MT, xs_bytes);
-  return launch_mt<MT, true, kXinRot16>(p, xs_bytes, st);
-}
+static int token_tiles(int64_t M) { return M <= 8 ? 1 : M <= 16 ? 2 : M <= 32 ? 4 : 8; }
 
 cudaError_t launch_quant16_decode(const __half* y, uint32_t* amax, int64_t M, int K, int Mp, int8_t* xq, float* xscale,
                                   int* gsum, cudaStream_t st);
 
-// When the rows are quantised by their own kernel instead of the GEMM's
-// prologue (measured on B200): always for large row blocks (the prologue
-// would read all of them into every CTA), and for any rows when each CTA
-// streams few records (its prologue is then most of its time: qkv / o at 1
-// token 8.5 / 6.7 us against 9.8 / 7.8 us).  Large layers keep the prologue
-// (gate_up at 1 token: 20.5 us against 24.7 us with the extra kernel).
-static bool use_quant_kernel(int64_t M, int K, const DecParams& p) {
-  const int64_t bytes = M * (int64_t)K * 2;
-  return bytes > 64 * 1024 || p.units <= 64 * (int64_t)p.ctas;
-}
+// Whether the GEMM stages the quantised rows in shared memory (kXinPreQS)
+// or reads each record's fragments from L2 (kXinPreQ), measured on B200:
+// staged for large layers (gate_up at 1 / 8 / 16 tokens: 19.3 / 20.8 / 26.2
+// us against 24.7 / 27.5 / 35.4 us from L2), from L2 when each CTA streams
+// few records (qkv, o: the copies' latency is most of their time, 0.2-0.3 us
+// more per linear staged) or the rows do not fit.  Both beat quantising
+// in the GEMM's own prologue, which this kernel did before (its exit
+// counter and row reads delayed every CTA's first records).
+static bool stage_rows(const DecParams& p) { return p.units > 64 * (int64_t)p.ctas; }
 
 static size_t al256(size_t b) { return (b + 255) & ~(size_t)255; }
 
 size_t linear_decode_scratch(int64_t M, int K) {
-  const size_t Mp = (size_t)8 * (M <= 8 ? 1 : M <= 16 ? 2 : M <= 32 ? 4 : 8);
+  const size_t Mp = (size_t)8 * token_tiles(M);
   return al256((size_t)M * K * 2) + al256((size_t)M * K) + al256((size_t)M * 4) + al256((size_t)(K / kGroup) * Mp * 4);
 }
 
 template <int MT>
 static cudaError_t launch_pick_preq(DecParams p, cudaStream_t st) {
+  const size_t xs_bytes = stage_rows(p) ? xs_bytes_for(MT, p.K, p.M) : 0;
+  if (xs_bytes) {
+    p.xrows_n = xrows_for(MT, p.M);
+    stages_for(p, MT, xs_bytes);
+    return launch_mt<MT, true, kXinPreQS>(p, xs_bytes, st);
+  }
   p.xrows_n = 0;
   stages_for(p, MT, 0);
   return launch_mt<MT, false, kXinPreQ>(p, 0, st);
 }
 
-// Returns cudaErrorNotSupported (nothing launched) for shapes whose int8
-// rows do not fit in shared memory; callers then run the two kernels.
+// Returns cudaErrorNotSupported (nothing launched) above kDecMaxTokens
+// tokens; callers then run the two-kernel path.
 cudaError_t launch_linear_decode(const void* x, int x_dtype, const uint16_t* cscale, const uint32_t* rtab, int64_t M,
                                  int N, int K, const void* packed, const void* bias, int bias_dtype, void* out,
                                  int out_dtype, void* ws, void* scratch, cudaStream_t st) {
   if (M > kDecMaxTokens || M <= 0) return cudaErrorNotSupported;
   DecParams p = dec_params(M, N, K, packed, bias, bias_dtype, out, out_dtype, ws);
-  const bool preq = use_quant_kernel(M, K, p);
-  if (!preq && !xs_bytes_for(fused_mt(M), K, M)) return cudaErrorNotSupported;
   uint8_t* tail = static_cast<uint8_t*>(ws) + gemm_decode_workspace(M, N);
   p.amax = reinterpret_cast<uint32_t*>(tail);
-  p.gsync = reinterpret_cast<uint32_t*>(tail + (((size_t)M * sizeof(uint32_t) + 255) & ~(size_t)255));
+  // rotation into the fp16 scratch, quantisation (fragment order + code
+  // sums), then the GEMM
   __half* rot16 = static_cast<__half*>(scratch);
-  p.rot16 = rot16;
   cudaError_t e = launch_rot16_decode(x_dtype, x, M, K, cscale, rtab, rot16, p.amax, st);
   if (e != cudaSuccess) return e;
-  if (preq) {
-    // rotation, quantisation (fragment order + code sums), then the GEMM
-    // reading its fragments from global memory
-    uint8_t* sp = static_cast<uint8_t*>(scratch) + al256((size_t)M * K * 2);
-    int8_t* xq = reinterpret_cast<int8_t*>(sp);
-    float* xs = reinterpret_cast<float*>(sp + al256((size_t)M * K));
-    int* gsum = reinterpret_cast<int*>(sp + al256((size_t)M * K) + al256((size_t)M * 4));
-    const int Mp = 8 * fused_mt(M);
-    e = launch_quant16_decode(rot16, p.amax, M, K, Mp, xq, xs, gsum, st);
-    if (e != cudaSuccess) return e;
-    p.xq = xq;
-    p.xscale = xs;
-    p.gsum = gsum;
-    p.gsum_mp = Mp;
-    switch (fused_mt(M)) {
-      case 1: return launch_pick_preq<1>(p, st);
-      case 2: return launch_pick_preq<2>(p, st);
-      case 4: return launch_pick_preq<4>(p, st);
-    }
-    return launch_pick_preq<8>(p, st);
+  uint8_t* sp = static_cast<uint8_t*>(scratch) + al256((size_t)M * K * 2);
+  int8_t* xq = reinterpret_cast<int8_t*>(sp);
+  float* xs = reinterpret_cast<float*>(sp + al256((size_t)M * K));
+  int* gsum = reinterpret_cast<int*>(sp + al256((size_t)M * K) + al256((size_t)M * 4));
+  const int Mp = 8 * token_tiles(M);
+  e = launch_quant16_decode(rot16, p.amax, M, K, Mp, xq, xs, gsum, st);
+  if (e != cudaSuccess) return e;
+  p.xq = xq;
+  p.xscale = xs;
+  p.gsum = gsum;
+  p.gsum_mp = Mp;
+  switch (token_tiles(M)) {
+    case 1: return launch_pick_preq<1>(p, st);
+    case 2: return launch_pick_preq<2>(p, st);
+    case 4: return launch_pick_preq<4>(p, st);
   }
-  switch (fused_mt(M)) {
-    case 1: return launch_pick_fused<1>(p, st);
-    case 2: return launch_pick_fused<2>(p, st);
-    case 4: return launch_pick_fused<4>(p, st);
-  }
-  return launch_pick_fused<8>(p, st);
+  return launch_pick_preq<8>(p, st);
 }
 
 }  // namespace paro

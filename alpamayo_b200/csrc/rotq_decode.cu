@@ -1,9 +1,8 @@
 // rotq_decode.cu — the rotation half of a decode-size rotated linear
 // (sm_100a): channel scale + 8 Givens layers per 128-channel group, rounded
 // to fp16, plus each token row's |max|.  The int8 quantisation that needs
-// the whole row's maximum is done by the GEMM that consumes these rows, in
-// its prologue (gemm_decode.cu, phase B), so no kernel here waits for
-// another CTA.
+// the whole row's maximum happens after the kernel boundary
+// (quant16_decode_kernel below), so no kernel here waits for another CTA.
 //
 // Geometry for a handful of tokens: one CTA per (group, token row) (the
 // kernel is written for blocks of R rows; R = 1 is launched), 128 threads,
@@ -23,8 +22,8 @@
 //
 // Output order: within each group the 32 quads of 4 channels are stored in
 // the order the GEMM's mma fragments read them (quad j*4 + t at position
-// t*8 + j), so the GEMM's quantising prologue writes its int8 codes straight
-// into fragment order.  The scratch is private to the linear.
+// t*8 + j), so the quantiser writes its int8 codes straight into fragment
+// order.  The scratch is private to the linear.
 #include "tc_ptx.cuh"
 
 namespace paro {
@@ -128,8 +127,7 @@ cudaError_t launch_rot16_decode(int x_dtype, const void* x, int64_t M, int K, co
   return cudaErrorInvalidValue;
 }
 
-// Quantisation of the rotated rows for long rows (the GEMM's prologue would
-// read every row from every CTA): per (group, block of 8 rows) a CTA of 128
+// Quantisation of the rotated rows: per (group, block of 8 rows) a CTA of 128
 // threads, 16 per row, each turning 8 fp16 values into int8 with the row's
 // scale (round half away from zero, vLLM's per_token_quant_int8,
 // int8_utils.py:106-128).  The codes keep the scratch's fragment order; each

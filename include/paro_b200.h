@@ -245,12 +245,12 @@ int paro_device_error_word(int clear);
  * One rotated W4A8 linear: y = paro_w4a8_gemm(paro_rotq_int8(x)), the whole
  * forward of RotateLinearInt4 / BF16RotateLinearWrapper
  * (src/alpamayo_r1/utils/quantization/paroquant_marlin_w4a8.py:47-71 with
- * rotation_linear.py:53-139).  Up to 64 tokens with fp16_round = 1 (when
- * the int8 rows fit in shared memory) it is two chained kernels: one
- * rotates the activations into the scratch (fp16, one CTA per 128-channel
- * group) and records each row's |max|; the GEMM, launched behind it with
- * programmatic dependent launch, streams its weights meanwhile and
- * quantises the rows in its prologue.  Otherwise it is the activation
+ * rotation_linear.py:53-139).  Up to 64 tokens with fp16_round = 1 (and
+ * not on the tensor-core GEMM's shapes) it is three chained kernels: one
+ * rotates the activations into the scratch (fp16, one CTA per (128-channel
+ * group, token)) and records each row's |max|, one quantises the rows to
+ * int8, and the GEMM, launched behind them with programmatic dependent
+ * launch, streams its weights meanwhile.  Otherwise it is the activation
  * kernel(s) followed by the GEMM.
  *   x             : [M, K] of x_dtype;  channel_scales : fp16 [K] or NULL.
  *   rot_table     : uint32 [8, K] from paro_prepare_rotation (group 128).
