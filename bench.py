@@ -4,11 +4,11 @@
 Headline workload ("decode sweep"): the four
 projection shapes of one 7B-class decoder layer (qkv 3584->4608, o 3584->3584,
 gate_up 3584->37888, down 18944->3584) at M = 1, 4 and 8 tokens; each linear
-runs through torch.ops.paro_b200.linear_w4a8: the activation kernel (channel
+runs through torch.ops.paro_b200.linear_w4a8: the activation (channel
 scale, 8 Givens layers, per-token int8) and the persistent W4A8 GEMM,
-chained by programmatic dependent launch (at these sizes the activation
-half is a rotation kernel and the GEMM quantises the rotated rows itself).  One step = STEP_SWEEPS passes over the 12 (shape, M)
-cases.  Three
+chained by programmatic dependent launch (at these sizes the activation is
+a rotation kernel and a quantiser, so three kernels per linear).  One step
+= STEP_SWEEPS passes over the 12 (shape, M) cases.  Three
 weight replicas (one per M) make the per-pass weight working set 363 MB
 (> 126 MB L2), so every GEMM streams its weights from HBM.  The metric value
 is weight-stream GB/s (algorithmic int4 code + fp16 scale + int4 zero bytes
@@ -16,8 +16,8 @@ per second), whole job.
 
 Timing: CUDA graph of one step, replayed; CUDA events around the timed
 replays, barrier + synchronize on both sides, max over ranks.  Per-kernel
-launch durations for the roofline: each case's linear (one fused kernel at
-these sizes) runs after an L2 flush (a 512 MiB write, then a 256 MiB read so
+launch durations for the roofline: each case's GEMM (the int8-input
+paro_w4a8_gemm) runs after an L2 flush (a 512 MiB write, then a 256 MiB read so
 that the lines left in the L2 are clean and the timed kernel pays for no
 write-backs), with CUDA events on the launching stream around it.
 
@@ -541,7 +541,9 @@ def main():
             sweep()
 
     bytes_per_step = STEP_SWEEPS * wset
-    launches_per_step = STEP_SWEEPS * 2 * len(DECODE_M) * len(SHAPES)   # rotation kernel + GEMM per linear
+    # rotation kernel + quantiser + GEMM per linear (every decode shape takes
+    # the three-kernel route: all of them stream on the mma.sync kernel)
+    launches_per_step = STEP_SWEEPS * 3 * len(DECODE_M) * len(SHAPES)
 
     # --- capture one step as a CUDA graph
     s = torch.cuda.Stream()
