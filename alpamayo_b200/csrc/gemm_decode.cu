@@ -725,7 +725,9 @@ size_t linear_decode_scratch(int64_t M, int K) {
 
 template <int MT>
 static cudaError_t launch_pick_preq(DecParams p, cudaStream_t st) {
-  const size_t xs_bytes = stage_rows(p) ? xs_bytes_for(MT, p.K, p.M) : 0;
+  // the staged copy lands the code sums as one block: their row pitch must
+  // be the kernel's (8 per token tile)
+  const size_t xs_bytes = stage_rows(p) && p.gsum_mp == 8 * MT ? xs_bytes_for(MT, p.K, p.M) : 0;
   if (xs_bytes) {
     p.xrows_n = xrows_for(MT, p.M);
     stages_for(p, MT, xs_bytes);
