@@ -163,10 +163,8 @@ def test_gemm_linearity_in_token_scale(ops):
                                    (3584, 3584, 100)])
 def test_tensor_core_gemm_tiles_match_oracle(ops, N, K, M):
     """The tcgen05 kernel (M > 64, or M > 24 on a layer with enough 256-row
-    tiles): full and partial 128-token x 256-row tiles, with split-K where
-    the tiles are fewer than the CTA pairs (K = 1024 at 300 tokens: 2
-    splits; qkv / o at 65-100 tokens: 4-5; down at 256 tokens: 5), against
-    the oracle on sampled rows and columns."""
+    tiles): full and partial 128-token x 256-row tiles, against the oracle
+    on sampled rows and columns."""
     from alpamayo_b200 import _native
     assert _native.capi().paro_w4a8_gemm_path(M, N, K) == 1
     codes, scales, zeros, packed = records_layer(N, K, seed=N // 16 + K + M)
