@@ -71,11 +71,15 @@ struct TcParams {
   int64_t M;
   int N, K;
   int tiles_n, tiles;   // tiles along N (256 rows each) and in total
+  int splits, gper;     // K splits per tile and groups per split (split-K when tiles are few)
+  int items;            // tiles * splits
   const uint8_t* packed;
   const void* bias;
   int bias_dtype;
   void* out;
   int out_dtype;
+  unsigned long long* ws;  // splits > 1: [M][N] int64 fixed-point (2^-28) partial sums, zero between calls
+  uint32_t* cnt;        // splits > 1: [tiles][2 CTAs][8 epilogue warps] counters, zero between calls
 };
 
 
@@ -174,6 +178,24 @@ __device__ __forceinline__ uint32_t ldg_nc_u16(const uint16_t* p) {
 }
 
 
+// split-K partial sums in 64-bit fixed point, 2^-28 units: range 2^35
+// (a partial is at most G * 2^18 * |group scale|, so group scales up to
+// ~900 in magnitude fit even for K = 18944; int4 weight scales are far
+// smaller) and resolution 3.7e-9, below float32's spacing for any partial
+// above 1e-3
+__device__ __forceinline__ void red_add_fx(unsigned long long* p, float v) {
+  const long long q = __float2ll_rn(v * 268435456.0f);
+  asm volatile("red.global.add.u64 [%0], %1;" ::"l"(p), "l"((unsigned long long)q) : "memory");
+}
+__device__ __forceinline__ float ld_cg_fx(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.global.cg.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return __ll2float_rn((long long)v) * 3.7252902984619141e-09f;   // 2^-28
+}
+__device__ __forceinline__ void st_cg_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.global.cg.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
 __device__ __forceinline__ float tc_bias(const void* bias, int dtype, int n) {
   if (!bias) return 0.f;
   if (dtype == PARO_F16) return __half2float(static_cast<const __half*>(bias)[n]);
@@ -219,6 +241,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
   auto tile_n0 = [&](int t) { return (t % p.tiles_n) * (2 * kTcRows) + (int)rank * kTcRows; };
   auto tile_m0 = [&](int t) { return (int64_t)(t / p.tiles_n) * kTcTok; };
   auto tile_nrec = [&](int n0) { return max(0, min(kTcRecs, (p.N - n0) / kRecRows)); };
+  // work item w: tile w / splits, groups [gb, ge) of its K split
+  auto item_groups = [&](int w, int& gb, int& ge) {
+    gb = (w - (w / p.splits) * p.splits) * p.gper;
+    ge = min(G, gb + p.gper);
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTcStages; ++s) {
@@ -249,10 +276,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     if (warp == 0 && lane == 0) {
       // producer
       uint32_t it = 0;  // groups issued by this CTA so far
-      for (int t = pair; t < p.tiles && !failed; t += pairs) {
+      for (int w = pair; w < p.items && !failed; w += pairs) {
+        const int t = w / p.splits;
+        int gb, ge;
+        item_groups(w, gb, ge);
         const int n0 = tile_n0(t);
         const int ty = (int)(tile_m0(t) + rank * kTcTokHalf);
-        for (int g = 0; g < G; ++g, ++it) {
+        for (int g = gb; g < ge; ++g, ++it) {
           const uint32_t s = it % kTcStages;
           if (it >= kTcStages && !mbar_wait(&freed[s], ((it / kTcStages) - 1) & 1)) {
             failed = true;
@@ -268,7 +298,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     } else if (warp == 1 && lane == 0 && leader) {
       // MMA issuer (leader CTA only)
       const uint32_t w_base = smem_u32(smem + kOffW), x_base = smem_u32(smem + kOffX);
-      const uint32_t total = (uint32_t)((p.tiles - pair + pairs - 1) / pairs) * (uint32_t)G;
+      uint32_t total = 0;
+      for (int w = pair; w < p.items; w += pairs) {
+        int gb, ge;
+        item_groups(w, gb, ge);
+        total += (uint32_t)(ge - gb);
+      }
       for (uint32_t it = 0; it < total && !failed; ++it) {
         const uint32_t s = it % kTcStages, b = it & 1;
         if (!mbar_wait_cluster(&ready[s], (it / kTcStages) & 1) || !mbar_wait_cluster(&acc_empty[b], (it >> 1) & 1)) {
@@ -294,9 +329,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     const int i = t >> 4, r = t & 15;
     const int sw = t & 7;
     uint32_t it = 0;
-    for (int tile = pair; tile < p.tiles && !failed; tile += pairs) {
-    const int nrec = tile_nrec(tile_n0(tile));
-    for (int g = 0; g < G; ++g, ++it) {
+    for (int w = pair; w < p.items && !failed; w += pairs) {
+    const int nrec = tile_nrec(tile_n0(w / p.splits));
+    int gb, ge;
+    item_groups(w, gb, ge);
+    for (int g = gb; g < ge; ++g, ++it) {
       const uint32_t s = it % kTcStages;
       if (!mbar_wait(&full[s], (it / kTcStages) & 1)) {
         failed = true;
@@ -352,7 +389,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
       mbar_arrive_cluster(&acc_empty[1], 0);
     }
     uint32_t it = 0;
-    for (int tile = pair; tile < p.tiles && !failed; tile += pairs) {
+    for (int w = pair; w < p.items && !failed; w += pairs) {
+      const int tile = w / p.splits;
+      int gb, ge;
+      item_groups(w, gb, ge);
       const int n0 = tile_n0(tile);
       const int64_t m0 = tile_m0(tile);
       const bool row_ok = (row >> 4) < tile_nrec(n0);
@@ -362,13 +402,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
       // are loaded three groups ahead and converted only where used, so the
       // load's latency never stalls the fold
       auto fetch_bits = [&](int g) -> uint32_t {
-        return (row_ok && g < G) ? ldg_nc_u16(sp + (size_t)g * (kRecBytes / 2)) : 0u;
+        return (row_ok && g < ge) ? ldg_nc_u16(sp + (size_t)g * (kRecBytes / 2)) : 0u;
       };
-      uint32_t r0 = fetch_bits(0), r1 = fetch_bits(1), r2 = fetch_bits(2);
+      uint32_t r0 = fetch_bits(gb), r1 = fetch_bits(gb + 1), r2 = fetch_bits(gb + 2);
       uint64_t y[64];
 #pragma unroll
       for (int j = 0; j < 64; ++j) y[j] = 0ull;  // (+0.0f, +0.0f)
-      for (int g = 0; g < G; ++g, ++it) {
+      for (int g = gb; g < ge; ++g, ++it) {
         const uint32_t b = it & 1;
         const uint32_t r_after = fetch_bits(g + 3);
         if (!mbar_wait(&acc_full[b], (it >> 1) & 1)) {
@@ -415,16 +455,65 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
       }
       __syncwarp();
       const int n = n0 + row;
-      if (!failed && row_ok) {
-        const float bn = tc_bias(p.bias, p.bias_dtype, n);
-        const int64_t mbase = m0 + col0;
-        const int valid = (int)(p.M - mbase < 128 ? (p.M - mbase > 0 ? p.M - mbase : 0) : 128);
-        if (p.out_dtype == PARO_BF16)
-          store_row(y, static_cast<__nv_bfloat16*>(p.out) + mbase * p.N + n, p.N, xs, bn, valid);
-        else if (p.out_dtype == PARO_F16)
-          store_row(y, static_cast<__half*>(p.out) + mbase * p.N + n, p.N, xs, bn, valid);
-        else
-          store_row(y, static_cast<float*>(p.out) + mbase * p.N + n, p.N, xs, bn, valid);
+      const int64_t mbase = m0 + col0;
+      const int valid = (int)(p.M - mbase < 128 ? (p.M - mbase > 0 ? p.M - mbase : 0) : 128);
+      if (p.splits == 1) {
+        if (!failed && row_ok) {
+          const float bn = tc_bias(p.bias, p.bias_dtype, n);
+          if (p.out_dtype == PARO_BF16)
+            store_row(y, static_cast<__nv_bfloat16*>(p.out) + mbase * p.N + n, p.N, xs, bn, valid);
+          else if (p.out_dtype == PARO_F16)
+            store_row(y, static_cast<__half*>(p.out) + mbase * p.N + n, p.N, xs, bn, valid);
+          else
+            store_row(y, static_cast<float*>(p.out) + mbase * p.N + n, p.N, xs, bn, valid);
+        }
+      } else {
+        // split-K: this split's partial sums are added into the workspace
+        // as 64-bit fixed point (red_add_fx: integer addition makes the
+        // total independent of the order the splits arrive in); the warp
+        // that completes the (tile, CTA, warp) count acquires every split's
+        // partial for its 32 rows x 128 tokens, stores the outputs and
+        // returns the workspace and the counter to zero
+        unsigned long long* wp = p.ws + (size_t)mbase * p.N + n;
+        if (!failed && row_ok) {
+#pragma unroll
+          for (int j = 0; j < 64; ++j) {
+            const float2 f = unpack2(y[j]);
+            if (2 * j < valid) red_add_fx(wp + (size_t)(2 * j) * p.N, f.x);
+            if (2 * j + 1 < valid) red_add_fx(wp + (size_t)(2 * j + 1) * p.N, f.y);
+          }
+        }
+        __syncwarp();
+        uint32_t* c = p.cnt + ((size_t)tile * 2 + rank) * 8 + (warp - 8);
+        int last = 0;
+        if (lane == 0) {
+          asm volatile("fence.acq_rel.gpu;" ::: "memory");
+          last = atomicAdd(c, 1u) + 1u == (uint32_t)p.splits;
+          if (last) asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (last) {
+          if (!failed && row_ok) {
+            const float bn = tc_bias(p.bias, p.bias_dtype, n);
+            for (int j0 = 0; j0 < valid; j0 += 8) {
+              float a[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) a[j] = j0 + j < valid ? ld_cg_fx(wp + (size_t)(j0 + j) * p.N) : 0.f;
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                if (j0 + j < valid) {
+                  const size_t o = (size_t)(j0 + j) * p.N;
+                  st_cg_u64(wp + o, 0ull);
+                  const float v = a[j] * xs[j0 + j] + bn;
+                  if (p.out_dtype == PARO_BF16) static_cast<__nv_bfloat16*>(p.out)[mbase * p.N + n + o] = __float2bfloat16_rn(v);
+                  else if (p.out_dtype == PARO_F16) static_cast<__half*>(p.out)[mbase * p.N + n + o] = __float2half_rn(v);
+                  else static_cast<float*>(p.out)[mbase * p.N + n + o] = v;
+                }
+            }
+          }
+          __syncwarp();
+          if (lane == 0) *c = 0u;
+        }
       }
       __syncwarp();  // the slice is rewritten for the next tile
     }
@@ -466,11 +555,34 @@ int gemm_tc_supported(int64_t M, int N, int K) {
   return M > 24 && (int64_t)((N + 2 * kTcRows - 1) / (2 * kTcRows)) * 5 >= (int64_t)tc_sms() * 4;
 }
 
-size_t gemm_tc_workspace(int64_t, int, int) { return 0; }
+static int tc_tiles(int64_t M, int N) {
+  return (int)(((int64_t)N + 2 * kTcRows - 1) / (2 * kTcRows) * ((M + kTcTok - 1) / kTcTok));
+}
 
+// Split-K when the tiles fill fewer than all CTA pairs: each tile's groups
+// are cut into up to pairs / tiles splits of at least 4 groups, so that
+// small layers at mid-size token counts use the whole GPU.
+static int tc_splits(int64_t M, int N, int K) {
+  const int pairs = tc_sms() / 2, tiles = tc_tiles(M, N), G = K / kGroup;
+  if (tiles >= pairs || M > 0x7FFFFFFF) return 1;
+  int s = min(pairs / tiles, G / 4);
+  if (s <= 1) return 1;
+  const int gper = (G + s - 1) / s;
+  return (G + gper - 1) / gper;
+}
+
+static size_t al256_tc(size_t b) { return (b + 255) & ~(size_t)255; }
+
+size_t gemm_tc_workspace(int64_t M, int N, int K) {
+  if (tc_splits(M, N, K) == 1) return 0;
+  return al256_tc((size_t)M * N * sizeof(unsigned long long)) + (size_t)tc_tiles(M, N) * 16 * sizeof(uint32_t);
+}
+
+// workspace: gemm_tc_workspace(M, N, K) bytes, zero-filled and left so, or
+// NULL (then no split-K).
 cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
-                           const void* bias, int bias_dtype, void* out, int out_dtype, void*, size_t,
-                           cudaStream_t st) {
+                           const void* bias, int bias_dtype, void* out, int out_dtype, void* workspace,
+                           size_t workspace_bytes, cudaStream_t st) {
   auto encode = get_encode();
   if (!encode) return cudaErrorNotSupported;
   if (M > 0x7FFFFFFF) return cudaErrorInvalidValue;
@@ -505,14 +617,26 @@ cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int
   p.bias_dtype = bias_dtype;
   p.out = out;
   p.out_dtype = out_dtype;
+  p.ws = nullptr;
+  p.cnt = nullptr;
+  p.splits = 1;
+  const size_t wsb = gemm_tc_workspace(M, N, K);
+  if (wsb && workspace && workspace_bytes >= wsb) {
+    p.splits = tc_splits(M, N, K);
+    p.ws = static_cast<unsigned long long*>(workspace);
+    p.cnt = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) +
+                                        al256_tc((size_t)M * N * sizeof(unsigned long long)));
+  }
+  p.gper = (G + p.splits - 1) / p.splits;
   cudaError_t e = ensure_smem_limit((const void*)gemm_tc_kernel, kTcSmem);
   if (e != cudaSuccess) return e;
   p.tiles_n = (N + 2 * kTcRows - 1) / (2 * kTcRows);
   const int64_t tiles = (int64_t)p.tiles_n * ((M + kTcTok - 1) / kTcTok);
   if (tiles > 0x7FFFFFFF) return cudaErrorInvalidValue;
   p.tiles = (int)tiles;
+  p.items = p.tiles * p.splits;
   tc_sms();
-  const int pairs = (int)(tiles < g_tc_sms / 2 ? tiles : g_tc_sms / 2);
+  const int pairs = (int)(p.items < g_tc_sms / 2 ? p.items : g_tc_sms / 2);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(2 * pairs));
   cfg.blockDim = dim3(kTcThreads);
