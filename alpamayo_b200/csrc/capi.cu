@@ -35,7 +35,7 @@ size_t gemm_decode_workspace(int64_t M, int N);
 cudaError_t launch_add_rmsnorm(const void* x, void* residual, const void* weight, int64_t M, int K, float eps,
                                void* out, cudaStream_t st);
 cudaError_t launch_silu_mul(const void* x, int64_t M, int I, void* out, cudaStream_t st);
-size_t linear_decode_workspace(int64_t M, int N);
+size_t linear_decode_workspace(int64_t M, int N, int K);
 size_t linear_decode_scratch(int64_t M, int K);
 cudaError_t launch_linear_decode(const void* x, int x_dtype, const uint16_t* cscale, const uint32_t* rtab, int64_t M,
                                  int N, int K, const void* packed, const void* bias, int bias_dtype, void* out,
@@ -237,7 +237,7 @@ extern "C" {
 size_t paro_w4a8_linear_workspace_size(int64_t M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0 || N % kRecRows || K % kGroup) return 0;
   size_t ws = paro_w4a8_gemm_workspace_size(M, N, K);
-  if (M <= kLinearFusedMaxM) ws = std::max(ws, linear_decode_workspace(M, N));
+  if (M <= kLinearFusedMaxM) ws = std::max(ws, linear_decode_workspace(M, N, K));
   return ws;
 }
 
@@ -270,7 +270,7 @@ int paro_w4a8_linear(const void* x, int x_dtype, int64_t M, int K, int N, const 
   // programmatic dependent launch (measured on B200 faster than the
   // activation kernel + GEMM pair, whose single-pass activation kernel
   // spreads a row over one 8-CTA cluster)
-  if (M <= kLinearFusedMaxM && fp16_round && !gemm_tc_supported(M, N, K)) {
+  if (M <= kLinearFusedMaxM && fp16_round) {
     const cudaError_t e = launch_linear_decode(x, x_dtype, channel_scales, rot_table, M, N, K, packed, bias,
                                                bias_dtype, out, out_dtype, workspace, scratch, st);
     if (e != cudaErrorNotSupported) return cuda_status(e);

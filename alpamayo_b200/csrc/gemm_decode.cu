@@ -695,10 +695,28 @@ cudaError_t launch_gemm_decode(const int8_t* xq, const float* xscale, int64_t M,
 // weight stream started during both, consumes them
 // ---------------------------------------------------------------------------
 cudaError_t launch_rot16_decode(int x_dtype, const void* x, int64_t M, int K, const uint16_t* scales,
-                                const uint32_t* rtab, __half* y, uint32_t* amax, cudaStream_t st);
+                                const uint32_t* rtab, __half* y, uint32_t* amax, int frag, cudaStream_t st);
+int gemm_tc_supported(int64_t M, int N, int K);
+size_t gemm_tc_workspace(int64_t M, int N, int K);
+cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
+                           const void* bias, int bias_dtype, void* out, int out_dtype, void* workspace,
+                           size_t workspace_bytes, cudaStream_t st);
 
-size_t linear_decode_workspace(int64_t M, int N) {
-  return gemm_decode_workspace(M, N) + (((size_t)M * sizeof(uint32_t) + 255) & ~(size_t)255);
+// Linears of 25-64 tokens whose GEMM is faster on the tensor cores (256-token
+// tiles, split-K over the CTA pairs): the layers gemm_tc_supported already
+// sends there (gate_up), and, from 33 tokens, long rows (K >= 8192: down,
+// where the streaming kernel is bound by its mma.sync rate: 72 us against
+// 41 us for the GEMM at 64 tokens, measured on B200).  Their rows still take
+// this file's rotation + quantiser chain, in channel order.
+int linear_decode_tc(int64_t M, int N, int K) {
+  if (M > kDecMaxTokens || N % kRecRows || K % kGroup) return 0;
+  return (M > 24 && gemm_tc_supported(M, N, K)) || (M > 32 && K / kGroup >= 64);
+}
+
+size_t linear_decode_workspace(int64_t M, int N, int K) {
+  const size_t tc = linear_decode_tc(M, N, K) ? gemm_tc_workspace(M, N, K) : 0;
+  const size_t dec = gemm_decode_workspace(M, N);
+  return (tc > dec ? tc : dec) + (((size_t)M * sizeof(uint32_t) + 255) & ~(size_t)255);
 }
 
 static int token_tiles(int64_t M) { return M <= 8 ? 1 : M <= 16 ? 2 : M <= 32 ? 4 : 8; }
@@ -745,12 +763,16 @@ cudaError_t launch_linear_decode(const void* x, int x_dtype, const uint16_t* csc
                                  int out_dtype, void* ws, void* scratch, cudaStream_t st) {
   if (M > kDecMaxTokens || M <= 0) return cudaErrorNotSupported;
   DecParams p = dec_params(M, N, K, packed, bias, bias_dtype, out, out_dtype, ws);
-  uint8_t* tail = static_cast<uint8_t*>(ws) + gemm_decode_workspace(M, N);
+  // (the tensor-core GEMM's row stores want a 16-byte aligned output)
+  const bool tc = linear_decode_tc(M, N, K) && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+  const size_t tcb = tc ? gemm_tc_workspace(M, N, K) : 0;
+  const size_t decb = gemm_decode_workspace(M, N);
+  uint8_t* tail = static_cast<uint8_t*>(ws) + (tcb > decb ? tcb : decb);
   p.amax = reinterpret_cast<uint32_t*>(tail);
   // rotation into the fp16 scratch, quantisation (fragment order + code
-  // sums), then the GEMM
+  // sums, or channel order for the tensor-core GEMM), then the GEMM
   __half* rot16 = static_cast<__half*>(scratch);
-  cudaError_t e = launch_rot16_decode(x_dtype, x, M, K, cscale, rtab, rot16, p.amax, st);
+  cudaError_t e = launch_rot16_decode(x_dtype, x, M, K, cscale, rtab, rot16, p.amax, tc ? 0 : 1, st);
   if (e != cudaSuccess) return e;
   uint8_t* sp = static_cast<uint8_t*>(scratch) + al256((size_t)M * K * 2);
   int8_t* xq = reinterpret_cast<int8_t*>(sp);
@@ -759,6 +781,13 @@ cudaError_t launch_linear_decode(const void* x, int x_dtype, const uint16_t* csc
   const int Mp = 8 * token_tiles(M);
   e = launch_quant16_decode(rot16, p.amax, M, K, Mp, xq, xs, gsum, st);
   if (e != cudaSuccess) return e;
+  if (tc) {
+    // the tensor-core GEMM does not read the row maxima: clear them here
+    // (behind the quantiser on the stream)
+    e = cudaMemsetAsync(p.amax, 0, (size_t)M * sizeof(uint32_t), st);
+    if (e != cudaSuccess) return e;
+    return launch_gemm_tc(xq, xs, M, N, K, packed, bias, bias_dtype, out, out_dtype, tcb ? ws : nullptr, tcb, st);
+  }
   p.xq = xq;
   p.xscale = xs;
   p.gsum = gsum;

@@ -20,15 +20,17 @@
 // bits), then one shared-memory atomic per warp and one global atomicMax per
 // row and CTA.
 //
-// Output order: within each group the 32 quads of 4 channels are stored in
-// the order the GEMM's mma fragments read them (quad j*4 + t at position
-// t*8 + j), so the quantiser writes its int8 codes straight into fragment
-// order.  The scratch is private to the linear.
+// Output order (FRAG, for the streaming GEMM): within each group the 32
+// quads of 4 channels are stored in the order its mma fragments read them
+// (quad j*4 + t at position t*8 + j), so the quantiser writes its int8 codes
+// straight into fragment order; without FRAG (for the tensor-core GEMM's
+// tiled loads) the channels keep their order.  The scratch is private to the
+// linear.
 #include "tc_ptx.cuh"
 
 namespace paro {
 
-template <typename InT, int R>
+template <typename InT, int R, bool FRAG>
 __global__ void __launch_bounds__(128)
 rot16_decode_kernel(const InT* x, int64_t M, int K, const uint16_t* __restrict__ scales,
                     const uint32_t* __restrict__ rtab, __half* __restrict__ y, uint32_t* __restrict__ amax) {
@@ -40,7 +42,7 @@ rot16_decode_kernel(const InT* x, int64_t M, int K, const uint16_t* __restrict__
   const int ch = threadIdx.x, lane = ch & 31;
   const int c = blockIdx.x * 128 + ch;
   // where this channel's value goes: quad w = ch / 4 to position (w % 4) * 8 + w / 4
-  const int cpos = blockIdx.x * 128 + ((((ch >> 2) & 3) << 3) + (ch >> 4)) * 4 + (ch & 3);
+  const int cpos = FRAG ? blockIdx.x * 128 + ((((ch >> 2) & 3) << 3) + (ch >> 4)) * 4 + (ch & 3) : c;
   const int64_t r0 = (int64_t)blockIdx.y * R;
   const int nrows = M - r0 < R ? (int)(M - r0) : R;
 
@@ -87,7 +89,7 @@ rot16_decode_kernel(const InT* x, int64_t M, int K, const uint16_t* __restrict__
   if (ch < nrows && cmax[ch]) atomicMax(amax + r0 + ch, cmax[ch]);
 }
 
-template <typename InT, int R>
+template <typename InT, int R, bool FRAG>
 static cudaError_t launch_r(const void* x, int64_t M, int K, const uint16_t* scales, const uint32_t* rtab, __half* y,
                             uint32_t* amax, cudaStream_t st) {
   cudaLaunchConfig_t cfg = {};
@@ -100,31 +102,40 @@ static cudaError_t launch_r(const void* x, int64_t M, int K, const uint16_t* sca
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, rot16_decode_kernel<InT, R>, static_cast<const InT*>(x), M, K, scales, rtab, y,
+  return cudaLaunchKernelEx(&cfg, rot16_decode_kernel<InT, R, FRAG>, static_cast<const InT*>(x), M, K, scales, rtab, y,
                             amax);
 }
 
-template <typename InT>
+template <typename InT, bool FRAG>
 static cudaError_t launch_t(const void* x, int64_t M, int K, const uint16_t* scales, const uint32_t* rtab, __half* y,
                             uint32_t* amax, cudaStream_t st) {
   // one row per CTA: a CTA with R rows runs its eight exchange rounds R
   // times longer, and at decode sizes the kernel's latency is what the
   // linear waits for (measured on B200, 8 tokens: R = 8 cost 2.3 us more per
   // qkv / o linear than R = 1, 16 tokens on down 7 us more)
-  return launch_r<InT, 1>(x, M, K, scales, rtab, y, amax, st);
+  return launch_r<InT, 1, FRAG>(x, M, K, scales, rtab, y, amax, st);
 }
 
-// amax must hold zeros for the M rows (the consuming GEMM returns it to
-// zero); y receives M x K fp16 values, quads in fragment order.
-cudaError_t launch_rot16_decode(int x_dtype, const void* x, int64_t M, int K, const uint16_t* scales,
-                                const uint32_t* rtab, __half* y, uint32_t* amax, cudaStream_t st) {
-  if (M <= 0 || M > 65535) return cudaErrorInvalidValue;
+template <bool FRAG>
+static cudaError_t launch_d(int x_dtype, const void* x, int64_t M, int K, const uint16_t* scales,
+                            const uint32_t* rtab, __half* y, uint32_t* amax, cudaStream_t st) {
   switch (x_dtype) {
-    case PARO_F32: return launch_t<float>(x, M, K, scales, rtab, y, amax, st);
-    case PARO_F16: return launch_t<__half>(x, M, K, scales, rtab, y, amax, st);
-    case PARO_BF16: return launch_t<__nv_bfloat16>(x, M, K, scales, rtab, y, amax, st);
+    case PARO_F32: return launch_t<float, FRAG>(x, M, K, scales, rtab, y, amax, st);
+    case PARO_F16: return launch_t<__half, FRAG>(x, M, K, scales, rtab, y, amax, st);
+    case PARO_BF16: return launch_t<__nv_bfloat16, FRAG>(x, M, K, scales, rtab, y, amax, st);
   }
   return cudaErrorInvalidValue;
+}
+
+// amax must hold zeros for the M rows (the consuming kernels return it to
+// zero); y receives M x K fp16 values, quads in fragment order when frag
+// (for the streaming GEMM), in channel order otherwise (for the tensor-core
+// GEMM's tiled loads).
+cudaError_t launch_rot16_decode(int x_dtype, const void* x, int64_t M, int K, const uint16_t* scales,
+                                const uint32_t* rtab, __half* y, uint32_t* amax, int frag, cudaStream_t st) {
+  if (M <= 0 || M > 65535) return cudaErrorInvalidValue;
+  return frag ? launch_d<true>(x_dtype, x, M, K, scales, rtab, y, amax, st)
+              : launch_d<false>(x_dtype, x, M, K, scales, rtab, y, amax, st);
 }
 
 // Quantisation of the rotated rows: per (group, block of 8 rows) a CTA of 128

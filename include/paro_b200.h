@@ -245,13 +245,14 @@ int paro_device_error_word(int clear);
  * One rotated W4A8 linear: y = paro_w4a8_gemm(paro_rotq_int8(x)), the whole
  * forward of RotateLinearInt4 / BF16RotateLinearWrapper
  * (src/alpamayo_r1/utils/quantization/paroquant_marlin_w4a8.py:47-71 with
- * rotation_linear.py:53-139).  Up to 64 tokens with fp16_round = 1 (and
- * not on the tensor-core GEMM's shapes) it is three chained kernels: one
- * rotates the activations into the scratch (fp16, one CTA per (128-channel
- * group, token)) and records each row's |max|, one quantises the rows to
- * int8, and the GEMM, launched behind them with programmatic dependent
- * launch, streams its weights meanwhile.  Otherwise it is the activation
- * kernel(s) followed by the GEMM.
+ * rotation_linear.py:53-139).  Up to 64 tokens with fp16_round = 1 it is
+ * three chained kernels: one rotates the activations into the scratch
+ * (fp16, one CTA per (128-channel group, token)) and records each row's
+ * |max|, one quantises the rows to int8, and the GEMM (the streaming kernel,
+ * launched behind them with programmatic dependent launch so that its weight
+ * stream starts early; or, for 25-64 tokens on gate_up-wide or K >= 8192
+ * layers, the tensor-core kernel).  Otherwise it is the activation kernel(s)
+ * followed by the GEMM.
  *   x             : [M, K] of x_dtype;  channel_scales : fp16 [K] or NULL.
  *   rot_table     : uint32 [8, K] from paro_prepare_rotation (group 128).
  *   workspace     : paro_w4a8_linear_workspace_size(M, N, K) bytes, 256-byte

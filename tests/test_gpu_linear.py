@@ -52,13 +52,15 @@ def test_linear_matches_two_kernel_route(ops, M, N, K):
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 3584, 18944), (3, 3584, 18944), (8, 3584, 18944), (4, 37888, 3584),
-                                   (16, 37888, 3584), (20, 37888, 3584), (64, 256, 18944), (40, 37888, 3584)])
+                                   (16, 37888, 3584), (20, 37888, 3584), (64, 256, 18944), (40, 37888, 3584),
+                                   (48, 3584, 18944)])
 def test_linear_large_shapes(ops, M, N, K):
     """down_proj / gate_up decode shapes: quantised rows staged in shared
     memory (down at 1 and 3 tokens; gate_up at 4, 16 and 20 tokens: one, two
     and four token tiles), read from L2 where they do not fit (down at 8
-    tokens; M = 64, K = 18944), and gate_up at 40 tokens (tensor-core GEMM
-    below 65 tokens)."""
+    tokens), and the tensor-core GEMM behind the same rotation + quantiser
+    chain below 65 tokens: gate_up at 40 tokens, down at 48, and K = 18944
+    at 64 tokens on one tile (split-K)."""
     L = synthetic_layer(N, K, seed=K + M)
     from alpamayo_b200 import synthetic as syn
     x = syn.make_activations(M, K, seed=M + 1)
