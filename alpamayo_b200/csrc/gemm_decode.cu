@@ -28,8 +28,9 @@
 //  * Segment end: partial sums of the warps are reduced in shared memory by
 //    an epilogue warp.  A segment covering a whole row block is finished in
 //    place (token scale, bias, store).  A boundary segment shared with a
-//    neighbouring CTA adds its partial into a float32 workspace
-//    (red.global.add) and bumps the row block's unit counter; the CTA that
+//    neighbouring CTA adds its partial into a 64-bit fixed-point workspace
+//    (red_add_fx: the total does not depend on the order the CTAs arrive
+//    in) and bumps the row block's unit counter; the CTA that
 //    completes the count applies the epilogue and returns the workspace
 //    slice and counter to zero, so the workspace is zero again after every
 //    call.
@@ -72,7 +73,7 @@ struct DecParams {
   int bias_dtype;
   void* out;
   int out_dtype;
-  float* ws;        // [N][M] float32 partial sums, zero between calls
+  unsigned long long* ws;  // [N][M] fixed-point (red_add_fx) partial sums, zero between calls
   uint32_t* cnt;    // [token slices][N/16] unit counters, zero between calls
   // linear entry point (kXinPreQ, kXinPreQS): the row maxima the
   // rotation kernel accumulated and the quantiser read; this kernel
@@ -324,7 +325,7 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
             store_out(p.out, p.out_dtype, (size_t)t * p.N + n,
                       v[sl] * tok_scale_s[t - tok0] + bias_at(p.bias, p.bias_dtype, n));
           else
-            red_add_f32(p.ws + (size_t)n * p.M + t, v[sl]);
+            red_add_fx(p.ws + (size_t)n * p.M + t, v[sl]);
         }
       }
       if (!whole) {
@@ -350,7 +351,7 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
               const int idx = base + j * 32 + lane;
               if (idx < nidx) {
                 const int r = idx / ntok, tt = idx - r * ntok;
-                a[j] = ld_cg_f32(p.ws + (size_t)(nb * kRecRows + r) * p.M + tok0 + tt);
+                a[j] = ld_cg_fx(p.ws + (size_t)(nb * kRecRows + r) * p.M + tok0 + tt);
               }
             }
 #pragma unroll
@@ -360,7 +361,7 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
                 const int r = idx / ntok, tt = idx - r * ntok;
                 const int n = nb * kRecRows + r;
                 const int64_t t = tok0 + tt;
-                st_cg_f32(p.ws + (size_t)n * p.M + t, 0.f);
+                st_cg_u64(p.ws + (size_t)n * p.M + t, 0ull);
                 store_out(p.out, p.out_dtype, (size_t)t * p.N + n,
                           a[j] * tok_scale_s[tt] + bias_at(p.bias, p.bias_dtype, n));
               }
@@ -635,7 +636,7 @@ static void init_sms() {
 
 size_t gemm_decode_workspace(int64_t M, int N) {
   const int64_t slices = (M + kDecMaxTokens - 1) / kDecMaxTokens;
-  size_t ws = (size_t)N * (size_t)M * sizeof(float);
+  size_t ws = (size_t)N * (size_t)M * sizeof(unsigned long long);
   ws = (ws + 255) & ~(size_t)255;
   return ws + (size_t)slices * (N / kRecRows) * sizeof(uint32_t);
 }
@@ -667,8 +668,8 @@ static DecParams dec_params(int64_t M, int N, int K, const void* packed, const v
   p.bias_dtype = bias_dtype;
   p.out = out;
   p.out_dtype = out_dtype;
-  const size_t wsf = ((size_t)N * (size_t)M * sizeof(float) + 255) & ~(size_t)255;
-  p.ws = static_cast<float*>(ws);
+  const size_t wsf = ((size_t)N * (size_t)M * sizeof(unsigned long long) + 255) & ~(size_t)255;
+  p.ws = static_cast<unsigned long long*>(ws);
   p.cnt = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(ws) + wsf);
   p.units = (int64_t)(N / kRecRows) * (K / kGroup);
   p.ctas = dec_ctas(N / kRecRows, K / kGroup);

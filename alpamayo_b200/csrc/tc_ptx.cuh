@@ -97,4 +97,24 @@ __device__ __forceinline__ void red_add_f32(float* p, float v) {
   asm volatile("red.global.add.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
 }
 
+// Partial sums shared between CTAs in 64-bit fixed point, 2^-28 units: range 2^35
+// (a partial is at most G * 2^18 * |group scale|, so group scales up to
+// ~900 in magnitude fit even for K = 18944; int4 weight scales are far
+// smaller) and resolution 3.7e-9, below float32's spacing for any partial
+// above 1e-3.  Integer addition makes a total independent of the order the
+// partials arrive in, so the kernels that add them are deterministic.
+__device__ __forceinline__ void red_add_fx(unsigned long long* p, float v) {
+  const long long q = __float2ll_rn(v * 268435456.0f);
+  asm volatile("red.global.add.u64 [%0], %1;" ::"l"(p), "l"((unsigned long long)q) : "memory");
+}
+__device__ __forceinline__ float ld_cg_fx(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.global.cg.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return __ll2float_rn((long long)v) * 3.7252902984619141e-09f;   // 2^-28
+}
+__device__ __forceinline__ void st_cg_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.global.cg.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+
 }  // namespace paro

@@ -290,7 +290,7 @@ int paro_w4a8_gemm_path(int64_t M, int N, int K);
  *    up the array's device address (cudaGetSymbolAddress).  Make that first
  *    call before any stream capture.
  *  - Limit: shapes that run the decode kernel (M <= 64) need
- *    paro_w4a8_gemm_workspace_size(M, N, K) bytes, about 4 * M * N; a call
+ *    paro_w4a8_gemm_workspace_size(M, N, K) bytes, about 8 * M * N; a call
  *    needing more than PARO_NOALLOC_SCRATCH_BYTES returns
  *    PARO_ERR_TOO_LARGE and launches nothing.  The tensor-core range
  *    (M > 64) needs no scratch.
