@@ -182,3 +182,22 @@ def test_tensor_core_gemm_tiles_match_oracle(ops, N, K, M):
     y32 = ops.w4a8_gemm(dev(xq), dev(xs), packed, N, bias_bf, torch.float32).cpu().numpy()
     assert rel_l2(y32[rows][:, cols], ref) <= 1e-6
     assert _native.capi().paro_device_error_word(1) == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(8, 1024, 18944), (65, 4608, 3584), (64, 256, 18944)])
+def test_gemm_repeats_bit_for_bit(ops, M, N, K):
+    """Partial sums that several CTAs add for one output (the streaming
+    kernel's shared row blocks: 1024 x 18944 at 8 tokens spreads a row block
+    over about three CTAs; the tensor-core kernel's split-K at 65 tokens and
+    on a single tile) go through fixed-point integer adds, so the result does
+    not depend on the order the CTAs finish in: two calls agree bit for bit."""
+    codes, scales, zeros, packed = records_layer(N, K, seed=N // 16 + K + M)
+    rng = np.random.default_rng(N + K + M)
+    xq = rng.integers(-127, 128, (M, K)).astype(np.int8)
+    xs = (rng.random(M) * 0.1 + 0.01).astype(np.float32)
+    y1 = _run(ops, xq, xs, packed, N, None, torch.float32)
+    y2 = _run(ops, xq, xs, packed, N, None, torch.float32)
+    assert torch.equal(y1, y2)
+    cols = np.sort(rng.choice(N, size=min(N, 256), replace=False))
+    ref = O.w4a8_linear(xq, xs, codes[cols], zeros[:, cols], scales[:, cols])
+    assert rel_l2(y1.cpu().numpy()[:, cols], ref) <= 1e-6
