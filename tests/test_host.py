@@ -91,6 +91,29 @@ def test_gemm_kernel_choice_by_shape():
     assert L.paro_w4a8_gemm_path(65, 100, 3584) == 0   # not a whole number of 16-row records
 
 
+def test_workspace_sizes_by_route():
+    """Workspace sizes are host arithmetic (no device work; the SM count falls
+    back to 148 without a GPU): the streaming kernel's [N][M] 64-bit
+    fixed-point partial sums plus a counter per 16-row block; the tensor-core
+    kernel's split-K sums ([M][N] 64-bit) plus 16 counters per 256x256 tile
+    when its tiles fill fewer than the CTA pairs, else nothing; the linear's
+    at least what its route needs."""
+    from alpamayo_b200._native import capi
+    import torch
+    L = capi()
+    if torch.cuda.is_available() and torch.cuda.get_device_properties(0).multi_processor_count != 148:
+        pytest.skip("sizes below assume 148 SMs")
+    al = lambda b: (b + 255) // 256 * 256
+    # streaming kernel (8 tokens): one token slice, N / 16 counters
+    assert L.paro_w4a8_gemm_workspace_size(8, 3584, 3584) == al(3584 * 8 * 8) + (3584 // 16) * 4
+    # tensor-core kernel with split-K: qkv at 65 tokens is 18 tiles < 74 pairs
+    assert L.paro_w4a8_gemm_workspace_size(65, 4608, 3584) == al(65 * 4608 * 8) + 18 * 16 * 4
+    # ... and without: 144 tiles at 2048 tokens fill the pairs
+    assert L.paro_w4a8_gemm_workspace_size(2048, 4608, 3584) == 0
+    # the linear for down at 64 tokens takes the tensor-core route (14 tiles)
+    assert L.paro_w4a8_linear_workspace_size(64, 3584, 18944) >= al(64 * 3584 * 8) + 14 * 16 * 4
+
+
 def test_header_has_reference_citations():
     src = open(os.path.join(ROOT, "include", "paro_b200.h")).read()
     for cite in ["rotation.cu:456-493", "int8_utils.py", "_custom_ops.py:1277-1318", "paroquant_marlin_w4a8.py"]:
