@@ -99,12 +99,15 @@ def test_linear_against_oracle(ops, M):
 
 def test_linear_c_abi_leaves_workspace_zero(ops):
     """Through the C ABI with an explicit zero-filled workspace: several
-    calls of different shapes in a row, the workspace is all zero after
-    each, and repeated calls give the same output."""
+    calls of different shapes and routes in a row (streaming GEMM; the
+    tensor-core GEMM behind the decode chain, with and without split-K; the
+    two-kernel path with split-K), the workspace is all zero after each, and
+    repeated calls give the same output bit for bit."""
     from alpamayo_b200 import _native
     from alpamayo_b200 import synthetic as syn
     Lc = _native.capi()
-    shapes = [(8, 4608, 3584), (1, 512, 1024), (37, 4608, 3584), (8, 4608, 3584)]
+    shapes = [(8, 4608, 3584), (1, 512, 1024), (37, 4608, 3584), (48, 3584, 18944), (40, 37888, 3584),
+              (100, 4608, 3584), (8, 4608, 3584), (48, 3584, 18944), (100, 4608, 3584)]
     layers = {(N, K): synthetic_layer(N, K, seed=N + K) for (_, N, K) in shapes}
     wsb = max(Lc.paro_w4a8_linear_workspace_size(M, N, K) for (M, N, K) in shapes)
     scb = max(Lc.paro_w4a8_linear_scratch_size(M, N, K, 1) for (M, N, K) in shapes)
@@ -122,7 +125,7 @@ def test_linear_c_abi_leaves_workspace_zero(ops):
         torch.cuda.synchronize()
         assert torch.count_nonzero(ws).item() == 0
         if (M, N, K) in first:
-            assert rel_l2(y.cpu().numpy(), first[(M, N, K)]) <= 1e-6
+            assert np.array_equal(y.cpu().numpy(), first[(M, N, K)])
         first[(M, N, K)] = y.cpu().numpy()
     assert Lc.paro_device_error_word(1) == 0
 
