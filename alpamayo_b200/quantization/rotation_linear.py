@@ -25,6 +25,11 @@ from .quantization_utils import pseudo_quantize_tensor
 
 
 def _default_device():
+    """Device of the default buffers ``Rotation`` creates when no tables are
+    given.  The reference hard-codes "cuda" (rotation_linear.py:25-29); here
+    it is "cuda" when a GPU is present and "cpu" otherwise, so modules can
+    be built and checkpoints loaded or converted on a machine without a GPU
+    (the forward still needs CUDA tensors)."""
     return "cuda" if torch.cuda.is_available() else "cpu"
 
 

@@ -9,6 +9,11 @@ runs on CPU only.  The fixtures it writes (``*.npz`` beside this file) are
 committed; tests never need the reference itself.
 
 Functions called from the reference (paths relative to its root):
+  src/alpamayo_r1/utils/quantization/rotation_linear.py:78-118 RotateLinearInt4.from_linear
+      (rotate_weight=True, init_only=False: rotate_tensor -> quantizer ->
+      pseudo_quantize_tensor -> WQLinear.from_linear); the reference moves
+      tensors to CUDA there (rotation_utils.py:49,83), so while it runs
+      Tensor.cuda / Module.cuda are no-ops and everything stays on the CPU
   src/alpamayo_r1/utils/quantization/rotation_utils.py:8-29   apply_rotation_step
   src/alpamayo_r1/utils/quantization/quantization_utils.py:18-73 pseudo_quantize_tensor
   src/alpamayo_r1/utils/quantization/qmodule.py:39-78,149-205  pack_intweight, WQLinear.from_linear
@@ -92,9 +97,89 @@ def ref_rotate(ru, t, pairs, theta, cs, divide):
     return t
 
 
+def sha256(a):
+    import hashlib
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def reference_from_linear(rl, qm, W, pairs, theta, cs, bias=None):
+    """The reference's offline path, RotateLinearInt4.from_linear(linear,
+    theta, pairs, cs, rotate_weight=True, init_only=False), on the CPU; also
+    returns the raw int codes its WQLinear.from_linear hands to
+    pack_intweight (before any packing, so out-of-range codes are seen)."""
+    N, K = W.shape
+    lin = torch.nn.Linear(K, N, bias=bias is not None)
+    with torch.no_grad():
+        lin.weight.copy_(W)
+        if bias is not None:
+            lin.bias.copy_(bias)
+    seen = {}
+    orig_pack = qm.pack_intweight
+
+    def recording_pack(intweight, *a, **k):
+        seen["codes"] = intweight.clone()
+        return orig_pack(intweight, *a, **k)
+
+    saved = (torch.Tensor.cuda, torch.nn.Module.cuda)
+    torch.Tensor.cuda = lambda self, *a, **k: self
+    torch.nn.Module.cuda = lambda self, *a, **k: self
+    qm.pack_intweight = recording_pack
+    try:
+        m = rl.RotateLinearInt4.from_linear(lin, theta, pairs, cs, rotate_weight=True, init_only=False)
+    finally:
+        torch.Tensor.cuda, torch.nn.Module.cuda = saved
+        qm.pack_intweight = orig_pack
+    q = m.qlinear
+    return q.qweight.clone(), q.scales.clone(), q.scaled_zeros.clone(), seen["codes"].to(torch.int32)
+
+
+def per_token_int8(v):
+    """vLLM per_token_quant_int8 (int8_utils.py:106-128), restated: absmax
+    clamped at 1e-10, scale absmax / 127, codes round-half-away of
+    v * (127 / absmax)."""
+    absmax = v.abs().amax(dim=-1, keepdim=True).clamp_min(1e-10)
+    t = v * (127.0 / absmax)
+    q = torch.sign(t) * torch.floor(t.abs() + 0.5)
+    return q.clamp(-127, 127), absmax / 127.0
+
+
 def main(root):
     ru, qu, qm, rl, pm, mu = import_reference(root)
     torch.set_num_threads(max(1, os.cpu_count() or 1))
+
+    # ---- the reference's offline from_linear on a small layer --------------
+    N, K = 128, 1024
+    pairs, theta, cs = make_rotation(K, 41)
+    W = torch.randn(N, K, generator=gen(42)) * 0.02
+    qweight, scales, szeros, raw = reference_from_linear(rl, qm, W, pairs, theta, cs)
+    np.savez_compressed(os.path.join(HERE, f"fromlinear_n{N}_k{K}.npz"), W=W.numpy(), pairs=pairs.numpy(),
+                        theta=theta.numpy(), channel_scales=cs.numpy(), qweight=qweight.numpy(),
+                        scales=scales.numpy(), scaled_zeros=szeros.numpy(), raw_codes=raw.numpy().astype(np.int8))
+
+    # ---- configs[0]: M=16, K=N=3584, fp32 activations ----------------------
+    # weights through the reference's from_linear; the activation half and
+    # the fake-quant matmul of the reference's CPU path: x * s, 8 x
+    # apply_rotation_step, per-token int8 quantise / dequantise, x_dq @ W_dq^T
+    # with W_dq = dequant_wqlinear of the WQLinear buffers, output bf16
+    N = K = 3584
+    M = 16
+    pairs, theta, cs = make_rotation(K, 31)
+    W = torch.randn(N, K, generator=gen(32)) * 0.02
+    qweight, scales, szeros, raw = reference_from_linear(rl, qm, W, pairs, theta, cs)
+    codes = raw.clamp(0, 15)
+    x = make_activations(M, K, 33)
+    rot_x = ref_rotate(ru, x, pairs, theta, cs, divide=False)
+    xq, xs = per_token_int8(rot_x)
+    w_dq = pm.dequant_wqlinear(codes, scales, szeros, GROUP)
+    y = (xq * xs) @ w_dq.t()
+    np.savez_compressed(
+        os.path.join(HERE, "cfg0_m16_k3584.npz"),
+        W_sha256=sha256(W.numpy()), pairs=pairs.numpy(), theta=theta.numpy(), channel_scales=cs.numpy(),
+        qweight_sha256=sha256(qweight.numpy()), codes_sha256=sha256(codes.numpy().astype(np.uint8)),
+        out_of_range_codes=np.int64(((raw < 0) | (raw > 15)).sum().item()),
+        scales=scales.numpy(), scaled_zeros=szeros.numpy(), x=x.numpy(), x_rotated=rot_x.numpy(),
+        xq=xq.numpy().astype(np.int8), xscale=xs.numpy().reshape(-1), y=y.numpy(),
+        y_bf16=y.to(torch.bfloat16).float().numpy())
 
     # ---- rotation fixtures (activation side) ------------------------------
     for (M, K, seed) in [(16, 1024, 11), (4, 3584, 12)]:

@@ -157,3 +157,76 @@ def test_fake_quant_path_close_to_exact_linear():
     # int4 weights + int8 activations: a few percent of error against the
     # unquantised product
     assert np.linalg.norm(y - ref) / np.linalg.norm(ref) < 0.15
+
+
+# ---------------------------------------------------------------------------
+# configs[0] (M=16, K=N=3584) against the reference's own pipeline
+# ---------------------------------------------------------------------------
+
+def test_config0_activation_chain_matches_reference():
+    """x * s -> 8 Givens layers -> per-token int8, at config-0 size, bit for
+    bit against the reference's functions (cfg0_m16_k3584.npz)."""
+    d = load("cfg0_m16_k3584.npz")
+    th = d["theta"].astype(np.float32)
+    cs = d["channel_scales"].astype(np.float32)
+    r = O.rotate_activations(d["x"], d["pairs"], th, cs)
+    assert np.array_equal(r, d["x_rotated"])
+    q, s = O.per_token_quant_int8(r)
+    assert np.array_equal(q, d["xq"])
+    assert np.array_equal(s, d["xscale"])
+
+
+def test_config0_fake_quant_output_matches_reference():
+    """The fake-quant linear of the oracle and of the timed CPU port
+    (oracle/cpu_baseline.py, the bench's CPU baseline and reference arm) on
+    config 0 against the reference pipeline's output: both restate the same
+    float32 arithmetic (the matmul's summation order is the BLAS's), so
+    1e-6 relative L2 in float32, and the same bf16 values but for ties."""
+    import torch
+    from oracle import cpu_baseline as C
+    from tests.helpers import rel_l2
+    d = load("cfg0_m16_k3584.npz")
+    th = d["theta"].astype(np.float32)
+    cs = d["channel_scales"].astype(np.float32)
+    codes, sc, sz = _cfg0_codes(d)
+    w_dq = (codes.astype(np.float32) * np.repeat(sc, 128, axis=0).T.astype(np.float32)
+            + np.repeat(sz, 128, axis=0).T.astype(np.float32))
+    y_or = O.fake_quant_linear(d["x"], d["pairs"], th, cs, w_dq)
+    assert rel_l2(y_or, d["y_bf16"]) <= 1e-3
+    assert np.mean(y_or != d["y_bf16"]) <= 0.01
+    y_cpu = C.fake_quant_linear(torch.from_numpy(d["x"]), torch.from_numpy(d["pairs"]), torch.from_numpy(th),
+                                torch.from_numpy(cs), torch.from_numpy(w_dq)).float().numpy()
+    assert rel_l2(y_cpu, d["y_bf16"]) <= 1e-3
+    assert np.mean(y_cpu != d["y_bf16"]) <= 0.01
+    # the port's activation half alone is the reference's bit for bit
+    t = torch.from_numpy(d["x"]) * torch.from_numpy(cs)
+    for r in range(8):
+        t = C.apply_rotation_step(t, torch.from_numpy(d["pairs"][r]), torch.from_numpy(th[r]))
+    assert np.array_equal(t.numpy(), d["x_rotated"])
+
+
+def _cfg0_codes(d):
+    """Config-0 weights regenerated by the oracle from the reference's seed
+    (torch.randn, as gen_golden.py draws them), checked against the
+    reference's hashes: W, then the int4 codes of the weight-side transform
+    + pseudo-quantisation (clamped, as WQLinear.from_linear computes them
+    from the fp16 weight)."""
+    import hashlib
+    import torch
+    W = (torch.randn(3584, 3584, generator=torch.Generator().manual_seed(32)) * 0.02).numpy()
+    assert hashlib.sha256(W.tobytes()).hexdigest() == str(d["W_sha256"])
+    G = 28
+    sc = d["scales"][:G].astype(np.float32)
+    sz = d["scaled_zeros"][:G].astype(np.float32)
+    from alpamayo_b200.quantization import RotateLinearInt4
+    lin = torch.nn.Linear(3584, 3584, bias=False)
+    with torch.no_grad():
+        lin.weight.copy_(torch.from_numpy(W))
+    m = RotateLinearInt4.from_linear(lin, torch.from_numpy(d["theta"]), torch.from_numpy(d["pairs"]),
+                                     torch.from_numpy(d["channel_scales"]), rotate_weight=True, init_only=False)
+    q = m.qlinear
+    assert np.array_equal(q.scales.numpy(), d["scales"]) and np.array_equal(q.scaled_zeros.numpy(), d["scaled_zeros"])
+    codes = O.unpack_wqlinear_qweight(q.qweight.numpy(), 3584, 3584)
+    assert hashlib.sha256(np.ascontiguousarray(codes.astype(np.uint8)).tobytes()).hexdigest() == str(d["codes_sha256"])
+    assert hashlib.sha256(q.qweight.numpy().tobytes()).hexdigest() == str(d["qweight_sha256"])
+    return codes, sc, sz
