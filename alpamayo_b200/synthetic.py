@@ -75,9 +75,11 @@ def pack_wqlinear_gpu(codes):
 
 
 @torch.no_grad()
-def make_layer(N, K, seed, device="cuda", checkpoint=True):
+def make_layer(N, K, seed, device="cuda", checkpoint=True, keep_awq=False):
     """A quantised layer: rotation buffers, WQLinear buffers (if
-    ``checkpoint``) and the derived tile records / uint8 pairs."""
+    ``checkpoint``) and the derived tile records / uint8 pairs; with
+    ``keep_awq`` (AWQ route only) also the AWQ int32 buffers
+    ``awq_qweight`` [K, N/8], ``awq_scales`` [G, N], ``awq_qzeros`` [G, N/8]."""
     pairs, theta, cs = make_rotation(K, seed, device)
     g = _gen(seed + 1, device)
     W = torch.randn(N, K, generator=g, device=device) * 0.02
@@ -106,8 +108,11 @@ def make_layer(N, K, seed, device="cuda", checkpoint=True):
     else:
         # AWQ int32 route: same codes / zero points, vectorised on the GPU
         zq = torch.clamp(torch.round(-szeros[:G].float() / scales[:G].float()), 0, 15)
-        layer["packed"] = ops.prepare_weights_awq(pack_awq_gpu(codes.t().contiguous()), scales[:G].contiguous(),
-                                                  pack_awq_gpu(zq.to(torch.uint8)), N, K)
+        awq = (pack_awq_gpu(codes.t().contiguous()), scales[:G].contiguous(), pack_awq_gpu(zq.to(torch.uint8)))
+        layer["packed"] = ops.prepare_weights_awq(awq[0], awq[1], awq[2], N, K)
+        if keep_awq:
+            layer["awq_qweight"], layer["awq_scales"], layer["awq_qzeros"] = awq
+        del awq
     del codes
     layer["rot_table"] = ops.prepare_rotation(pairs, theta, GROUP)
     layer["cs_vec"] = cs.reshape(-1).contiguous()
