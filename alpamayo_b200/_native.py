@@ -70,6 +70,8 @@ def capi() -> ctypes.CDLL:
         "paro_w4a8_linear_scratch_size": (sz, [i64, i32, i32, i32]),
         "paro_w4a8_linear": (i32, [vp, i32, i64, i32, i32, vp, vp, i32, vp, vp, i32, vp, i32, vp, sz, vp, sz, vp]),
         "paro_device_error_word": (i32, [i32]),
+        "paro_selftest_wait_timeout": (i32, [ctypes.c_longlong, vp]),
+        "paro_w4a8_gemm_noalloc": (i32, [vp, vp, i64, i32, i32, vp, vp, i32, vp, i32, vp]),
         "paro_add_rmsnorm": (i32, [vp, vp, vp, i64, i32, ctypes.c_float, vp, vp]),
         "paro_silu_mul": (i32, [vp, i64, i32, vp, vp]),
     }
@@ -79,6 +81,21 @@ def capi() -> ctypes.CDLL:
         f.argtypes = args
     _capi = L
     return L
+
+
+_shim = None
+
+
+def shim() -> ctypes.CDLL:
+    """The torch operator shim as a ctypes library (its few extern "C"
+    helpers, e.g. paro_torch_reset_workspaces)."""
+    global _shim
+    if _shim is None:
+        load_ops()
+        _shim = ctypes.CDLL(TORCH_LIB)
+        _shim.paro_torch_reset_workspaces.restype = ctypes.c_int
+        _shim.paro_torch_reset_workspaces.argtypes = []
+    return _shim
 
 
 DTYPE_CODE = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}

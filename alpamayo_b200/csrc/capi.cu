@@ -42,6 +42,7 @@ cudaError_t launch_linear_decode(const void* x, int x_dtype, const uint16_t* csc
                                  int out_dtype, void* ws, void* scratch, cudaStream_t st);
 int gemm_tc_supported(int64_t M, int N, int K);
 size_t gemm_tc_workspace(int64_t M, int N, int K);
+cudaError_t launch_selftest_wait(long long limit_cycles, cudaStream_t st);
 cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
                            const void* bias, int bias_dtype, void* out, int out_dtype, void* ws, size_t ws_bytes,
                            cudaStream_t st);
@@ -54,6 +55,7 @@ namespace paro {
 uint32_t error_word_decode(int clear);
 uint32_t error_word_tc(int clear);
 uint32_t error_word_rtc(int clear);
+uint32_t error_word_rows(int clear);
 
 cudaError_t ensure_smem_limit(const void* kernel, int bytes) {
   static std::mutex mu;
@@ -313,9 +315,16 @@ int paro_silu_mul(const void* x, int64_t M, int I, void* out, paro_stream_t stre
 }
 
 int paro_device_error_word(int clear) {
-  const uint32_t a = error_word_decode(clear), b = error_word_tc(clear), c = error_word_rtc(clear);
-  if (a == ~0u || b == ~0u || c == ~0u) return -1;
-  return (int)(a | b | c);
+  const uint32_t a = error_word_decode(clear), b = error_word_tc(clear), c = error_word_rtc(clear),
+                 d = error_word_rows(clear);
+  if (a == ~0u || b == ~0u || c == ~0u || d == ~0u) return -1;
+  return (int)(a | b | c | d);
+}
+
+int paro_selftest_wait_timeout(long long limit_cycles, paro_stream_t stream) {
+  if (limit_cycles < 1 || limit_cycles > 2000000000LL) return PARO_ERR_INVALID_ARGUMENT;
+  if (int d = device_check()) return d;
+  return cuda_status(launch_selftest_wait(limit_cycles, (cudaStream_t)stream));
 }
 
 int paro_w4a8_gemm(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
@@ -384,8 +393,18 @@ int paro_w4a8_gemm_noalloc(const int8_t* xq, const float* xscale, int64_t M, int
   if (int d = device_check()) return d;
   if (gemm_tc_supported(M, N, K)) {
     if (!aligned(out, 16)) return PARO_ERR_MISALIGNED;
-    return cuda_status(
-        launch_gemm_tc(xq, xscale, M, N, K, packed, bias, bias_dtype, out, out_dtype, nullptr, 0, (cudaStream_t)stream));
+    // split-K partial sums go to the fixed array when they fit (the same
+    // kernel and splits as paro_w4a8_gemm, so the same bits); beyond the
+    // array the kernel runs unsplit, which needs no scratch
+    const size_t tcb = gemm_tc_workspace(M, N, K);
+    void* tws = nullptr;
+    if (tcb && tcb <= (size_t)PARO_NOALLOC_SCRATCH_BYTES) {
+      if (int st = noalloc_scratch(&tws)) return st;
+      const cudaError_t e = cudaMemsetAsync(tws, 0, tcb, (cudaStream_t)stream);
+      if (e != cudaSuccess) return cuda_status(e);
+    }
+    return cuda_status(launch_gemm_tc(xq, xscale, M, N, K, packed, bias, bias_dtype, out, out_dtype, tws,
+                                      tws ? tcb : 0, (cudaStream_t)stream));
   }
   const size_t need = gemm_decode_workspace(M, N);
   if (need > (size_t)PARO_NOALLOC_SCRATCH_BYTES) return PARO_ERR_TOO_LARGE;

@@ -43,10 +43,15 @@ paro_stream_t cur_stream() { return reinterpret_cast<paro_stream_t>(at::cuda::ge
 // concurrent calls do not share it).  It is allocated with at least 16 MiB on
 // first use so later, larger calls (and CUDA graphs captured after a warm-up
 // call) keep a stable address; it only grows for larger shapes.
-void* workspace_for(const c10::Device& dev, size_t bytes) {
-  static std::mutex mu;
+std::mutex g_ws_mu;
+std::map<std::pair<int, cudaStream_t>, at::Tensor>& ws_cache() {
   static std::map<std::pair<int, cudaStream_t>, at::Tensor> cache;
-  std::lock_guard<std::mutex> lock(mu);
+  return cache;
+}
+
+void* workspace_for(const c10::Device& dev, size_t bytes) {
+  auto& cache = ws_cache();
+  std::lock_guard<std::mutex> lock(g_ws_mu);
   const auto key = std::make_pair((int)dev.index(), at::cuda::getCurrentCUDAStream().stream());
   auto it = cache.find(key);
   if (it == cache.end() || (size_t)it->second.numel() < bytes) {
@@ -337,6 +342,24 @@ at::Tensor silu_mul(const at::Tensor& x_in) {
 }
 
 }  // namespace
+
+// Zero-fill every cached GEMM workspace again (after a kernel's bounded
+// wait ran out, an unfinished cross-CTA fix-up may have left partial sums or
+// counters in one).  Synchronises the device first, so no kernel is still
+// using them.  Returns the number of workspaces cleared, or -1 on a CUDA
+// error.
+extern "C" int paro_torch_reset_workspaces() {
+  if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+  std::lock_guard<std::mutex> lock(g_ws_mu);
+  int n = 0;
+  for (auto& kv : ws_cache()) {
+    c10::cuda::CUDAGuard guard((c10::DeviceIndex)kv.first.first);
+    if (cudaMemset(kv.second.data_ptr(), 0, (size_t)kv.second.numel()) != cudaSuccess) return -1;
+    ++n;
+  }
+  if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+  return n;
+}
 
 TORCH_LIBRARY(paro_b200, m) {
   m.def("rotate(Tensor x, Tensor idx_ij, Tensor theta, Tensor? scales, int group_size) -> Tensor");

@@ -128,3 +128,22 @@ def add_rmsnorm(x, residual, weight, eps=1e-6):
 def silu_mul(x):
     """SiLU(gate) * up of a fused gate_up output [..., 2I] -> [..., I] (bf16)."""
     return _ops.silu_mul(x)
+
+
+def device_error_word(clear=True):
+    """Error bits the kernels raised instead of hanging (1 = a bounded
+    pipeline wait ran out, 2 = tensor-memory allocation failed); 0 when all
+    is well, -1 if the word could not be read.  Synchronises the device.
+
+    A non-zero word means the outputs of the calls since the last clean read
+    are invalid and a GEMM workspace may hold the partial sums or counters
+    of an unfinished cross-CTA fix-up, so this also zero-fills every
+    workspace the operators own before returning; the next call then starts
+    from a clean workspace.  (Callers of the C ABI with their own workspaces
+    must zero-fill those themselves.)"""
+    from . import _native
+    w = _native.capi().paro_device_error_word(1 if clear else 0)
+    if w != 0:
+        if _native.shim().paro_torch_reset_workspaces() < 0:
+            raise RuntimeError("paro_b200: could not reset the operator workspaces after a device error")
+    return w

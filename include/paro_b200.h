@@ -238,8 +238,26 @@ int paro_silu_mul(const void* x, int64_t M, int I, void* out, paro_stream_t stre
 
 /* Error bits kernels raise instead of hanging (1 = a pipeline wait timed
  * out, 2 = tensor-memory allocation failed); synchronises with the device to
- * read them.  clear != 0 resets the word.  Returns -1 if it cannot be read. */
+ * read them.  clear != 0 resets the word.  Returns -1 if it cannot be read.
+ *
+ * Recovery: a kernel whose wait ran out stops where it was, so the outputs
+ * of the calls made since the last clean read are invalid, and the
+ * workspaces those calls used (paro_w4a8_gemm, paro_w4a8_linear) may hold
+ * partial sums or unit counters of an unfinished cross-CTA fix-up.  After a
+ * non-zero word, zero-fill every such workspace again before its next use
+ * (the torch operators do this for the workspaces they own when
+ * alpamayo_b200.ops.device_error_word() sees a non-zero word). */
 int paro_device_error_word(int clear);
+
+/* Diagnostics (no counterpart in the reference, which has no bounded
+ * waits): launches one thread that waits, through the same bounded
+ * mbarrier wait every pipelined kernel here uses, on a barrier nothing
+ * arrives on, with a limit of limit_cycles SM clocks (1 .. 2e9).  No copy
+ * is in flight, so the wait runs out, sets bit 1 of the device error word
+ * and the kernel returns; the context stays usable.  Lets a deployment
+ * check that its error polling sees a timed-out wait without breaking
+ * anything. */
+int paro_selftest_wait_timeout(long long limit_cycles, paro_stream_t stream);
 
 /*
  * One rotated W4A8 linear: y = paro_w4a8_gemm(paro_rotq_int8(x)), the whole
@@ -289,11 +307,16 @@ int paro_w4a8_gemm_path(int64_t M, int N, int K);
  *  - Set-up: the first call on a device, with that device current, looks
  *    up the array's device address (cudaGetSymbolAddress).  Make that first
  *    call before any stream capture.
- *  - Limit: shapes that run the decode kernel (M <= 64) need
- *    paro_w4a8_gemm_workspace_size(M, N, K) bytes, about 8 * M * N; a call
- *    needing more than PARO_NOALLOC_SCRATCH_BYTES returns
- *    PARO_ERR_TOO_LARGE and launches nothing.  The tensor-core range
- *    (M > 64) needs no scratch.
+ *  - Limit: a shape uses paro_w4a8_gemm_workspace_size(M, N, K) bytes of
+ *    the array (about 8 * M * N where it is not 0).  Shapes for which
+ *    paro_w4a8_gemm_path returns 0 (the streaming kernel) and that need
+ *    more than PARO_NOALLOC_SCRATCH_BYTES return PARO_ERR_TOO_LARGE and
+ *    launch nothing.  Shapes for which it returns 1 (the tensor-core
+ *    kernel) always run: with split-K through the array when their size
+ *    fits (then bit for bit the result of paro_w4a8_gemm), otherwise
+ *    without split-K, which needs no scratch but is slower on small layers
+ *    at 65 to about 1,300 tokens and rounds the cross-group sums in float32
+ *    instead of 64-bit fixed point (results agree to float32 rounding).
  *  - State: the array keeps whatever the previous call left, so every call
  *    first clears the part it uses (cudaMemsetAsync on `stream`).
  *  - Concurrency: all calls on a device share the one array.  Calls whose

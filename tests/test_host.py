@@ -200,3 +200,90 @@ def test_replace_and_wrap_on_fake_model():
     _wrap_rotate_linears(model)
     w = layer0.self_attn.q_proj
     assert isinstance(w, BF16RotateLinearWrapper) and w.in_features == 256
+
+
+def test_selftest_wait_rejects_bad_limits_on_the_host():
+    from alpamayo_b200._native import capi
+    L = capi()
+    assert L.paro_selftest_wait_timeout(0, None) == 1
+    assert L.paro_selftest_wait_timeout(3_000_000_000, None) == 1
+
+
+def test_device_error_recovery_resets_operator_workspaces(monkeypatch):
+    """The documented recovery after a non-zero device error word: the
+    operator workspaces are zero-filled again before the next call (fakes
+    stand in for the two native libraries)."""
+    import alpamayo_b200._native as N
+    import alpamayo_b200.ops as ops
+    calls = {"read": [], "reset": 0}
+    word = {"v": 0}
+
+    class FakeCapi:
+        def paro_device_error_word(self, clear):
+            calls["read"].append(clear)
+            v = word["v"]
+            if clear:
+                word["v"] = 0
+            return v
+
+    class FakeShim:
+        def paro_torch_reset_workspaces(self):
+            calls["reset"] += 1
+            return 3
+
+    monkeypatch.setattr(N, "capi", lambda: FakeCapi())
+    monkeypatch.setattr(N, "shim", lambda: FakeShim())
+    assert ops.device_error_word() == 0 and calls["reset"] == 0   # clean: nothing reset
+    word["v"] = 1
+    assert ops.device_error_word() == 1 and calls["reset"] == 1   # timed-out wait: workspaces reset
+    assert ops.device_error_word() == 0 and calls["reset"] == 1   # cleared by the read
+    word["v"] = 2
+    assert ops.device_error_word(clear=False) == 2 and calls["reset"] == 2
+    assert calls["read"] == [1, 1, 1, 0]
+
+    class BrokenShim:
+        def paro_torch_reset_workspaces(self):
+            return -1
+
+    monkeypatch.setattr(N, "shim", lambda: BrokenShim())
+    with pytest.raises(RuntimeError):
+        ops.device_error_word()
+
+
+# ---------------------------------------------------------------------------
+# the product's offline quantisation helpers against the reference's outputs
+# ---------------------------------------------------------------------------
+
+def test_product_rotate_tensor_matches_reference_bit_exact():
+    from alpamayo_b200.quantization import rotate_tensor
+    d = np.load(os.path.join(GOLD, "wq_n128_k1024.npz"))
+    w = rotate_tensor(torch.from_numpy(d["W"]), torch.from_numpy(d["theta"]), torch.from_numpy(d["pairs"]),
+                      torch.from_numpy(d["channel_scales"]))
+    assert np.array_equal(w.numpy(), d["w_rot"])
+
+
+def test_product_pseudo_quantize_matches_reference_bit_exact():
+    from alpamayo_b200.quantization import pseudo_quantize_tensor
+    d = np.load(os.path.join(GOLD, "wq_n128_k1024.npz"))
+    wq, s, z = pseudo_quantize_tensor(torch.from_numpy(d["w_rot"]), n_bit=4, q_group_size=128, get_scale_zp=True)
+    assert np.array_equal(wq.numpy(), d["w_dq"])
+    assert np.array_equal(s.numpy(), d["pq_scales"])
+    assert np.array_equal(z.numpy(), d["pq_zeros"])
+
+
+def test_product_from_linear_rotate_weight_matches_reference():
+    """RotateLinearInt4.from_linear(rotate_weight=True, init_only=False):
+    rotate_tensor -> quantizer -> pseudo_quantize_tensor -> WQLinear, on the
+    CPU, equals the reference's checkpoint buffers bit for bit
+    (fromlinear_n128_k1024.npz, written by the reference's own from_linear)."""
+    from alpamayo_b200.quantization import RotateLinearInt4
+    d = np.load(os.path.join(GOLD, "fromlinear_n128_k1024.npz"))
+    lin = torch.nn.Linear(1024, 128, bias=False)
+    with torch.no_grad():
+        lin.weight.copy_(torch.from_numpy(d["W"]))
+    m = RotateLinearInt4.from_linear(lin, torch.from_numpy(d["theta"]), torch.from_numpy(d["pairs"]),
+                                     torch.from_numpy(d["channel_scales"]), rotate_weight=True, init_only=False)
+    assert np.array_equal(m.qlinear.qweight.numpy(), d["qweight"])
+    assert np.array_equal(m.qlinear.scales.numpy(), d["scales"])
+    assert np.array_equal(m.qlinear.scaled_zeros.numpy(), d["scaled_zeros"])
+    assert m.qlinear.qweight.dtype == torch.int16 and m.qlinear.scales.dtype == torch.float16
