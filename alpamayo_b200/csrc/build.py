@@ -25,7 +25,7 @@ OBJ = os.path.join(PKG, "_build")
 CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.path.join(CUDA_HOME, "bin", "nvcc")
 
-CU_SOURCES = ["capi.cu", "rotq.cu", "rotq_fused.cu", "rotq_rows.cu", "rotq_decode.cu", "rotq_tc.cu", "prepare.cu", "gemm_decode.cu", "gemm_tc.cu", "elementwise.cu"]
+CU_SOURCES = ["capi.cu", "rotq.cu", "rotq_fused.cu", "rotq_rows.cu", "rotq_decode.cu", "rotq_tc.cu", "prepare.cu", "gemm_decode.cu", "gemm_rows.cu", "gemm_tc.cu", "elementwise.cu"]
 HEADERS = ["paro_common.cuh", "tc_ptx.cuh", "umma.cuh", "stream_segs.cuh"]
 GENCODE = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",

@@ -42,6 +42,9 @@
 // Record layout: for lane (gid = lane/4, tig = lane%4), the A fragment words
 // of rows gid and gid+8 for the four 32-channel steps of a group are one
 // 16-byte chunk each: low nibbles give a0/a1, high nibbles a2/a3.
+#include <cstdlib>
+#include <cstring>
+
 #include "stream_segs.cuh"
 #include "tc_ptx.cuh"
 
@@ -572,6 +575,25 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
 
 PARO_DEFINE_ERROR_ACCESSOR(decode)
 
+// Self-test of the bounded-wait error path: one thread waits, with the
+// library's own mbar_wait, on a barrier that nothing arrives on.  No copy
+// or other asynchronous operation is in flight, so the wait simply runs out
+// after ~limit_cycles SM clocks, reports kErrMbarTimeout into this file's
+// error word and the kernel returns normally.
+__global__ void selftest_wait_kernel(long long limit_cycles) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    mbar_wait(&bar, 0, limit_cycles);
+  }
+}
+
+cudaError_t launch_selftest_wait(long long limit_cycles, cudaStream_t st) {
+  selftest_wait_kernel<<<1, 32, 0, st>>>(limit_cycles);
+  return cudaGetLastError();
+}
+
 static size_t fixed_smem(int MT) {
   // full/empty rings, seg_full/seg_free pairs, xbar (+1 slot keeps 16-byte
   // alignment), then the reduction slices
@@ -677,9 +699,30 @@ static DecParams dec_params(int64_t M, int N, int K, const void* packed, const v
   return p;
 }
 
+cudaError_t launch_gemm_rows(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
+                             const void* bias, int bias_dtype, void* out, int out_dtype, void* ws, uint32_t* amax,
+                             const int* gsum, int gsum_mp, cudaStream_t st);
+
+// Which decode GEMM runs where both take the shape: gemm_rows_kernel
+// (gemm_rows.cu) unless the environment sets PARO_DECODE_GEMM=stream, which
+// keeps every shape on gemm_stream_kernel (read once per process; for
+// comparing the two).
+static bool rows_kernel_enabled() {
+  static const int on = [] {
+    const char* v = getenv("PARO_DECODE_GEMM");
+    return (v && strcmp(v, "stream") == 0) ? 0 : 1;
+  }();
+  return on != 0;
+}
+
 cudaError_t launch_gemm_decode(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
                                const void* bias, int bias_dtype, void* out, int out_dtype, void* ws,
                                cudaStream_t st) {
+  if (rows_kernel_enabled()) {
+    const cudaError_t e = launch_gemm_rows(xq, xscale, M, N, K, packed, bias, bias_dtype, out, out_dtype, ws, nullptr,
+                                           nullptr, 0, st);
+    if (e != cudaErrorNotSupported) return e;
+  }
   DecParams p = dec_params(M, N, K, packed, bias, bias_dtype, out, out_dtype, ws);
   p.xq = xq;
   p.xscale = xscale;
@@ -788,6 +831,10 @@ cudaError_t launch_linear_decode(const void* x, int x_dtype, const uint16_t* csc
     e = cudaMemsetAsync(p.amax, 0, (size_t)M * sizeof(uint32_t), st);
     if (e != cudaSuccess) return e;
     return launch_gemm_tc(xq, xs, M, N, K, packed, bias, bias_dtype, out, out_dtype, tcb ? ws : nullptr, tcb, st);
+  }
+  if (rows_kernel_enabled()) {
+    e = launch_gemm_rows(xq, xs, M, N, K, packed, bias, bias_dtype, out, out_dtype, ws, p.amax, gsum, Mp, st);
+    if (e != cudaErrorNotSupported) return e;
   }
   p.xq = xq;
   p.xscale = xs;
