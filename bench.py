@@ -15,11 +15,19 @@ is weight-stream GB/s (algorithmic int4 code + fp16 scale + int4 zero bytes
 per second), whole job.
 
 Timing: CUDA graph of one step, replayed; CUDA events around the timed
-replays, barrier + synchronize on both sides, max over ranks.  Per-kernel
-launch durations for the roofline: each case's GEMM (the int8-input
-paro_w4a8_gemm) runs after an L2 flush (a 512 MiB write, then a 256 MiB read so
-that the lines left in the L2 are clean and the timed kernel pays for no
-write-backs), with CUDA events on the launching stream around it.
+replays, barrier + synchronize on both sides, max over ranks.  Roofline of
+the dominant kernel (the decode GEMM): its average launch duration over the
+step's own 192 GEMM launches (16 sweeps x 12 cases on the same three weight
+replicas, working set > L2), replayed back to back as a CUDA graph of the
+int8-input paro_w4a8_gemm and timed with CUDA events on the launching
+stream.  Beside it, each case's single launch after an L2 flush (a 512 MiB
+write, then a 256 MiB read so that the lines left in the L2 are clean and
+the timed kernel pays for no write-backs), which adds a cold launch's fixed
+start-up to every figure.
+
+reference_gpu: the reference's own GPU path on the same B200 (its rotate
+kernel compiled from its source, vLLM's per-token int8 quantiser and Marlin
+W4A8 GEMM, bf16 <-> fp16 casts), timed the same way on the same cases.
 
 Prefill (configs[2], the "prefill" object): the same four projections at
 M = 2048, 4096, 8192 through the tcgen05 GEMM, TOPS against the dense int8
@@ -62,6 +70,13 @@ def args_():
     p.add_argument("--no-prefill", action="store_true")
     p.add_argument("--no-stack", action="store_true")
     p.add_argument("--no-sharded", action="store_true")
+    p.add_argument("--no-reference-gpu", action="store_true",
+                   help="skip timing the reference's own GPU path (its rotate kernel + vLLM Marlin)")
+    p.add_argument("--case", default=None, metavar="SHAPE:M",
+                   help="profiling mode: run one case (e.g. gate_up:8) --case-iters times and exit")
+    p.add_argument("--case-iters", type=int, default=4)
+    p.add_argument("--case-linear", action="store_true",
+                   help="with --case: run the whole linear op (linear_w4a8) instead of activation kernel + GEMM")
     return p.parse_args()
 
 
@@ -353,6 +368,93 @@ def sharded_section(torch, world, rank):
             "copy_engine_gather": (p2p.get("unavailable") and p2p) or ce or None}
 
 
+def reference_gpu_section(torch, syn, flush, steps, warmup):
+    """The reference's own GPU path on this B200, timed like ours: its rotate
+    kernel (compiled from the reference's source by oracle/build_ref.py) and
+    vLLM's per-token int8 quantiser + Marlin W4A8 GEMM, called as
+    BF16RotateLinearWrapper -> RotateLinearInt4 -> MarlinW4A8Linear do
+    (oracle/ref_gpu.py).  Decode sweep: the same 12 (shape, M)
+    linears, 16 sweeps per step over three weight replicas, CUDA graph,
+    weight-stream GB/s.  Prefill: each shape at M = 2048, 4096,
+    8192, one call after an L2 flush, CUDA events, int8 TOPS."""
+    from oracle import ref_gpu as R
+    rot_ok, marlin_ok, why = R.available()
+    if not (rot_ok and marlin_ok):
+        return {"unavailable": why}
+    reps = []
+    for ri, M in enumerate(DECODE_M):
+        layer = {}
+        for si, (name, N, K) in enumerate(SHAPES):
+            L = syn.make_layer(N, K, seed=5000 + 100 * ri + si, checkpoint=False, keep_awq=True)
+            layer[name] = R.ReferenceLinear(L["pairs"], L["theta"], L["channel_scales"], L["awq_qweight"],
+                                            L["awq_scales"], L["awq_qzeros"], K, N)
+            del L
+        reps.append(layer)
+    xs = {(M, K): syn.make_activations(M, K, seed=7 * M + K) for M in DECODE_M for K in {3584, 18944}}
+
+    def step():
+        for _ in range(STEP_SWEEPS):
+            for ri, M in enumerate(DECODE_M):
+                for (name, N, K) in SHAPES:
+                    reps[ri][name](xs[(M, K)])
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()
+    torch.cuda.current_stream().wait_stream(s)
+    mode = "CUDA graph of one step"
+    try:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step()
+        run = g.replay
+    except Exception as e:  # the reference's ops not capturable: time eager launches
+        g, run, mode = None, step, f"eager launches ({type(e).__name__} under capture)"
+    for _ in range(warmup):
+        run()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    wset = sum(weight_bytes(N, K) for (_, N, K) in SHAPES) * len(DECODE_M)
+    dec = {"weight_GBps": round(STEP_SWEEPS * wset / (ms * 1e-3) / 1e9, 1), "ms_per_step": round(ms, 4),
+           "timing": mode}
+    cases = {}
+    for (name, N, K) in SHAPES:
+        lin = reps[0][name]
+        for M in (1, 8):
+            x = xs[(M, K)]
+            ts = kernel_times(torch, flush, lambda: lin(x), PAIR_REPS)
+            cases[f"{name}_m{M}"] = {"linear_us": round(1e6 * statistics.median(ts), 2)}
+    del g, reps
+    torch.cuda.empty_cache()
+    pre, ops_sum, t_sum = {}, 0.0, 0.0
+    for (name, N, K) in SHAPES:
+        L = syn.make_layer(N, K, seed=6000 + N, checkpoint=False, keep_awq=True)
+        lin = R.ReferenceLinear(L["pairs"], L["theta"], L["channel_scales"], L["awq_qweight"], L["awq_scales"],
+                                L["awq_qzeros"], K, N)
+        del L
+        for M in PREFILL_M:
+            x = syn.make_activations(M, K, seed=M + K)
+            t = statistics.median(kernel_times(torch, flush, lambda: lin(x), 3))
+            ops_sum += 2 * M * N * K
+            t_sum += t
+            pre[f"{name}_m{M}"] = {"linear_us": round(t * 1e6, 1), "tops": round(2 * M * N * K / t / 1e12, 1)}
+            del x
+        del lin
+        torch.cuda.empty_cache()
+    return {"path": "reference rotate kernel (sm_100a build of kernels/paroquant_kernels/src/rotation.cu) + "
+                    "vLLM per_token_quant_int8 + marlin_gemm (uint4 x int8), bf16 <-> fp16 casts",
+            "decode_sweep": dec, "decode_cases": cases,
+            "prefill": {"tops": round(ops_sum / t_sum / 1e12, 1), "cases": pre,
+                        "timing": "one whole linear per call after an L2 flush, CUDA events, median of 3"}}
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -506,10 +608,47 @@ def run_reference(a):
     return 0
 
 
+def run_case(a):
+    """Profiling mode (--case SHAPE:M): one seeded synthetic layer of the
+    named projection shape, then the activation kernel and the GEMM (or,
+    with --case-linear, the whole linear op) --case-iters times on the
+    current GPU; prints the CUDA-event time of the last iteration and the
+    device error word.  Meant to be launched under ``ncu -k <kernel>`` with a
+    small launch count: it holds at most a few hundred MB on the device."""
+    import torch
+    import alpamayo_b200.ops as ops
+    from alpamayo_b200 import _native
+    from alpamayo_b200 import synthetic as syn
+    shape, m = a.case.split(":")
+    N, K = {name: (n, k) for (name, n, k) in SHAPES}[shape]
+    M = int(m)
+    L = syn.make_layer(N, K, seed=1, checkpoint=False)
+    x = syn.make_activations(M, K, seed=2)
+    torch.cuda.synchronize()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    for _ in range(a.case_iters):
+        ev[0].record()
+        if a.case_linear:
+            ops.linear_w4a8(x, L["rot_table"], L["cs_vec"], L["packed"], N, None, True, torch.bfloat16)
+            ev[1].record()
+        else:
+            q, s = ops.rotq_int8(x, L["rot_table"], L["cs_vec"], 128, True)
+            ev[1].record()
+            ops.w4a8_gemm(q, s, L["packed"], N, None, torch.bfloat16)
+        ev[2].record()
+    torch.cuda.synchronize()
+    err = _native.capi().paro_device_error_word(1)
+    print(f"{shape} M={M}: activation {ev[0].elapsed_time(ev[1]) * 1e3:.1f} us, "
+          f"gemm {ev[1].elapsed_time(ev[2]) * 1e3:.1f} us, device error word {err}")
+    return 1 if err else 0
+
+
 def main():
     a = args_()
     if a.impl == "reference":
         return run_reference(a)
+    if a.case:
+        return run_case(a)
     import torch
     world, rank, local = dist_setup(a.gpus)
     import alpamayo_b200.ops as ops
@@ -598,8 +737,50 @@ def main():
                                      "linear_us": round(1e6 * statistics.median(tl), 2),
                                      "weight_GBps": round(weight_bytes(N, K) / statistics.median(tg_l) / 1e9, 1)}
     hbm, peak_kind = peaks()
-    gemm_gbs = gemm_b / gemm_t / 1e9
+    cold_gbs = gemm_b / gemm_t / 1e9
     case_out = cases
+
+    # --- the decode GEMM's average launch duration over the step's own
+    # launches: the benchmark step's 16 sweeps x 12 GEMMs (same cases, same
+    # three weight replicas, same order; 346 MiB of weights per sweep > L2),
+    # int8 rows already quantised, captured back to back as a CUDA graph and
+    # timed with CUDA events on the launching stream
+    qx = {}
+    for ri, M in enumerate(DECODE_M):
+        for (name, N, K) in SHAPES:
+            L = reps[ri][name]
+            qx[(ri, name)] = ops.rotq_int8(xs[(M, K)], L["rot_table"], L["cs_vec"], 128, True)
+    gy = {k: None for k in qx}
+
+    def gemm_step():
+        for _ in range(STEP_SWEEPS):
+            for ri, M in enumerate(DECODE_M):
+                for (name, N, K) in SHAPES:
+                    q = qx[(ri, name)]
+                    gy[(ri, name)] = ops.w4a8_gemm(q[0], q[1], reps[ri][name]["packed"], N, None, torch.bfloat16)
+
+    sg = torch.cuda.Stream()
+    sg.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(sg):
+        gemm_step()
+    torch.cuda.current_stream().wait_stream(sg)
+    gg = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gg):
+        gemm_step()
+    for _ in range(a.warmup):
+        gg.replay()
+    torch.cuda.synchronize()
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record()
+    for _ in range(a.steps):
+        gg.replay()
+    g1.record()
+    torch.cuda.synchronize()
+    gemm_launches = STEP_SWEEPS * len(DECODE_M) * len(SHAPES)
+    gemm_step_s = g0.elapsed_time(g1) * 1e-3 / a.steps
+    gemm_step_bytes = STEP_SWEEPS * sum(gemm_alg_bytes(M, N, K) for M in DECODE_M for (_, N, K) in SHAPES)
+    gemm_gbs = gemm_step_bytes / gemm_step_s / 1e9
+    del gg, qx, gy
     traffic = profile_traffic("gemm_decode_gate_up_m8.md")
 
     # --- prefill: tcgen05 GEMM and activation kernel per shape
@@ -608,6 +789,13 @@ def main():
     prefill = None
     if not a.no_prefill:
         prefill = prefill_section(torch, ops, syn, reps[0], flush, rank)
+    ref_gpu = None
+    if rank == 0 and world == 1 and not a.no_reference_gpu:
+        try:
+            ref_gpu = reference_gpu_section(torch, syn, flush, a.steps, a.warmup)
+        except Exception as e:  # report why, keep the rest of the line
+            ref_gpu = {"unavailable": f"{type(e).__name__}: {str(e).splitlines()[0][:200]}"}
+            torch.cuda.empty_cache()
     del flush
 
     # --- end to end through the public op with host buffers (graph of the step)
@@ -676,13 +864,19 @@ def main():
                        "l2": f"weight working set {wset / 2**20:.0f} MiB per sweep > L2 {L2_BYTES / 2**20:.0f} MiB "
                              "(3 replicas, one per M); inputs not flushed",
                        "parallelism": f"dp{world} (independent replicas, no collective)"},
-            "roofline": {"kernel": "gemm_stream_kernel (decode W4A8 GEMM: TMA weight stream, mma.sync "
-                                   "int4 x int8, stream-K)", "bound": "hbm",
+            "roofline": {"kernel": "decode W4A8 GEMM (gemm_rows_kernel: TMA bulk weight stream, one row block "
+                                   "per warp, mma.sync int4 x int8, stream-K)", "bound": "hbm",
                          "achieved": round(gemm_gbs, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(gemm_gbs / hbm, 4), "peak_kind": peak_kind,
                          "traffic": traffic,
                          "alg_bytes": "N*K/2 + G*N*2 + G*N/2 + M*K + 4M + 2*M*N per launch",
-                         "timing": "per launch, L2 flushed (512 MiB write, then 256 MiB read) before each launch, CUDA events"},
+                         "avg_launch_us": round(gemm_step_s / gemm_launches * 1e6, 3),
+                         "timing": f"the step's {gemm_launches} GEMM launches (16 sweeps x 12 cases, 3 weight "
+                                   "replicas > L2) back to back in a CUDA graph, CUDA events on the launching "
+                                   "stream; achieved = algorithmic bytes / time",
+                         "cold_launch": {"achieved": round(cold_gbs, 1), "frac": round(cold_gbs / hbm, 4),
+                                         "timing": "one launch after an L2 flush (512 MiB write, then 256 MiB "
+                                                   "read), CUDA events, median of 5 per case"}},
             "activation_kernel": {"achieved_GBps": round(act_b / act_t / 1e9, 1),
                                   "frac": round(act_b / act_t / 1e9 / hbm, 4),
                                   "alg_bytes": "2MK + MK + 4M + tables 2LK + LK + 2K (L = 8) per launch"},
@@ -694,6 +888,7 @@ def main():
             "clocks": clk,
             "cpu_baseline": cpu,
             "e2e": e2e,
+            "reference_gpu": ref_gpu,
         }
         print(json.dumps(line), flush=True)
     del g

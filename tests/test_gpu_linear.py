@@ -1,8 +1,9 @@
 """paro_w4a8_linear (torch.ops.paro_b200.linear_w4a8): the whole rotated
-linear.  Up to 64 tokens it is a rotation kernel (fp16 rows + row maxima)
-chained to the decode GEMM, which quantises the rows in its prologue; the
-tests hold it to the activation-kernel route (paro_rotq_int8 +
-paro_w4a8_gemm) and to the oracle.
+linear.  Up to 64 tokens it is three chained kernels: a rotation kernel
+(fp16 rows + row maxima), a quantiser (int8 codes in the GEMM's fragment
+order + code sums + token scales) and the GEMM; the tests hold it to the
+activation-kernel route (paro_rotq_int8 + paro_w4a8_gemm) and to the
+oracle.
 
 Tolerances: the two routes compute the same int8 codes and int32 group sums;
 only the order of float32 additions across CTAs may differ, so float32
