@@ -25,11 +25,16 @@ from . import synthetic as syn
 HIDDEN, HEADS, KV_HEADS, HEAD_DIM, INTER = 3584, 28, 4, 128, 18944
 
 
-def serving_layer(N, K, seed, device="cuda"):
+def serving_layer(N, K, seed, device="cuda", keep=False):
     """A seeded quantised linear reduced to what the forward reads: tile
-    records, rotation table, channel scales."""
-    L = syn.make_layer(N, K, seed=seed, device=device, checkpoint=False)
-    return {"N": N, "K": K, "packed": L["packed"], "rot_table": L["rot_table"], "cs_vec": L["cs_vec"]}
+    records, rotation table, channel scales (with ``keep``, also the
+    rotation buffers and AWQ int32 weights it was built from, for checks)."""
+    L = syn.make_layer(N, K, seed=seed, device=device, checkpoint=False, keep_awq=keep)
+    out = {"N": N, "K": K, "packed": L["packed"], "rot_table": L["rot_table"], "cs_vec": L["cs_vec"]}
+    if keep:
+        for k in ("pairs", "theta", "channel_scales", "awq_qweight", "awq_scales", "awq_qzeros"):
+            out[k] = L[k]
+    return out
 
 
 def linear(L, x, out_dtype=torch.bfloat16):
@@ -65,7 +70,7 @@ def linear_into(L, x, out):
 
 
 class DecoderStack:
-    def __init__(self, layers=28, seed=0, device="cuda", eps=1e-6):
+    def __init__(self, layers=28, seed=0, device="cuda", eps=1e-6, keep=False):
         qkv_n = (HEADS + 2 * KV_HEADS) * HEAD_DIM
         g = torch.Generator(device=device)
         g.manual_seed(seed)
@@ -76,10 +81,10 @@ class DecoderStack:
             norm = lambda: (0.9 + 0.2 * torch.rand(HIDDEN, generator=g, device=device)).to(torch.bfloat16)
             self.layers.append({
                 "in_norm": norm(), "post_norm": norm(),
-                "qkv": serving_layer(qkv_n, HIDDEN, s + 1, device),
-                "o": serving_layer(HIDDEN, HEADS * HEAD_DIM, s + 2, device),
-                "gate_up": serving_layer(2 * INTER, HIDDEN, s + 3, device),
-                "down": serving_layer(HIDDEN, INTER, s + 4, device),
+                "qkv": serving_layer(qkv_n, HIDDEN, s + 1, device, keep),
+                "o": serving_layer(HIDDEN, HEADS * HEAD_DIM, s + 2, device, keep),
+                "gate_up": serving_layer(2 * INTER, HIDDEN, s + 3, device, keep),
+                "down": serving_layer(HIDDEN, INTER, s + 4, device, keep),
             })
         self.final_norm = (0.9 + 0.2 * torch.rand(HIDDEN, generator=g, device=device)).to(torch.bfloat16)
 

@@ -84,3 +84,23 @@ def expected_records(codes, scales_gn, zeros_gn):
     out[:, 1024:1056] = s16.T.reshape(N // 16, 16, G).transpose(0, 2, 1).reshape(-1, 16).view(np.uint8).reshape(-1, 32)
     out[:, 1056:1072] = np.asarray(zeros_gn).astype(np.uint8).T.reshape(N // 16, 16, G).transpose(0, 2, 1).reshape(-1, 16)
     return out.reshape(-1)
+
+
+_AWQ_ORDER = [0, 2, 4, 6, 1, 3, 5, 7]
+
+
+def awq_columns(layer, cols):
+    """Codes [len(cols), K], zero points [G, len(cols)] and fp32 group scales
+    [G, len(cols)] of the given output columns, read back from a synthetic
+    layer's AWQ int32 buffers (alpamayo_b200.synthetic.make_layer with
+    keep_awq=True): column c = 8 j + AWQ_ORDER[i] sits in nibble i of word j."""
+    import torch
+    cols = np.asarray(cols)
+    c_t = torch.from_numpy(cols).to(layer["awq_qweight"].device)
+    nib = torch.tensor([_AWQ_ORDER.index(o) for o in range(8)], device=c_t.device)[c_t % 8]
+    w = layer["awq_qweight"][:, c_t // 8].to(torch.int64) & 0xFFFFFFFF        # [K, n]
+    codes = ((w >> (4 * nib)[None, :]) & 0xF).t().contiguous().cpu().numpy()
+    zw = layer["awq_qzeros"][:, c_t // 8].to(torch.int64) & 0xFFFFFFFF        # [G, n]
+    zeros = ((zw >> (4 * nib)[None, :]) & 0xF).cpu().numpy()
+    scales = layer["awq_scales"][:, c_t].float().cpu().numpy()
+    return codes, zeros, scales
