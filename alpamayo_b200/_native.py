@@ -71,6 +71,13 @@ def capi() -> ctypes.CDLL:
         "paro_w4a8_linear": (i32, [vp, i32, i64, i32, i32, vp, vp, i32, vp, vp, i32, vp, i32, vp, sz, vp, sz, vp]),
         "paro_device_error_word": (i32, [i32]),
         "paro_selftest_wait_timeout": (i32, [ctypes.c_longlong, vp]),
+        "paro_w4a8_linear_prologue_scratch_size": (sz, [i32, i64, i32, i32, i32]),
+        "paro_w4a8_linear_prologue": (i32, [i32, vp, vp, vp, vp, ctypes.c_float, i64, i32, i32, vp, vp, i32, vp, vp,
+                                            i32, vp, i32, vp, sz, vp, sz, vp]),
+        "paro_w4a8_linear_group_workspace_size": (sz, [i64, i32, vp, i32]),
+        "paro_w4a8_linear_group_scratch_size": (sz, [i32, i64, i32, vp, i32, i32]),
+        "paro_w4a8_linear_group": (i32, [i32, vp, i32, vp, vp, vp, ctypes.c_float, i64, i32, i32, vp, vp, vp, i32,
+                                         vp, vp, i32, vp, i32, vp, sz, vp, sz, vp]),
         "paro_w4a8_gemm_noalloc": (i32, [vp, vp, i64, i32, i32, vp, vp, i32, vp, i32, vp]),
         "paro_add_rmsnorm": (i32, [vp, vp, vp, i64, i32, ctypes.c_float, vp, vp]),
         "paro_silu_mul": (i32, [vp, i64, i32, vp, vp]),

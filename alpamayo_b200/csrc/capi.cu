@@ -35,11 +35,16 @@ size_t gemm_decode_workspace(int64_t M, int N);
 cudaError_t launch_add_rmsnorm(const void* x, void* residual, const void* weight, int64_t M, int K, float eps,
                                void* out, cudaStream_t st);
 cudaError_t launch_silu_mul(const void* x, int64_t M, int I, void* out, cudaStream_t st);
-size_t linear_decode_workspace(int64_t M, int N, int K);
-size_t linear_decode_scratch(int64_t M, int K);
+size_t linear_decode_workspace(int64_t M, int N, int K, int T);
+size_t linear_decode_scratch(int64_t M, int K, int T);
+cudaError_t launch_linear_decode_tables(const void* x, int x_dtype, const RotTables& tabs, int T, const int* tab_nb,
+                                        int64_t M, int N, int K, const void* packed, const void* bias, int bias_dtype,
+                                        void* out, int out_dtype, void* ws, void* scratch, int pro_kind,
+                                        const RotPro& pro, cudaStream_t st);
 cudaError_t launch_linear_decode(const void* x, int x_dtype, const uint16_t* cscale, const uint32_t* rtab, int64_t M,
                                  int N, int K, const void* packed, const void* bias, int bias_dtype, void* out,
-                                 int out_dtype, void* ws, void* scratch, cudaStream_t st);
+                                 int out_dtype, void* ws, void* scratch, int pro_kind, const RotPro& pro,
+                                 cudaStream_t st);
 int gemm_tc_supported(int64_t M, int N, int K);
 size_t gemm_tc_workspace(int64_t M, int N, int K);
 cudaError_t launch_selftest_wait(long long limit_cycles, cudaStream_t st);
@@ -239,14 +244,14 @@ extern "C" {
 size_t paro_w4a8_linear_workspace_size(int64_t M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0 || N % kRecRows || K % kGroup) return 0;
   size_t ws = paro_w4a8_gemm_workspace_size(M, N, K);
-  if (M <= kLinearFusedMaxM) ws = std::max(ws, linear_decode_workspace(M, N, K));
+  if (M <= kLinearFusedMaxM) ws = std::max(ws, linear_decode_workspace(M, N, K, 1));
   return ws;
 }
 
 size_t paro_w4a8_linear_scratch_size(int64_t M, int N, int K, int fp16_round) {
   if (M <= 0 || N <= 0 || K <= 0 || N % kRecRows || K % kGroup) return 0;
   size_t sc = linear_unfused_scratch(M, K, fp16_round);
-  if (M <= kLinearFusedMaxM) sc = std::max(sc, linear_decode_scratch(M, K));
+  if (M <= kLinearFusedMaxM) sc = std::max(sc, linear_decode_scratch(M, K, 1));
   return sc;
 }
 
@@ -274,7 +279,8 @@ int paro_w4a8_linear(const void* x, int x_dtype, int64_t M, int K, int N, const 
   // spreads a row over one 8-CTA cluster)
   if (M <= kLinearFusedMaxM && fp16_round) {
     const cudaError_t e = launch_linear_decode(x, x_dtype, channel_scales, rot_table, M, N, K, packed, bias,
-                                               bias_dtype, out, out_dtype, workspace, scratch, st);
+                                               bias_dtype, out, out_dtype, workspace, scratch, kProNone, RotPro{},
+                                               st);
     if (e != cudaErrorNotSupported) return cuda_status(e);
   }
   // two kernels: activation into the scratch, then the GEMM
@@ -288,6 +294,233 @@ int paro_w4a8_linear(const void* x, int x_dtype, int64_t M, int K, int N, const 
   if (rc != PARO_OK) return rc;
   return paro_w4a8_gemm(xq, xs, M, N, K, packed, bias, bias_dtype, out, out_dtype, workspace, workspace_bytes,
                         stream);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// one rotated linear with the decoder-layer step before it fused in
+// ---------------------------------------------------------------------------
+namespace {
+bool overlaps(const void* a, size_t an, const void* b, size_t bn) {
+  const uintptr_t pa = reinterpret_cast<uintptr_t>(a), pb = reinterpret_cast<uintptr_t>(b);
+  return pa < pb + bn && pb < pa + an;
+}
+}  // namespace
+
+extern "C" {
+
+size_t paro_w4a8_linear_prologue_scratch_size(int prologue, int64_t M, int N, int K, int fp16_round) {
+  if (prologue < PARO_PROLOGUE_NONE || prologue > PARO_PROLOGUE_SILU_MUL) return 0;
+  const size_t lin = paro_w4a8_linear_scratch_size(M, N, K, fp16_round);
+  if (!lin) return 0;
+  // the unfused route (prefill sizes) keeps the prologue's bf16 output
+  return prologue == PARO_PROLOGUE_NONE ? lin : al256((size_t)M * K * 2) + lin;
+}
+
+int paro_w4a8_linear_prologue(int prologue, const void* x, const void* residual_in, void* residual_out,
+                              const void* norm_weight, float eps, int64_t M, int K, int N,
+                              const uint16_t* channel_scales, const uint32_t* rot_table, int fp16_round,
+                              const void* packed, const void* bias, int bias_dtype, void* out, int out_dtype,
+                              void* workspace, size_t workspace_bytes, void* scratch, size_t scratch_bytes,
+                              paro_stream_t stream) {
+  if (prologue == PARO_PROLOGUE_NONE)
+    return paro_w4a8_linear(x, PARO_BF16, M, K, N, channel_scales, rot_table, fp16_round, packed, bias, bias_dtype,
+                            out, out_dtype, workspace, workspace_bytes, scratch, scratch_bytes, stream);
+  if (prologue != PARO_PROLOGUE_ADD_RMSNORM && prologue != PARO_PROLOGUE_SILU_MUL) return PARO_ERR_UNSUPPORTED;
+  if (M == 0 && N > 0 && K > 0) return PARO_OK;
+  if (!x || !rot_table || !packed || !out || M < 0 || N <= 0 || K <= 0) return PARO_ERR_INVALID_ARGUMENT;
+  const bool rms = prologue == PARO_PROLOGUE_ADD_RMSNORM;
+  if (rms && (!residual_out || !norm_weight)) return PARO_ERR_INVALID_ARGUMENT;
+  if (!valid_dtype(out_dtype) || (bias && !valid_dtype(bias_dtype))) return PARO_ERR_UNSUPPORTED;
+  if (N % kRecRows || K % kGroup) return PARO_ERR_SHAPE;
+  if (!aligned(x, 16) || (rms && (!aligned(norm_weight, 16) || !aligned(residual_out, 16))) ||
+      (residual_in && !aligned(residual_in, 16)) || (channel_scales && !aligned(channel_scales, 2)) ||
+      !aligned(rot_table, 4) || !aligned(packed, 16))
+    return PARO_ERR_MISALIGNED;
+  const size_t row_bytes = (size_t)M * K * 2;
+  // every CTA of a row reads the whole input row while others write their
+  // channels of the residual output: the two must be separate buffers
+  if (rms && (overlaps(residual_out, row_bytes, x, row_bytes) ||
+              (residual_in && overlaps(residual_out, row_bytes, residual_in, row_bytes))))
+    return PARO_ERR_INVALID_ARGUMENT;
+  if (workspace_bytes < paro_w4a8_linear_workspace_size(M, N, K) ||
+      scratch_bytes < paro_w4a8_linear_prologue_scratch_size(prologue, M, N, K, fp16_round) || !workspace ||
+      !scratch)
+    return PARO_ERR_WORKSPACE;
+  if (!aligned(workspace, 256) || !aligned(scratch, 256)) return PARO_ERR_MISALIGNED;
+  if (int d = device_check()) return d;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (M <= kLinearFusedMaxM && fp16_round) {
+    RotPro pro{};
+    pro.res_in = static_cast<const __nv_bfloat16*>(residual_in);
+    pro.res_out = static_cast<__nv_bfloat16*>(residual_out);
+    pro.w = static_cast<const __nv_bfloat16*>(norm_weight);
+    pro.eps = eps;
+    const cudaError_t e =
+        launch_linear_decode(x, PARO_BF16, channel_scales, rot_table, M, N, K, packed, bias, bias_dtype, out, out_dtype,
+                             workspace, scratch, rms ? kProAddRmsnorm : kProSiluMul, pro, st);
+    if (e != cudaErrorNotSupported) return cuda_status(e);
+  }
+  // prefill sizes: the prologue's own kernel into the scratch, then the linear
+  uint8_t* h = static_cast<uint8_t*>(scratch);
+  cudaError_t e;
+  if (rms) {
+    // the separate kernel updates the residual in place: copy it over first
+    const void* src = residual_in ? residual_in : x;
+    e = cudaMemcpyAsync(residual_out, src, row_bytes, cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) return cuda_status(e);
+    e = launch_add_rmsnorm(residual_in ? x : residual_out, residual_in ? residual_out : nullptr, norm_weight, M, K,
+                           eps, h, st);
+  } else {
+    e = launch_silu_mul(x, M, K, h, st);
+  }
+  if (e != cudaSuccess) return cuda_status(e);
+  return paro_w4a8_linear(h, PARO_BF16, M, K, N, channel_scales, rot_table, fp16_round, packed, bias, bias_dtype, out,
+                          out_dtype, workspace, workspace_bytes, h + al256(row_bytes), scratch_bytes - al256(row_bytes),
+                          stream);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// a group of rotated linears sharing their input, one rotation table each
+// ---------------------------------------------------------------------------
+namespace {
+size_t elem_bytes(int dtype) { return dtype == PARO_F32 ? 4 : 2; }
+
+int group_check(int T, const int* n_per_table, int K, int* n_total, int* nb_start) {
+  if (T < 1 || T > kMaxTables || !n_per_table) return PARO_ERR_INVALID_ARGUMENT;
+  int n = 0;
+  for (int t = 0; t < T; ++t) {
+    if (n_per_table[t] <= 0) return PARO_ERR_INVALID_ARGUMENT;
+    if (n_per_table[t] % kRecRows) return PARO_ERR_SHAPE;
+    nb_start[t] = n / kRecRows;
+    n += n_per_table[t];
+  }
+  if (K <= 0 || K % kGroup) return PARO_ERR_SHAPE;
+  *n_total = n;
+  return PARO_OK;
+}
+}  // namespace
+
+extern "C" {
+
+size_t paro_w4a8_linear_group_workspace_size(int64_t M, int T, const int* n_per_table, int K) {
+  int nt = 0, nb[kMaxTables];
+  if (M <= 0 || group_check(T, n_per_table, K, &nt, nb)) return 0;
+  size_t ws = M <= kLinearFusedMaxM ? linear_decode_workspace(M, nt, K, T) : 0;
+  for (int t = 0; t < T; ++t) ws = std::max(ws, paro_w4a8_linear_workspace_size(M, n_per_table[t], K));
+  return ws;
+}
+
+size_t paro_w4a8_linear_group_scratch_size(int prologue, int64_t M, int T, const int* n_per_table, int K,
+                                           int fp16_round) {
+  int nt = 0, nb[kMaxTables];
+  if (M <= 0 || group_check(T, n_per_table, K, &nt, nb)) return 0;
+  if (prologue < PARO_PROLOGUE_NONE || prologue > PARO_PROLOGUE_SILU_MUL) return 0;
+  size_t sc = M <= kLinearFusedMaxM && fp16_round ? linear_decode_scratch(M, K, T) : 0;
+  // per-table route: the prologue's output, one table's output in fp32 and
+  // that linear's scratch
+  size_t per = 0;
+  for (int t = 0; t < T; ++t)
+    per = std::max(per, al256((size_t)M * n_per_table[t] * 4) +
+                            paro_w4a8_linear_scratch_size(M, n_per_table[t], K, fp16_round));
+  per += prologue == PARO_PROLOGUE_NONE ? 0 : al256((size_t)M * K * 2);
+  return std::max(sc, per);
+}
+
+int paro_w4a8_linear_group(int prologue, const void* x, int x_dtype, const void* residual_in, void* residual_out,
+                           const void* norm_weight, float eps, int64_t M, int K, int T, const int* n_per_table,
+                           const uint16_t* const* channel_scales, const uint32_t* const* rot_tables, int fp16_round,
+                           const void* packed, const void* bias, int bias_dtype, void* out, int out_dtype,
+                           void* workspace, size_t workspace_bytes, void* scratch, size_t scratch_bytes,
+                           paro_stream_t stream) {
+  int N = 0, nb[kMaxTables];
+  if (int rc = group_check(T, n_per_table, K, &N, nb)) return rc;
+  if (prologue < PARO_PROLOGUE_NONE || prologue > PARO_PROLOGUE_SILU_MUL) return PARO_ERR_UNSUPPORTED;
+  if (M == 0) return PARO_OK;
+  if (!x || !rot_tables || !packed || !out || M < 0) return PARO_ERR_INVALID_ARGUMENT;
+  for (int t = 0; t < T; ++t) {
+    if (!rot_tables[t]) return PARO_ERR_INVALID_ARGUMENT;
+    if (!aligned(rot_tables[t], 4) || (channel_scales && channel_scales[t] && !aligned(channel_scales[t], 2)))
+      return PARO_ERR_MISALIGNED;
+  }
+  const bool rms = prologue == PARO_PROLOGUE_ADD_RMSNORM;
+  if (!valid_dtype(x_dtype) || !valid_dtype(out_dtype) || (bias && !valid_dtype(bias_dtype)))
+    return PARO_ERR_UNSUPPORTED;
+  if (prologue != PARO_PROLOGUE_NONE && x_dtype != PARO_BF16) return PARO_ERR_UNSUPPORTED;
+  if (rms && (!residual_out || !norm_weight)) return PARO_ERR_INVALID_ARGUMENT;
+  const size_t row_bytes = (size_t)M * K * 2;
+  if (rms && (overlaps(residual_out, row_bytes, x, row_bytes) ||
+              (residual_in && overlaps(residual_out, row_bytes, residual_in, row_bytes))))
+    return PARO_ERR_INVALID_ARGUMENT;
+  if (!aligned(x, 16) || !aligned(packed, 16) || !aligned(out, 16) || (residual_in && !aligned(residual_in, 16)) ||
+      (rms && (!aligned(residual_out, 16) || !aligned(norm_weight, 16))))
+    return PARO_ERR_MISALIGNED;
+  if (!workspace || !scratch || workspace_bytes < paro_w4a8_linear_group_workspace_size(M, T, n_per_table, K) ||
+      scratch_bytes < paro_w4a8_linear_group_scratch_size(prologue, M, T, n_per_table, K, fp16_round))
+    return PARO_ERR_WORKSPACE;
+  if (!aligned(workspace, 256) || !aligned(scratch, 256)) return PARO_ERR_MISALIGNED;
+  if (int d = device_check()) return d;
+  cudaStream_t st = (cudaStream_t)stream;
+  RotPro pro{};
+  if (rms) {
+    pro.res_in = static_cast<const __nv_bfloat16*>(residual_in);
+    pro.res_out = static_cast<__nv_bfloat16*>(residual_out);
+    pro.w = static_cast<const __nv_bfloat16*>(norm_weight);
+    pro.eps = eps;
+  }
+  if (M <= kLinearFusedMaxM && fp16_round) {
+    // one rotation kernel and one quantiser over all T tables, one GEMM over
+    // the concatenated weights
+    RotTables tabs = {};
+    for (int t = 0; t < T; ++t) {
+      tabs.rtab[t] = rot_tables[t];
+      tabs.cs[t] = channel_scales ? channel_scales[t] : nullptr;
+    }
+    const int pk = prologue == PARO_PROLOGUE_NONE ? kProNone : rms ? kProAddRmsnorm : kProSiluMul;
+    const cudaError_t e = launch_linear_decode_tables(x, x_dtype, tabs, T, nb, M, N, K, packed, bias, bias_dtype,
+                                                      out, out_dtype, workspace, scratch, pk, pro, st);
+    if (e != cudaErrorNotSupported) return cuda_status(e);
+  }
+  // otherwise one linear per table into the scratch, copied into its columns
+  uint8_t* sp = static_cast<uint8_t*>(scratch);
+  const void* xin = x;
+  int xdt = x_dtype;
+  if (prologue != PARO_PROLOGUE_NONE) {
+    cudaError_t e;
+    if (rms) {
+      const void* src = residual_in ? residual_in : x;
+      e = cudaMemcpyAsync(residual_out, src, row_bytes, cudaMemcpyDeviceToDevice, st);
+      if (e != cudaSuccess) return cuda_status(e);
+      e = launch_add_rmsnorm(residual_in ? x : residual_out, residual_in ? residual_out : nullptr, norm_weight, M, K,
+                             eps, sp, st);
+    } else {
+      e = launch_silu_mul(x, M, K, sp, st);
+    }
+    if (e != cudaSuccess) return cuda_status(e);
+    xin = sp;
+    xdt = PARO_BF16;
+    sp += al256(row_bytes);
+  }
+  const size_t rec_bytes_per_nb = (size_t)(K / kGroup) * kRecBytes;
+  const size_t oe = elem_bytes(out_dtype);
+  for (int t = 0; t < T; ++t) {
+    const int nt = n_per_table[t], n0 = nb[t] * kRecRows;
+    const size_t tmp_bytes = al256((size_t)M * nt * 4);
+    const uint8_t* pk = static_cast<const uint8_t*>(packed) + (size_t)nb[t] * rec_bytes_per_nb;
+    const void* bt = bias ? static_cast<const uint8_t*>(bias) + (size_t)n0 * elem_bytes(bias_dtype) : nullptr;
+    int rc = paro_w4a8_linear(xin, xdt, M, K, nt, channel_scales ? channel_scales[t] : nullptr, rot_tables[t],
+                              fp16_round, pk, bt, bias_dtype, sp, out_dtype, workspace, workspace_bytes,
+                              sp + tmp_bytes, scratch_bytes - (size_t)(sp - static_cast<uint8_t*>(scratch)) - tmp_bytes,
+                              stream);
+    if (rc != PARO_OK) return rc;
+    const cudaError_t e = cudaMemcpy2DAsync(static_cast<uint8_t*>(out) + (size_t)n0 * oe, (size_t)N * oe, sp,
+                                            (size_t)nt * oe, (size_t)nt * oe, (size_t)M, cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) return cuda_status(e);
+  }
+  return PARO_OK;
 }
 
 }  // extern "C"

@@ -88,7 +88,22 @@ struct DecParams {
   int xrows_n;      // token rows staged in shared memory (XS)
   const int* gsum;  // kXinPreQ: per (group, token) code sums, [G][gsum_mp]
   int gsum_mp;
+  // kXinPreQ with several rotation tables (a group of linears sharing their
+  // input, weights concatenated along N): row blocks [tab_nb[t],
+  // tab_nb[t + 1]) use activation set t; set t of xq / gsum / xscale / amax
+  // starts t * set_xq bytes / t * set_gsum ints / t * M floats in
+  int tables;
+  int tab_nb[kMaxTables];
+  int64_t set_xq, set_gsum;
 };
+
+// The activation set (rotation table) of row block nb.
+__device__ __forceinline__ int table_of(const DecParams& p, int nb) {
+  int t = 0;
+#pragma unroll
+  for (int i = 1; i < kMaxTables; ++i) t += (i < p.tables && nb >= p.tab_nb[i]) ? 1 : 0;
+  return t;
+}
 
 
 // A = unsigned 8-bit codes (q, or 16*q from a high nibble), B = signed int8
@@ -197,7 +212,7 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
   constexpr int NC = dec_consumers(MT);
   constexpr int NCT = NC * 32;
   constexpr int SLOTS = kDecChunkGroups / NC;   // records per warp per chunk
-  __shared__ float tok_scale_s[kDecMaxTokens];
+  __shared__ float tok_scale_s[kMaxTables][kDecMaxTokens];
   extern __shared__ __align__(128) uint8_t smem[];
   const int S = p.stages;
   const int G = p.K / kGroup;
@@ -272,13 +287,14 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
     const int ew = warp - (NC + 1);
     grid_dependency_wait();  // token scales (and rows) come from the previous kernel
     // both warps write the same token scales; each reads back its own
-    for (int t = lane; t < ntok_slice; t += 32) tok_scale_s[t] = p.xscale[tok0 + t];
+    for (int tb = 0; tb < p.tables; ++tb)
+      for (int t = lane; t < ntok_slice; t += 32) tok_scale_s[tb][t] = p.xscale[tb * p.M + tok0 + t];
     __syncwarp();
     if constexpr (PREQ || PREQS) {
       // the quantiser that read the row maxima has finished: return them to
       // zero for the next call's rotation kernel
       if (blockIdx.x == 0 && blockIdx.y == 0 && ew == 0)
-        for (int64_t t = lane; t < p.M; t += 32) p.amax[t] = 0u;
+        for (int64_t t = lane; t < p.M * p.tables; t += 32) p.amax[t] = 0u;
     }
     uint32_t* cnt = p.cnt + (size_t)blockIdx.y * (p.N / kRecRows);
     if constexpr (PREQS) {
@@ -318,6 +334,7 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
       __syncwarp();
       if (lane == 0) mbar_arrive(&seg_free[par]);
       const bool whole = seg_units == G;
+      const float* tsc = tok_scale_s[table_of(p, nb)];
 #pragma unroll
       for (int sl = 0; sl < MT * 4; ++sl) {
         const int mt = sl >> 2, i = sl & 3;
@@ -326,7 +343,7 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
         if (t < p.M) {
           if (whole)
             store_out(p.out, p.out_dtype, (size_t)t * p.N + n,
-                      v[sl] * tok_scale_s[t - tok0] + bias_at(p.bias, p.bias_dtype, n));
+                      v[sl] * tsc[t - tok0] + bias_at(p.bias, p.bias_dtype, n));
           else
             red_add_fx(p.ws + (size_t)n * p.M + t, v[sl]);
         }
@@ -366,7 +383,7 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
                 const int64_t t = tok0 + tt;
                 st_cg_u64(p.ws + (size_t)n * p.M + t, 0ull);
                 store_out(p.out, p.out_dtype, (size_t)t * p.N + n,
-                          a[j] * tok_scale_s[tt] + bias_at(p.bias, p.bias_dtype, n));
+                          a[j] * tsc[tt] + bias_at(p.bias, p.bias_dtype, n));
               }
             }
           }
@@ -487,9 +504,40 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
   for (int q = 0; q < sg.n; ++q) {
     int nb, g, ge;
     sg.get(q, nb, g, ge);
+    // this row block's activation set (several rotation tables: L2 route only)
+    const int tset = PREQ ? table_of(p, nb) : 0;
+    const int64_t xoff = tset * p.set_xq, goff = tset * p.set_gsum;
     while (g < ge) {
       const int n = min((g | (kDecChunkGroups - 1)) + 1, ge) - g;
       const int gbase = g & ~(kDecChunkGroups - 1);
+      // pre-quantised rows from L2, one token tile: both slots' fragments and
+      // code sums are requested before the wait for the weights, so their L2
+      // latency overlaps it
+      constexpr bool HOIST = PREQ && MT == 1;
+      uint32_t hb[HOIST ? SLOTS : 1][8];
+      int2 hs[HOIST ? SLOTS : 1];
+      if constexpr (HOIST) {
+#pragma unroll
+        for (int slot = 0; slot < SLOTS; ++slot) {
+          const int gg = min(gbase + slot * NC + cw, G - 1);
+          if (xvalid[0]) {
+            const uint4 b0 = ld_l2_v4(xrowf[0] + xoff + (size_t)gg * kGroup);
+            const uint4 b1 = ld_l2_v4(xrowf[0] + xoff + (size_t)gg * kGroup + 16);
+            hb[slot][0] = b0.x;
+            hb[slot][1] = b0.y;
+            hb[slot][2] = b0.z;
+            hb[slot][3] = b0.w;
+            hb[slot][4] = b1.x;
+            hb[slot][5] = b1.y;
+            hb[slot][6] = b1.z;
+            hb[slot][7] = b1.w;
+          } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) hb[slot][i] = 0u;
+          }
+          hs[slot] = ld_l2_v2(p.gsum + goff + (size_t)gg * p.gsum_mp + tok0 + 2 * tig);
+        }
+      }
       if (!mbar_wait(&full[s], rnd & 1)) return;
 #pragma unroll
       for (int slot = 0; slot < SLOTS; ++slot) {
@@ -499,7 +547,12 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
           int sx[MT][2];
 #pragma unroll
           for (int mt = 0; mt < MT; ++mt) {
-            if constexpr (XS) {
+            if constexpr (HOIST) {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) bf[mt][i] = hb[slot][i];
+              sx[mt][0] = hs[slot].x;
+              sx[mt][1] = hs[slot].y;
+            } else if constexpr (XS) {
               const uint4* xb = reinterpret_cast<const uint4*>(xrows + (size_t)xr[mt] * xstride +
                                                                (size_t)gg * kGroup + 32 * tig);
               const uint4 b0 = xb[0], b1 = xb[1];
@@ -518,8 +571,8 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
               // fragment-order rows and code sums in global memory (L2; .cg:
               // a previous call's lines in this SM's L1 could be stale)
               if (xvalid[mt]) {
-                const uint4 b0 = ld_l2_v4(xrowf[mt] + (size_t)gg * kGroup);
-                const uint4 b1 = ld_l2_v4(xrowf[mt] + (size_t)gg * kGroup + 16);
+                const uint4 b0 = ld_l2_v4(xrowf[mt] + xoff + (size_t)gg * kGroup);
+                const uint4 b1 = ld_l2_v4(xrowf[mt] + xoff + (size_t)gg * kGroup + 16);
                 bf[mt][0] = b0.x;
                 bf[mt][1] = b0.y;
                 bf[mt][2] = b0.z;
@@ -532,7 +585,7 @@ __global__ void __launch_bounds__(dec_threads(MT), 1) gemm_stream_kernel(DecPara
 #pragma unroll
                 for (int i = 0; i < 8; ++i) bf[mt][i] = 0u;
               }
-              const int2 s2 = ld_l2_v2(p.gsum + (size_t)gg * p.gsum_mp + tok0 + mt * 8 + 2 * tig);
+              const int2 s2 = ld_l2_v2(p.gsum + goff + (size_t)gg * p.gsum_mp + tok0 + mt * 8 + 2 * tig);
               sx[mt][0] = s2.x;
               sx[mt][1] = s2.y;
             } else {
@@ -696,6 +749,7 @@ static DecParams dec_params(int64_t M, int N, int K, const void* packed, const v
   p.units = (int64_t)(N / kRecRows) * (K / kGroup);
   p.ctas = dec_ctas(N / kRecRows, K / kGroup);
   p.stages = 0;
+  p.tables = 1;
   return p;
 }
 
@@ -738,8 +792,8 @@ cudaError_t launch_gemm_decode(const int8_t* xq, const float* xscale, int64_t M,
 // int8 codes in fragment order with their group sums, and the GEMM, whose
 // weight stream started during both, consumes them
 // ---------------------------------------------------------------------------
-cudaError_t launch_rot16_decode(int x_dtype, const void* x, int64_t M, int K, const uint16_t* scales,
-                                const uint32_t* rtab, __half* y, uint32_t* amax, int frag, cudaStream_t st);
+cudaError_t launch_rot16_decode(int x_dtype, const void* x, int64_t M, int K, const RotTables& tabs, int T, __half* y,
+                                uint32_t* amax, int frag, int pro_kind, const RotPro& pro, cudaStream_t st);
 int gemm_tc_supported(int64_t M, int N, int K);
 size_t gemm_tc_workspace(int64_t M, int N, int K);
 cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
@@ -757,16 +811,18 @@ int linear_decode_tc(int64_t M, int N, int K) {
   return (M > 24 && gemm_tc_supported(M, N, K)) || (M > 32 && K / kGroup >= 64);
 }
 
-size_t linear_decode_workspace(int64_t M, int N, int K) {
-  const size_t tc = linear_decode_tc(M, N, K) ? gemm_tc_workspace(M, N, K) : 0;
+// Workspace of the decode linear for T rotation tables (the GEMM's, then
+// the row maxima of the T activation sets).
+size_t linear_decode_workspace(int64_t M, int N, int K, int T) {
+  const size_t tc = T == 1 && linear_decode_tc(M, N, K) ? gemm_tc_workspace(M, N, K) : 0;
   const size_t dec = gemm_decode_workspace(M, N);
-  return (tc > dec ? tc : dec) + (((size_t)M * sizeof(uint32_t) + 255) & ~(size_t)255);
+  return (tc > dec ? tc : dec) + (((size_t)T * M * sizeof(uint32_t) + 255) & ~(size_t)255);
 }
 
 static int token_tiles(int64_t M) { return M <= 8 ? 1 : M <= 16 ? 2 : M <= 32 ? 4 : 8; }
 
 cudaError_t launch_quant16_decode(const __half* y, uint32_t* amax, int64_t M, int K, int Mp, int8_t* xq, float* xscale,
-                                  int* gsum, cudaStream_t st);
+                                  int* gsum, int T, cudaStream_t st);
 
 // Whether the GEMM stages the quantised rows in shared memory (kXinPreQS)
 // or reads each record's fragments from L2 (kXinPreQ), measured on B200:
@@ -780,9 +836,12 @@ static bool stage_rows(const DecParams& p) { return p.units > 64 * (int64_t)p.ct
 
 static size_t al256(size_t b) { return (b + 255) & ~(size_t)255; }
 
-size_t linear_decode_scratch(int64_t M, int K) {
+// Scratch of the decode linear for T rotation tables: T activation sets of
+// fp16 rotated rows, int8 codes, token scales and per-group code sums.
+size_t linear_decode_scratch(int64_t M, int K, int T) {
   const size_t Mp = (size_t)8 * token_tiles(M);
-  return al256((size_t)M * K * 2) + al256((size_t)M * K) + al256((size_t)M * 4) + al256((size_t)(K / kGroup) * Mp * 4);
+  return al256((size_t)T * M * K * 2) + al256((size_t)T * M * K) + al256((size_t)T * M * 4) +
+         al256((size_t)T * (K / kGroup) * Mp * 4);
 }
 
 template <int MT>
@@ -801,14 +860,20 @@ static cudaError_t launch_pick_preq(DecParams p, cudaStream_t st) {
 }
 
 // Returns cudaErrorNotSupported (nothing launched) above kDecMaxTokens
-// tokens; callers then run the two-kernel path.
-cudaError_t launch_linear_decode(const void* x, int x_dtype, const uint16_t* cscale, const uint32_t* rtab, int64_t M,
-                                 int N, int K, const void* packed, const void* bias, int bias_dtype, void* out,
-                                 int out_dtype, void* ws, void* scratch, cudaStream_t st) {
+// tokens; callers then run the two-kernel path.  T rotation tables (a group
+// of linears sharing x, weights concatenated along N): tabs.rtab / cs[t]
+// apply to row blocks [tab_nb[t], tab_nb[t + 1]) (tab_nb[0] = 0); with
+// T > 1 the GEMM is the streaming kernel reading each set's fragments from
+// L2.
+cudaError_t launch_linear_decode_tables(const void* x, int x_dtype, const RotTables& tabs, int T, const int* tab_nb,
+                                        int64_t M, int N, int K, const void* packed, const void* bias, int bias_dtype,
+                                        void* out, int out_dtype, void* ws, void* scratch, int pro_kind,
+                                        const RotPro& pro, cudaStream_t st) {
   if (M > kDecMaxTokens || M <= 0) return cudaErrorNotSupported;
+  if (T < 1 || T > kMaxTables) return cudaErrorInvalidValue;
   DecParams p = dec_params(M, N, K, packed, bias, bias_dtype, out, out_dtype, ws);
   // (the tensor-core GEMM's row stores want a 16-byte aligned output)
-  const bool tc = linear_decode_tc(M, N, K) && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+  const bool tc = T == 1 && linear_decode_tc(M, N, K) && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
   const size_t tcb = tc ? gemm_tc_workspace(M, N, K) : 0;
   const size_t decb = gemm_decode_workspace(M, N);
   uint8_t* tail = static_cast<uint8_t*>(ws) + (tcb > decb ? tcb : decb);
@@ -816,14 +881,14 @@ cudaError_t launch_linear_decode(const void* x, int x_dtype, const uint16_t* csc
   // rotation into the fp16 scratch, quantisation (fragment order + code
   // sums, or channel order for the tensor-core GEMM), then the GEMM
   __half* rot16 = static_cast<__half*>(scratch);
-  cudaError_t e = launch_rot16_decode(x_dtype, x, M, K, cscale, rtab, rot16, p.amax, tc ? 0 : 1, st);
+  cudaError_t e = launch_rot16_decode(x_dtype, x, M, K, tabs, T, rot16, p.amax, tc ? 0 : 1, pro_kind, pro, st);
   if (e != cudaSuccess) return e;
-  uint8_t* sp = static_cast<uint8_t*>(scratch) + al256((size_t)M * K * 2);
+  uint8_t* sp = static_cast<uint8_t*>(scratch) + al256((size_t)T * M * K * 2);
   int8_t* xq = reinterpret_cast<int8_t*>(sp);
-  float* xs = reinterpret_cast<float*>(sp + al256((size_t)M * K));
-  int* gsum = reinterpret_cast<int*>(sp + al256((size_t)M * K) + al256((size_t)M * 4));
+  float* xs = reinterpret_cast<float*>(sp + al256((size_t)T * M * K));
+  int* gsum = reinterpret_cast<int*>(sp + al256((size_t)T * M * K) + al256((size_t)T * M * 4));
   const int Mp = 8 * token_tiles(M);
-  e = launch_quant16_decode(rot16, p.amax, M, K, Mp, xq, xs, gsum, st);
+  e = launch_quant16_decode(rot16, p.amax, M, K, Mp, xq, xs, gsum, T, st);
   if (e != cudaSuccess) return e;
   if (tc) {
     // the tensor-core GEMM does not read the row maxima: clear them here
@@ -832,7 +897,7 @@ cudaError_t launch_linear_decode(const void* x, int x_dtype, const uint16_t* csc
     if (e != cudaSuccess) return e;
     return launch_gemm_tc(xq, xs, M, N, K, packed, bias, bias_dtype, out, out_dtype, tcb ? ws : nullptr, tcb, st);
   }
-  if (rows_kernel_enabled()) {
+  if (T == 1 && rows_kernel_enabled()) {
     e = launch_gemm_rows(xq, xs, M, N, K, packed, bias, bias_dtype, out, out_dtype, ws, p.amax, gsum, Mp, st);
     if (e != cudaErrorNotSupported) return e;
   }
@@ -840,12 +905,38 @@ cudaError_t launch_linear_decode(const void* x, int x_dtype, const uint16_t* csc
   p.xscale = xs;
   p.gsum = gsum;
   p.gsum_mp = Mp;
+  if (T > 1) {
+    p.tables = T;
+    for (int t = 0; t < T; ++t) p.tab_nb[t] = tab_nb[t];
+    p.set_xq = M * (int64_t)K;
+    p.set_gsum = (int64_t)(K / kGroup) * Mp;
+    p.xrows_n = 0;
+    switch (token_tiles(M)) {
+      case 1: stages_for(p, 1, 0); return launch_mt<1, false, kXinPreQ>(p, 0, st);
+      case 2: stages_for(p, 2, 0); return launch_mt<2, false, kXinPreQ>(p, 0, st);
+      case 4: stages_for(p, 4, 0); return launch_mt<4, false, kXinPreQ>(p, 0, st);
+    }
+    stages_for(p, 8, 0);
+    return launch_mt<8, false, kXinPreQ>(p, 0, st);
+  }
   switch (token_tiles(M)) {
     case 1: return launch_pick_preq<1>(p, st);
     case 2: return launch_pick_preq<2>(p, st);
     case 4: return launch_pick_preq<4>(p, st);
   }
   return launch_pick_preq<8>(p, st);
+}
+
+cudaError_t launch_linear_decode(const void* x, int x_dtype, const uint16_t* cscale, const uint32_t* rtab, int64_t M,
+                                 int N, int K, const void* packed, const void* bias, int bias_dtype, void* out,
+                                 int out_dtype, void* ws, void* scratch, int pro_kind, const RotPro& pro,
+                                 cudaStream_t st) {
+  RotTables tabs = {};
+  tabs.rtab[0] = rtab;
+  tabs.cs[0] = cscale;
+  const int nb0 = 0;
+  return launch_linear_decode_tables(x, x_dtype, tabs, 1, &nb0, M, N, K, packed, bias, bias_dtype, out, out_dtype, ws,
+                                     scratch, pro_kind, pro, st);
 }
 
 }  // namespace paro

@@ -191,10 +191,31 @@ constexpr unsigned kFull = 0xffffffffu;
 // `lane` (slots >= the number of pieces get an empty item), the round's
 // ring stages (its longest piece / C) and whether any of its segments needs
 // the epilogue warps (cut into pieces, or shared with another CTA).
+// Rounds of a CTA: when its range has whole row blocks between two end
+// segments and at least one end is shared with a neighbouring CTA, the two
+// ends form round 0 (their fix-up through the workspace then overlaps the
+// stream of the rest), and the whole row blocks follow in rounds of up to
+// kRwWarps; otherwise all segments are dealt out evenly.
+__device__ __forceinline__ int rw_head(const RwSegs& sg) {
+  return (sg.n > 2 && (sg.gL1 < sg.G || sg.g0 > 0)) ? 2 : 0;
+}
+__device__ __forceinline__ int rw_rounds(const RwSegs& sg) {
+  const int head = rw_head(sg);
+  return (head ? 1 : 0) + (sg.n - head + kRwWarps - 1) / kRwWarps;
+}
+
 __device__ __forceinline__ RwItem rw_round(const RwSegs& sg, int rounds, int r, int G, int C, int lane, int& nst,
                                            int& epi) {
-  const int s0 = (sg.n * r) / rounds;
-  const int m = (sg.n * (r + 1)) / rounds - s0;
+  const int head = rw_head(sg);
+  int s0, m;
+  if (head && r == 0) {
+    s0 = 0;
+    m = head;
+  } else {
+    const int rb = r - (head ? 1 : 0), nbr = rounds - (head ? 1 : 0), body = sg.n - head;
+    s0 = head + (body * rb) / nbr;
+    m = head + (body * (rb + 1)) / nbr - s0;
+  }
   int nb = 0, gb = 0, ge = 0;
   if (lane < m) sg.get(s0 + lane, nb, gb, ge);
   const int L = lane < m ? ge - gb : 0;
@@ -286,7 +307,7 @@ __global__ void __launch_bounds__(kRwThreads, 1) gemm_rows_kernel(RwParams p) {
   const int gid = lane >> 2, tig = lane & 3;
   const unsigned units = (unsigned)p.units, ctas = (unsigned)p.ctas;
   const RwSegs sg((int)(blockIdx.x * units / ctas), (int)((blockIdx.x + 1) * units / ctas), G);
-  const int rounds = (sg.n + NC - 1) / NC;
+  const int rounds = rw_rounds(sg);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -336,18 +357,19 @@ __global__ void __launch_bounds__(kRwThreads, 1) gemm_rows_kernel(RwParams p) {
   if (warp > NC) {  // epilogue warps: warp NC + 1 + e takes the epilogue rounds e (mod 2)
     const int ew = warp - (NC + 1);
     grid_dependency_wait_rw();  // token scales (and rows) come from the previous kernel
+    if (ew == 0 && (FRAGIN || p.M * p.K > kRwBulkXBytes)) {
+      // rows (and, in fragment order, their code sums) by bulk copies, one
+      // per lane, issued before anything else: the consumers wait for them
+      if (lane == 0)
+        mbar_arrive_expect_tx(xbar, (uint32_t)p.M * p.K + (FRAGIN ? (uint32_t)(G * MP * 4) : 0u));
+      __syncwarp();
+      if (lane < p.M) bulk_g2s(xrows + (size_t)lane * xstride, p.xq + (int64_t)lane * p.K, (uint32_t)p.K, xbar);
+      if (FRAGIN && lane == 31) bulk_g2s(sxs, p.gsum, (uint32_t)(G * MP * 4), xbar);
+    }
     for (int t = lane; t < p.M; t += 32) tok_scale_s[t] = ld_dep(p.xscale + t);
     __syncwarp();
     if (FRAGIN && p.amax && blockIdx.x == 0 && ew == 0)
       for (int t = lane; t < p.M; t += 32) p.amax[t] = 0u;   // the quantiser that read them has finished
-    if (ew == 0 && lane == 0 && (FRAGIN || p.M * p.K > kRwBulkXBytes)) {
-      // rows (and, in fragment order, their code sums) by bulk copies
-      const uint32_t xb = (uint32_t)p.M * p.K + (FRAGIN ? (uint32_t)(G * MP * 4) : 0u);
-      mbar_arrive_expect_tx(xbar, xb);
-      for (int r = 0; r < p.M; ++r)
-        bulk_g2s(xrows + (size_t)r * xstride, p.xq + (int64_t)r * p.K, (uint32_t)p.K, xbar);
-      if (FRAGIN) bulk_g2s(sxs, p.gsum, (uint32_t)(G * MP * 4), xbar);
-    }
     int e = 0;
     for (int r = 0; r < rounds; ++r) {
       int nst, epi;
@@ -654,19 +676,25 @@ static bool rw_plan(int64_t M, int N, int K, RwPlan& pl) {
   const int G = K / kGroup, nbk = N / kRecRows;
   pl.MT = M <= 8 ? 1 : 2;
   pl.ctas = rw_ctas(nbk, G);
+  // Where this kernel measured at least as fast as gemm_stream_kernel on
+  // B200 (per-launch times in a CUDA graph, weights > L2): up to 8 tokens on
+  // layers whose CTAs own 16 or more whole row blocks each (gate_up at 1 /
+  // 4 / 8 tokens: 16.6 / 16.8 / 17.0 us against 16.5 / 17.0 / 18.3).  Where
+  // its row blocks are cut into pieces (qkv, o, down) the streaming kernel
+  // was 2-5 us faster per launch.
+  if (M > 8 || (int64_t)nbk < 16 * (int64_t)pl.ctas) return false;
   // the kernel walks its unit range in 32-bit arithmetic
   const int64_t units = (int64_t)nbk * G;
   if (units * (pl.ctas + 1) >= (int64_t)1 << 31 || (int64_t)M * K >= (int64_t)1 << 31) return false;
   const size_t base = rw_fixed_smem(pl.MT) + rw_xs_bytes(pl.MT, K, (int)M);
   if (base >= (size_t)kRwSmemBudget) return false;
   const size_t room = (size_t)kRwSmemBudget - base;
-  // two records per warp per stage when that leaves at least 4 stages,
-  // otherwise one (at least 3 stages either way)
-  const size_t stage2 = (size_t)kRwWarps * 2 * kRecBytes, stage1 = stage2 / 2;
-  pl.C = room / stage2 >= 4 ? 2 : 1;
-  const size_t stage = pl.C == 2 ? stage2 : stage1;
+  // two records (2 KB bulk copies) per warp per stage, at least 4 stages
+  // (1 KB copies streamed at about half the rate on B200)
+  pl.C = 2;
+  const size_t stage = (size_t)kRwWarps * 2 * kRecBytes;
   const int st = (int)(room / stage);
-  if (st < 3) return false;
+  if (st < 4) return false;
   pl.stages = st > kRwMaxStages ? kRwMaxStages : st;
   pl.smem = base + (size_t)pl.stages * stage;
   return true;

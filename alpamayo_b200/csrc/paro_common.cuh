@@ -146,6 +146,30 @@ __device__ __forceinline__ void st_cg_f32(float* p, float v) {
   asm volatile("st.global.cg.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
 }
 
+// The decoder-layer step a decode-size linear can fuse into its rotation
+// kernel's input load (rotq_decode.cu): none, residual add + RMSNorm, or
+// SiLU(gate) * up.
+constexpr int kProNone = 0;
+constexpr int kProAddRmsnorm = 1;
+constexpr int kProSiluMul = 2;
+
+struct RotPro {
+  const __nv_bfloat16* res_in;   // residual stream in [M, K] or null
+  __nv_bfloat16* res_out;        // bf16(x + res_in) (x when null) [M, K]; must not overlap res_in or x
+  const __nv_bfloat16* w;        // RMSNorm weight [K]
+  float eps;
+};
+
+// Per-projection rotation tables of a group of linears that share their
+// input (q / k / v, gate / up of a real checkpoint): the decode activation
+// kernels take the table index from blockIdx.z and write one activation
+// set per table.
+constexpr int kMaxTables = 4;
+struct RotTables {
+  const uint32_t* rtab[kMaxTables];
+  const uint16_t* cs[kMaxTables];
+};
+
 // Raise a kernel's dynamic shared-memory limit to `bytes` once per (kernel,
 // device); later calls are a map lookup instead of a driver call.
 cudaError_t ensure_smem_limit(const void* kernel, int bytes);

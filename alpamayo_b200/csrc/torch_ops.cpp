@@ -15,6 +15,7 @@
 #include <map>
 #include <mutex>
 #include <utility>
+#include <vector>
 
 #include "../../include/paro_b200.h"
 
@@ -299,6 +300,174 @@ at::Tensor linear_w4a8(const at::Tensor& x_in, const at::Tensor& rot_table,
   return out;
 }
 
+// One rotated linear with the decoder-layer step before it fused in
+// (paro_w4a8_linear_prologue): returns (y, new residual stream); the
+// residual output is a fresh tensor (never the input's storage).
+std::tuple<at::Tensor, at::Tensor> linear_prologue(int prologue, const at::Tensor& x_in,
+                                                   const c10::optional<at::Tensor>& residual_opt,
+                                                   const c10::optional<at::Tensor>& norm_weight, double eps,
+                                                   const at::Tensor& rot_table,
+                                                   const c10::optional<at::Tensor>& channel_scales,
+                                                   const at::Tensor& packed, int64_t N,
+                                                   const c10::optional<at::Tensor>& bias_opt, bool fp16_round,
+                                                   at::ScalarType out_dtype) {
+  at::Tensor x = x_in.contiguous();
+  check_cuda(x, "x");
+  check_cuda(rot_table, "rot_table");
+  check_cuda(packed, "packed");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16, "fused prologue: bf16 input expected");
+  TORCH_CHECK(rot_table.scalar_type() == at::kInt, "rot_table must be the int32 tensor from prepare_rotation");
+  const bool rms = prologue == PARO_PROLOGUE_ADD_RMSNORM;
+  const int64_t K = rms ? x.size(-1) : x.size(-1) / 2;
+  TORCH_CHECK(rms || x.size(-1) == 2 * K, "silu prologue: input must be [..., 2K]");
+  TORCH_CHECK(rot_table.size(-1) == K && rot_table.size(0) == 8, "rot_table must be [8, K]");
+  TORCH_CHECK((size_t)packed.numel() == paro_packed_weight_bytes((int)N, (int)K), "packed weight size mismatch");
+  const int64_t M = x.numel() / x.size(-1);
+  const uint16_t* csp = nullptr;
+  at::Tensor cs;
+  if (channel_scales.has_value() && channel_scales->defined() && channel_scales->numel() > 0) {
+    cs = channel_scales->to(at::kHalf).contiguous();
+    check_cuda(cs, "channel_scales");
+    csp = reinterpret_cast<const uint16_t*>(cs.data_ptr());
+  }
+  const void* bp = nullptr;
+  int bdt = PARO_F32;
+  at::Tensor bias;
+  if (bias_opt.has_value() && bias_opt->defined()) {
+    bias = bias_opt->contiguous();
+    check_cuda(bias, "bias");
+    TORCH_CHECK(bias.numel() == N, "bias must have N elements");
+    bp = bias.data_ptr();
+    bdt = to_paro_dtype(bias.scalar_type());
+  }
+  at::Tensor res_in, res_out, w;
+  if (rms) {
+    TORCH_CHECK(norm_weight.has_value() && norm_weight->defined(), "add_rmsnorm prologue needs the norm weight");
+    w = norm_weight->contiguous();
+    check_cuda(w, "norm_weight");
+    TORCH_CHECK(w.scalar_type() == at::kBFloat16 && w.numel() == K, "norm_weight must be bf16 [K]");
+    if (residual_opt.has_value() && residual_opt->defined()) {
+      res_in = residual_opt->contiguous();
+      TORCH_CHECK(res_in.sizes() == x.sizes() && res_in.scalar_type() == at::kBFloat16, "residual must match x");
+    }
+    res_out = at::empty_like(x);
+  }
+  c10::cuda::CUDAGuard guard(x.device());
+  auto osz = x.sizes().vec();
+  osz.back() = N;
+  at::Tensor out = at::empty(osz, x.options().dtype(out_dtype));
+  if (M == 0) return {out, rms ? res_out : x};
+  const size_t wsb = paro_w4a8_linear_workspace_size(M, (int)N, (int)K);
+  void* wsp = workspace_for(x.device(), wsb);
+  const size_t scb = paro_w4a8_linear_prologue_scratch_size(prologue, M, (int)N, (int)K, fp16_round ? 1 : 0);
+  at::Tensor sct = at::empty({(int64_t)scb + 256}, x.options().dtype(at::kByte));
+  void* scp = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(sct.data_ptr()) + 255) & ~(uintptr_t)255);
+  check_status(paro_w4a8_linear_prologue(prologue, x.data_ptr(), res_in.defined() ? res_in.data_ptr() : nullptr,
+                                         rms ? res_out.data_ptr() : nullptr, rms ? w.data_ptr() : nullptr,
+                                         (float)eps, M, (int)K, (int)N, csp,
+                                         reinterpret_cast<const uint32_t*>(rot_table.data_ptr<int32_t>()),
+                                         fp16_round ? 1 : 0, packed.data_ptr(), bp, bdt, out.data_ptr(),
+                                         to_paro_dtype(out_dtype), wsp, wsb, scp, scb, cur_stream()),
+               "linear_w4a8 (fused prologue)");
+  return {out, rms ? res_out : x};
+}
+
+std::tuple<at::Tensor, at::Tensor> linear_w4a8_rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual,
+                                                       const at::Tensor& norm_weight, double eps,
+                                                       const at::Tensor& rot_table,
+                                                       const c10::optional<at::Tensor>& channel_scales,
+                                                       const at::Tensor& packed, int64_t N,
+                                                       const c10::optional<at::Tensor>& bias, bool fp16_round,
+                                                       at::ScalarType out_dtype) {
+  return linear_prologue(PARO_PROLOGUE_ADD_RMSNORM, x, residual, norm_weight, eps, rot_table, channel_scales, packed, N,
+                         bias, fp16_round, out_dtype);
+}
+
+at::Tensor linear_w4a8_silu(const at::Tensor& gate_up, const at::Tensor& rot_table,
+                            const c10::optional<at::Tensor>& channel_scales, const at::Tensor& packed, int64_t N,
+                            const c10::optional<at::Tensor>& bias, bool fp16_round, at::ScalarType out_dtype) {
+  return std::get<0>(linear_prologue(PARO_PROLOGUE_SILU_MUL, gate_up, c10::nullopt, c10::nullopt, 0.0, rot_table,
+                                     channel_scales, packed, N, bias, fp16_round, out_dtype));
+}
+
+// A group of rotated linears sharing x, one rotation table each, weights
+// concatenated along N (paro_w4a8_linear_group): returns ([..., sum N],
+// new residual stream or x).
+std::tuple<at::Tensor, at::Tensor> linear_w4a8_group(const at::Tensor& x_in, const c10::optional<at::Tensor>& residual,
+                                                     const c10::optional<at::Tensor>& norm_weight, double eps,
+                                                     int64_t prologue, at::TensorList rot_tables,
+                                                     at::TensorList channel_scales, const at::Tensor& packed,
+                                                     at::IntArrayRef n_per_table,
+                                                     const c10::optional<at::Tensor>& bias_opt, bool fp16_round,
+                                                     at::ScalarType out_dtype) {
+  at::Tensor x = x_in.contiguous();
+  check_cuda(x, "x");
+  check_cuda(packed, "packed");
+  const int T = (int)rot_tables.size();
+  TORCH_CHECK(T >= 1 && T <= 4, "linear group: 1 to 4 rotation tables");
+  TORCH_CHECK((int)n_per_table.size() == T, "one output width per table");
+  TORCH_CHECK(channel_scales.empty() || (int)channel_scales.size() == T, "one channel-scale vector per table");
+  const bool rms = prologue == PARO_PROLOGUE_ADD_RMSNORM, silu = prologue == PARO_PROLOGUE_SILU_MUL;
+  const int64_t K = silu ? x.size(-1) / 2 : x.size(-1);
+  const int64_t M = x.numel() / x.size(-1);
+  std::vector<int> ns(T);
+  int64_t N = 0;
+  std::vector<const uint32_t*> tabs(T);
+  std::vector<const uint16_t*> css(T, nullptr);
+  std::vector<at::Tensor> keep;
+  for (int t = 0; t < T; ++t) {
+    ns[t] = (int)n_per_table[t];
+    N += ns[t];
+    check_cuda(rot_tables[t], "rot_table");
+    TORCH_CHECK(rot_tables[t].scalar_type() == at::kInt && rot_tables[t].size(-1) == K && rot_tables[t].size(0) == 8,
+                "rot_tables must be int32 [8, K] tensors from prepare_rotation");
+    tabs[t] = reinterpret_cast<const uint32_t*>(rot_tables[t].data_ptr<int32_t>());
+    if (!channel_scales.empty() && channel_scales[t].defined() && channel_scales[t].numel() > 0) {
+      at::Tensor c = channel_scales[t].to(at::kHalf).contiguous();
+      check_cuda(c, "channel_scales");
+      keep.push_back(c);
+      css[t] = reinterpret_cast<const uint16_t*>(c.data_ptr());
+    }
+  }
+  TORCH_CHECK((size_t)packed.numel() == paro_packed_weight_bytes((int)N, (int)K), "packed weight size mismatch");
+  const void* bp = nullptr;
+  int bdt = PARO_F32;
+  at::Tensor bias;
+  if (bias_opt.has_value() && bias_opt->defined()) {
+    bias = bias_opt->contiguous();
+    check_cuda(bias, "bias");
+    TORCH_CHECK(bias.numel() == N, "bias must have sum(n_per_table) elements");
+    bp = bias.data_ptr();
+    bdt = to_paro_dtype(bias.scalar_type());
+  }
+  at::Tensor res_in, res_out, w;
+  if (rms) {
+    TORCH_CHECK(norm_weight.has_value() && norm_weight->defined(), "add_rmsnorm prologue needs the norm weight");
+    w = norm_weight->contiguous();
+    TORCH_CHECK(w.scalar_type() == at::kBFloat16 && w.numel() == K, "norm_weight must be bf16 [K]");
+    if (residual.has_value() && residual->defined()) res_in = residual->contiguous();
+    res_out = at::empty_like(x);
+  }
+  c10::cuda::CUDAGuard guard(x.device());
+  auto osz = x.sizes().vec();
+  osz.back() = N;
+  at::Tensor out = at::empty(osz, x.options().dtype(out_dtype));
+  if (M == 0) return {out, rms ? res_out : x};
+  const size_t wsb = paro_w4a8_linear_group_workspace_size(M, T, ns.data(), (int)K);
+  void* wsp = workspace_for(x.device(), wsb);
+  const size_t scb = paro_w4a8_linear_group_scratch_size((int)prologue, M, T, ns.data(), (int)K, fp16_round ? 1 : 0);
+  at::Tensor sct = at::empty({(int64_t)scb + 256}, x.options().dtype(at::kByte));
+  void* scp = reinterpret_cast<void*>((reinterpret_cast<uintptr_t>(sct.data_ptr()) + 255) & ~(uintptr_t)255);
+  check_status(paro_w4a8_linear_group((int)prologue, x.data_ptr(), to_paro_dtype(x.scalar_type()),
+                                      res_in.defined() ? res_in.data_ptr() : nullptr,
+                                      rms ? res_out.data_ptr() : nullptr, rms ? w.data_ptr() : nullptr, (float)eps, M,
+                                      (int)K, T, ns.data(), css.data(), tabs.data(), fp16_round ? 1 : 0,
+                                      packed.data_ptr(), bp, bdt, out.data_ptr(), to_paro_dtype(out_dtype), wsp, wsb,
+                                      scp, scb, cur_stream()),
+               "linear_w4a8_group");
+  return {out, rms ? res_out : x};
+}
+
 // residual add + RMSNorm: returns (normalised, new residual); residual may be
 // None (then the new residual is x itself)
 std::tuple<at::Tensor, at::Tensor> add_rmsnorm(const at::Tensor& x_in, const c10::optional<at::Tensor>& residual_opt,
@@ -373,6 +542,14 @@ TORCH_LIBRARY(paro_b200, m) {
         "bool fp16_round, ScalarType out_dtype) -> Tensor");
   m.def("add_rmsnorm(Tensor x, Tensor? residual, Tensor weight, float eps) -> (Tensor, Tensor)");
   m.def("silu_mul(Tensor x) -> Tensor");
+  m.def("linear_w4a8_rmsnorm(Tensor x, Tensor? residual, Tensor norm_weight, float eps, Tensor rot_table, "
+        "Tensor? channel_scales, Tensor packed, int N, Tensor? bias, bool fp16_round, ScalarType out_dtype) "
+        "-> (Tensor, Tensor)");
+  m.def("linear_w4a8_group(Tensor x, Tensor? residual, Tensor? norm_weight, float eps, int prologue, "
+        "Tensor[] rot_tables, Tensor[] channel_scales, Tensor packed, int[] n_per_table, Tensor? bias, "
+        "bool fp16_round, ScalarType out_dtype) -> (Tensor, Tensor)");
+  m.def("linear_w4a8_silu(Tensor gate_up, Tensor rot_table, Tensor? channel_scales, Tensor packed, int N, "
+        "Tensor? bias, bool fp16_round, ScalarType out_dtype) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(paro_b200, CUDA, m) {
@@ -386,4 +563,7 @@ TORCH_LIBRARY_IMPL(paro_b200, CUDA, m) {
   m.impl("linear_w4a8", &linear_w4a8);
   m.impl("add_rmsnorm", &add_rmsnorm);
   m.impl("silu_mul", &silu_mul);
+  m.impl("linear_w4a8_rmsnorm", &linear_w4a8_rmsnorm);
+  m.impl("linear_w4a8_silu", &linear_w4a8_silu);
+  m.impl("linear_w4a8_group", &linear_w4a8_group);
 }

@@ -119,6 +119,51 @@ def _silu_mul_fake(x):
     return x.new_empty((*x.shape[:-1], x.shape[-1] // 2))
 
 
+@torch.library.register_fake("paro_b200::linear_w4a8_rmsnorm")
+def _linear_rmsnorm_fake(x, residual, norm_weight, eps, rot_table, channel_scales, packed, N, bias, fp16_round,
+                         out_dtype):
+    return x.new_empty((*x.shape[:-1], N), dtype=out_dtype), torch.empty_like(x)
+
+
+@torch.library.register_fake("paro_b200::linear_w4a8_silu")
+def _linear_silu_fake(gate_up, rot_table, channel_scales, packed, N, bias, fp16_round, out_dtype):
+    return gate_up.new_empty((*gate_up.shape[:-1], N), dtype=out_dtype)
+
+
+def linear_w4a8_rmsnorm(x, residual, norm_weight, rot_table, channel_scales, packed, N, bias=None, eps=1e-6,
+                        fp16_round=True, out_dtype=torch.bfloat16):
+    """Residual add + RMSNorm fused into the rotated linear that follows it
+    (decoder layer: input_layernorm -> qkv, post_attention_layernorm ->
+    gate_up): returns (y, new residual stream)."""
+    return _ops.linear_w4a8_rmsnorm(x, residual, norm_weight, eps, rot_table, channel_scales, packed, N, bias,
+                                    fp16_round, out_dtype)
+
+
+def linear_w4a8_silu(gate_up, rot_table, channel_scales, packed, N, bias=None, fp16_round=True,
+                     out_dtype=torch.bfloat16):
+    """SiLU(gate) * up fused into the rotated down projection: gate_up is the
+    fused [..., 2K] output, gate columns first."""
+    return _ops.linear_w4a8_silu(gate_up, rot_table, channel_scales, packed, N, bias, fp16_round, out_dtype)
+
+
+@torch.library.register_fake("paro_b200::linear_w4a8_group")
+def _linear_group_fake(x, residual, norm_weight, eps, prologue, rot_tables, channel_scales, packed, n_per_table, bias,
+                       fp16_round, out_dtype):
+    return x.new_empty((*x.shape[:-1], sum(n_per_table)), dtype=out_dtype), torch.empty_like(x)
+
+
+PROLOGUE = {"none": 0, "add_rmsnorm": 1, "silu_mul": 2}
+
+
+def linear_w4a8_group(x, rot_tables, channel_scales, packed, n_per_table, bias=None, prologue="none", residual=None,
+                      norm_weight=None, eps=1e-6, fp16_round=True, out_dtype=torch.bfloat16):
+    """A group of rotated linears that share x, one rotation table each
+    (q / k / v, gate / up of a real checkpoint), weights concatenated along
+    N: returns ([..., sum(n_per_table)], new residual stream or x)."""
+    return _ops.linear_w4a8_group(x, residual, norm_weight, eps, PROLOGUE[prologue], list(rot_tables),
+                                  list(channel_scales), packed, list(n_per_table), bias, fp16_round, out_dtype)
+
+
 def add_rmsnorm(x, residual, weight, eps=1e-6):
     """Residual add + Qwen3VLTextRMSNorm (bf16): returns (normalised, new
     residual stream)."""

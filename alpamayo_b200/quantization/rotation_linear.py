@@ -133,3 +133,50 @@ class RotateLinearInt4(nn.Module):
         elif buffer_name == "rotation.channel_scales":
             return self.rotation.channel_scales
         raise ValueError(f"Invalid buffer name: {buffer_name}")
+
+
+class RotateLinearGroup(nn.Module):
+    """Several RotateLinearInt4 that read the same input, each keeping its own
+    rotation (the q / k / v or gate / up projections of a real ParoQuant
+    checkpoint, which the reference loads as separate modules with separate
+    tables: paroquant_marlin_w4a8.py:455-460), run as one group: one rotation
+    and one quantisation launch over all tables and one GEMM over the
+    concatenated weights at decode sizes.  ``forward(x)`` returns
+    ``[..., sum(out_features)]``, the members' outputs side by side; the
+    members stay usable on their own and keep their state-dict keys."""
+
+    def __init__(self, linears):
+        super().__init__()
+        mods = [getattr(m, "rotate_linear", m) for m in linears]
+        if not 1 <= len(mods) <= 4:
+            raise ValueError("a group holds 1 to 4 rotated linears")
+        if len({m.in_features for m in mods}) != 1:
+            raise ValueError("the linears of a group must share in_features")
+        self.members = nn.ModuleList(mods)
+        self.in_features = mods[0].in_features
+        self.out_features = sum(m.out_features for m in mods)
+        self._packed = None
+        self._key = None
+
+    def _parts(self):
+        packs, biases = zip(*(m._packed_and_bias() for m in self.members))
+        key = tuple(p.data_ptr() for p in packs)
+        if self._packed is None or self._key != key:
+            self._packed = torch.cat([p.reshape(-1) for p in packs]).contiguous()
+            self._key = key
+        bias = None
+        if any(b is not None for b in biases):
+            ref = next(b for b in biases if b is not None)
+            bias = torch.cat([b.reshape(-1) if b is not None else ref.new_zeros(m.out_features)
+                              for b, m in zip(biases, self.members)])
+        return self._packed, bias
+
+    @torch.no_grad()
+    def forward(self, x, out_dtype=None, prologue="none", residual=None, norm_weight=None, eps=1e-6):
+        packed, bias = self._parts()
+        tabs = [m.rotation.rot_table() for m in self.members]
+        css = [m.rotation.channel_scales.reshape(-1).to(torch.float16) for m in self.members]
+        y, res = ops.linear_w4a8_group(x, tabs, css, packed, [m.out_features for m in self.members], bias,
+                                       prologue=prologue, residual=residual, norm_weight=norm_weight, eps=eps,
+                                       out_dtype=out_dtype if out_dtype is not None else x.dtype)
+        return (y, res) if prologue == "add_rmsnorm" else y

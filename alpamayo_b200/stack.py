@@ -41,6 +41,30 @@ def linear(L, x, out_dtype=torch.bfloat16):
     return ops.linear_w4a8(x, L["rot_table"], L["cs_vec"], L["packed"], L["N"], None, True, out_dtype)
 
 
+def linear_rmsnorm(L, x, residual, norm_weight, eps, out_dtype=torch.bfloat16):
+    """Residual add + RMSNorm fused into the rotated linear L: (y, new residual)."""
+    return ops.linear_w4a8_rmsnorm(x, residual, norm_weight, L["rot_table"], L["cs_vec"], L["packed"], L["N"], None,
+                                   eps, True, out_dtype)
+
+
+def linear_silu(L, gate_up, out_dtype=torch.bfloat16):
+    """SiLU(gate) * up fused into the rotated linear L."""
+    return ops.linear_w4a8_silu(gate_up, L["rot_table"], L["cs_vec"], L["packed"], L["N"], None, True, out_dtype)
+
+
+def group_rmsnorm(G, x, residual, norm_weight, eps, fused=True, out_dtype=torch.bfloat16):
+    """Residual add + RMSNorm, then a projection group (fused into the
+    group's rotation kernel, or as a separate kernel): (y, new residual)."""
+    if fused:
+        return ops.linear_w4a8_group(x, G["rot_tables"], G["channel_scales"], G["packed"], G["n_per_table"],
+                                     prologue="add_rmsnorm", residual=residual, norm_weight=norm_weight, eps=eps,
+                                     out_dtype=out_dtype)
+    h, res = ops.add_rmsnorm(x, residual, norm_weight, eps)
+    y, _ = ops.linear_w4a8_group(h, G["rot_tables"], G["channel_scales"], G["packed"], G["n_per_table"],
+                                 out_dtype=out_dtype)
+    return y, res
+
+
 _ws_cache = {}
 
 
@@ -69,23 +93,46 @@ def linear_into(L, x, out):
     return out
 
 
+def projection_group(parts):
+    """Layers that share their input, each with its own rotation, as one
+    group for ops.linear_w4a8_group: concatenated tile records, per-part
+    tables and channel scales, output widths."""
+    return {"N": sum(L["N"] for L in parts), "K": parts[0]["K"], "parts": parts,
+            "packed": torch.cat([L["packed"] for L in parts]),
+            "rot_tables": [L["rot_table"] for L in parts], "channel_scales": [L["cs_vec"] for L in parts],
+            "n_per_table": [L["N"] for L in parts]}
+
+
 class DecoderStack:
-    def __init__(self, layers=28, seed=0, device="cuda", eps=1e-6, keep=False):
+    """per_projection: q / k / v and gate / up as separate linears with their
+    own rotation tables (the layout of a real ParoQuant checkpoint), run as
+    groups (one rotation + quantisation launch over the tables, one GEMM over
+    the concatenated weights); otherwise fused qkv and gate_up with one table
+    each (the synthetic BASELINE shapes)."""
+
+    def __init__(self, layers=28, seed=0, device="cuda", eps=1e-6, keep=False, per_projection=False):
         qkv_n = (HEADS + 2 * KV_HEADS) * HEAD_DIM
         g = torch.Generator(device=device)
         g.manual_seed(seed)
         self.eps = eps
+        self.per_projection = per_projection
         self.layers = []
         for i in range(layers):
             s = seed * 1000 + 10 * i
             norm = lambda: (0.9 + 0.2 * torch.rand(HIDDEN, generator=g, device=device)).to(torch.bfloat16)
-            self.layers.append({
-                "in_norm": norm(), "post_norm": norm(),
-                "qkv": serving_layer(qkv_n, HIDDEN, s + 1, device, keep),
-                "o": serving_layer(HIDDEN, HEADS * HEAD_DIM, s + 2, device, keep),
-                "gate_up": serving_layer(2 * INTER, HIDDEN, s + 3, device, keep),
-                "down": serving_layer(HIDDEN, INTER, s + 4, device, keep),
-            })
+            L = {"in_norm": norm(), "post_norm": norm(),
+                 "o": serving_layer(HIDDEN, HEADS * HEAD_DIM, s + 2, device, keep),
+                 "down": serving_layer(HIDDEN, INTER, s + 4, device, keep)}
+            if per_projection:
+                L["qkv"] = projection_group([serving_layer(n, HIDDEN, s + 100 + j, device, keep)
+                                             for j, n in enumerate((HEADS * HEAD_DIM, KV_HEADS * HEAD_DIM,
+                                                                    KV_HEADS * HEAD_DIM))])
+                L["gate_up"] = projection_group([serving_layer(INTER, HIDDEN, s + 110 + j, device, keep)
+                                                 for j in range(2)])
+            else:
+                L["qkv"] = serving_layer(qkv_n, HIDDEN, s + 1, device, keep)
+                L["gate_up"] = serving_layer(2 * INTER, HIDDEN, s + 3, device, keep)
+            self.layers.append(L)
         self.final_norm = (0.9 + 0.2 * torch.rand(HIDDEN, generator=g, device=device)).to(torch.bfloat16)
 
     def weight_bytes(self):
@@ -94,18 +141,35 @@ class DecoderStack:
         return sum(syn.weight_stream_bytes(L[k]["N"], L[k]["K"]) for L in self.layers
                    for k in ("qkv", "o", "gate_up", "down"))
 
-    def forward(self, x):
-        """x: bf16 [M, 3584] (one token per clip) -> bf16 [M, 3584]."""
+    def forward(self, x, fused=True):
+        """x: bf16 [M, 3584] (one token per clip) -> bf16 [M, 3584].
+
+        fused: the residual add + RMSNorm before qkv and gate_up and the
+        SiLU * up before down run inside those linears' activation kernels
+        (linear_w4a8_rmsnorm / linear_w4a8_silu); otherwise as separate
+        kernels (add_rmsnorm, silu_mul).  Both give the same bits."""
         res = None
         mlp_out = x
         for L in self.layers:
-            h, res = ops.add_rmsnorm(mlp_out, res, L["in_norm"], self.eps)
-            qkv = linear(L["qkv"], h)
+            if self.per_projection:
+                qkv, res = group_rmsnorm(L["qkv"], mlp_out, res, L["in_norm"], self.eps, fused)
+            elif fused:
+                qkv, res = linear_rmsnorm(L["qkv"], mlp_out, res, L["in_norm"], self.eps)
+            else:
+                h, res = ops.add_rmsnorm(mlp_out, res, L["in_norm"], self.eps)
+                qkv = linear(L["qkv"], h)
             attn = qkv[:, :HEADS * HEAD_DIM].contiguous()   # identity attention
             o = linear(L["o"], attn)
-            h, res = ops.add_rmsnorm(o, res, L["post_norm"], self.eps)
-            a = ops.silu_mul(linear(L["gate_up"], h))
-            mlp_out = linear(L["down"], a)
+            if self.per_projection:
+                gu, res = group_rmsnorm(L["gate_up"], o, res, L["post_norm"], self.eps, fused)
+                mlp_out = linear_silu(L["down"], gu) if fused else linear(L["down"], ops.silu_mul(gu))
+            elif fused:
+                gu, res = linear_rmsnorm(L["gate_up"], o, res, L["post_norm"], self.eps)
+                mlp_out = linear_silu(L["down"], gu)
+            else:
+                h, res = ops.add_rmsnorm(o, res, L["post_norm"], self.eps)
+                a = ops.silu_mul(linear(L["gate_up"], h))
+                mlp_out = linear(L["down"], a)
         out, _ = ops.add_rmsnorm(mlp_out, res, self.final_norm, self.eps)
         return out
 

@@ -70,6 +70,7 @@ def args_():
     p.add_argument("--no-prefill", action="store_true")
     p.add_argument("--no-stack", action="store_true")
     p.add_argument("--no-sharded", action="store_true")
+    p.add_argument("--no-verify", action="store_true", help="skip the DFlash verify / decode-loop section")
     p.add_argument("--no-reference-gpu", action="store_true",
                    help="skip timing the reference's own GPU path (its rotate kernel + vLLM Marlin)")
     p.add_argument("--case", default=None, metavar="SHAPE:M",
@@ -220,17 +221,18 @@ STACK_LAYERS = 28
 SHARD_M, SHARD_N, SHARD_K = 16384, 37888, 3584
 
 
-def stack_section(torch, world, rank):
+def stack_section(torch, world, rank, per_projection=False):
     """28 rotated W4A8 decoder layers at decode, 64 independent
     clips x 1 token split across the ranks (no collective); tokens/s of the
     whole job and weight-stream GB/s per GPU, CUDA-graph timed, max over
-    ranks."""
+    ranks.  per_projection: q / k / v and gate / up with their own rotation
+    tables (a real checkpoint's layout), run as projection groups."""
     from alpamayo_b200 import synthetic as syn
     from alpamayo_b200.stack import DecoderStack
     if STACK_CLIPS % world:
         return {"skipped": f"{STACK_CLIPS} clips do not split over {world} ranks"}
     M = STACK_CLIPS // world
-    st = DecoderStack(layers=STACK_LAYERS, seed=0)
+    st = DecoderStack(layers=STACK_LAYERS, seed=0, per_projection=per_projection)
     x = syn.make_activations(M, 3584, seed=500 + rank)
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())
@@ -256,11 +258,83 @@ def stack_section(torch, world, rank):
     del g, st
     torch.cuda.empty_cache()
     return {"workload": "configs[3]: 28-layer decode stack (RMSNorm -> qkv, identity attention -> o, RMSNorm -> "
-                        "gate_up -> SiLU*up -> down), 64 clips x 1 token split over the ranks, no collective",
+                        "gate_up -> SiLU*up -> down), 64 clips x 1 token split over the ranks, no collective"
+                        + ("; q/k/v and gate/up with per-projection rotation tables" if per_projection else "")
+                        + "; RMSNorm and SiLU*up fused into the following linear's rotation kernel",
             "tokens_per_rank": M, "ms_per_forward": round(t * 1e3, 3),
             "tokens_per_s": round(STACK_CLIPS / t, 1),
             "weight_GBps_per_gpu": round(wb / t / 1e9, 1), "weight_bytes_per_forward": wb,
             "outputs_finite": finite}
+
+
+VERIFY_M = [8, 16, 48, 96]
+LOOP_TOKENS = 32
+
+
+def verify_section(torch, world, rank):
+    """Next consumers of the linear (the scope table's next rows): DFlash's
+    verify step runs the target model on a draft block (block_size 8, or 16
+    for the b16 draft model: src/alpamayo_r1/utils/dflash/
+    dflash_integration.py:144,276), times the trajectory samples (1 or 6);
+    the streaming rollout's decode loop replays the language model's CUDA
+    graph once per token with a host check of the stop condition in between
+    (src/alpamayo_r1/models/alpamayo_r1_unified.py:585-640,1677-1700).  Here
+    the 28-layer decode stack stands in for the language model: one forward
+    per verify block at M = 8, 16, 48, 96 (graph replays, CUDA events), and a
+    32-token loop at M = 1 and 6 with a host synchronisation after every
+    replay (host wall clock per token).  Per rank, no collective."""
+    from alpamayo_b200 import synthetic as syn
+    from alpamayo_b200.stack import DecoderStack
+    st = DecoderStack(layers=STACK_LAYERS, seed=0)
+    wb = st.weight_bytes()
+
+    def graph_of(x):
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            st.forward(x)
+        torch.cuda.current_stream().wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            y = st.forward(x)
+        return g, y
+
+    blocks = {}
+    for M in VERIFY_M:
+        x = syn.make_activations(M, 3584, seed=600 + M + rank)
+        g, _ = graph_of(x)
+        for _ in range(3):
+            g.replay()
+        reps = 5
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) * 1e-3 / reps
+        blocks[f"m{M}"] = {"ms_per_forward": round(t * 1e3, 3), "tokens_per_s": round(M / t, 1),
+                           "weight_GBps": round(wb / t / 1e9, 1)}
+        del g
+    loop = {}
+    for M in (1, 6):
+        x = syn.make_activations(M, 3584, seed=700 + M + rank)
+        g, y = graph_of(x)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(LOOP_TOKENS):
+            g.replay()
+            bool(torch.isfinite(y[0, 0]).item())   # the loop's per-token host check
+        el = (time.perf_counter() - t0) / LOOP_TOKENS
+        loop[f"m{M}"] = {"ms_per_token": round(el * 1e3, 3), "tokens_per_s": round(M / el, 1),
+                         "weight_GBps": round(wb / el / 1e9, 1)}
+        del g
+    del st
+    torch.cuda.empty_cache()
+    return {"workload": "28-layer decode stack as the target model: DFlash verify blocks and the per-token "
+                        "graph-replay decode loop", "verify_blocks": blocks, "decode_loop": loop}
 
 
 def sharded_section(torch, world, rank):
@@ -353,17 +427,22 @@ def sharded_section(torch, world, rank):
                "ms_exposed_gather": round((t_ov - t_lin) * 1e3, 3),
                "int8_tops_end_to_end": round(ops_total / t_ov / 1e12, 1)}
     ce = [v for k, v in p2p.items() if k != "unavailable"]
-    best = min(ce, key=lambda v: v["_t"]) if ce else None
+    # the headline is the fastest of every gather measured
+    variants = [("NCCL all_gather_into_tensor after the linear", t_tot, nccl),
+                (f"NCCL all_gather in {CH} row blocks overlapped with the linear", t_ov, nccl_ov)]
+    variants += [(f"copy-engine peer copies in {v['row_blocks']} row blocks overlapped with the next block's GEMM",
+                  v["_t"], v) for v in ce]
     for v in ce:
         v.pop("_t")
-    head = best if best is not None else nccl
+    name, t_best, head = min(variants, key=lambda z: z[1])
     return {"workload": "configs[4]: gate_up K=3584 N=37888 at M=16384, N split over the ranks, bf16 output "
                         "blocks gathered on every rank", "world": world, "block_columns": c1 - c0,
-            "gathered_shape": shape, "gather": ("copy-engine peer copies overlapped with the next row block's GEMM"
-                                                if best is not None else "NCCL all_gather_into_tensor"),
+            "gathered_shape": shape, "gather": name if world > 1 else "none (one rank)",
             "ms_end_to_end": head["ms_end_to_end"], "ms_linear": round(t_lin * 1e3, 3),
             "ms_exposed_gather": head.get("ms_exposed_gather", 0.0),
             "int8_tops_end_to_end": head.get("int8_tops_end_to_end", round(ops_total / t_lin / 1e12, 1)),
+            "gather_GBps_per_rank": (round((world - 1) / world * SHARD_M * SHARD_N * 2 /
+                                           max(t_best - t_lin, 1e-9) / 1e9, 1) if world > 1 else None),
             "nccl_all_gather": nccl, "nccl_all_gather_overlapped": nccl_ov,
             "copy_engine_gather": (p2p.get("unavailable") and p2p) or ce or None}
 
@@ -785,6 +864,9 @@ def main():
 
     # --- prefill: tcgen05 GEMM and activation kernel per shape
     stack = None if a.no_stack else stack_section(torch, world, rank)
+    if stack is not None and "skipped" not in stack:
+        stack["per_projection_tables"] = stack_section(torch, world, rank, per_projection=True)
+    verify = None if a.no_verify else verify_section(torch, world, rank)
     sharded = None if a.no_sharded else sharded_section(torch, world, rank)
     prefill = None
     if not a.no_prefill:
@@ -853,7 +935,8 @@ def main():
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": a.steps,
+            "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
+            "value_per_gpu": round(value / world, 1), "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int4xint8->int32 (bf16 act/out)", "data": "synthetic",
             "config": {"workload": "decode sweep, BASELINE configs[1]: qkv 3584->4608, o 3584->3584, "
@@ -882,6 +965,7 @@ def main():
                                   "alg_bytes": "2MK + MK + 4M + tables 2LK + LK + 2K (L = 8) per launch"},
             "prefill": prefill,
             "stack": stack,
+            "verify_and_decode_loop": verify,
             "sharded_prefill": sharded,
             "cases": case_out,
             "gpu_launches": launches_per_step * a.steps,

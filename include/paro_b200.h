@@ -289,6 +289,75 @@ int paro_w4a8_linear(const void* x, int x_dtype, int64_t M, int K, int N,
                      void* out, int out_dtype, void* workspace, size_t workspace_bytes,
                      void* scratch, size_t scratch_bytes, paro_stream_t stream);
 
+/*
+ * paro_w4a8_linear with the decoder-layer step in front of it fused into
+ * the activation kernel: the residual add + Qwen3VLTextRMSNorm before qkv
+ * and gate_up (src/alpamayo_r1/models/qwen3_vl/modeling_qwen3_vl.py:340-357,
+ * the decoder layer's `residual + hidden_states`), or SiLU(gate) * up before
+ * down (src/alpamayo_r1/utils/system/patches.py:540-547,
+ * `down_proj(act_fn(gate) * up)`).
+ *   PARO_PROLOGUE_ADD_RMSNORM: x bf16 [M, K]; residual_in bf16 [M, K] or
+ *     NULL; residual_out bf16 [M, K] receives bf16(x + residual_in) (x when
+ *     NULL) and must not overlap x or residual_in; norm_weight bf16 [K]; the
+ *     linear's input is bf16(w * bf16(s * rsqrt(mean(s^2) + eps))).
+ *   PARO_PROLOGUE_SILU_MUL: x bf16 [M, 2K], gate columns first; the linear's
+ *     input is bf16(bf16(silu(gate)) * up).  residual_* / norm_weight unused.
+ *   PARO_PROLOGUE_NONE: paro_w4a8_linear on bf16 x.
+ * Up to 64 tokens (fp16_round = 1) the step runs inside the rotation kernel
+ * (one kernel fewer per linear; same bits as the separate kernels:
+ * paro_add_rmsnorm / paro_silu_mul, then paro_w4a8_linear); above, the
+ * separate kernel writes into the scratch and the linear follows.  16-byte
+ * aligned bf16 buffers; other arguments as paro_w4a8_linear, with
+ * scratch_bytes >= paro_w4a8_linear_prologue_scratch_size().
+ */
+typedef enum paro_prologue {
+  PARO_PROLOGUE_NONE = 0,
+  PARO_PROLOGUE_ADD_RMSNORM = 1,
+  PARO_PROLOGUE_SILU_MUL = 2
+} paro_prologue;
+
+size_t paro_w4a8_linear_prologue_scratch_size(int prologue, int64_t M, int N, int K, int fp16_round);
+
+int paro_w4a8_linear_prologue(int prologue, const void* x, const void* residual_in, void* residual_out,
+                              const void* norm_weight, float eps, int64_t M, int K, int N,
+                              const uint16_t* channel_scales, const uint32_t* rot_table, int fp16_round,
+                              const void* packed, const void* bias, int bias_dtype,
+                              void* out, int out_dtype, void* workspace, size_t workspace_bytes,
+                              void* scratch, size_t scratch_bytes, paro_stream_t stream);
+
+/*
+ * A group of T (1..4) rotated linears that read the same input, each with
+ * its own rotation: q / k / v after input_layernorm, gate / up after
+ * post_attention_layernorm, as a real checkpoint holds them (the reference
+ * loads them unfused, each its own RotateLinearInt4 with its own tables:
+ * src/alpamayo_r1/utils/quantization/paroquant_marlin_w4a8.py:455-460).
+ * y = [linear_0(x) | linear_1(x) | ...], the fused-projection layout
+ * (patches.py:144-263).
+ *   n_per_table   : host array of T output widths (each a multiple of 16).
+ *   rot_tables    : host array of T device tables from paro_prepare_rotation.
+ *   channel_scales: host array of T device fp16 [K] pointers (entries may be
+ *                   NULL), or NULL.
+ *   packed        : the T layers' tile records concatenated (records are
+ *                   row-block major, so this is their byte concatenation).
+ *   bias          : [sum n] of bias_dtype or NULL;  out : [M, sum n].
+ *   prologue      : as paro_w4a8_linear_prologue (x bf16 for the fused
+ *                   steps; the residual output is written once).
+ * Up to 64 tokens (fp16_round = 1): one rotation kernel and one quantiser
+ * for all T tables (the table index is a grid dimension) and one GEMM over
+ * the concatenated weights, each row block reading its table's activations.
+ * Otherwise one paro_w4a8_linear per table into the scratch, copied into its
+ * columns of out.  Workspace (zero-filled, left so) and scratch as sized.
+ */
+size_t paro_w4a8_linear_group_workspace_size(int64_t M, int T, const int* n_per_table, int K);
+size_t paro_w4a8_linear_group_scratch_size(int prologue, int64_t M, int T, const int* n_per_table, int K,
+                                           int fp16_round);
+int paro_w4a8_linear_group(int prologue, const void* x, int x_dtype, const void* residual_in, void* residual_out,
+                           const void* norm_weight, float eps, int64_t M, int K, int T, const int* n_per_table,
+                           const uint16_t* const* channel_scales, const uint32_t* const* rot_tables,
+                           int fp16_round, const void* packed, const void* bias, int bias_dtype,
+                           void* out, int out_dtype, void* workspace, size_t workspace_bytes,
+                           void* scratch, size_t scratch_bytes, paro_stream_t stream);
+
 /* Which GEMM kernel paro_w4a8_gemm would launch for this shape
  * (0 = streaming decode kernel, 1 = tcgen05 tensor-core kernel). */
 int paro_w4a8_gemm_path(int64_t M, int N, int K);
