@@ -51,6 +51,10 @@ cudaError_t launch_selftest_wait(long long limit_cycles, cudaStream_t st);
 cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
                            const void* bias, int bias_dtype, void* out, int out_dtype, void* ws, size_t ws_bytes,
                            cudaStream_t st);
+cudaError_t launch_gemm_tc_sets(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
+                                const void* bias, int bias_dtype, void* out, int out_dtype, void* workspace,
+                                size_t workspace_bytes, int T, const int* tab_nb, cudaStream_t st);
+int gemm_tc_sets_ok(int T, const int* tab_nb);
 }  // namespace paro
 
 #include <map>
@@ -410,6 +414,7 @@ size_t paro_w4a8_linear_group_workspace_size(int64_t M, int T, const int* n_per_
   int nt = 0, nb[kMaxTables];
   if (M <= 0 || group_check(T, n_per_table, K, &nt, nb)) return 0;
   size_t ws = M <= kLinearFusedMaxM ? linear_decode_workspace(M, nt, K, T) : 0;
+  if (gemm_tc_supported(M, nt, K)) ws = std::max(ws, gemm_tc_workspace(M, nt, K));
   for (int t = 0; t < T; ++t) ws = std::max(ws, paro_w4a8_linear_workspace_size(M, n_per_table[t], K));
   return ws;
 }
@@ -426,6 +431,10 @@ size_t paro_w4a8_linear_group_scratch_size(int prologue, int64_t M, int T, const
   for (int t = 0; t < T; ++t)
     per = std::max(per, al256((size_t)M * n_per_table[t] * 4) +
                             paro_w4a8_linear_scratch_size(M, n_per_table[t], K, fp16_round));
+  // prefill route with every table on a 256-row tile: T activation sets,
+  // then one tensor-core GEMM
+  const size_t sets = al256((size_t)T * M * K) + al256((size_t)T * M * 4) + paro_rotq_int8_workspace_size(M, K, fp16_round);
+  per = std::max(per, sets);
   per += prologue == PARO_PROLOGUE_NONE ? 0 : al256((size_t)M * K * 2);
   return std::max(sc, per);
 }
@@ -503,6 +512,23 @@ int paro_w4a8_linear_group(int prologue, const void* x, int x_dtype, const void*
     xin = sp;
     xdt = PARO_BF16;
     sp += al256(row_bytes);
+  }
+  if (gemm_tc_supported(M, N, K) && gemm_tc_sets_ok(T, nb) && aligned(out, 16)) {
+    // every table starts on a 256-row tile: one activation set per table,
+    // then one tensor-core GEMM over the concatenated weights
+    int8_t* xq = reinterpret_cast<int8_t*>(sp);
+    float* xs = reinterpret_cast<float*>(sp + al256((size_t)T * M * K));
+    uint8_t* aws = sp + al256((size_t)T * M * K) + al256((size_t)T * M * 4);
+    const size_t awb = paro_rotq_int8_workspace_size(M, K, fp16_round);
+    for (int t = 0; t < T; ++t) {
+      const int rc = paro_rotq_int8_ws(xin, xdt, M, K, channel_scales ? channel_scales[t] : nullptr, rot_tables[t], 8,
+                                       kGroup, fp16_round, xq + (size_t)t * M * K, xs + (size_t)t * M,
+                                       awb ? aws : nullptr, awb, stream);
+      if (rc != PARO_OK) return rc;
+    }
+    const size_t tcb = gemm_tc_workspace(M, N, K);
+    return cuda_status(launch_gemm_tc_sets(xq, xs, M, N, K, packed, bias, bias_dtype, out, out_dtype,
+                                           tcb ? workspace : nullptr, tcb, T, nb, st));
   }
   const size_t rec_bytes_per_nb = (size_t)(K / kGroup) * kRecBytes;
   const size_t oe = elem_bytes(out_dtype);

@@ -799,6 +799,10 @@ size_t gemm_tc_workspace(int64_t M, int N, int K);
 cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
                            const void* bias, int bias_dtype, void* out, int out_dtype, void* workspace,
                            size_t workspace_bytes, cudaStream_t st);
+cudaError_t launch_gemm_tc_sets(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
+                                const void* bias, int bias_dtype, void* out, int out_dtype, void* workspace,
+                                size_t workspace_bytes, int T, const int* tab_nb, cudaStream_t st);
+int gemm_tc_sets_ok(int T, const int* tab_nb);
 
 // Linears of 25-64 tokens whose GEMM is faster on the tensor cores (256-token
 // tiles, split-K over the CTA pairs): the layers gemm_tc_supported already
@@ -814,7 +818,7 @@ int linear_decode_tc(int64_t M, int N, int K) {
 // Workspace of the decode linear for T rotation tables (the GEMM's, then
 // the row maxima of the T activation sets).
 size_t linear_decode_workspace(int64_t M, int N, int K, int T) {
-  const size_t tc = T == 1 && linear_decode_tc(M, N, K) ? gemm_tc_workspace(M, N, K) : 0;
+  const size_t tc = linear_decode_tc(M, N, K) ? gemm_tc_workspace(M, N, K) : 0;
   const size_t dec = gemm_decode_workspace(M, N);
   return (tc > dec ? tc : dec) + (((size_t)T * M * sizeof(uint32_t) + 255) & ~(size_t)255);
 }
@@ -863,8 +867,10 @@ static cudaError_t launch_pick_preq(DecParams p, cudaStream_t st) {
 // tokens; callers then run the two-kernel path.  T rotation tables (a group
 // of linears sharing x, weights concatenated along N): tabs.rtab / cs[t]
 // apply to row blocks [tab_nb[t], tab_nb[t + 1]) (tab_nb[0] = 0); with
-// T > 1 the GEMM is the streaming kernel reading each set's fragments from
-// L2.
+// T > 1 the GEMM is the tensor-core kernel where the combined shape takes
+// it and every table starts on a 256-row tile (each tile loads its table's
+// activation set), otherwise the streaming kernel reading each set's
+// fragments from L2.
 cudaError_t launch_linear_decode_tables(const void* x, int x_dtype, const RotTables& tabs, int T, const int* tab_nb,
                                         int64_t M, int N, int K, const void* packed, const void* bias, int bias_dtype,
                                         void* out, int out_dtype, void* ws, void* scratch, int pro_kind,
@@ -872,8 +878,10 @@ cudaError_t launch_linear_decode_tables(const void* x, int x_dtype, const RotTab
   if (M > kDecMaxTokens || M <= 0) return cudaErrorNotSupported;
   if (T < 1 || T > kMaxTables) return cudaErrorInvalidValue;
   DecParams p = dec_params(M, N, K, packed, bias, bias_dtype, out, out_dtype, ws);
-  // (the tensor-core GEMM's row stores want a 16-byte aligned output)
-  const bool tc = T == 1 && linear_decode_tc(M, N, K) && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+  // (the tensor-core GEMM's row stores want a 16-byte aligned output; with
+  // several tables, each table must start on one of its 256-row tiles)
+  const bool tc = linear_decode_tc(M, N, K) && (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
+                  gemm_tc_sets_ok(T, tab_nb);
   const size_t tcb = tc ? gemm_tc_workspace(M, N, K) : 0;
   const size_t decb = gemm_decode_workspace(M, N);
   uint8_t* tail = static_cast<uint8_t*>(ws) + (tcb > decb ? tcb : decb);
@@ -893,9 +901,10 @@ cudaError_t launch_linear_decode_tables(const void* x, int x_dtype, const RotTab
   if (tc) {
     // the tensor-core GEMM does not read the row maxima: clear them here
     // (behind the quantiser on the stream)
-    e = cudaMemsetAsync(p.amax, 0, (size_t)M * sizeof(uint32_t), st);
+    e = cudaMemsetAsync(p.amax, 0, (size_t)T * M * sizeof(uint32_t), st);
     if (e != cudaSuccess) return e;
-    return launch_gemm_tc(xq, xs, M, N, K, packed, bias, bias_dtype, out, out_dtype, tcb ? ws : nullptr, tcb, st);
+    return launch_gemm_tc_sets(xq, xs, M, N, K, packed, bias, bias_dtype, out, out_dtype, tcb ? ws : nullptr, tcb, T,
+                               tab_nb, st);
   }
   if (T == 1 && rows_kernel_enabled()) {
     e = launch_gemm_rows(xq, xs, M, N, K, packed, bias, bias_dtype, out, out_dtype, ws, p.amax, gsum, Mp, st);

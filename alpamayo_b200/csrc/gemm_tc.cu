@@ -80,7 +80,21 @@ struct TcParams {
   int out_dtype;
   unsigned long long* ws;  // splits > 1: [M][N] int64 fixed-point (2^-28) partial sums, zero between calls
   uint32_t* cnt;        // splits > 1: [tiles][2 CTAs][8 epilogue warps] counters, zero between calls
+  // activation sets (one per rotation table of a projection group, weights
+  // concatenated along N): the activations are [tables][M][K], the token
+  // scales [tables][M]; rows from 16 * tab_nb[t] on use set t, and every
+  // table starts on a 256-row tile
+  int tables;
+  int tab_nb[kMaxTables];
 };
+
+// The activation set of the 256-row tile starting at output row n.
+__device__ __forceinline__ int tc_set(const TcParams& p, int n) {
+  int t = 0;
+#pragma unroll
+  for (int i = 1; i < kMaxTables; ++i) t += (i < p.tables && n >= p.tab_nb[i] * kRecRows) ? 1 : 0;
+  return t;
+}
 
 
 // instruction descriptor: s32 accumulate, A s8, B s8, both K-major,
@@ -264,6 +278,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
         item_groups(w, gb, ge);
         const int n0 = tile_n0(t);
         const int ty = (int)(tile_m0(t) + rank * kTcTokHalf);
+        const int xset = tc_set(p, (t % p.tiles_n) * (2 * kTcRows));
         for (int g = gb; g < ge; ++g, ++it) {
           const uint32_t s = it % kTcStages;
           if (it >= kTcStages && !mbar_wait(&freed[s], ((it / kTcStages) - 1) & 1)) {
@@ -273,7 +288,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
           // a box always delivers all its bytes (rows past the layer's end
           // read as zeros)
           mbar_arrive_expect_tx(&full[s], (uint32_t)(kTcXBytes + kTcRecs * kRecBytes));
-          tma_load_2d(smem + kOffX + s * kTcXBytes, &xmap, g * kGroup, ty, &full[s]);
+          tma_load_3d(smem + kOffX + s * kTcXBytes, &xmap, g * kGroup, ty, xset, &full[s]);
           tma_load_3d(smem + kOffW + s * kTcWBytes, &wmap, 0, g, n0 / kRecRows, &full[s]);
         }
       }
@@ -433,7 +448,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const int64_t m = m0 + col0 + lane * 4 + q;
-        xs[lane * 4 + q] = m < p.M ? __ldg(p.xscale + m) : 0.f;
+        xs[lane * 4 + q] = m < p.M ? __ldg(p.xscale + tc_set(p, (tile % p.tiles_n) * (2 * kTcRows)) * p.M + m) : 0.f;
       }
       __syncwarp();
       const int n = n0 + row;
@@ -560,20 +575,30 @@ size_t gemm_tc_workspace(int64_t M, int N, int K) {
   return al256_tc((size_t)M * N * sizeof(unsigned long long)) + (size_t)tc_tiles(M, N) * 16 * sizeof(uint32_t);
 }
 
+// Whether T activation sets with these row-block starts can share one
+// launch: every table starts on a 256-row tile.
+int gemm_tc_sets_ok(int T, const int* tab_nb) {
+  if (T < 1 || T > kMaxTables || tab_nb[0] != 0) return 0;
+  for (int t = 1; t < T; ++t)
+    if ((tab_nb[t] * kRecRows) % (2 * kTcRows) || tab_nb[t] <= tab_nb[t - 1]) return 0;
+  return 1;
+}
+
 // workspace: gemm_tc_workspace(M, N, K) bytes, zero-filled and left so, or
-// NULL (then no split-K).
-cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
-                           const void* bias, int bias_dtype, void* out, int out_dtype, void* workspace,
-                           size_t workspace_bytes, cudaStream_t st) {
+// NULL (then no split-K).  T activation sets: xq is [T][M][K], xscale
+// [T][M], rows from 16 * tab_nb[t] on read set t (gemm_tc_sets_ok).
+cudaError_t launch_gemm_tc_sets(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
+                                const void* bias, int bias_dtype, void* out, int out_dtype, void* workspace,
+                                size_t workspace_bytes, int T, const int* tab_nb, cudaStream_t st) {
   auto encode = get_encode();
   if (!encode) return cudaErrorNotSupported;
-  if (M > 0x7FFFFFFF) return cudaErrorInvalidValue;
+  if (M > 0x7FFFFFFF || !gemm_tc_sets_ok(T, tab_nb)) return cudaErrorInvalidValue;
   CUtensorMap xmap;
-  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
-  const cuuint64_t strides[1] = {(cuuint64_t)K};
-  const cuuint32_t box[2] = {(cuuint32_t)kGroup, (cuuint32_t)kTcTokHalf};
-  const cuuint32_t estr[2] = {1, 1};
-  CUresult r = encode(&xmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(xq), dims, strides, box, estr,
+  const cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)M, (cuuint64_t)T};
+  const cuuint64_t strides[2] = {(cuuint64_t)K, (cuuint64_t)M * K};
+  const cuuint32_t box[3] = {(cuuint32_t)kGroup, (cuuint32_t)kTcTokHalf, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode(&xmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t*>(xq), dims, strides, box, estr,
                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
@@ -602,6 +627,8 @@ cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int
   p.ws = nullptr;
   p.cnt = nullptr;
   p.splits = 1;
+  p.tables = T;
+  for (int t = 0; t < kMaxTables; ++t) p.tab_nb[t] = t < T ? tab_nb[t] : 0;
   const size_t wsb = gemm_tc_workspace(M, N, K);
   if (wsb && workspace && workspace_bytes >= wsb) {
     p.splits = tc_splits(M, N, K);
@@ -632,6 +659,14 @@ cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, gemm_tc_kernel, xmap, wmap, p);
+}
+
+cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
+                           const void* bias, int bias_dtype, void* out, int out_dtype, void* workspace,
+                           size_t workspace_bytes, cudaStream_t st) {
+  const int nb0 = 0;
+  return launch_gemm_tc_sets(xq, xscale, M, N, K, packed, bias, bias_dtype, out, out_dtype, workspace, workspace_bytes,
+                             1, &nb0, st);
 }
 
 }  // namespace paro
