@@ -66,6 +66,8 @@ def capi() -> ctypes.CDLL:
         "paro_w4a8_gemm_workspace_size": (sz, [i64, i32, i32]),
         "paro_w4a8_gemm": (i32, [vp, vp, i64, i32, i32, vp, vp, i32, vp, i32, vp, sz, vp]),
         "paro_w4a8_gemm_path": (i32, [i64, i32, i32]),
+        "paro_w4a8_gemm_route_workspace_size": (sz, [i32, i64, i32, i32]),
+        "paro_w4a8_gemm_route": (i32, [i32, vp, vp, i64, i32, i32, vp, vp, i32, vp, i32, vp, sz, vp]),
         "paro_w4a8_linear_workspace_size": (sz, [i64, i32, i32]),
         "paro_w4a8_linear_scratch_size": (sz, [i64, i32, i32, i32]),
         "paro_w4a8_linear": (i32, [vp, i32, i64, i32, i32, vp, vp, i32, vp, vp, i32, vp, i32, vp, sz, vp, sz, vp]),

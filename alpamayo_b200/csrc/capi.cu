@@ -47,6 +47,10 @@ cudaError_t launch_linear_decode(const void* x, int x_dtype, const uint16_t* csc
                                  cudaStream_t st);
 int gemm_tc_supported(int64_t M, int N, int K);
 size_t gemm_tc_workspace(int64_t M, int N, int K);
+size_t gemm_tc_workspace_tile(int64_t M, int N, int K, int bt);
+cudaError_t launch_gemm_tc_tile(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
+                                const void* bias, int bias_dtype, void* out, int out_dtype, void* workspace,
+                                size_t workspace_bytes, int T, const int* tab_nb, int bt, cudaStream_t st);
 cudaError_t launch_selftest_wait(long long limit_cycles, cudaStream_t st);
 cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
                            const void* bias, int bias_dtype, void* out, int out_dtype, void* ws, size_t ws_bytes,
@@ -608,6 +612,51 @@ int paro_w4a8_gemm(const int8_t* xq, const float* xscale, int64_t M, int N, int 
   if (!aligned(workspace, 256)) return PARO_ERR_MISALIGNED;
   return cuda_status(launch_gemm_decode(xq, xscale, M, N, K, packed, bias, bias_dtype, out, out_dtype, workspace,
                                         (cudaStream_t)stream));
+}
+
+// tokens the streaming decode kernel is built and tuned for
+constexpr int64_t kStreamMaxTokens = 64;
+
+size_t paro_w4a8_gemm_route_workspace_size(int route, int64_t M, int N, int K) {
+  if (M <= 0 || N <= 0 || K <= 0 || N % kRecRows || K % kGroup) return 0;
+  switch (route) {
+    case PARO_ROUTE_AUTO: return paro_w4a8_gemm_workspace_size(M, N, K);
+    case PARO_ROUTE_STREAM: return M <= kStreamMaxTokens ? gemm_decode_workspace(M, N) : 0;
+    case PARO_ROUTE_TC256: return gemm_tc_workspace_tile(M, N, K, 256);
+    case PARO_ROUTE_TC64: return gemm_tc_workspace_tile(M, N, K, 64);
+  }
+  return 0;
+}
+
+int paro_w4a8_gemm_route(int route, const int8_t* xq, const float* xscale, int64_t M, int N, int K,
+                         const void* packed, const void* bias, int bias_dtype, void* out, int out_dtype,
+                         void* workspace, size_t workspace_bytes, paro_stream_t stream) {
+  if (route == PARO_ROUTE_AUTO)
+    return paro_w4a8_gemm(xq, xscale, M, N, K, packed, bias, bias_dtype, out, out_dtype, workspace,
+                          workspace_bytes, stream);
+  if (route != PARO_ROUTE_STREAM && route != PARO_ROUTE_TC256 && route != PARO_ROUTE_TC64)
+    return PARO_ERR_INVALID_ARGUMENT;
+  if (M == 0 && N > 0 && K > 0) return PARO_OK;
+  if (!xq || !xscale || !packed || !out || M < 0 || N <= 0 || K <= 0) return PARO_ERR_INVALID_ARGUMENT;
+  if (!valid_dtype(out_dtype) || (bias && !valid_dtype(bias_dtype))) return PARO_ERR_UNSUPPORTED;
+  if (N % kRecRows || K % kGroup) return PARO_ERR_SHAPE;
+  if (!aligned(packed, 16) || !aligned(xq, 16)) return PARO_ERR_MISALIGNED;
+  if (int d = device_check()) return d;
+  if (route == PARO_ROUTE_STREAM) {
+    if (M > kStreamMaxTokens) return PARO_ERR_TOO_LARGE;
+    const size_t need = gemm_decode_workspace(M, N);
+    if (!workspace || workspace_bytes < need) return PARO_ERR_WORKSPACE;
+    if (!aligned(workspace, 256)) return PARO_ERR_MISALIGNED;
+    return cuda_status(launch_gemm_decode(xq, xscale, M, N, K, packed, bias, bias_dtype, out, out_dtype, workspace,
+                                          (cudaStream_t)stream));
+  }
+  const int bt = route == PARO_ROUTE_TC64 ? 64 : 256;
+  if (!aligned(out, 16)) return PARO_ERR_MISALIGNED;
+  const size_t need = gemm_tc_workspace_tile(M, N, K, bt);
+  if (workspace_bytes < need || (need && !workspace)) return PARO_ERR_WORKSPACE;
+  const int nb0 = 0;
+  return cuda_status(launch_gemm_tc_tile(xq, xscale, M, N, K, packed, bias, bias_dtype, out, out_dtype, workspace,
+                                         workspace_bytes, 1, &nb0, bt, (cudaStream_t)stream));
 }
 
 }  // extern "C"

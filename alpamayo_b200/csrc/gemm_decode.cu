@@ -804,15 +804,14 @@ cudaError_t launch_gemm_tc_sets(const int8_t* xq, const float* xscale, int64_t M
                                 size_t workspace_bytes, int T, const int* tab_nb, cudaStream_t st);
 int gemm_tc_sets_ok(int T, const int* tab_nb);
 
-// Linears of 25-64 tokens whose GEMM is faster on the tensor cores (256-token
-// tiles, split-K over the CTA pairs): the layers gemm_tc_supported already
-// sends there (gate_up), and, from 33 tokens, long rows (K >= 8192: down,
-// where the streaming kernel is bound by its mma.sync rate: 72 us against
-// 41 us for the GEMM at 64 tokens, measured on B200).  Their rows still take
-// this file's rotation + quantiser chain, in channel order.
+// Linears of up to 64 tokens whose GEMM is faster on the tensor cores
+// (64-token tiles, split-K over the CTA pairs): from 13 tokens on long rows
+// (down), 17 on gate_up-wide layers, 24 on the rest (gemm_tc_supported's
+// measured crossovers).  Their rows still take this file's rotation +
+// quantiser chain, in channel order.
 int linear_decode_tc(int64_t M, int N, int K) {
   if (M > kDecMaxTokens || N % kRecRows || K % kGroup) return 0;
-  return (M > 24 && gemm_tc_supported(M, N, K)) || (M > 32 && K / kGroup >= 64);
+  return gemm_tc_supported(M, N, K);
 }
 
 // Workspace of the decode linear for T rotation tables (the GEMM's, then

@@ -4,19 +4,20 @@
 // y[m, n] = xscale[m] * sum_g s[g, n] * sum_{k in g} (q[n, k] - z[g, n]) x[m, k] (+ bias[n])
 //
 // Persistent grid of CTA pairs (clusters of two): pair P walks the tiles
-// P, P + pairs, ... of the (N / 256) x (M / 256) tile grid, so one tile's
+// P, P + pairs, ... of the (N / 256) x (M / BT) tile grid, so one tile's
 // final stores overlap the next tile's loads and MMAs.  A pair computes a
-// 256 (output rows n) x 256 (tokens m) tile of y^T with cta_group::2 MMAs (M = 256,
-// N = 256, K = 32): each CTA holds 128 weight rows (half of the MMA's A
-// operand) and 128 tokens (half of its B operand) in shared memory, and its
-// tensor memory holds the int32 sums of its own 128 rows for all 256 tokens.
+// 256 (output rows n) x BT (tokens m) tile of y^T with cta_group::2 MMAs
+// (M = 256, N = BT, K = 32); BT is 256 for prefill and 64 for 17-128 tokens
+// (TcTile).  Each CTA holds 128 weight rows (half of the MMA's A operand)
+// and BT / 2 tokens (half of its B operand) in shared memory, and its tensor
+// memory holds the int32 sums of its own 128 rows for all BT tokens.
 // The weights are the MMA's M operand and the tokens its N operand, so a TMEM
 // lane is one output row and each epilogue thread owns one row (its group
 // scale is one scalar per group).  K is walked one 128-channel group per
-// pipeline stage (6 stages):
+// pipeline stage (6 stages for BT = 256, 8 for BT = 64):
 //
 //  * warp 0 (producer, each CTA): per group, one tensor TMA of the CTA's
-//    activation half (128 tokens x 128 int8 channels, 128-byte swizzle =
+//    activation half (BT / 2 tokens x 128 int8 channels, 128-byte swizzle =
 //    the UMMA K-major canonical layout) and one 3-D tensor TMA of its 8
 //    weight records (16 rows x 128 channels each; the packed buffer viewed
 //    as [N/16][G][1072 bytes]), which land in the stage's weight area.
@@ -27,7 +28,8 @@
 //    the leader CTA's "stage ready" barrier.
 //  * warp 1 of the leader CTA (MMA): once both CTAs' stage is ready and the
 //    accumulator buffer has been drained by both epilogues, issues 4 MMAs
-//    into one of two 256-column TMEM buffers (the first overwriting it) and
+//    into one of 2 (BT = 256) or 4 (BT = 64) BT-column TMEM buffers (the
+//    first overwriting it) and
 //    commits completion to the stage-free and accumulator-full barriers of
 //    both CTAs (tcgen05.commit multicast).
 //  * warpgroups 2-3 (epilogue, each CTA): fold each finished group into
@@ -37,8 +39,8 @@
 //    scale; then each warp arrives on the leader's "buffer drained" barrier.
 //    After the last group: token scale, bias, convert, store.
 //
-// Per SM and group this moves 24.5 KB from L2 (16 KB activations + 8.5 KB
-// records) for 128 x 256 x 128 MACs.  No load uses cluster multicast.  All
+// Per SM and group this moves 8.5 KB of records + BT / 2 x 128 bytes of
+// activations from L2 for 128 x BT x 128 MACs.  No load uses cluster multicast.  All
 // mbarrier waits are bounded (report kErrMbarTimeout and drop out), and the
 // tensor memory is freed on every path out of the kernel, after both CTAs
 // have stopped using it.
@@ -49,22 +51,42 @@ namespace paro {
 PARO_DEFINE_ERROR_ACCESSOR(tc)
 
 constexpr int kTcRows = 128;                              // output rows per CTA (half the MMA's M)
-constexpr int kTcTok = 256;                               // tokens per tile (MMA N)
-constexpr int kTcTokHalf = kTcTok / 2;                    // tokens staged per CTA
-constexpr int kTcStages = 6;
 constexpr int kTcThreads = 512;
 constexpr int kTcRecs = kTcRows / kRecRows;               // 8 records per group
 constexpr int kTcWBytes = kTcRows * kGroup;               // 16 KB expanded weights
-constexpr int kTcXBytes = kTcTokHalf * kGroup;            // 16 KB activations
 static_assert(kTcRecs * kRecBytes <= kTcWBytes, "records land in the expanded-weight area");
 
-// shared memory plan (offsets from a 1024-byte aligned base; identical in
-// both CTAs, which the pair MMA's descriptors rely on)
-constexpr int kOffW = 0;
-constexpr int kOffX = kOffW + kTcStages * kTcWBytes;
-constexpr int kOffXs = kOffX + kTcStages * kTcXBytes;                // [8 warps][128] float token scales
-constexpr int kOffBar = kOffXs + 8 * 128 * 4;
-constexpr int kTcSmem = kOffBar + 256 + 1024;                         // + alignment slack
+// Tile shapes: BT tokens per tile (the MMA's N), 256 for prefill and 64 for
+// 17-128 tokens, where a 256-token tile would spend most of every MMA and
+// of the epilogue's per-group fold on padding.
+template <int BT>
+struct TcTile {
+  static_assert(BT == 256 || BT == 64, "tile tokens");
+  static constexpr int kTok = BT;                        // tokens per tile (MMA N)
+  static constexpr int kTokHalf = BT / 2;                // tokens staged per CTA
+#ifndef PARO_TC64_STAGES
+#define PARO_TC64_STAGES 8
+#endif
+  static constexpr int kStages = BT == 256 ? 6 : PARO_TC64_STAGES;
+  static constexpr int kBufs = BT == 256 ? 2 : 4;        // TMEM accumulators in flight
+  static constexpr int kTmemCols = kBufs * BT;           // 512 or 256 (a power of two)
+  static constexpr int kXBytes = kTokHalf * kGroup;      // 16 KB or 4 KB activations per stage
+  static constexpr int kCols = kTokHalf;                 // token columns per epilogue thread
+  static constexpr int kPairs = kCols / 2;               // packed f32x2 accumulators per thread
+  // shared memory plan (offsets from a 1024-byte aligned base; identical in
+  // both CTAs, which the pair MMA's descriptors rely on)
+  static constexpr int kOffW = 0;
+  static constexpr int kOffX = kOffW + kStages * kTcWBytes;
+  static constexpr int kOffXs = kOffX + kStages * kXBytes;   // [8 warps][kTokHalf] float token scales
+  static constexpr int kOffBar = kOffXs + 8 * kTokHalf * 4;
+  static constexpr int kSmem = kOffBar + 512 + 1024;         // barriers + alignment slack
+  // instruction descriptor: s32 accumulate, A s8, B s8, both K-major,
+  // N = BT, M = 256 (the CTA pair)
+  static constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BT >> 3) << 17) |
+                                     ((uint32_t)((2 * kTcRows) >> 4) << 24);
+  static_assert((3 * kStages + 2 * kBufs + 1) * 8 + 4 <= 512, "barrier area");
+  static_assert(kXBytes % 1024 == 0, "128-byte swizzle atoms stay 1024-byte aligned");
+};
 
 struct TcParams {
   const float* xscale;
@@ -97,16 +119,12 @@ __device__ __forceinline__ int tc_set(const TcParams& p, int n) {
 }
 
 
-// instruction descriptor: s32 accumulate, A s8, B s8, both K-major,
-// N = 256, M = 256 (the CTA pair)
-constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTcTok >> 3) << 17) |
-                            ((uint32_t)((2 * kTcRows) >> 4) << 24);
-
-__device__ __forceinline__ void mma_i8_pair(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+__device__ __forceinline__ void mma_i8_pair(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
+                                            uint32_t accumulate) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
       " tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
-      "l"(da), "l"(db), "r"(kIdesc), "r"(accumulate)
+      "l"(da), "l"(db), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -199,13 +217,13 @@ __device__ __forceinline__ float tc_bias(const void* bias, int dtype, int n) {
   return static_cast<const float*>(bias)[n];
 }
 
-// Stores one output row's `valid` (<= 128) tokens: out[j * N] = y_j * xs[j] + bias,
+// Stores one output row's `valid` (<= 2 NP) tokens: out[j * N] = y_j * xs[j] + bias,
 // with the token scales xs staged in shared memory.
-template <typename T>
-__device__ __forceinline__ void store_row(const uint64_t (&y)[64], T* __restrict__ out, int N,
+template <typename T, int NP>
+__device__ __forceinline__ void store_row(const uint64_t (&y)[NP], T* __restrict__ out, int N,
                                           const float* __restrict__ xs, float bias, int valid) {
 #pragma unroll
-  for (int j = 0; j < 64; ++j) {
+  for (int j = 0; j < NP; ++j) {
     if (2 * j < valid) {
       const float2 f = unpack2(y[j]);
       const float2 a = *reinterpret_cast<const float2*>(xs + 2 * j);
@@ -215,16 +233,19 @@ __device__ __forceinline__ void store_row(const uint64_t (&y)[64], T* __restrict
   }
 }
 
+template <int BT>
 __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap xmap,
                                                                 const __grid_constant__ CUtensorMap wmap, TcParams p) {
+  using C = TcTile<BT>;
+  constexpr int kStages = C::kStages, kBufs = C::kBufs, kTokHalf = C::kTokHalf;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBar);        // [6] this CTA's loads landed
-  uint64_t* ready = full + kTcStages;                                   // [6] leader: both CTAs' stage expanded
-  uint64_t* freed = ready + kTcStages;                                  // [6] MMAs done with the stage
-  uint64_t* acc_full = freed + kTcStages;                               // [2] group's MMAs complete
-  uint64_t* acc_empty = acc_full + 2;                                   // [2] leader: both epilogues drained
-  uint64_t* mma_done = acc_empty + 2;                                   // [1] leader: every MMA complete
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kOffBar);     // [stages] this CTA's loads landed
+  uint64_t* ready = full + kStages;                                     // [stages] leader: both CTAs' stage expanded
+  uint64_t* freed = ready + kStages;                                    // [stages] MMAs done with the stage
+  uint64_t* acc_full = freed + kStages;                                 // [bufs] group's MMAs complete
+  uint64_t* acc_empty = acc_full + kBufs;                               // [bufs] leader: both epilogues drained
+  uint64_t* mma_done = acc_empty + kBufs;                               // [1] leader: every MMA complete
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -235,7 +256,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
   // tile t: output rows (t % tiles_n) * 256 + rank * 128 .. (this CTA's
   // half), tokens (t / tiles_n) * 256 ..
   auto tile_n0 = [&](int t) { return (t % p.tiles_n) * (2 * kTcRows) + (int)rank * kTcRows; };
-  auto tile_m0 = [&](int t) { return (int64_t)(t / p.tiles_n) * kTcTok; };
+  auto tile_m0 = [&](int t) { return (int64_t)(t / p.tiles_n) * BT; };
   auto tile_nrec = [&](int n0) { return max(0, min(kTcRecs, (p.N - n0) / kRecRows)); };
   // work item w: tile w / splits, groups [gb, ge) of its K split
   auto item_groups = [&](int w, int& gb, int& ge) {
@@ -244,12 +265,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
   };
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kTcStages; ++s) {
+    for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&ready[s], 8);      // 4 expansion warps x 2 CTAs
       mbar_init(&freed[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kBufs; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 16); // 8 epilogue warps x 2 CTAs
     }
@@ -257,7 +278,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     fence_mbar_init();
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot))
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "n"(C::kTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
   }
@@ -277,24 +299,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
         int gb, ge;
         item_groups(w, gb, ge);
         const int n0 = tile_n0(t);
-        const int ty = (int)(tile_m0(t) + rank * kTcTokHalf);
+        const int ty = (int)(tile_m0(t) + rank * kTokHalf);
         const int xset = tc_set(p, (t % p.tiles_n) * (2 * kTcRows));
         for (int g = gb; g < ge; ++g, ++it) {
-          const uint32_t s = it % kTcStages;
-          if (it >= kTcStages && !mbar_wait(&freed[s], ((it / kTcStages) - 1) & 1)) {
+          const uint32_t s = it % kStages;
+          if (it >= kStages && !mbar_wait(&freed[s], ((it / kStages) - 1) & 1)) {
             failed = true;
             break;
           }
           // a box always delivers all its bytes (rows past the layer's end
           // read as zeros)
-          mbar_arrive_expect_tx(&full[s], (uint32_t)(kTcXBytes + kTcRecs * kRecBytes));
-          tma_load_3d(smem + kOffX + s * kTcXBytes, &xmap, g * kGroup, ty, xset, &full[s]);
-          tma_load_3d(smem + kOffW + s * kTcWBytes, &wmap, 0, g, n0 / kRecRows, &full[s]);
+          mbar_arrive_expect_tx(&full[s], (uint32_t)(C::kXBytes + kTcRecs * kRecBytes));
+          tma_load_3d(smem + C::kOffX + s * C::kXBytes, &xmap, g * kGroup, ty, xset, &full[s]);
+          tma_load_3d(smem + C::kOffW + s * kTcWBytes, &wmap, 0, g, n0 / kRecRows, &full[s]);
         }
       }
     } else if (warp == 1 && lane == 0 && leader) {
       // MMA issuer (leader CTA only)
-      const uint32_t w_base = smem_u32(smem + kOffW), x_base = smem_u32(smem + kOffX);
+      const uint32_t w_base = smem_u32(smem + C::kOffW), x_base = smem_u32(smem + C::kOffX);
       uint32_t total = 0;
       for (int w = pair; w < p.items; w += pairs) {
         int gb, ge;
@@ -302,16 +324,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
         total += (uint32_t)(ge - gb);
       }
       for (uint32_t it = 0; it < total && !failed; ++it) {
-        const uint32_t s = it % kTcStages, b = it & 1;
-        if (!mbar_wait_cluster(&ready[s], (it / kTcStages) & 1) || !mbar_wait_cluster(&acc_empty[b], (it >> 1) & 1)) {
+        const uint32_t s = it % kStages, b = it % kBufs;
+        if (!mbar_wait_cluster(&ready[s], (it / kStages) & 1) || !mbar_wait_cluster(&acc_empty[b], (it / kBufs) & 1)) {
           failed = true;
           break;
         }
         tc_fence_after();
         const uint64_t da = umma_desc_sw128(w_base + s * kTcWBytes);
-        const uint64_t db = umma_desc_sw128(x_base + s * kTcXBytes);
+        const uint64_t db = umma_desc_sw128(x_base + s * C::kXBytes);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) mma_i8_pair(tmem + b * kTcTok, da + 2 * kk, db + 2 * kk, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < 4; ++kk)
+          mma_i8_pair(tmem + b * BT, da + 2 * kk, db + 2 * kk, C::kIdesc, kk > 0 ? 1u : 0u);
         umma_commit_pair(&freed[s]);
         umma_commit_pair(&acc_full[b]);
       }
@@ -331,12 +354,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     int gb, ge;
     item_groups(w, gb, ge);
     for (int g = gb; g < ge; ++g, ++it) {
-      const uint32_t s = it % kTcStages;
-      if (!mbar_wait(&full[s], (it / kTcStages) & 1)) {
+      const uint32_t s = it % kStages;
+      if (!mbar_wait(&full[s], (it / kStages) & 1)) {
         failed = true;
         break;
       }
-      uint8_t* area = smem + kOffW + s * kTcWBytes;
+      uint8_t* area = smem + C::kOffW + s * kTcWBytes;
       uint32_t w[4][4];  // [t][j] code words of row t
       uint32_t zz = 0;
       if (i < nrec) {
@@ -375,15 +398,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 184;");
     // epilogue: warp w reads TMEM lanes 32*(w%4).. (output rows) and token
-    // columns 128*((w-8)/4)..
+    // columns kCols*((w-8)/4)..
+    constexpr int kCols = C::kCols, kNP = C::kPairs, kChunks = kCols / 16;
     const int q4 = warp & 3, half = (warp - 8) >> 2;
     const int row = q4 * 32 + lane;                       // output row within this CTA's half
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
-    const int col0 = half * 128;
-    // both accumulator buffers start free
+    const int col0 = half * kCols;
+    // every accumulator buffer starts free
     if (lane == 0) {
-      mbar_arrive_cluster(&acc_empty[0], 0);
-      mbar_arrive_cluster(&acc_empty[1], 0);
+#pragma unroll
+      for (int b = 0; b < kBufs; ++b) mbar_arrive_cluster(&acc_empty[b], 0);
     }
     uint32_t it = 0;
     for (int w = pair; w < p.items && !failed; w += pairs) {
@@ -402,13 +426,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
         return (row_ok && g < ge) ? ldg_nc_u16(sp + (size_t)g * (kRecBytes / 2)) : 0u;
       };
       uint32_t r0 = fetch_bits(gb), r1 = fetch_bits(gb + 1), r2 = fetch_bits(gb + 2);
-      uint64_t y[64];
+      uint64_t y[kNP];
 #pragma unroll
-      for (int j = 0; j < 64; ++j) y[j] = 0ull;  // (+0.0f, +0.0f)
+      for (int j = 0; j < kNP; ++j) y[j] = 0ull;  // (+0.0f, +0.0f)
       for (int g = gb; g < ge; ++g, ++it) {
-        const uint32_t b = it & 1;
+        const uint32_t b = it % kBufs;
         const uint32_t r_after = fetch_bits(g + 3);
-        if (!mbar_wait(&acc_full[b], (it >> 1) & 1)) {
+        if (!mbar_wait(&acc_full[b], (it / kBufs) & 1)) {
           failed = true;
           break;
         }
@@ -416,22 +440,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
         const float sc = half_bits_to_f32((uint16_t)r0);
         const uint64_t s2 = pack2(sc, sc);
         // chunk c + 1 is read from tensor memory while chunk c is folded
-        const uint32_t tb = tmem + lane_base + b * kTcTok + col0;
+        const uint32_t tb = tmem + lane_base + b * BT + col0;
         uint32_t va[16], vb[16];
         tmem_ld16(tb, va);
         tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 8; c += 2) {
+        for (int c = 0; c < kChunks; c += 2) {
           tmem_ld16(tb + (c + 1) * 16, vb);
 #pragma unroll
           for (int j = 0; j < 8; ++j)
             y[c * 8 + j] = fma2(s2, pack2((float)(int)va[2 * j], (float)(int)va[2 * j + 1]), y[c * 8 + j]);
           tmem_wait_ld();
-          if (c + 2 < 8) tmem_ld16(tb + (c + 2) * 16, va);
+          if (c + 2 < kChunks) tmem_ld16(tb + (c + 2) * 16, va);
 #pragma unroll
           for (int j = 0; j < 8; ++j)
             y[c * 8 + 8 + j] = fma2(s2, pack2((float)(int)vb[2 * j], (float)(int)vb[2 * j + 1]), y[c * 8 + 8 + j]);
-          if (c + 2 < 8) tmem_wait_ld();
+          if (c + 2 < kChunks) tmem_wait_ld();
         }
         tc_fence_before();
         __syncwarp();
@@ -441,19 +465,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
         r2 = r_after;
       }
       // token scale, bias, convert, store: this thread holds output row
-      // n0 + row for tokens m0 + col0 + (0..127); the tensor core is already
-      // on the next tile.  The warp first stages its 128 token scales in its
-      // own slice of shared memory (4 per lane).
-      float* xs = reinterpret_cast<float*>(smem + kOffXs) + (warp - 8) * 128;
+      // n0 + row for tokens m0 + col0 + (0..kCols-1); the tensor core is
+      // already on the next tile.  The warp first stages its token scales in
+      // its own slice of shared memory (kCols / 32 per lane).
+      float* xs = reinterpret_cast<float*>(smem + C::kOffXs) + (warp - 8) * kCols;
+      constexpr int kPerLane = kCols / 32;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int64_t m = m0 + col0 + lane * 4 + q;
-        xs[lane * 4 + q] = m < p.M ? __ldg(p.xscale + tc_set(p, (tile % p.tiles_n) * (2 * kTcRows)) * p.M + m) : 0.f;
+      for (int q = 0; q < kPerLane; ++q) {
+        const int64_t m = m0 + col0 + lane * kPerLane + q;
+        xs[lane * kPerLane + q] =
+            m < p.M ? __ldg(p.xscale + tc_set(p, (tile % p.tiles_n) * (2 * kTcRows)) * p.M + m) : 0.f;
       }
       __syncwarp();
       const int n = n0 + row;
       const int64_t mbase = m0 + col0;
-      const int valid = (int)(p.M - mbase < 128 ? (p.M - mbase > 0 ? p.M - mbase : 0) : 128);
+      const int valid = (int)(p.M - mbase < kCols ? (p.M - mbase > 0 ? p.M - mbase : 0) : kCols);
       if (p.splits == 1) {
         if (!failed && row_ok) {
           const float bn = tc_bias(p.bias, p.bias_dtype, n);
@@ -474,7 +500,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
         unsigned long long* wp = p.ws + (size_t)mbase * p.N + n;
         if (!failed && row_ok) {
 #pragma unroll
-          for (int j = 0; j < 64; ++j) {
+          for (int j = 0; j < kNP; ++j) {
             const float2 f = unpack2(y[j]);
             if (2 * j < valid) red_add_fx(wp + (size_t)(2 * j) * p.N, f.x);
             if (2 * j + 1 < valid) red_add_fx(wp + (size_t)(2 * j + 1) * p.N, f.y);
@@ -521,7 +547,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
   tc_fence_before();
   cluster_sync_all();
   tc_fence_after();
-  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(C::kTmemCols) : "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -541,26 +568,15 @@ static int tc_sms() {
   return g_tc_sms;
 }
 
-// The tensor-core kernel from 65 tokens; from 25 tokens too when the layer
-// alone has enough 256-row tiles to occupy most SMs (gate_up: 148), where the
-// streaming kernel's mma.sync throughput bounds it (measured on B200, the
-// whole gate_up linear: 126 us streaming vs 59 us here at 64 tokens, 61 vs
-// 58 us at 32; at 16 tokens streaming wins, 38 vs 57 us).
-int gemm_tc_supported(int64_t M, int N, int K) {
-  if (N % kRecRows || K % kGroup) return 0;
-  if (M > 64) return 1;
-  return M > 24 && (int64_t)((N + 2 * kTcRows - 1) / (2 * kTcRows)) * 5 >= (int64_t)tc_sms() * 4;
-}
-
-static int tc_tiles(int64_t M, int N) {
-  return (int)(((int64_t)N + 2 * kTcRows - 1) / (2 * kTcRows) * ((M + kTcTok - 1) / kTcTok));
+static int tc_tiles(int64_t M, int N, int bt) {
+  return (int)(((int64_t)N + 2 * kTcRows - 1) / (2 * kTcRows) * ((M + bt - 1) / bt));
 }
 
 // Split-K when the tiles fill fewer than all CTA pairs: each tile's groups
 // are cut into up to pairs / tiles splits of at least 4 groups, so that
 // small layers at mid-size token counts use the whole GPU.
-static int tc_splits(int64_t M, int N, int K) {
-  const int pairs = tc_sms() / 2, tiles = tc_tiles(M, N), G = K / kGroup;
+static int tc_splits(int64_t M, int N, int K, int bt) {
+  const int pairs = tc_sms() / 2, tiles = tc_tiles(M, N, bt), G = K / kGroup;
   if (tiles >= pairs || M > 0x7FFFFFFF) return 1;
   int s = min(pairs / tiles, G / 4);
   if (s <= 1) return 1;
@@ -568,12 +584,64 @@ static int tc_splits(int64_t M, int N, int K) {
   return (G + gper - 1) / gper;
 }
 
+// Tokens from which the tensor-core kernel (64-token tiles) beats the
+// streaming decode kernel, measured per launch in CUDA graphs on B200 with
+// weights beyond L2: long rows (down, K = 18944) from 13 tokens (23.6 us
+// against 29.6 at 16 tokens, 22.2 against 18.6 at 8); layers with at least
+// 0.8 x SMs 256-row tiles (gate_up: 148) from 17 (33.3 against 78.4 us at
+// 24, 32.9 against 26.3 at 16); the rest (qkv, o) from 24 (13.6 against
+// 13.9 us on qkv, 13.0 against 12.9 on o; 15.1 against 27.2 at 64).
+static int tc_min_tokens(int N, int K) {
+  if (K >= 8192) return 13;
+  if ((int64_t)((N + 2 * kTcRows - 1) / (2 * kTcRows)) * 5 >= (int64_t)tc_sms() * 4) return 17;
+  return 24;
+}
+
+int gemm_tc_supported(int64_t M, int N, int K) {
+  if (N % kRecRows || K % kGroup || M <= 0) return 0;
+  return M > 64 || M >= tc_min_tokens(N, K);
+}
+
+// Estimated duration (ns) of the kernel with bt-token tiles: waves of work
+// items over the CTA pairs, each item's groups at a per-group cost, plus the
+// split-K partial sums (64-bit atomic adds into [M][N], then a pass that
+// reads them back).  Fitted to graph-timed launches on B200 (0.55 us per
+// group of a 64-token tile, 1.0 us of a 256-token tile, whose per-group fold
+// of 256 columns bounds it; ~0.75 ns per KB of partial sums); it ranks the
+// two tiles within ~15 % of the measured times for qkv, o, gate_up and down
+// at 96-256 tokens.
+static double tc_estimate_ns(int64_t M, int N, int K, int bt) {
+  const int pairs = tc_sms() / 2, G = K / kGroup;
+  const int splits = tc_splits(M, N, K, bt);
+  const int gper = (G + splits - 1) / splits;
+  const int64_t items = (int64_t)tc_tiles(M, N, bt) * splits;
+  const int64_t waves = (items + pairs - 1) / pairs;
+  double ns = (double)waves * gper * (bt == 64 ? 550.0 : 1000.0);
+  if (splits > 1) ns += (double)M * N * 8.0 * splits * 0.00075;
+  return ns;
+}
+
+// Tokens per tile: 64 up to 64 tokens (a 256-token tile spends most of each
+// MMA and of the per-group fold on padding: gate_up at 64 tokens 34 us
+// against 55), beyond that the tile the estimate prefers (small layers keep
+// 64-token tiles to a few hundred tokens: qkv at 256 tokens 18.9 us against
+// 34.9), and 256 from 2048 tokens.
+int gemm_tc_tile(int64_t M, int N, int K) {
+  if (M <= 64) return 64;
+  if (M >= 2048) return 256;
+  return tc_estimate_ns(M, N, K, 64) < tc_estimate_ns(M, N, K, 256) ? 64 : 256;
+}
+
 static size_t al256_tc(size_t b) { return (b + 255) & ~(size_t)255; }
 
-size_t gemm_tc_workspace(int64_t M, int N, int K) {
-  if (tc_splits(M, N, K) == 1) return 0;
-  return al256_tc((size_t)M * N * sizeof(unsigned long long)) + (size_t)tc_tiles(M, N) * 16 * sizeof(uint32_t);
+// Workspace of the kernel with bt-token tiles (0: the tile gemm_tc_tile picks).
+size_t gemm_tc_workspace_tile(int64_t M, int N, int K, int bt) {
+  if (bt == 0) bt = gemm_tc_tile(M, N, K);
+  if (tc_splits(M, N, K, bt) == 1) return 0;
+  return al256_tc((size_t)M * N * sizeof(unsigned long long)) + (size_t)tc_tiles(M, N, bt) * 16 * sizeof(uint32_t);
 }
+
+size_t gemm_tc_workspace(int64_t M, int N, int K) { return gemm_tc_workspace_tile(M, N, K, 0); }
 
 // Whether T activation sets with these row-block starts can share one
 // launch: every table starts on a 256-row tile.
@@ -584,19 +652,21 @@ int gemm_tc_sets_ok(int T, const int* tab_nb) {
   return 1;
 }
 
-// workspace: gemm_tc_workspace(M, N, K) bytes, zero-filled and left so, or
-// NULL (then no split-K).  T activation sets: xq is [T][M][K], xscale
-// [T][M], rows from 16 * tab_nb[t] on read set t (gemm_tc_sets_ok).
-cudaError_t launch_gemm_tc_sets(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
+// workspace: gemm_tc_workspace_tile(M, N, K, bt) bytes, zero-filled and
+// left so, or NULL (then no split-K).  T activation sets: xq is [T][M][K],
+// xscale [T][M], rows from 16 * tab_nb[t] on read set t (gemm_tc_sets_ok).
+// bt: tokens per tile, 64 or 256 (0: gemm_tc_tile's choice).
+cudaError_t launch_gemm_tc_tile(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
                                 const void* bias, int bias_dtype, void* out, int out_dtype, void* workspace,
-                                size_t workspace_bytes, int T, const int* tab_nb, cudaStream_t st) {
+                                size_t workspace_bytes, int T, const int* tab_nb, int bt, cudaStream_t st) {
   auto encode = get_encode();
   if (!encode) return cudaErrorNotSupported;
-  if (M > 0x7FFFFFFF || !gemm_tc_sets_ok(T, tab_nb)) return cudaErrorInvalidValue;
+  if (bt == 0) bt = gemm_tc_tile(M, N, K);
+  if (M > 0x7FFFFFFF || !gemm_tc_sets_ok(T, tab_nb) || (bt != 64 && bt != 256)) return cudaErrorInvalidValue;
   CUtensorMap xmap;
   const cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)M, (cuuint64_t)T};
   const cuuint64_t strides[2] = {(cuuint64_t)K, (cuuint64_t)M * K};
-  const cuuint32_t box[3] = {(cuuint32_t)kGroup, (cuuint32_t)kTcTokHalf, 1};
+  const cuuint32_t box[3] = {(cuuint32_t)kGroup, (cuuint32_t)(bt / 2), 1};
   const cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = encode(&xmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t*>(xq), dims, strides, box, estr,
                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -629,18 +699,20 @@ cudaError_t launch_gemm_tc_sets(const int8_t* xq, const float* xscale, int64_t M
   p.splits = 1;
   p.tables = T;
   for (int t = 0; t < kMaxTables; ++t) p.tab_nb[t] = t < T ? tab_nb[t] : 0;
-  const size_t wsb = gemm_tc_workspace(M, N, K);
+  const size_t wsb = gemm_tc_workspace_tile(M, N, K, bt);
   if (wsb && workspace && workspace_bytes >= wsb) {
-    p.splits = tc_splits(M, N, K);
+    p.splits = tc_splits(M, N, K, bt);
     p.ws = static_cast<unsigned long long*>(workspace);
     p.cnt = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) +
                                         al256_tc((size_t)M * N * sizeof(unsigned long long)));
   }
   p.gper = (G + p.splits - 1) / p.splits;
-  cudaError_t e = ensure_smem_limit((const void*)gemm_tc_kernel, kTcSmem);
+  const void* fn = bt == 64 ? (const void*)gemm_tc_kernel<64> : (const void*)gemm_tc_kernel<256>;
+  const int smem = bt == 64 ? TcTile<64>::kSmem : TcTile<256>::kSmem;
+  cudaError_t e = ensure_smem_limit(fn, smem);
   if (e != cudaSuccess) return e;
   p.tiles_n = (N + 2 * kTcRows - 1) / (2 * kTcRows);
-  const int64_t tiles = (int64_t)p.tiles_n * ((M + kTcTok - 1) / kTcTok);
+  const int64_t tiles = (int64_t)p.tiles_n * ((M + bt - 1) / bt);
   if (tiles > 0x7FFFFFFF) return cudaErrorInvalidValue;
   p.tiles = (int)tiles;
   p.items = p.tiles * p.splits;
@@ -649,7 +721,7 @@ cudaError_t launch_gemm_tc_sets(const int8_t* xq, const float* xscale, int64_t M
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(2 * pairs));
   cfg.blockDim = dim3(kTcThreads);
-  cfg.dynamicSmemBytes = kTcSmem;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -658,15 +730,23 @@ cudaError_t launch_gemm_tc_sets(const int8_t* xq, const float* xscale, int64_t M
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel, xmap, wmap, p);
+  if (bt == 64) return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<64>, xmap, wmap, p);
+  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<256>, xmap, wmap, p);
+}
+
+cudaError_t launch_gemm_tc_sets(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
+                                const void* bias, int bias_dtype, void* out, int out_dtype, void* workspace,
+                                size_t workspace_bytes, int T, const int* tab_nb, cudaStream_t st) {
+  return launch_gemm_tc_tile(xq, xscale, M, N, K, packed, bias, bias_dtype, out, out_dtype, workspace,
+                             workspace_bytes, T, tab_nb, 0, st);
 }
 
 cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
                            const void* bias, int bias_dtype, void* out, int out_dtype, void* workspace,
                            size_t workspace_bytes, cudaStream_t st) {
   const int nb0 = 0;
-  return launch_gemm_tc_sets(xq, xscale, M, N, K, packed, bias, bias_dtype, out, out_dtype, workspace, workspace_bytes,
-                             1, &nb0, st);
+  return launch_gemm_tc_tile(xq, xscale, M, N, K, packed, bias, bias_dtype, out, out_dtype, workspace,
+                             workspace_bytes, 1, &nb0, 0, st);
 }
 
 }  // namespace paro

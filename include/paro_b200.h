@@ -206,10 +206,12 @@ int paro_prepare_weights_awq(const int32_t* awq_qweight, const uint16_t* awq_sca
  *               call leaves it zero-filled again (the kernels clear what they
  *               use), so one buffer serves all calls on one stream; calls that
  *               may run concurrently need separate workspaces.
- * Requires N % 16 == 0, K % 128 == 0, M >= 1.  Above 64 tokens (above 24
- * for layers with at least 0.8 x SMs 256-row tiles) the tensor-core kernel
- * runs (paro_w4a8_gemm_path); it needs no workspace and
- * writes `out` with 16-byte stores, so `out` must then be 16-byte aligned.
+ * Requires N % 16 == 0, K % 128 == 0, M >= 1.  From 24 tokens (13 for
+ * K >= 8192, 17 for layers with at least 0.8 x SMs 256-row tiles), and
+ * always above 64, the tensor-core kernel runs (paro_w4a8_gemm_path), with
+ * 64-token tiles up to 64 tokens and the tile its cost estimate prefers
+ * beyond; it writes `out` with 16-byte stores, so `out` must then be
+ * 16-byte aligned.
  */
 size_t paro_w4a8_gemm_workspace_size(int64_t M, int N, int K);
 
@@ -268,8 +270,8 @@ int paro_selftest_wait_timeout(long long limit_cycles, paro_stream_t stream);
  * (fp16, one CTA per (128-channel group, token)) and records each row's
  * |max|, one quantises the rows to int8, and the GEMM (the streaming kernel,
  * launched behind them with programmatic dependent launch so that its weight
- * stream starts early; or, for 25-64 tokens on gate_up-wide or K >= 8192
- * layers, the tensor-core kernel).  Otherwise it is the activation kernel(s)
+ * stream starts early; or, where paro_w4a8_gemm_path picks it, the
+ * tensor-core kernel with 64-token tiles).  Otherwise it is the activation kernel(s)
  * followed by the GEMM.
  *   x             : [M, K] of x_dtype;  channel_scales : fp16 [K] or NULL.
  *   rot_table     : uint32 [8, K] from paro_prepare_rotation (group 128).
@@ -361,6 +363,35 @@ int paro_w4a8_linear_group(int prologue, const void* x, int x_dtype, const void*
 /* Which GEMM kernel paro_w4a8_gemm would launch for this shape
  * (0 = streaming decode kernel, 1 = tcgen05 tensor-core kernel). */
 int paro_w4a8_gemm_path(int64_t M, int N, int K);
+
+/* ---- GEMM with an explicit kernel (no counterpart in the reference) ------
+ * paro_w4a8_gemm with the kernel named instead of picked by shape, for tests
+ * that hold the kernels to one another and for measuring where one
+ * overtakes another:
+ *   PARO_ROUTE_AUTO    the kernel paro_w4a8_gemm picks;
+ *   PARO_ROUTE_STREAM  the streaming decode kernel (M <= 64, else
+ *                      PARO_ERR_TOO_LARGE);
+ *   PARO_ROUTE_TC256   the tensor-core kernel with 256-token tiles;
+ *   PARO_ROUTE_TC64    the tensor-core kernel with 64-token tiles.
+ * The tensor-core routes want `out` 16-byte aligned.  Workspace: at least
+ * paro_w4a8_gemm_route_workspace_size(route, M, N, K) bytes, zero-filled
+ * before the first call and left zero by every call.  Results of the two
+ * tensor-core routes are equal bit for bit when neither splits K (which
+ * happens when the shape's tiles fill the GPU's CTA pairs); the int32 group
+ * sums are exact on every route, and routes otherwise differ only in the
+ * order float32 partial sums are added. */
+typedef enum paro_route {
+  PARO_ROUTE_AUTO = 0,
+  PARO_ROUTE_STREAM = 1,
+  PARO_ROUTE_TC256 = 2,
+  PARO_ROUTE_TC64 = 3
+} paro_route;
+
+size_t paro_w4a8_gemm_route_workspace_size(int route, int64_t M, int N, int K);
+
+int paro_w4a8_gemm_route(int route, const int8_t* xq, const float* xscale, int64_t M, int N, int K,
+                         const void* packed, const void* bias, int bias_dtype, void* out, int out_dtype,
+                         void* workspace, size_t workspace_bytes, paro_stream_t stream);
 
 /* ---- Allocation-free GEMM (no counterpart in the reference) --------------
  * paro_w4a8_gemm without a caller-provided workspace, for callers that may

@@ -40,21 +40,21 @@ def _layer(N, K, seed):
 def test_rows_kernel_matches_oracle_and_repeats(N, K, M):
     from alpamayo_b200 import _native
     L = _native.capi()
-    assert L.paro_w4a8_gemm_path(M, N, K) == 0
+    STREAM = 1   # PARO_ROUTE_STREAM: the decode kernels, whatever paro_w4a8_gemm_path picks
     codes, scales, zeros, packed = _layer(N, K, seed=N + K + M)
     rng = np.random.default_rng(N * 7 + M)
     xq = rng.integers(-127, 128, (M, K)).astype(np.int8)
     xs = (rng.random(M) * 0.1 + 0.01).astype(np.float32)
     bias = (rng.standard_normal(N) * 0.1).astype(np.float32)
     dq, ds, db = (torch.from_numpy(a).cuda() for a in (xq, xs, bias))
-    wsb = L.paro_w4a8_gemm_workspace_size(M, N, K)
+    wsb = L.paro_w4a8_gemm_route_workspace_size(STREAM, M, N, K)
     ws = torch.zeros(wsb, dtype=torch.uint8, device="cuda")
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     outs = []
     for _ in range(2):
         y = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
-        st = L.paro_w4a8_gemm(dq.data_ptr(), ds.data_ptr(), M, N, K, packed.data_ptr(), db.data_ptr(), 0,
-                              y.data_ptr(), 0, ws.data_ptr(), wsb, stream)
+        st = L.paro_w4a8_gemm_route(STREAM, dq.data_ptr(), ds.data_ptr(), M, N, K, packed.data_ptr(),
+                                    db.data_ptr(), 0, y.data_ptr(), 0, ws.data_ptr(), wsb, stream)
         assert st == 0, L.paro_status_string(st)
         outs.append(y)
     torch.cuda.synchronize()

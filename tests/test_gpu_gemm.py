@@ -160,11 +160,11 @@ def test_gemm_linearity_in_token_scale(ops):
 
 @pytest.mark.parametrize("N,K,M", [(272, 256, 65), (512, 128, 129), (768, 1024, 300), (4608, 3584, 2048),
                                    (3584, 18944, 256), (37888, 3584, 160), (37888, 3584, 40), (4608, 3584, 65),
-                                   (3584, 3584, 100)])
+                                   (3584, 3584, 100), (3584, 18944, 16), (4608, 3584, 24), (37888, 3584, 17)])
 def test_tensor_core_gemm_tiles_match_oracle(ops, N, K, M):
-    """The tcgen05 kernel (M > 64, or M > 24 on a layer with enough 256-row
-    tiles): full and partial 128-token x 256-row tiles, against the oracle
-    on sampled rows and columns."""
+    """The tcgen05 kernel on the shapes paro_w4a8_gemm_path sends to it:
+    full and partial 64- and 256-token x 256-row tiles, split-K and not,
+    against the oracle on sampled rows and columns."""
     from alpamayo_b200 import _native
     assert _native.capi().paro_w4a8_gemm_path(M, N, K) == 1
     codes, scales, zeros, packed = records_layer(N, K, seed=N // 16 + K + M)

@@ -75,27 +75,39 @@ def test_argument_validation_before_launch():
 
 def test_gemm_kernel_choice_by_shape():
     """The GEMM route is a pure function of the shape (host logic, no device
-    work): the streaming kernel up to 64 tokens, the tensor-core kernel
-    above, and from 25 tokens on layers with at least 0.8 x SMs 256-row
-    tiles (gate_up: N = 37888; the SM count falls back to 148 without a GPU)."""
+    work; the SM count falls back to 148 without a GPU): the streaming
+    kernel for few tokens, the tensor-core kernel (64-token tiles) from 24
+    tokens, from 13 on long rows (K >= 8192) and from 17 on layers with at
+    least 0.8 x SMs 256-row tiles (gate_up: N = 37888), and always above 64;
+    beyond 64 tokens its tile follows the cost estimate."""
     from alpamayo_b200._native import capi
     import torch
     L = capi()
     sms = torch.cuda.get_device_properties(0).multi_processor_count if torch.cuda.is_available() else 148
+    wide = 37888 // 256 * 5 >= sms * 4
     assert L.paro_w4a8_gemm_path(8, 37888, 3584) == 0
-    assert L.paro_w4a8_gemm_path(24, 37888, 3584) == 0
-    assert L.paro_w4a8_gemm_path(25, 37888, 3584) == (1 if 37888 // 256 * 5 >= sms * 4 else 0)
-    assert L.paro_w4a8_gemm_path(64, 4608, 3584) == 0
-    assert L.paro_w4a8_gemm_path(64, 3584, 18944) == 0
+    assert L.paro_w4a8_gemm_path(16, 37888, 3584) == 0
+    assert L.paro_w4a8_gemm_path(17, 37888, 3584) == (1 if wide else 0)
+    assert L.paro_w4a8_gemm_path(23, 4608, 3584) == 0
+    assert L.paro_w4a8_gemm_path(24, 4608, 3584) == 1
+    assert L.paro_w4a8_gemm_path(12, 3584, 18944) == 0
+    assert L.paro_w4a8_gemm_path(13, 3584, 18944) == 1
+    assert L.paro_w4a8_gemm_path(64, 3584, 3584) == 1
     assert L.paro_w4a8_gemm_path(65, 4608, 3584) == 1
     assert L.paro_w4a8_gemm_path(65, 100, 3584) == 0   # not a whole number of 16-row records
+    if sms == 148:
+        # the tile follows the estimate: a split-K 256-token tile for down at
+        # 400 tokens (workspace), unsplit 64-token tiles at 300 (none)
+        assert L.paro_w4a8_gemm_workspace_size(400, 3584, 18944) > 0
+        assert L.paro_w4a8_gemm_workspace_size(300, 3584, 18944) == 0
 
 
 def test_workspace_sizes_by_route():
     """Workspace sizes are host arithmetic (no device work; the SM count falls
     back to 148 without a GPU): the streaming kernel's [N][M] 64-bit
     fixed-point partial sums plus a counter per 16-row block; the tensor-core
-    kernel's split-K sums ([M][N] 64-bit) plus 16 counters per 256x256 tile
+    kernel's split-K sums ([M][N] 64-bit) plus 16 counters per tile (256 rows x
+    64 or 256 tokens)
     when its tiles fill fewer than the CTA pairs, else nothing; the linear's
     at least what its route needs."""
     from alpamayo_b200._native import capi
@@ -106,8 +118,16 @@ def test_workspace_sizes_by_route():
     al = lambda b: (b + 255) // 256 * 256
     # streaming kernel (8 tokens): one token slice, N / 16 counters
     assert L.paro_w4a8_gemm_workspace_size(8, 3584, 3584) == al(3584 * 8 * 8) + (3584 // 16) * 4
-    # tensor-core kernel with split-K: qkv at 65 tokens is 18 tiles < 74 pairs
-    assert L.paro_w4a8_gemm_workspace_size(65, 4608, 3584) == al(65 * 4608 * 8) + 18 * 16 * 4
+    # tensor-core kernel with split-K: qkv at 65 tokens is 18 x 2 tiles of
+    # 256 rows x 64 tokens < 74 pairs
+    assert L.paro_w4a8_gemm_workspace_size(65, 4608, 3584) == al(65 * 4608 * 8) + 36 * 16 * 4
+    # the explicit routes: 256-token tiles (18 tiles), the streaming kernel
+    # only up to 64 tokens
+    assert L.paro_w4a8_gemm_route_workspace_size(2, 65, 4608, 3584) == al(65 * 4608 * 8) + 18 * 16 * 4
+    assert L.paro_w4a8_gemm_route_workspace_size(3, 65, 4608, 3584) == al(65 * 4608 * 8) + 36 * 16 * 4
+    assert L.paro_w4a8_gemm_route_workspace_size(1, 65, 4608, 3584) == 0
+    assert L.paro_w4a8_gemm_route_workspace_size(1, 8, 3584, 3584) == al(3584 * 8 * 8) + (3584 // 16) * 4
+    assert L.paro_w4a8_gemm_route_workspace_size(0, 65, 4608, 3584) == L.paro_w4a8_gemm_workspace_size(65, 4608, 3584)
     # ... and without: 144 tiles at 2048 tokens fill the pairs
     assert L.paro_w4a8_gemm_workspace_size(2048, 4608, 3584) == 0
     # the linear for down at 64 tokens takes the tensor-core route (14 tiles)

@@ -79,7 +79,7 @@ def test_noalloc_matches_workspace_entry_two_calls_in_a_row(L, out_dtype):
     # shapes alternating, so each call starts from the previous one's
     # leftovers in the shared array: two streaming-kernel shapes (one with
     # cross-CTA partial sums), a tensor-core shape with split-K through the
-    # array (qkv at 65 tokens) and a 25-64-token gate_up-wide shape
+    # array (qkv at 65 tokens) and gate_up at 40 tokens (64-token tiles)
     cases = [_layer(3584, 3584, 8, seed=1), _layer(4608, 3584, 3, seed=2), _layer(4608, 3584, 65, seed=4),
              _layer(37888, 3584, 40, seed=5)]
     assert [L.paro_w4a8_gemm_path(c["M"], c["N"], c["K"]) for c in cases] == [0, 0, 1, 1]
@@ -95,8 +95,9 @@ def test_noalloc_matches_workspace_entry_two_calls_in_a_row(L, out_dtype):
 
 
 def test_noalloc_tensor_core_shape_beyond_the_array_runs_unsplit(L):
-    # down at 300 tokens: split-K would need ~8.6 MB of partial sums
-    M, N, K = 300, 3584, 18944
+    # down at 400 tokens (256-token tiles, two splits): split-K would need
+    # ~11.5 MB of partial sums
+    M, N, K = 400, 3584, 18944
     assert L.paro_w4a8_gemm_path(M, N, K) == 1
     assert L.paro_w4a8_gemm_workspace_size(M, N, K) > SCRATCH_BYTES
     c = _layer(N, K, M, seed=6)
@@ -111,7 +112,8 @@ def test_noalloc_tensor_core_shape_beyond_the_array_runs_unsplit(L):
 
 
 def test_noalloc_rejects_shapes_beyond_its_scratch(L):
-    M, N, K = 24, 98304, 256   # streaming-kernel range, needs ~9.4 MB > 8 MiB
+    M, N, K = 16, 98304, 256   # streaming-kernel range, needs ~12.6 MB > 8 MiB
+    assert L.paro_w4a8_gemm_path(M, N, K) == 0
     assert L.paro_w4a8_gemm_workspace_size(M, N, K) > SCRATCH_BYTES
     c = _layer(N, K, M, seed=3)
     out = torch.zeros(M, N, dtype=torch.float32, device="cuda")
