@@ -48,9 +48,13 @@ cudaError_t launch_linear_decode(const void* x, int x_dtype, const uint16_t* csc
 int gemm_tc_supported(int64_t M, int N, int K);
 size_t gemm_tc_workspace(int64_t M, int N, int K);
 size_t gemm_tc_workspace_tile(int64_t M, int N, int K, int bt);
+cudaError_t launch_gemm_rows(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
+                             const void* bias, int bias_dtype, void* out, int out_dtype, void* ws, uint32_t* amax,
+                             const int* gsum, int gsum_mp, cudaStream_t st, int any_shape);
 cudaError_t launch_gemm_tc_tile(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
                                 const void* bias, int bias_dtype, void* out, int out_dtype, void* workspace,
-                                size_t workspace_bytes, int T, const int* tab_nb, int bt, cudaStream_t st);
+                                size_t workspace_bytes, int T, const int* tab_nb, int bt, cudaStream_t st,
+                                uint32_t* zero_after, int zero_n);
 cudaError_t launch_selftest_wait(long long limit_cycles, cudaStream_t st);
 cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
                            const void* bias, int bias_dtype, void* out, int out_dtype, void* ws, size_t ws_bytes,
@@ -616,12 +620,15 @@ int paro_w4a8_gemm(const int8_t* xq, const float* xscale, int64_t M, int N, int 
 
 // tokens the streaming decode kernel is built and tuned for
 constexpr int64_t kStreamMaxTokens = 64;
+// ... and the one-row-block-per-warp decode kernel
+constexpr int64_t kRowsMaxTokens = 16;
 
 size_t paro_w4a8_gemm_route_workspace_size(int route, int64_t M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0 || N % kRecRows || K % kGroup) return 0;
   switch (route) {
     case PARO_ROUTE_AUTO: return paro_w4a8_gemm_workspace_size(M, N, K);
     case PARO_ROUTE_STREAM: return M <= kStreamMaxTokens ? gemm_decode_workspace(M, N) : 0;
+    case PARO_ROUTE_ROWS: return M <= kRowsMaxTokens ? gemm_decode_workspace(M, N) : 0;
     case PARO_ROUTE_TC256: return gemm_tc_workspace_tile(M, N, K, 256);
     case PARO_ROUTE_TC64: return gemm_tc_workspace_tile(M, N, K, 64);
   }
@@ -634,7 +641,7 @@ int paro_w4a8_gemm_route(int route, const int8_t* xq, const float* xscale, int64
   if (route == PARO_ROUTE_AUTO)
     return paro_w4a8_gemm(xq, xscale, M, N, K, packed, bias, bias_dtype, out, out_dtype, workspace,
                           workspace_bytes, stream);
-  if (route != PARO_ROUTE_STREAM && route != PARO_ROUTE_TC256 && route != PARO_ROUTE_TC64)
+  if (route != PARO_ROUTE_STREAM && route != PARO_ROUTE_TC256 && route != PARO_ROUTE_TC64 && route != PARO_ROUTE_ROWS)
     return PARO_ERR_INVALID_ARGUMENT;
   if (M == 0 && N > 0 && K > 0) return PARO_OK;
   if (!xq || !xscale || !packed || !out || M < 0 || N <= 0 || K <= 0) return PARO_ERR_INVALID_ARGUMENT;
@@ -642,6 +649,15 @@ int paro_w4a8_gemm_route(int route, const int8_t* xq, const float* xscale, int64
   if (N % kRecRows || K % kGroup) return PARO_ERR_SHAPE;
   if (!aligned(packed, 16) || !aligned(xq, 16)) return PARO_ERR_MISALIGNED;
   if (int d = device_check()) return d;
+  if (route == PARO_ROUTE_ROWS) {
+    if (M > kRowsMaxTokens) return PARO_ERR_TOO_LARGE;
+    const size_t need = gemm_decode_workspace(M, N);
+    if (!workspace || workspace_bytes < need) return PARO_ERR_WORKSPACE;
+    if (!aligned(workspace, 256)) return PARO_ERR_MISALIGNED;
+    const cudaError_t e = launch_gemm_rows(xq, xscale, M, N, K, packed, bias, bias_dtype, out, out_dtype, workspace,
+                                           nullptr, nullptr, 0, (cudaStream_t)stream, 1);
+    return e == cudaErrorNotSupported ? PARO_ERR_UNSUPPORTED : cuda_status(e);
+  }
   if (route == PARO_ROUTE_STREAM) {
     if (M > kStreamMaxTokens) return PARO_ERR_TOO_LARGE;
     const size_t need = gemm_decode_workspace(M, N);
@@ -656,7 +672,7 @@ int paro_w4a8_gemm_route(int route, const int8_t* xq, const float* xscale, int64
   if (workspace_bytes < need || (need && !workspace)) return PARO_ERR_WORKSPACE;
   const int nb0 = 0;
   return cuda_status(launch_gemm_tc_tile(xq, xscale, M, N, K, packed, bias, bias_dtype, out, out_dtype, workspace,
-                                         workspace_bytes, 1, &nb0, bt, (cudaStream_t)stream));
+                                         workspace_bytes, 1, &nb0, bt, (cudaStream_t)stream, nullptr, 0));
 }
 
 }  // extern "C"

@@ -755,16 +755,18 @@ static DecParams dec_params(int64_t M, int N, int K, const void* packed, const v
 
 cudaError_t launch_gemm_rows(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
                              const void* bias, int bias_dtype, void* out, int out_dtype, void* ws, uint32_t* amax,
-                             const int* gsum, int gsum_mp, cudaStream_t st);
+                             const int* gsum, int gsum_mp, cudaStream_t st, int any_shape);
 
-// Which decode GEMM runs where both take the shape: gemm_rows_kernel
-// (gemm_rows.cu) unless the environment sets PARO_DECODE_GEMM=stream, which
-// keeps every shape on gemm_stream_kernel (read once per process; for
-// comparing the two).
+// Which decode GEMM runs: gemm_stream_kernel, unless the environment sets
+// PARO_DECODE_GEMM=rows (read once per process), which sends the shapes
+// where gemm_rows_kernel (gemm_rows.cu) measured at least as fast per launch
+// (gate_up-wide layers, up to 8 tokens) to it.  Off by default: in the
+// decode sweep of all four projections the streaming kernel alone was 2 %
+// faster (2,249 against 2,205 GB/s of weights on B200).
 static bool rows_kernel_enabled() {
   static const int on = [] {
     const char* v = getenv("PARO_DECODE_GEMM");
-    return (v && strcmp(v, "stream") == 0) ? 0 : 1;
+    return (v && strcmp(v, "rows") == 0) ? 1 : 0;
   }();
   return on != 0;
 }
@@ -774,7 +776,7 @@ cudaError_t launch_gemm_decode(const int8_t* xq, const float* xscale, int64_t M,
                                cudaStream_t st) {
   if (rows_kernel_enabled()) {
     const cudaError_t e = launch_gemm_rows(xq, xscale, M, N, K, packed, bias, bias_dtype, out, out_dtype, ws, nullptr,
-                                           nullptr, 0, st);
+                                           nullptr, 0, st, 0);
     if (e != cudaErrorNotSupported) return e;
   }
   DecParams p = dec_params(M, N, K, packed, bias, bias_dtype, out, out_dtype, ws);
@@ -802,6 +804,10 @@ cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int
 cudaError_t launch_gemm_tc_sets(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
                                 const void* bias, int bias_dtype, void* out, int out_dtype, void* workspace,
                                 size_t workspace_bytes, int T, const int* tab_nb, cudaStream_t st);
+cudaError_t launch_gemm_tc_tile(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
+                                const void* bias, int bias_dtype, void* out, int out_dtype, void* workspace,
+                                size_t workspace_bytes, int T, const int* tab_nb, int bt, cudaStream_t st,
+                                uint32_t* zero_after, int zero_n);
 int gemm_tc_sets_ok(int T, const int* tab_nb);
 
 // Linears of up to 64 tokens whose GEMM is faster on the tensor cores
@@ -898,15 +904,14 @@ cudaError_t launch_linear_decode_tables(const void* x, int x_dtype, const RotTab
   e = launch_quant16_decode(rot16, p.amax, M, K, Mp, xq, xs, gsum, T, st);
   if (e != cudaSuccess) return e;
   if (tc) {
-    // the tensor-core GEMM does not read the row maxima: clear them here
-    // (behind the quantiser on the stream)
-    e = cudaMemsetAsync(p.amax, 0, (size_t)T * M * sizeof(uint32_t), st);
-    if (e != cudaSuccess) return e;
-    return launch_gemm_tc_sets(xq, xs, M, N, K, packed, bias, bias_dtype, out, out_dtype, tcb ? ws : nullptr, tcb, T,
-                               tab_nb, st);
+    // the tensor-core GEMM (launched behind the quantiser with programmatic
+    // dependent launch) returns the row maxima to zero once the quantiser has
+    // completed
+    return launch_gemm_tc_tile(xq, xs, M, N, K, packed, bias, bias_dtype, out, out_dtype, tcb ? ws : nullptr, tcb, T,
+                               tab_nb, 0, st, p.amax, (int)(T * M));
   }
   if (T == 1 && rows_kernel_enabled()) {
-    e = launch_gemm_rows(xq, xs, M, N, K, packed, bias, bias_dtype, out, out_dtype, ws, p.amax, gsum, Mp, st);
+    e = launch_gemm_rows(xq, xs, M, N, K, packed, bias, bias_dtype, out, out_dtype, ws, p.amax, gsum, Mp, st, 0);
     if (e != cudaErrorNotSupported) return e;
   }
   p.xq = xq;

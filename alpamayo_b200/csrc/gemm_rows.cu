@@ -671,7 +671,9 @@ struct RwPlan {
   size_t smem;
 };
 
-static bool rw_plan(int64_t M, int N, int K, RwPlan& pl) {
+// any_shape: every shape the kernel handles (the explicit route), otherwise
+// only where it measured at least as fast as the streaming kernel.
+static bool rw_plan(int64_t M, int N, int K, RwPlan& pl, bool any_shape = false) {
   if (M < 1 || M > kRwMaxTokens || N % kRecRows || K % kGroup) return false;
   const int G = K / kGroup, nbk = N / kRecRows;
   pl.MT = M <= 8 ? 1 : 2;
@@ -682,7 +684,7 @@ static bool rw_plan(int64_t M, int N, int K, RwPlan& pl) {
   // 4 / 8 tokens: 16.6 / 16.8 / 17.0 us against 16.5 / 17.0 / 18.3).  Where
   // its row blocks are cut into pieces (qkv, o, down) the streaming kernel
   // was 2-5 us faster per launch.
-  if (M > 8 || (int64_t)nbk < 16 * (int64_t)pl.ctas) return false;
+  if (!any_shape && (M > 8 || (int64_t)nbk < 16 * (int64_t)pl.ctas)) return false;
   // the kernel walks its unit range in 32-bit arithmetic
   const int64_t units = (int64_t)nbk * G;
   if (units * (pl.ctas + 1) >= (int64_t)1 << 31 || (int64_t)M * K >= (int64_t)1 << 31) return false;
@@ -737,9 +739,9 @@ static cudaError_t rw_dispatch(const RwParams& p, const RwPlan& pl, cudaStream_t
 // (nothing launched) for shapes rw_plan does not take.
 cudaError_t launch_gemm_rows(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
                              const void* bias, int bias_dtype, void* out, int out_dtype, void* ws, uint32_t* amax,
-                             const int* gsum, int gsum_mp, cudaStream_t st) {
+                             const int* gsum, int gsum_mp, cudaStream_t st, int any_shape) {
   RwPlan pl;
-  if (!rw_plan(M, N, K, pl)) return cudaErrorNotSupported;
+  if (!rw_plan(M, N, K, pl, any_shape != 0)) return cudaErrorNotSupported;
   if (gsum && gsum_mp != 8 * pl.MT) return cudaErrorNotSupported;
   RwParams p = {};
   p.xq = xq;

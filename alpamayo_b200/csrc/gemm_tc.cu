@@ -39,6 +39,11 @@
 //    scale; then each warp arrives on the leader's "buffer drained" barrier.
 //    After the last group: token scale, bias, convert, store.
 //
+// Launched with programmatic dependent launch: set-up (barriers, tensor
+// memory) and the first stages' weight boxes overlap the previous kernel on
+// the stream; the activation boxes, the token scales and every store wait
+// for it (griddepcontrol.wait).
+//
 // Per SM and group this moves 8.5 KB of records + BT / 2 x 128 bytes of
 // activations from L2 for 128 x BT x 128 MACs.  No load uses cluster multicast.  All
 // mbarrier waits are bounded (report kErrMbarTimeout and drop out), and the
@@ -64,10 +69,7 @@ struct TcTile {
   static_assert(BT == 256 || BT == 64, "tile tokens");
   static constexpr int kTok = BT;                        // tokens per tile (MMA N)
   static constexpr int kTokHalf = BT / 2;                // tokens staged per CTA
-#ifndef PARO_TC64_STAGES
-#define PARO_TC64_STAGES 8
-#endif
-  static constexpr int kStages = BT == 256 ? 6 : PARO_TC64_STAGES;
+  static constexpr int kStages = BT == 256 ? 6 : 8;
   static constexpr int kBufs = BT == 256 ? 2 : 4;        // TMEM accumulators in flight
   static constexpr int kTmemCols = kBufs * BT;           // 512 or 256 (a power of two)
   static constexpr int kXBytes = kTokHalf * kGroup;      // 16 KB or 4 KB activations per stage
@@ -108,6 +110,10 @@ struct TcParams {
   // table starts on a 256-row tile
   int tables;
   int tab_nb[kMaxTables];
+  // words the previous kernel on the stream read last (the decode chain's
+  // row maxima): zeroed once that kernel has completed, or null
+  uint32_t* zero_after;
+  int zero_n;
 };
 
 // The activation set of the 256-row tile starting at output row n.
@@ -185,6 +191,8 @@ __device__ __forceinline__ void cluster_sync_all() {
 
 
 
+
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // packed float32 pair arithmetic (sm_100)
 __device__ __forceinline__ uint64_t pack2(float a, float b) {
@@ -287,12 +295,30 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
   cluster_sync_all();  // barriers initialised and tensor memory allocated in both CTAs
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // the next kernel on the stream may launch as SMs free up (it waits for
+  // this grid's completion before reading what it writes)
+  asm volatile("griddepcontrol.launch_dependents;");
   bool failed = false;
 
   if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 56;");
     if (warp == 0 && lane == 0) {
-      // producer
+      // producer.  The weights do not depend on the previous kernel on the
+      // stream (the launch may overlap it): the first stages' weight boxes
+      // go out before griddepcontrol.wait, every activation box after it.
+      uint32_t npre = 0;
+      for (int w = pair; w < p.items && npre < (uint32_t)kStages; w += pairs) {
+        int gb, ge;
+        item_groups(w, gb, ge);
+        const int n0 = tile_n0(w / p.splits);
+        for (int g = gb; g < ge && npre < (uint32_t)kStages; ++g, ++npre) {
+          // a box always delivers all its bytes (rows past the layer's end
+          // read as zeros)
+          mbar_arrive_expect_tx(&full[npre], (uint32_t)(C::kXBytes + kTcRecs * kRecBytes));
+          tma_load_3d(smem + C::kOffW + npre * kTcWBytes, &wmap, 0, g, n0 / kRecRows, &full[npre]);
+        }
+      }
+      grid_dep_wait();
       uint32_t it = 0;  // groups issued by this CTA so far
       for (int w = pair; w < p.items && !failed; w += pairs) {
         const int t = w / p.splits;
@@ -303,15 +329,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
         const int xset = tc_set(p, (t % p.tiles_n) * (2 * kTcRows));
         for (int g = gb; g < ge; ++g, ++it) {
           const uint32_t s = it % kStages;
-          if (it >= kStages && !mbar_wait(&freed[s], ((it / kStages) - 1) & 1)) {
-            failed = true;
-            break;
+          if (it >= (uint32_t)kStages) {
+            if (!mbar_wait(&freed[s], ((it / kStages) - 1) & 1)) {
+              failed = true;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[s], (uint32_t)(C::kXBytes + kTcRecs * kRecBytes));
+            tma_load_3d(smem + C::kOffW + s * kTcWBytes, &wmap, 0, g, n0 / kRecRows, &full[s]);
           }
-          // a box always delivers all its bytes (rows past the layer's end
-          // read as zeros)
-          mbar_arrive_expect_tx(&full[s], (uint32_t)(C::kXBytes + kTcRecs * kRecBytes));
           tma_load_3d(smem + C::kOffX + s * C::kXBytes, &xmap, g * kGroup, ty, xset, &full[s]);
-          tma_load_3d(smem + C::kOffW + s * kTcWBytes, &wmap, 0, g, n0 / kRecRows, &full[s]);
         }
       }
     } else if (warp == 1 && lane == 0 && leader) {
@@ -341,6 +367,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
       // every MMA issued above completes before the pair frees its tensor memory
       umma_commit_pair(mma_done);
       mbar_wait(mma_done, 0);
+    } else if (warp == 2 && blockIdx.x == 0 && p.zero_after) {
+      grid_dep_wait();   // the previous kernel has read them
+      for (int i = lane; i < p.zero_n; i += 32) p.zero_after[i] = 0u;
     }
   } else if (warp < 8) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 88;");
@@ -409,6 +438,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
 #pragma unroll
       for (int b = 0; b < kBufs; ++b) mbar_arrive_cluster(&acc_empty[b], 0);
     }
+    grid_dep_wait();   // the token scales come from the previous kernel
     uint32_t it = 0;
     for (int w = pair; w < p.items && !failed; w += pairs) {
       const int tile = w / p.splits;
@@ -474,7 +504,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
       for (int q = 0; q < kPerLane; ++q) {
         const int64_t m = m0 + col0 + lane * kPerLane + q;
         xs[lane * kPerLane + q] =
-            m < p.M ? __ldg(p.xscale + tc_set(p, (tile % p.tiles_n) * (2 * kTcRows)) * p.M + m) : 0.f;
+            m < p.M ? ld_dep(p.xscale + tc_set(p, (tile % p.tiles_n) * (2 * kTcRows)) * p.M + m) : 0.f;
       }
       __syncwarp();
       const int n = n0 + row;
@@ -658,7 +688,8 @@ int gemm_tc_sets_ok(int T, const int* tab_nb) {
 // bt: tokens per tile, 64 or 256 (0: gemm_tc_tile's choice).
 cudaError_t launch_gemm_tc_tile(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
                                 const void* bias, int bias_dtype, void* out, int out_dtype, void* workspace,
-                                size_t workspace_bytes, int T, const int* tab_nb, int bt, cudaStream_t st) {
+                                size_t workspace_bytes, int T, const int* tab_nb, int bt, cudaStream_t st,
+                                uint32_t* zero_after, int zero_n) {
   auto encode = get_encode();
   if (!encode) return cudaErrorNotSupported;
   if (bt == 0) bt = gemm_tc_tile(M, N, K);
@@ -699,6 +730,8 @@ cudaError_t launch_gemm_tc_tile(const int8_t* xq, const float* xscale, int64_t M
   p.splits = 1;
   p.tables = T;
   for (int t = 0; t < kMaxTables; ++t) p.tab_nb[t] = t < T ? tab_nb[t] : 0;
+  p.zero_after = zero_n > 0 ? zero_after : nullptr;
+  p.zero_n = zero_n > 0 ? zero_n : 0;
   const size_t wsb = gemm_tc_workspace_tile(M, N, K, bt);
   if (wsb && workspace && workspace_bytes >= wsb) {
     p.splits = tc_splits(M, N, K, bt);
@@ -723,13 +756,17 @@ cudaError_t launch_gemm_tc_tile(const int8_t* xq, const float* xscale, int64_t M
   cfg.blockDim = dim3(kTcThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // programmatic dependent launch: setup and the first weight boxes overlap
+  // the previous kernel
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   if (bt == 64) return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<64>, xmap, wmap, p);
   return cudaLaunchKernelEx(&cfg, gemm_tc_kernel<256>, xmap, wmap, p);
 }
@@ -738,7 +775,7 @@ cudaError_t launch_gemm_tc_sets(const int8_t* xq, const float* xscale, int64_t M
                                 const void* bias, int bias_dtype, void* out, int out_dtype, void* workspace,
                                 size_t workspace_bytes, int T, const int* tab_nb, cudaStream_t st) {
   return launch_gemm_tc_tile(xq, xscale, M, N, K, packed, bias, bias_dtype, out, out_dtype, workspace,
-                             workspace_bytes, T, tab_nb, 0, st);
+                             workspace_bytes, T, tab_nb, 0, st, nullptr, 0);
 }
 
 cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
@@ -746,7 +783,7 @@ cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int
                            size_t workspace_bytes, cudaStream_t st) {
   const int nb0 = 0;
   return launch_gemm_tc_tile(xq, xscale, M, N, K, packed, bias, bias_dtype, out, out_dtype, workspace,
-                             workspace_bytes, 1, &nb0, 0, st);
+                             workspace_bytes, 1, &nb0, 0, st, nullptr, 0);
 }
 
 }  // namespace paro

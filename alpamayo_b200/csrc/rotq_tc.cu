@@ -20,17 +20,15 @@
 //  * Producer thread: tensor TMA of the 128-row x 128-channel bf16 tile
 //    (two 64-channel boxes, 128-byte swizzle), 3 stages.
 //  * MMA thread: 8 MMAs (M = 128 rows, N = 128 channels, K = 16) with R'_hi,
-//    then 8 with R'_lo, into one of four 128-column TMEM buffers.  x is exact
+//    then 8 with R'_lo, into one of two 128-column TMEM buffers.  x is exact
 //    in bf16, so Y = X hi^T + X lo^T carries R' to about 2^-16 relative:
 //    far below the fp16 spacing the result is rounded to.
 //  * Epilogue (8 warps, TMEM lanes = rows, two warps per lane quarter): each
 //    thread reads 64 of its row's 128 outputs, rounds them to fp16 — the
 //    value the reference's rotate kernel stores (rotation.cuh:333-334) —
-//    stores them (128 contiguous bytes of its row, straight from registers:
-//    no staging, no barrier between the epilogue warps), and folds their
-//    |max| into the row's maximum (atomicMax on the bit pattern).
-//    quant_rows_kernel then quantises per token (rotq_rows.cu), reading the
-//    rows back from L2.
+//    stores them, and folds their |max| into the row's maximum (atomicMax
+//    on the bit pattern).  quant_rows_kernel
+//    then quantises per token (rotq_rows.cu).
 //
 // A CTA owns one group and a contiguous range of its row tiles (groups are
 // spread over the grid first).  Waits are bounded (kErrMbarTimeout), tensor
@@ -55,11 +53,11 @@ constexpr int kRtRBytes = 128 * 128 * 2;         // one bf16 128 x 128 matrix
 constexpr int kOffRhi = 0;
 constexpr int kOffRlo = kOffRhi + kRtRBytes;
 constexpr int kOffX = kOffRlo + kRtRBytes;
-constexpr int kOffEx = kOffX + kRtStages * kRtTileBytes;   // build: [2 halves][32 cols][128 rows] f32 exchange
+constexpr int kOffEx = kOffX + kRtStages * kRtTileBytes;   // build: [2 halves][32 cols][128 rows] f32 exchange;
+                                                            // epilogue: the fp16 output tile (32 KB)
 constexpr int kOffTab = kOffEx + 2 * 32 * 128 * 4;          // [8 layers][128] table words
 constexpr int kOffBar = kOffTab + 8 * 128 * 4;
 constexpr int kRtSmem = kOffBar + 256 + 1024;
-constexpr int kRtBufs = 4;                                  // 128-column TMEM accumulators
 
 // kind::f16 instruction descriptor: f32 accumulate, A and B bf16, both
 // K-major, N = 128, M = 128
@@ -129,14 +127,15 @@ struct RtParams {
   uint32_t* amax;          // [M] row |max| bits (zero on entry)
 };
 
-__global__ void __launch_bounds__(kRtThreads, 1) rot_tc_kernel(const __grid_constant__ CUtensorMap xmap, RtParams p) {
+__global__ void __launch_bounds__(kRtThreads, 1) rot_tc_kernel(const __grid_constant__ CUtensorMap xmap,
+                                                               const __grid_constant__ CUtensorMap ymap, RtParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBar);   // [3] tile landed
   uint64_t* freed = full + kRtStages;                               // [3] MMAs done with the tile
-  uint64_t* acc_full = freed + kRtStages;                           // [bufs]
-  uint64_t* acc_empty = acc_full + kRtBufs;                         // [bufs] 8 epilogue warps
-  uint64_t* mma_done = acc_empty + kRtBufs;                         // [1]
+  uint64_t* acc_full = freed + kRtStages;                           // [2]
+  uint64_t* acc_empty = acc_full + 2;                               // [2] 8 epilogue warps
+  uint64_t* mma_done = acc_empty + 2;                               // [1]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -153,7 +152,7 @@ __global__ void __launch_bounds__(kRtThreads, 1) rot_tc_kernel(const __grid_cons
       mbar_init(&full[s], 1);
       mbar_init(&freed[s], 1);
     }
-    for (int b = 0; b < kRtBufs; ++b) {
+    for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 8);
     }
@@ -161,8 +160,7 @@ __global__ void __launch_bounds__(kRtThreads, 1) rot_tc_kernel(const __grid_cons
     fence_mbar_init();
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "n"(kRtBufs * 128)
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_u32(tmem_slot))
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -253,8 +251,8 @@ __global__ void __launch_bounds__(kRtThreads, 1) rot_tc_kernel(const __grid_cons
       const uint32_t x_base = smem_u32(smem + kOffX);
       const uint32_t rh = smem_u32(smem + kOffRhi), rl = smem_u32(smem + kOffRlo);
       for (int i = 0; i < ntile; ++i) {
-        const int s = i % kRtStages, b = i % kRtBufs;
-        if (!mbar_wait(&full[s], (i / kRtStages) & 1) || !mbar_wait(&acc_empty[b], ((i / kRtBufs) & 1) ^ 1)) break;
+        const int s = i % kRtStages, b = i & 1;
+        if (!mbar_wait(&full[s], (i / kRtStages) & 1) || !mbar_wait(&acc_empty[b], ((i >> 1) & 1) ^ 1)) break;
         fence_after();
         const uint32_t d = tmem + (uint32_t)(b * 128);
 #pragma unroll
@@ -275,34 +273,40 @@ __global__ void __launch_bounds__(kRtThreads, 1) rot_tc_kernel(const __grid_cons
     }
   } else if (warp >= 4) {
     // epilogue: thread = row within the tile (TMEM lane), warps 4-7 take
-    // channels 0-63, warps 8-11 channels 64-127; each thread stores its 64
-    // fp16 values (128 contiguous bytes of its row) itself
+    // channels 0-63, warps 8-11 channels 64-127.  The fp16 tile is staged in
+    // shared memory (the build's exchange area, 128-byte swizzle) and written
+    // by two tensor TMA stores, so each row's 256 bytes leave as whole lines.
     const int q4 = warp & 3, chh = (warp - 4) >> 2;
     const int r = q4 * 32 + lane;
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
-    for (int i = 0; i < ntile && !failed; ++i) {
-      const int b = i % kRtBufs;
-      if (!mbar_wait(&acc_full[b], (i / kRtBufs) & 1)) {
-        failed = true;
-        break;
-      }
-      fence_after();
+    const bool issuer = warp == 4 && lane == 0;
+    uint8_t* stage_out = smem + kOffEx;
+    // every epilogue thread passes both named barriers of every tile, also
+    // after a timed-out wait (then it only skips the work)
+    for (int i = 0; i < ntile; ++i) {
+      const int b = i & 1;
+      if (!failed && !mbar_wait(&acc_full[b], (i >> 1) & 1)) failed = true;
       uint32_t v[64];
-      tmem_ld32(tmem + lane_base + (uint32_t)(b * 128 + chh * 64), *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-      tmem_ld32(tmem + lane_base + (uint32_t)(b * 128 + chh * 64 + 32), *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
-      tmem_wait_ld();
-      fence_before();
+      if (!failed) {
+        fence_after();
+        tmem_ld32(tmem + lane_base + (uint32_t)(b * 128 + chh * 64), *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        tmem_ld32(tmem + lane_base + (uint32_t)(b * 128 + chh * 64 + 32),
+                  *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        tmem_wait_ld();
+        fence_before();
+      }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[b]);   // the MMA may reuse the buffer
-      const int64_t row = (int64_t)(tb + i) * kRtRows + r;
+      if (!failed && lane == 0) mbar_arrive(&acc_empty[b]);   // the MMA may reuse the buffer
+      // the previous tile's stores have read the staging area
+      if (issuer) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+      named_barrier(3, 256);
       // the row's |max| of the fp16-rounded values: rounding to nearest is
       // monotonic and symmetric, so it is the fp16 rounding of the float32
       // |max| (one conversion instead of one per element); the bit patterns
       // of non-negative floats order as unsigned integers
       uint32_t mx = 0u;
-      uint4* dst = reinterpret_cast<uint4*>(p.y + row * p.K + g * 128 + chh * 64);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
+      for (int q = 0; q < 8 && !failed; ++q) {
         uint32_t hv[4];
 #pragma unroll
         for (int j2 = 0; j2 < 4; ++j2) {
@@ -311,18 +315,32 @@ __global__ void __launch_bounds__(kRtThreads, 1) rot_tc_kernel(const __grid_cons
           hv[j2] = *reinterpret_cast<const uint32_t*>(&hh);
           mx = max(mx, max(v[e] & 0x7FFFFFFFu, v[e + 1] & 0x7FFFFFFFu));
         }
-        if (row < p.M) dst[q] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+        *reinterpret_cast<uint4*>(stage_out + sw128_off(r, chh * 64 + q * 8)) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
       }
       mx = __float_as_uint(__half2float(__float2half_rn(__uint_as_float(mx))));
-      if (row < p.M && mx) atomicMax(p.amax + row, mx);
+      fence_proxy_async_smem();
+      named_barrier(3, 256);
+      const int y0 = (tb + i) * kRtRows;
+      if (issuer && !failed) {
+        // rows past M are clipped by the tensor map
+        asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(&ymap),
+                     "r"(g * 128), "r"(y0), "r"(smem_u32(stage_out))
+                     : "memory");
+        asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(&ymap),
+                     "r"(g * 128 + 64), "r"(y0), "r"(smem_u32(stage_out + 16384))
+                     : "memory");
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      }
+      const int64_t row = (int64_t)y0 + r;
+      if (!failed && row < p.M && mx) atomicMax(p.amax + row, mx);
     }
+    if (issuer) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   }
 
   fence_before();
   __syncthreads();
   fence_after();
-  if (warp == 1)
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "n"(kRtBufs * 128) : "memory");
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem) : "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -364,6 +382,10 @@ cudaError_t launch_rot_tc(const void* x, int64_t M, int K, const uint16_t* scale
                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  CUtensorMap ymap;
+  r = encode(&ymap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
   RtParams p;
   p.M = M;
   p.K = K;
@@ -379,7 +401,7 @@ cudaError_t launch_rot_tc(const void* x, int64_t M, int K, const uint16_t* scale
   p.amax = amax;
   cudaError_t e = ensure_smem_limit((const void*)rot_tc_kernel, kRtSmem);
   if (e != cudaSuccess) return e;
-  rot_tc_kernel<<<(unsigned)(p.G * splits), kRtThreads, kRtSmem, st>>>(xmap, p);
+  rot_tc_kernel<<<(unsigned)(p.G * splits), kRtThreads, kRtSmem, st>>>(xmap, ymap, p);
   return cudaGetLastError();
 }
 

@@ -372,7 +372,12 @@ int paro_w4a8_gemm_path(int64_t M, int N, int K);
  *   PARO_ROUTE_STREAM  the streaming decode kernel (M <= 64, else
  *                      PARO_ERR_TOO_LARGE);
  *   PARO_ROUTE_TC256   the tensor-core kernel with 256-token tiles;
- *   PARO_ROUTE_TC64    the tensor-core kernel with 64-token tiles.
+ *   PARO_ROUTE_TC64    the tensor-core kernel with 64-token tiles;
+ *   PARO_ROUTE_ROWS    the decode kernel with one row block per warp (M <= 16,
+ *                      else PARO_ERR_TOO_LARGE; PARO_ERR_UNSUPPORTED where its
+ *                      shared memory plan does not fit), which no automatic
+ *                      choice uses unless the environment sets
+ *                      PARO_DECODE_GEMM=rows.
  * The tensor-core routes want `out` 16-byte aligned.  Workspace: at least
  * paro_w4a8_gemm_route_workspace_size(route, M, N, K) bytes, zero-filled
  * before the first call and left zero by every call.  Results of the two
@@ -384,7 +389,8 @@ typedef enum paro_route {
   PARO_ROUTE_AUTO = 0,
   PARO_ROUTE_STREAM = 1,
   PARO_ROUTE_TC256 = 2,
-  PARO_ROUTE_TC64 = 3
+  PARO_ROUTE_TC64 = 3,
+  PARO_ROUTE_ROWS = 4
 } paro_route;
 
 size_t paro_w4a8_gemm_route_workspace_size(int route, int64_t M, int N, int K);

@@ -1,5 +1,6 @@
 """The decode GEMM with one row block per consumer warp (gemm_rows_kernel,
-up to 16 tokens) on the shapes that exercise each part of its schedule:
+up to 16 tokens; through PARO_ROUTE_ROWS, since no automatic choice uses it
+by default) on the shapes that exercise each part of its schedule:
 whole row blocks cut into pieces across warps (qkv-like: two row blocks per
 CTA), stream-K segments shared with neighbouring CTAs and fixed up through
 the workspace (down-like, and an odd group count), exactly one row block per
@@ -40,21 +41,24 @@ def _layer(N, K, seed):
 def test_rows_kernel_matches_oracle_and_repeats(N, K, M):
     from alpamayo_b200 import _native
     L = _native.capi()
-    STREAM = 1   # PARO_ROUTE_STREAM: the decode kernels, whatever paro_w4a8_gemm_path picks
+    ROWS = 4   # PARO_ROUTE_ROWS: this kernel on every shape it handles
     codes, scales, zeros, packed = _layer(N, K, seed=N + K + M)
     rng = np.random.default_rng(N * 7 + M)
     xq = rng.integers(-127, 128, (M, K)).astype(np.int8)
     xs = (rng.random(M) * 0.1 + 0.01).astype(np.float32)
     bias = (rng.standard_normal(N) * 0.1).astype(np.float32)
     dq, ds, db = (torch.from_numpy(a).cuda() for a in (xq, xs, bias))
-    wsb = L.paro_w4a8_gemm_route_workspace_size(STREAM, M, N, K)
+    wsb = L.paro_w4a8_gemm_route_workspace_size(ROWS, M, N, K)
     ws = torch.zeros(wsb, dtype=torch.uint8, device="cuda")
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     outs = []
     for _ in range(2):
         y = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
-        st = L.paro_w4a8_gemm_route(STREAM, dq.data_ptr(), ds.data_ptr(), M, N, K, packed.data_ptr(),
+        st = L.paro_w4a8_gemm_route(ROWS, dq.data_ptr(), ds.data_ptr(), M, N, K, packed.data_ptr(),
                                     db.data_ptr(), 0, y.data_ptr(), 0, ws.data_ptr(), wsb, stream)
+        if st == 3:   # PARO_ERR_UNSUPPORTED: the staged token rows leave too few ring stages
+            assert M > 8 or K > 4096, "one token tile of rows up to K = 4096 always fits"
+            pytest.skip("token rows beyond the kernel's shared-memory plan")
         assert st == 0, L.paro_status_string(st)
         outs.append(y)
     torch.cuda.synchronize()
