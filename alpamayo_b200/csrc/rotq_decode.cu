@@ -87,7 +87,7 @@ template <typename InT, int R, bool FRAG, int PRO>
 __global__ void __launch_bounds__(128)
 rot16_decode_kernel(const InT* x, int64_t M, int K, RotTables tabs, __half* __restrict__ y,
                     uint32_t* __restrict__ amax, RotPro pro) {
-  static_assert(PRO == kProNone || R == 1, "prologues run one token row per CTA");
+  static_assert(PRO != kProAddRmsnorm || R == 1, "the RMSNorm prologue runs one token row per CTA");
   // the GEMM that consumes these rows may launch now and start its weight
   // stream; it waits for this grid before reading y and amax
   asm volatile("griddepcontrol.launch_dependents;");
@@ -100,8 +100,12 @@ rot16_decode_kernel(const InT* x, int64_t M, int K, RotTables tabs, __half* __re
   const int64_t r0 = (int64_t)blockIdx.y * R;
   const int nrows = M - r0 < R ? (int)(M - r0) : R;
   // table blockIdx.z: its rotation, its channel scales, its activation set
-  const uint32_t* __restrict__ rtab = tabs.rtab[blockIdx.z];
-  const uint16_t* __restrict__ scales = tabs.cs[blockIdx.z];
+  // (picked by constant indices: a runtime index into the parameter's
+  // arrays would copy them to local memory in every CTA)
+  const int z = blockIdx.z;
+  const uint32_t* __restrict__ rtab = z == 0 ? tabs.rtab[0] : z == 1 ? tabs.rtab[1] : z == 2 ? tabs.rtab[2] : tabs.rtab[3];
+  const uint16_t* __restrict__ scales = z == 0 ? tabs.cs[0] : z == 1 ? tabs.cs[1] : z == 2 ? tabs.cs[2] : tabs.cs[3];
+  static_assert(kMaxTables == 4, "table selection above");
   y += (size_t)blockIdx.z * M * K;
   amax += (size_t)blockIdx.z * M;
 
@@ -147,9 +151,15 @@ rot16_decode_kernel(const InT* x, int64_t M, int K, RotTables tabs, __half* __re
     if (blockIdx.z == 0) pro.res_out[r0 * (int64_t)K + c] = __float2bfloat16_rn(sv);
     v[0] = bfr(__bfloat162float(pro.w[c]) * bfr(sv * inv)) * sc;
   } else if constexpr (PRO == kProSiluMul) {
-    const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(x) + r0 * (int64_t)(2 * K);
-    const float g = ld_dep(xr + c), u = ld_dep(xr + K + c);
-    v[0] = bfr(bfr(g / (1.0f + expf(-g))) * u) * sc;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      v[r] = 0.f;
+      if (r < nrows) {
+        const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(x) + (r0 + r) * (int64_t)(2 * K);
+        const float g = ld_dep(xr + c), u = ld_dep(xr + K + c);
+        v[r] = bfr(bfr(g / (1.0f + expf(-g))) * u) * sc;
+      }
+    }
   } else {
 #pragma unroll
     for (int r = 0; r < R; ++r) v[r] = r < nrows ? ld_dep(x + (r0 + r) * (int64_t)K + c) * sc : 0.f;
@@ -197,10 +207,17 @@ static cudaError_t launch_r(const void* x, int64_t M, int K, const RotTables& ta
 template <typename InT, bool FRAG, int PRO>
 static cudaError_t launch_t(const void* x, int64_t M, int K, const RotTables& tabs, int T, __half* y, uint32_t* amax,
                             const RotPro& pro, cudaStream_t st) {
-  // one row per CTA: a CTA with R rows runs its eight exchange rounds R
-  // times longer, and at decode sizes the kernel's latency is what the
-  // linear waits for (measured on B200, 8 tokens: R = 8 cost 2.3 us more per
-  // qkv / o linear than R = 1, 16 tokens on down 7 us more)
+  // one row per CTA at decode sizes: a CTA with R rows runs its eight
+  // exchange rounds R times longer, and there the kernel's latency is what
+  // the linear waits for (measured on B200, 8 tokens: R = 8 cost 2.3 us more
+  // per qkv / o linear than R = 1, 16 tokens on down 7 us more).  From 32
+  // tokens the CTAs outnumber the SMs many times over and each one's table
+  // loads and eight angle evaluations dominate: 2 or 4 rows share them (not
+  // with the RMSNorm prologue, which reduces over whole rows).
+  if constexpr (PRO != kProAddRmsnorm) {
+    if (M >= 48) return launch_r<InT, 4, FRAG, PRO>(x, M, K, tabs, T, y, amax, pro, st);
+    if (M >= 32) return launch_r<InT, 2, FRAG, PRO>(x, M, K, tabs, T, y, amax, pro, st);
+  }
   return launch_r<InT, 1, FRAG, PRO>(x, M, K, tabs, T, y, amax, pro, st);
 }
 

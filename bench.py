@@ -947,8 +947,8 @@ def main():
                        "l2": f"weight working set {wset / 2**20:.0f} MiB per sweep > L2 {L2_BYTES / 2**20:.0f} MiB "
                              "(3 replicas, one per M); inputs not flushed",
                        "parallelism": f"dp{world} (independent replicas, no collective)"},
-            "roofline": {"kernel": "decode W4A8 GEMM (gemm_rows_kernel: TMA bulk weight stream, one row block "
-                                   "per warp, mma.sync int4 x int8, stream-K)", "bound": "hbm",
+            "roofline": {"kernel": "decode W4A8 GEMM (gemm_stream_kernel: TMA bulk weight stream, mma.sync "
+                                   "int4 x int8, stream-K)", "bound": "hbm",
                          "achieved": round(gemm_gbs, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(gemm_gbs / hbm, 4), "peak_kind": peak_kind,
                          "traffic": traffic,
