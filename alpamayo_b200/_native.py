@@ -81,6 +81,7 @@ def capi() -> ctypes.CDLL:
         "paro_w4a8_linear_group": (i32, [i32, vp, i32, vp, vp, vp, ctypes.c_float, i64, i32, i32, vp, vp, vp, i32,
                                          vp, vp, i32, vp, i32, vp, sz, vp, sz, vp]),
         "paro_w4a8_gemm_noalloc": (i32, [vp, vp, i64, i32, i32, vp, vp, i32, vp, i32, vp]),
+        "paro_w4a8_gemm_multicast": (i32, [vp, vp, i64, i32, i32, vp, vp, i32, vp, vp]),
         "paro_add_rmsnorm": (i32, [vp, vp, vp, i64, i32, ctypes.c_float, vp, vp]),
         "paro_silu_mul": (i32, [vp, i64, i32, vp, vp]),
     }

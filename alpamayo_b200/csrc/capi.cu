@@ -54,7 +54,7 @@ cudaError_t launch_gemm_rows(const int8_t* xq, const float* xscale, int64_t M, i
 cudaError_t launch_gemm_tc_tile(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
                                 const void* bias, int bias_dtype, void* out, int out_dtype, void* workspace,
                                 size_t workspace_bytes, int T, const int* tab_nb, int bt, cudaStream_t st,
-                                uint32_t* zero_after, int zero_n);
+                                uint32_t* zero_after, int zero_n, int out_mc);
 cudaError_t launch_selftest_wait(long long limit_cycles, cudaStream_t st);
 cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
                            const void* bias, int bias_dtype, void* out, int out_dtype, void* ws, size_t ws_bytes,
@@ -618,6 +618,19 @@ int paro_w4a8_gemm(const int8_t* xq, const float* xscale, int64_t M, int N, int 
                                         (cudaStream_t)stream));
 }
 
+int paro_w4a8_gemm_multicast(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
+                             const void* bias, int bias_dtype, void* out_multicast, paro_stream_t stream) {
+  if (M == 0 && N > 0 && K > 0) return PARO_OK;
+  if (!xq || !xscale || !packed || !out_multicast || M < 0 || N <= 0 || K <= 0) return PARO_ERR_INVALID_ARGUMENT;
+  if (bias && !valid_dtype(bias_dtype)) return PARO_ERR_UNSUPPORTED;
+  if (N % kRecRows || K % kGroup) return PARO_ERR_SHAPE;
+  if (!aligned(packed, 16) || !aligned(xq, 16) || !aligned(out_multicast, 16)) return PARO_ERR_MISALIGNED;
+  if (int d = device_check()) return d;
+  const int nb0 = 0;
+  return cuda_status(launch_gemm_tc_tile(xq, xscale, M, N, K, packed, bias, bias_dtype, out_multicast, PARO_BF16,
+                                         nullptr, 0, 1, &nb0, 0, (cudaStream_t)stream, nullptr, 0, 1));
+}
+
 // tokens the streaming decode kernel is built and tuned for
 constexpr int64_t kStreamMaxTokens = 64;
 // ... and the one-row-block-per-warp decode kernel
@@ -672,7 +685,7 @@ int paro_w4a8_gemm_route(int route, const int8_t* xq, const float* xscale, int64
   if (workspace_bytes < need || (need && !workspace)) return PARO_ERR_WORKSPACE;
   const int nb0 = 0;
   return cuda_status(launch_gemm_tc_tile(xq, xscale, M, N, K, packed, bias, bias_dtype, out, out_dtype, workspace,
-                                         workspace_bytes, 1, &nb0, bt, (cudaStream_t)stream, nullptr, 0));
+                                         workspace_bytes, 1, &nb0, bt, (cudaStream_t)stream, nullptr, 0, 0));
 }
 
 }  // extern "C"

@@ -807,7 +807,7 @@ cudaError_t launch_gemm_tc_sets(const int8_t* xq, const float* xscale, int64_t M
 cudaError_t launch_gemm_tc_tile(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
                                 const void* bias, int bias_dtype, void* out, int out_dtype, void* workspace,
                                 size_t workspace_bytes, int T, const int* tab_nb, int bt, cudaStream_t st,
-                                uint32_t* zero_after, int zero_n);
+                                uint32_t* zero_after, int zero_n, int out_mc);
 int gemm_tc_sets_ok(int T, const int* tab_nb);
 
 // Linears of up to 64 tokens whose GEMM is faster on the tensor cores
@@ -908,7 +908,7 @@ cudaError_t launch_linear_decode_tables(const void* x, int x_dtype, const RotTab
     // dependent launch) returns the row maxima to zero once the quantiser has
     // completed
     return launch_gemm_tc_tile(xq, xs, M, N, K, packed, bias, bias_dtype, out, out_dtype, tcb ? ws : nullptr, tcb, T,
-                               tab_nb, 0, st, p.amax, (int)(T * M));
+                               tab_nb, 0, st, p.amax, (int)(T * M), 0);
   }
   if (T == 1 && rows_kernel_enabled()) {
     e = launch_gemm_rows(xq, xs, M, N, K, packed, bias, bias_dtype, out, out_dtype, ws, p.amax, gsum, Mp, st, 0);

@@ -114,6 +114,9 @@ struct TcParams {
   // row maxima): zeroed once that kernel has completed, or null
   uint32_t* zero_after;
   int zero_n;
+  // out is an NVLink multicast address: bf16 stores as multimem.st (the
+  // other ranks' copies of the buffer receive them too)
+  int out_mc;
 };
 
 // The activation set of the 256-row tile starting at output row n.
@@ -238,6 +241,32 @@ __device__ __forceinline__ void store_row(const uint64_t (&y)[NP], T* __restrict
       out[(size_t)(2 * j) * N] = from_f32<T>(f.x * a.x + bias);
       if (2 * j + 1 < valid) out[(size_t)(2 * j + 1) * N] = from_f32<T>(f.y * a.y + bias);
     }
+  }
+}
+
+// The same stores as store_row for bf16 output written through an NVLink
+// multicast address (every GPU bound to the multicast object receives them;
+// multimem stores are at least 32 bits wide): lanes 2i and 2i + 1 hold
+// output columns n and n + 1; per token pair the even lane stores token 2j's
+// two columns and the odd lane token 2j + 1's, after one exchange.  All lanes
+// of the warp call it (ok: this lane's row is inside the layer).
+template <int NP>
+__device__ __forceinline__ void store_row_mc(const uint64_t (&y)[NP], __nv_bfloat16* out, int N,
+                                             const float* __restrict__ xs, float bias, int valid, bool ok,
+                                             int lane) {
+  const bool odd = lane & 1;
+#pragma unroll
+  for (int j = 0; j < NP; ++j) {
+    const float2 f = unpack2(y[j]);
+    const float2 a = *reinterpret_cast<const float2*>(xs + 2 * j);
+    const float v0 = f.x * a.x + bias, v1 = f.y * a.y + bias;   // tokens 2j, 2j + 1 of this column
+    const float recv = __shfl_xor_sync(0xffffffffu, odd ? v0 : v1, 1);
+    const int tok = 2 * j + (odd ? 1 : 0);
+    const __nv_bfloat16 lo = __float2bfloat16_rn(odd ? recv : v0), hi = __float2bfloat16_rn(odd ? v1 : recv);
+    const uint32_t w = (uint32_t)__bfloat16_as_ushort(lo) | ((uint32_t)__bfloat16_as_ushort(hi) << 16);
+    __nv_bfloat16* dst = out + (size_t)tok * N - (odd ? 1 : 0);
+    if (ok && tok < valid)
+      asm volatile("multimem.st.global.bf16x2 [%0], %1;" ::"l"(dst), "r"(w) : "memory");
   }
 }
 
@@ -520,7 +549,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
       const int n = n0 + row;
       const int64_t mbase = m0 + col0;
       const int valid = (int)(p.M - mbase < kCols ? (p.M - mbase > 0 ? p.M - mbase : 0) : kCols);
-      if (p.splits == 1) {
+      if (p.out_mc) {
+        // bf16 through the multicast address (no split-K in this mode)
+        const float bn = row_ok ? tc_bias(p.bias, p.bias_dtype, n) : 0.f;
+        store_row_mc(y, static_cast<__nv_bfloat16*>(p.out) + mbase * p.N + n, p.N, xs, bn, valid,
+                     !failed && row_ok, lane);
+      } else if (p.splits == 1) {
         if (!failed && row_ok) {
           const float bn = tc_bias(p.bias, p.bias_dtype, n);
           if (p.out_dtype == PARO_BF16)
@@ -582,6 +616,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     }
   }
 
+  // multicast stores: ordered before whatever follows the kernel at system
+  // scope (the caller's cross-rank barrier)
+  if (p.out_mc && warp >= 8) __threadfence_system();
   // every role of both CTAs reaches this point; the pair's tensor memory is
   // freed once neither CTA reads it any more
   tc_fence_before();
@@ -699,7 +736,7 @@ int gemm_tc_sets_ok(int T, const int* tab_nb) {
 cudaError_t launch_gemm_tc_tile(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
                                 const void* bias, int bias_dtype, void* out, int out_dtype, void* workspace,
                                 size_t workspace_bytes, int T, const int* tab_nb, int bt, cudaStream_t st,
-                                uint32_t* zero_after, int zero_n) {
+                                uint32_t* zero_after, int zero_n, int out_mc) {
   auto encode = get_encode();
   if (!encode) return cudaErrorNotSupported;
   if (bt == 0) bt = gemm_tc_tile(M, N, K);
@@ -742,8 +779,10 @@ cudaError_t launch_gemm_tc_tile(const int8_t* xq, const float* xscale, int64_t M
   for (int t = 0; t < kMaxTables; ++t) p.tab_nb[t] = t < T ? tab_nb[t] : 0;
   p.zero_after = zero_n > 0 ? zero_after : nullptr;
   p.zero_n = zero_n > 0 ? zero_n : 0;
+  p.out_mc = out_mc ? 1 : 0;
+  if (out_mc && out_dtype != PARO_BF16) return cudaErrorInvalidValue;
   const size_t wsb = gemm_tc_workspace_tile(M, N, K, bt);
-  if (wsb && workspace && workspace_bytes >= wsb) {
+  if (wsb && workspace && workspace_bytes >= wsb && !out_mc) {
     p.splits = tc_splits(M, N, K, bt);
     p.ws = static_cast<unsigned long long*>(workspace);
     p.cnt = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(workspace) +
@@ -785,7 +824,7 @@ cudaError_t launch_gemm_tc_sets(const int8_t* xq, const float* xscale, int64_t M
                                 const void* bias, int bias_dtype, void* out, int out_dtype, void* workspace,
                                 size_t workspace_bytes, int T, const int* tab_nb, cudaStream_t st) {
   return launch_gemm_tc_tile(xq, xscale, M, N, K, packed, bias, bias_dtype, out, out_dtype, workspace,
-                             workspace_bytes, T, tab_nb, 0, st, nullptr, 0);
+                             workspace_bytes, T, tab_nb, 0, st, nullptr, 0, 0);
 }
 
 cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int N, int K, const void* packed,
@@ -793,7 +832,7 @@ cudaError_t launch_gemm_tc(const int8_t* xq, const float* xscale, int64_t M, int
                            size_t workspace_bytes, cudaStream_t st) {
   const int nb0 = 0;
   return launch_gemm_tc_tile(xq, xscale, M, N, K, packed, bias, bias_dtype, out, out_dtype, workspace,
-                             workspace_bytes, 1, &nb0, 0, st, nullptr, 0);
+                             workspace_bytes, 1, &nb0, 0, st, nullptr, 0, 0);
 }
 
 }  // namespace paro

@@ -284,6 +284,71 @@ class ColumnShardedLinear:
         dist.all_reduce(self._flag, group=self.group)
         return out
 
+    def multicast_gathered(self, x, quantise, packed, K):
+        """The gather done by the GEMM's own epilogue: every rank's copy of a
+        [world, M, N / world] bf16 buffer in torch symmetric memory is bound
+        to one NVLink multicast object, and this rank's W4A8 GEMM
+        (paro_w4a8_gemm_multicast) stores its block through the multicast
+        address, so the NVSwitch delivers it to every rank while the GEMM
+        runs; a one-word all-reduce then makes the whole buffer valid.
+        `quantise(x)` returns the int8 activations and token scales of x
+        (the rotation + quantiser of the linear); `packed` is this rank's
+        column block of tile records.  Two buffers alternate, so the result
+        of a call stays valid until the call after next (the closing
+        all-reduce of the next call orders a peer's writes after this rank's
+        use).
+        Raises RuntimeError where the GPUs have no multicast support.
+        close_multicast_buffers() frees the buffers (collective)."""
+        import ctypes
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+        from ._native import capi
+        M = x.shape[0]
+        if self.world == 1:
+            raise RuntimeError("multicast gather needs more than one rank")
+        key = (M, self._n, x.device)
+        if getattr(self, "_mc", None) is None or self._mc["key"] != key:
+            self.close_multicast_buffers()
+            group = self.group if self.group is not None else dist.group.WORLD
+            bufs, hdls = [], []
+            for _ in range(2):
+                buf = symm_mem.empty((self.world, M, self._n), dtype=torch.bfloat16, device=x.device)
+                hdl = symm_mem.rendezvous(buf, group)
+                if not hdl.has_multicast_support or not hdl.multicast_ptr:
+                    raise RuntimeError("no NVLink multicast support for this group")
+                bufs.append(buf)
+                hdls.append(hdl)
+            self._mc = {"key": key, "bufs": bufs, "hdls": hdls, "next": 0,
+                        "flag": torch.zeros(1, dtype=torch.int32, device=x.device)}
+        mc = self._mc
+        b = mc["next"]
+        mc["next"] ^= 1
+        hdl = mc["hdls"][b]
+        xq, xs = quantise(x)
+        dst = hdl.multicast_ptr + hdl.rank * M * self._n * 2
+        st = capi().paro_w4a8_gemm_multicast(xq.data_ptr(), xs.data_ptr(), M, self._n, K, packed.data_ptr(), None, 0,
+                                             ctypes.c_void_p(dst),
+                                             ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        if st:
+            raise RuntimeError(f"paro_w4a8_gemm_multicast: {capi().paro_status_string(st).decode()}")
+        # a one-word all-reduce as the cross-rank barrier (the process
+        # group's timeout bounds it on the host): a peer's contribution
+        # arrives only after its GEMM's multicast stores, which the kernel
+        # orders at system scope
+        dist.all_reduce(mc["flag"], group=self.group)
+        return mc["bufs"][b]
+
+    def close_multicast_buffers(self):
+        """Drop the multicast_gathered buffers (every rank calls it, after a
+        barrier, so that no peer still writes into them)."""
+        mc = getattr(self, "_mc", None)
+        if mc is not None:
+            import torch.distributed as dist
+            torch.cuda.synchronize()
+            dist.barrier(group=self.group)
+            self._mc = None
+            del mc
+
     def close_peer_buffers(self):
         """Unmap and free the peer_gathered buffers (every rank calls it)."""
         pb = getattr(self, "_peer", None)

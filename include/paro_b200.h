@@ -399,6 +399,23 @@ int paro_w4a8_gemm_route(int route, const int8_t* xq, const float* xscale, int64
                          const void* packed, const void* bias, int bias_dtype, void* out, int out_dtype,
                          void* workspace, size_t workspace_bytes, paro_stream_t stream);
 
+/* ---- GEMM into every rank's copy of a buffer (no counterpart in the
+ * reference) --------------------------------------------------------------
+ * The tensor-core GEMM with bf16 output stored through an NVLink multicast
+ * address (multimem.st): every GPU whose memory is bound to the multicast
+ * object receives the [M, N] result at the same offset, so a column-sharded
+ * linear's blocks reach every rank from the GEMM's own epilogue, with no
+ * separate gather.  out_multicast: the multicast address of this rank's
+ * [M, N] block (16-byte aligned), e.g. a torch symmetric-memory buffer's
+ * multicast pointer plus the block's byte offset.  No split-K (no
+ * workspace).  The stores are ordered before whatever follows on the stream
+ * at system scope; the caller's cross-rank barrier then makes the whole
+ * buffer valid on every rank.  Arguments are otherwise those of
+ * paro_w4a8_gemm. */
+int paro_w4a8_gemm_multicast(const int8_t* xq, const float* xscale, int64_t M, int N, int K,
+                             const void* packed, const void* bias, int bias_dtype,
+                             void* out_multicast, paro_stream_t stream);
+
 /* ---- Allocation-free GEMM (no counterpart in the reference) --------------
  * paro_w4a8_gemm without a caller-provided workspace, for callers that may
  * not allocate device memory when they run a layer: an engine whose memory
