@@ -71,6 +71,20 @@ def test_argument_validation_before_launch():
     assert L.paro_prepare_weights(dummy, dummy, dummy, 256, 256, 0, dummy, None) == 2  # G_pad < K/128
     # M == 0 is a no-op success
     assert L.paro_quant_int8(dummy, 2, 0, 256, dummy, dummy, None) == 0
+    # explicit-route GEMM: unknown route, shape, misaligned weights, the
+    # streaming kernel above 64 tokens and the row-block kernel above 16
+    args = (dummy, dummy, 4, 256, 256, dummy, None, 0, dummy, 0, dummy, 1 << 20, None)
+    assert L.paro_w4a8_gemm_route(9, *args) == 1
+    assert L.paro_w4a8_gemm_route(3, dummy, dummy, 4, 100, 256, dummy, None, 0, dummy, 0, dummy, 1 << 20, None) == 2
+    assert L.paro_w4a8_gemm_route(3, dummy, dummy, 4, 256, 256, ctypes.c_void_p(8), None, 0, dummy, 0, dummy,
+                                  1 << 20, None) == 4
+    assert L.paro_w4a8_gemm_route_workspace_size(1, 65, 256, 256) == 0
+    assert L.paro_w4a8_gemm_route_workspace_size(4, 17, 256, 256) == 0
+    assert L.paro_w4a8_gemm_route(3, dummy, dummy, 0, 256, 256, dummy, None, 0, dummy, 0, None, 0, None) == 0
+    # multicast GEMM: null or misaligned destination, shape
+    assert L.paro_w4a8_gemm_multicast(dummy, dummy, 4, 256, 256, dummy, None, 0, None, None) == 1
+    assert L.paro_w4a8_gemm_multicast(dummy, dummy, 4, 256, 256, dummy, None, 0, ctypes.c_void_p(20), None) == 4
+    assert L.paro_w4a8_gemm_multicast(dummy, dummy, 4, 100, 256, dummy, None, 0, dummy, None) == 2
 
 
 def test_gemm_kernel_choice_by_shape():
