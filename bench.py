@@ -922,50 +922,69 @@ def main():
     e2e = None
     if not a.no_e2e:
         hx = {k: v.cpu().pin_memory() for k, v in xs.items()}
-        dx = {k: torch.empty_like(v) for k, v in xs.items()}
+        dxs = [{k: torch.empty_like(v) for k, v in xs.items()} for _ in range(2)]
         hy = {(ri, name): torch.empty((M, N), dtype=torch.bfloat16).pin_memory()
               for ri, M in enumerate(DECODE_M) for (name, N, K) in SHAPES}
         h2d = sum(v.numel() * 2 for v in xs.values())
         d2h = sum(v.numel() * 2 for v in hy.values())
+        copy_stream = torch.cuda.Stream()
 
-        def e2e_step():
-            # the benchmark step (STEP_SWEEPS sweeps) with its inputs copied
-            # in from pinned host memory first and the last sweep's outputs
-            # copied out at the end
-            for k in dx:
-                dx[k].copy_(hx[k], non_blocking=True)
+        def e2e_step(par):
+            # the benchmark step (STEP_SWEEPS sweeps) as a serving loop runs
+            # it: its inputs were copied in from pinned host memory during
+            # the step before (double-buffered device inputs); the next
+            # step's inputs are copied in on a side stream while this one
+            # computes, and the last sweep's outputs are copied out on that
+            # stream as soon as each is produced; the step ends when every
+            # copy has landed
+            main = torch.cuda.current_stream()
+            cur, nxt = dxs[par], dxs[1 - par]
+            copy_stream.wait_stream(main)
+            with torch.cuda.stream(copy_stream):
+                for k in nxt:
+                    nxt[k].copy_(hx[k], non_blocking=True)
             for sw in range(STEP_SWEEPS):
                 for ri, M in enumerate(DECODE_M):
                     for (name, N, K) in SHAPES:
                         L = reps[ri][name]
-                        y = ops.linear_w4a8(dx[(M, K)], L["rot_table"], L["cs_vec"], L["packed"], N, None, True,
+                        y = ops.linear_w4a8(cur[(M, K)], L["rot_table"], L["cs_vec"], L["packed"], N, None, True,
                                             torch.bfloat16)
                         if sw == STEP_SWEEPS - 1:
-                            hy[(ri, name)].copy_(y, non_blocking=True)
+                            copy_stream.wait_stream(main)
+                            with torch.cuda.stream(copy_stream):
+                                hy[(ri, name)].copy_(y, non_blocking=True)
+            main.wait_stream(copy_stream)
 
-        s2 = torch.cuda.Stream()
-        s2.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(s2):
-            e2e_step()
-        torch.cuda.current_stream().wait_stream(s2)
-        g2 = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g2):
-            e2e_step()
-        for _ in range(a.warmup):
-            g2.replay()
+        for k in dxs[0]:
+            dxs[0][k].copy_(hx[k])
+        graphs = []
+        for par in range(2):
+            s2 = torch.cuda.Stream()
+            s2.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s2):
+                e2e_step(par)
+            torch.cuda.current_stream().wait_stream(s2)
+            g2 = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g2):
+                e2e_step(par)
+            graphs.append(g2)
+        for i in range(2 * a.warmup):
+            graphs[i % 2].replay()
+        torch.cuda.synchronize()
         barrier_sync(world)
         t0 = time.perf_counter()
-        for _ in range(a.steps):
-            g2.replay()
+        for i in range(a.steps):
+            graphs[i % 2].replay()
             torch.cuda.synchronize()  # the step's results are read on the host
         barrier_sync(world)
         el = max_over_ranks((time.perf_counter() - t0) / a.steps, world)
         e2e = {"value": world * STEP_SWEEPS * wset / el / 1e9, "unit": "GB/s", "h2d_bytes_per_step": h2d,
                "d2h_bytes_per_step": d2h, "ms_per_step": el * 1e3,
                "path": f"torch.ops.paro_b200.linear_w4a8 per linear, the benchmark step ({STEP_SWEEPS} sweeps) "
-                       "with pinned host inputs copied in and outputs copied out, CUDA graph replay + host "
-                       "sync per step, host wall clock"}
-        del g2
+                       "with pinned host inputs copied in (double-buffered: the next step's during this one) and "
+                       "the outputs copied out as they are produced, CUDA graph replay + host sync per step, host "
+                       "wall clock"}
+        del graphs
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
