@@ -898,7 +898,7 @@ def main():
     gemm_step_bytes = STEP_SWEEPS * sum(gemm_alg_bytes(M, N, K) for M in DECODE_M for (_, N, K) in SHAPES)
     gemm_gbs = gemm_step_bytes / gemm_step_s / 1e9
     del gg, qx, gy
-    traffic = profile_traffic("gemm_decode_gate_up_m8.md")
+    traffic = profile_traffic("gemm_decode_sweep_traffic.md")
 
     # --- prefill: tcgen05 GEMM and activation kernel per shape
     stack = None if a.no_stack else stack_section(torch, world, rank)
@@ -1009,6 +1009,8 @@ def main():
                          "achieved": round(gemm_gbs, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(gemm_gbs / hbm, 4), "peak_kind": peak_kind,
                          "traffic": traffic,
+                         "traffic_source": "mean DRAM bytes per launch of the sweep's 12 GEMM launches, one ncu "
+                                           "capture (profiles/gemm_decode_sweep_traffic.md)",
                          "alg_bytes": "N*K/2 + G*N*2 + G*N/2 + M*K + 4M + 2*M*N per launch",
                          "avg_launch_us": round(gemm_step_s / gemm_launches * 1e6, 3),
                          "timing": f"the step's {gemm_launches} GEMM launches (16 sweeps x 12 cases, 3 weight "
