@@ -55,6 +55,8 @@ def capi() -> ctypes.CDLL:
         "paro_version": (i32, []),
         "paro_last_cuda_error": (ctypes.c_char_p, []),
         "paro_prepare_rotation": (i32, [vp, vp, i32, i32, i32, vp, vp, vp]),
+        "paro_rotation_table_words": (sz, [i32, i32]),
+        "paro_prepare_rotation_matrices": (i32, [vp, i32, vp]),
         "paro_rotate": (i32, [vp, i32, i64, i32, vp, vp, i32, vp, i32, i32, vp, vp]),
         "paro_rotq_int8": (i32, [vp, i32, i64, i32, vp, vp, i32, i32, i32, vp, vp, vp]),
         "paro_rotq_int8_workspace_size": (sz, [i64, i32, i32]),

@@ -24,6 +24,7 @@ cudaError_t launch_rotq_rows(int x_dtype, const void* x, int64_t M, int K, const
 cudaError_t launch_quant(int x_dtype, const void* x, int64_t M, int K, int8_t* q, float* s, cudaStream_t st);
 cudaError_t launch_prepare_rotation(const int16_t* pairs, const uint16_t* theta, int krot, int K, int group,
                                     uint32_t* out, int32_t* bad, cudaStream_t st);
+cudaError_t launch_prepare_rotation_matrices(uint32_t* table, int K, cudaStream_t st);
 cudaError_t launch_prepare_wq(const int16_t* qweight, const uint16_t* scales, const uint16_t* scaled_zeros, int N,
                               int K, void* packed, cudaStream_t st);
 cudaError_t launch_prepare_awq(const int32_t* qweight, const uint16_t* scales, const int32_t* qzeros, int N, int K,
@@ -141,6 +142,19 @@ int paro_prepare_rotation(const int16_t* pairs, const uint16_t* theta, int krot,
   if (K % group) return PARO_ERR_SHAPE;
   if (int d = device_check()) return d;
   return cuda_status(launch_prepare_rotation(pairs, theta, krot, K, group, out_table, bad, (cudaStream_t)stream));
+}
+
+size_t paro_rotation_table_words(int K, int with_matrices) {
+  if (K <= 0 || K % kGroup) return 0;
+  return (size_t)(with_matrices ? 8 + 128 : 8) * (size_t)K;
+}
+
+int paro_prepare_rotation_matrices(uint32_t* table, int K, paro_stream_t stream) {
+  if (!table || K <= 0) return PARO_ERR_INVALID_ARGUMENT;
+  if (K % kGroup) return PARO_ERR_SHAPE;
+  if (!aligned(table, 16)) return PARO_ERR_MISALIGNED;
+  if (int d = device_check()) return d;
+  return cuda_status(launch_prepare_rotation_matrices(table, K, (cudaStream_t)stream));
 }
 
 int paro_rotate(const void* x, int x_dtype, int64_t M, int K, const void* scales, const void* theta,

@@ -16,7 +16,10 @@
 //    partner's thread through shared memory once per layer; column k is
 //    then scaled by s_k.  R' is split into bf16 hi + lo (hi = bf16(R'), lo =
 //    bf16(R' - hi)) and written in the UMMA K-major 128-byte-swizzle layout.
-//    The first tiles' loads are issued before it.
+//    The first tiles' loads are issued before it.  A table that carries
+//    the matrices (paro_prepare_rotation_matrices: the same build, once per
+//    group at load time) skips the eight layers: each thread loads its 64
+//    entries of R_g and only scales and splits them (bit-identical).
 //  * Producer thread: tensor TMA of the 128-row x 128-channel bf16 tile
 //    (two 64-channel boxes, 128-byte swizzle), 3 stages.
 //  * MMA thread: 8 MMAs (M = 128 rows, N = 128 channels, K = 16) with R'_hi,
@@ -49,6 +52,9 @@ constexpr int kRtStages = 3;
 constexpr int kRtRows = 128;                     // rows per tile (MMA M)
 constexpr int kRtTileBytes = kRtRows * 128 * 2;  // 32 KB bf16 tile
 constexpr int kRtRBytes = 128 * 128 * 2;         // one bf16 128 x 128 matrix
+// bit 15 of table word 0 (never set by the table builder): the table carries
+// each group's rotation matrix after its 8 x K words
+constexpr uint32_t kRotMatricesFlag = 0x8000u;
 // shared memory plan (from a 1024-byte aligned base)
 constexpr int kOffRhi = 0;
 constexpr int kOffRlo = kOffRhi + kRtRBytes;
@@ -114,6 +120,58 @@ __device__ __forceinline__ uint32_t sw128_off(int n, int k) {
   return (uint32_t)(h * 16384 + (n >> 3) * 1024 + (n & 7) * 128 + ((c ^ (n & 7)) << 4) + e * 2);
 }
 
+// Component n of R_g e_k for the 32 columns k = k0 .. k0 + 31, by thread n
+// of a 128-thread half h (named barrier 1 + h): v[j] starts as e_{k0+j}[n]
+// and goes through the eight layers, exchanging with the partner's thread
+// through ex ([32 columns][128 rows] f32) once per layer.  The rotation
+// kernel's own build and the load-time kernel below both run this function,
+// so a matrix built ahead of time is bit-identical to one built in place.
+__device__ __forceinline__ void rt_build_columns(const uint32_t* tab, float* ex, int h, int n, int k0,
+                                                 float (&v)[32]) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = (n == k0 + j) ? 1.f : 0.f;
+#pragma unroll 1
+  for (int l = 0; l < 8; ++l) {
+    const uint32_t w = tab[l * 128 + n];
+    const int partner = (int)(w & 0x7F);
+    // exchange slots from the table (bits 8-14): every warp's 32 writes
+    // and 32 reads fall in 32 different banks
+    const int s_me = (int)((w >> 8) & 0x7F), s_pt = (int)((tab[l * 128 + partner] >> 8) & 0x7F);
+    float s_, c_;
+    __sincosf(half_bits_to_f32((uint16_t)(w >> 16)), &s_, &c_);
+    const float cp = ((w >> 7) & 1) ? -s_ : s_;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) ex[j * 128 + s_me] = v[j];
+    named_barrier(1 + h, 128);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = givens(v[j], ex[j * 128 + s_pt], c_, cp);
+    named_barrier(1 + h, 128);
+  }
+}
+
+// Row n, columns k .. k + 7 of R'_g = R_g diag(s_g) from the unscaled r[0..7]:
+// scaled in f32, split into bf16 hi = bf16(R'), lo = bf16(R' - hi), written
+// at their places in the two swizzled matrices.
+__device__ __forceinline__ void rt_store_split(uint8_t* smem, const uint16_t* scales, int g, int n, int k,
+                                               const float* r) {
+  uint32_t hi[4], lo[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    float a[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e)
+      a[e] = r[2 * q + e] * (scales ? half_bits_to_f32(scales[g * 128 + k + 2 * q + e]) : 1.f);
+    const __nv_bfloat162 bh = __floats2bfloat162_rn(a[0], a[1]);
+    const float2 fh = __bfloat1622float2(bh);
+    const __nv_bfloat162 bl = __floats2bfloat162_rn(a[0] - fh.x, a[1] - fh.y);
+    hi[q] = *reinterpret_cast<const uint32_t*>(&bh);
+    lo[q] = *reinterpret_cast<const uint32_t*>(&bl);
+  }
+  const uint32_t off = sw128_off(n, k);
+  *reinterpret_cast<uint4*>(smem + kOffRhi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+  *reinterpret_cast<uint4*>(smem + kOffRlo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+}
+
 }  // namespace
 
 struct RtParams {
@@ -164,9 +222,13 @@ __global__ void __launch_bounds__(kRtThreads, 1) rot_tc_kernel(const __grid_cons
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  // the group's table words, for the build
+  // R_g prebuilt at load time (flag in word 0, 16-byte aligned trailer), or
+  // the group's table words for the build
+  const bool prebuilt =
+      (__ldg(p.rtab) & kRotMatricesFlag) != 0 && (reinterpret_cast<uintptr_t>(p.rtab) & 15) == 0;
   uint32_t* tab = reinterpret_cast<uint32_t*>(smem + kOffTab);
-  for (int i = t; i < 8 * 128; i += kRtThreads) tab[i] = __ldg(p.rtab + (size_t)(i >> 7) * p.K + g * 128 + (i & 127));
+  if (!prebuilt)
+    for (int i = t; i < 8 * 128; i += kRtThreads) tab[i] = __ldg(p.rtab + (size_t)(i >> 7) * p.K + g * 128 + (i & 127));
   fence_before();
   __syncthreads();
   fence_after();
@@ -182,51 +244,30 @@ __global__ void __launch_bounds__(kRtThreads, 1) rot_tc_kernel(const __grid_cons
     }
   }
 
-  // ---- build R'_g = R_g diag(s_g), split into bf16 hi + lo -------------
+  // ---- R'_g = R_g diag(s_g), split into bf16 hi + lo ---------------------
   if (t < 256) {
     const int h = t >> 7, n = t & 127;   // half h: columns k = 64h .. 64h + 63
-    float* ex = reinterpret_cast<float*>(smem + kOffEx) + h * (32 * 128);   // [32 cols][128 rows]
-    for (int c0 = 0; c0 < 64; c0 += 32) {
-      float v[32];
+    if (prebuilt) {
+      // R_g from the table's trailer: row n's 64 columns of half h, eight
+      // chunks of 8 (each warp's 32 rows are 1 KB contiguous per chunk)
+      const float4* src = reinterpret_cast<const float4*>(p.rtab + (size_t)8 * p.K) + (size_t)g * 4096;
+      float r[64];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = (n == 64 * h + c0 + j) ? 1.f : 0.f;
-#pragma unroll 1
-      for (int l = 0; l < 8; ++l) {
-        const uint32_t w = tab[l * 128 + n];
-        const int partner = (int)(w & 0x7F);
-        // exchange slots from the table (bits 8-14): every warp's 32 writes
-        // and 32 reads fall in 32 different banks
-        const int s_me = (int)((w >> 8) & 0x7F), s_pt = (int)((tab[l * 128 + partner] >> 8) & 0x7F);
-        float s_, c_;
-        __sincosf(half_bits_to_f32((uint16_t)(w >> 16)), &s_, &c_);
-        const float cp = ((w >> 7) & 1) ? -s_ : s_;
-#pragma unroll
-        for (int j = 0; j < 32; ++j) ex[j * 128 + s_me] = v[j];
-        named_barrier(1 + h, 128);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = givens(v[j], ex[j * 128 + s_pt], c_, cp);
-        named_barrier(1 + h, 128);
+      for (int q = 0; q < 8; ++q) {
+        const size_t i = ((size_t)(8 * h + q) * 128 + n) * 2;
+        const float4 u0 = __ldg(src + i), u1 = __ldg(src + i + 1);
+        r[8 * q + 0] = u0.x; r[8 * q + 1] = u0.y; r[8 * q + 2] = u0.z; r[8 * q + 3] = u0.w;
+        r[8 * q + 4] = u1.x; r[8 * q + 5] = u1.y; r[8 * q + 6] = u1.z; r[8 * q + 7] = u1.w;
       }
 #pragma unroll
-      for (int j = 0; j < 32; j += 8) {
-        uint32_t hi[4], lo[4];
+      for (int q = 0; q < 8; ++q) rt_store_split(smem, p.scales, g, n, 64 * h + 8 * q, &r[8 * q]);
+    } else {
+      float* ex = reinterpret_cast<float*>(smem + kOffEx) + h * (32 * 128);   // [32 cols][128 rows]
+      for (int c0 = 0; c0 < 64; c0 += 32) {
+        float v[32];
+        rt_build_columns(tab, ex, h, n, 64 * h + c0, v);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          float a[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int k = 64 * h + c0 + j + 2 * q + e;
-            a[e] = v[j + 2 * q + e] * (p.scales ? half_bits_to_f32(p.scales[g * 128 + k]) : 1.f);
-          }
-          const __nv_bfloat162 bh = __floats2bfloat162_rn(a[0], a[1]);
-          const float2 fh = __bfloat1622float2(bh);
-          const __nv_bfloat162 bl = __floats2bfloat162_rn(a[0] - fh.x, a[1] - fh.y);
-          hi[q] = *reinterpret_cast<const uint32_t*>(&bh);
-          lo[q] = *reinterpret_cast<const uint32_t*>(&bl);
-        }
-        const uint32_t off = sw128_off(n, 64 * h + c0 + j);
-        *reinterpret_cast<uint4*>(smem + kOffRhi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        *reinterpret_cast<uint4*>(smem + kOffRlo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        for (int j = 0; j < 32; j += 8) rt_store_split(smem, p.scales, g, n, 64 * h + c0 + j, &v[j]);
       }
     }
   }
@@ -402,6 +443,39 @@ cudaError_t launch_rot_tc(const void* x, int64_t M, int K, const uint16_t* scale
   cudaError_t e = ensure_smem_limit((const void*)rot_tc_kernel, kRtSmem);
   if (e != cudaSuccess) return e;
   rot_tc_kernel<<<(unsigned)(p.G * splits), kRtThreads, kRtSmem, st>>>(xmap, ymap, p);
+  return cudaGetLastError();
+}
+
+// Load-time: the rotation matrix R_g of every group of a krot-8, group-128
+// table, written after the table's 8 x K words (g * 16384 floats from there,
+// element (n, k) at ((k / 8) * 128 + n) * 8 + k % 8), then the flag set in
+// word 0.  One CTA per group, the rotation kernel's build arithmetic
+// (rt_build_columns); the flag is set by group 0's CTA after it has read
+// word 0 (no other CTA reads it).
+__global__ void __launch_bounds__(256) rot_matrices_kernel(uint32_t* table, int K) {
+  __shared__ uint32_t tab[8 * 128];
+  __shared__ float ex_all[2 * 32 * 128];
+  const int g = blockIdx.x, t = threadIdx.x, h = t >> 7, n = t & 127;
+  for (int i = t; i < 8 * 128; i += 256) tab[i] = table[(size_t)(i >> 7) * K + g * 128 + (i & 127)];
+  __syncthreads();
+  if (g == 0 && t == 0) atomicOr(table, kRotMatricesFlag);
+  float* ex = ex_all + h * (32 * 128);
+  float4* dst = reinterpret_cast<float4*>(table + (size_t)8 * K) + (size_t)g * 4096;
+  for (int c0 = 0; c0 < 64; c0 += 32) {
+    float v[32];
+    rt_build_columns(tab, ex, h, n, 64 * h + c0, v);
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      const size_t i = ((size_t)((64 * h + c0 + j) >> 3) * 128 + n) * 2;
+      dst[i] = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+      dst[i + 1] = make_float4(v[j + 4], v[j + 5], v[j + 6], v[j + 7]);
+    }
+  }
+}
+
+cudaError_t launch_prepare_rotation_matrices(uint32_t* table, int K, cudaStream_t st) {
+  if (K <= 0 || K % kGroup) return cudaErrorInvalidValue;
+  rot_matrices_kernel<<<(unsigned)(K / kGroup), 256, 0, st>>>(table, K);
   return cudaGetLastError();
 }
 

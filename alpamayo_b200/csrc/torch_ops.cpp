@@ -121,6 +121,29 @@ at::Tensor prepare_rotation(const at::Tensor& pairs, const at::Tensor& theta, in
   return out;
 }
 
+// The table extended with each group's rotation matrix (load time, one
+// launch): int32 [136, K], rows 0-7 the table's words with the matrices flag
+// in word 0, rows 8-135 the matrices (paro_prepare_rotation_matrices).
+at::Tensor prepare_rotation_matrices(const at::Tensor& rot_table) {
+  check_cuda(rot_table, "rot_table");
+  TORCH_CHECK(rot_table.scalar_type() == at::kInt && rot_table.dim() == 2 && rot_table.size(0) == 8,
+              "rot_table must be the int32 [8, K] tensor from prepare_rotation");
+  const int64_t K = rot_table.size(1);
+  TORCH_CHECK(K > 0 && K % 128 == 0, "rot_table: K must be a positive multiple of 128");
+  c10::cuda::CUDAGuard guard(rot_table.device());
+  at::Tensor out = at::empty({(int64_t)(paro_rotation_table_words((int)K, 1) / K), K}, rot_table.options());
+  out.narrow(0, 0, 8).copy_(rot_table);
+  check_status(paro_prepare_rotation_matrices(reinterpret_cast<uint32_t*>(out.data_ptr<int32_t>()), (int)K,
+                                              cur_stream()),
+               "prepare_rotation_matrices");
+  return out;
+}
+
+// A krot-8 table: [8, K], or [136, K] carrying the matrices.
+bool rot8_table(const at::Tensor& t, int64_t K) {
+  return t.dim() == 2 && t.size(1) == K && (t.size(0) == 8 || t.size(0) == 136);
+}
+
 std::tuple<at::Tensor, at::Tensor> rotq_int8(const at::Tensor& x_in, const at::Tensor& rot_table,
                                              const c10::optional<at::Tensor>& scales_opt, int64_t group_size,
                                              bool fp16_round) {
@@ -152,7 +175,8 @@ std::tuple<at::Tensor, at::Tensor> rotq_int8(const at::Tensor& x_in, const at::T
                   : nullptr;
   check_status(paro_rotq_int8_ws(x.data_ptr(), to_paro_dtype(x.scalar_type()), M, (int)K, sp,
                                  reinterpret_cast<const uint32_t*>(rot_table.data_ptr<int32_t>()),
-                                 (int)rot_table.size(0), (int)group_size, fp16_round ? 1 : 0, q.data_ptr<int8_t>(),
+                                 rot8_table(rot_table, K) ? 8 : (int)rot_table.size(0), (int)group_size,
+                                 fp16_round ? 1 : 0, q.data_ptr<int8_t>(),
                                  s.data_ptr<float>(), wsp, wsb, cur_stream()),
                "rotq_int8");
   return {q, s};
@@ -261,7 +285,7 @@ at::Tensor linear_w4a8(const at::Tensor& x_in, const at::Tensor& rot_table,
   check_cuda(packed, "packed");
   TORCH_CHECK(rot_table.scalar_type() == at::kInt, "rot_table must be the int32 tensor from prepare_rotation");
   const int64_t K = x.size(-1);
-  TORCH_CHECK(rot_table.size(-1) == K && rot_table.size(0) == 8, "rot_table must be [8, K]");
+  TORCH_CHECK(rot8_table(rot_table, K), "rot_table must be [8, K] (or [136, K] with the matrices)");
   TORCH_CHECK((size_t)packed.numel() == paro_packed_weight_bytes((int)N, (int)K), "packed weight size mismatch");
   const int64_t M = x.numel() / K;
   const uint16_t* csp = nullptr;
@@ -320,7 +344,7 @@ std::tuple<at::Tensor, at::Tensor> linear_prologue(int prologue, const at::Tenso
   const bool rms = prologue == PARO_PROLOGUE_ADD_RMSNORM;
   const int64_t K = rms ? x.size(-1) : x.size(-1) / 2;
   TORCH_CHECK(rms || x.size(-1) == 2 * K, "silu prologue: input must be [..., 2K]");
-  TORCH_CHECK(rot_table.size(-1) == K && rot_table.size(0) == 8, "rot_table must be [8, K]");
+  TORCH_CHECK(rot8_table(rot_table, K), "rot_table must be [8, K] (or [136, K] with the matrices)");
   TORCH_CHECK((size_t)packed.numel() == paro_packed_weight_bytes((int)N, (int)K), "packed weight size mismatch");
   const int64_t M = x.numel() / x.size(-1);
   const uint16_t* csp = nullptr;
@@ -419,8 +443,8 @@ std::tuple<at::Tensor, at::Tensor> linear_w4a8_group(const at::Tensor& x_in, con
     ns[t] = (int)n_per_table[t];
     N += ns[t];
     check_cuda(rot_tables[t], "rot_table");
-    TORCH_CHECK(rot_tables[t].scalar_type() == at::kInt && rot_tables[t].size(-1) == K && rot_tables[t].size(0) == 8,
-                "rot_tables must be int32 [8, K] tensors from prepare_rotation");
+    TORCH_CHECK(rot_tables[t].scalar_type() == at::kInt && rot8_table(rot_tables[t], K),
+                "rot_tables must be int32 [8, K] (or [136, K]) tensors from prepare_rotation");
     tabs[t] = reinterpret_cast<const uint32_t*>(rot_tables[t].data_ptr<int32_t>());
     if (!channel_scales.empty() && channel_scales[t].defined() && channel_scales[t].numel() > 0) {
       at::Tensor c = channel_scales[t].to(at::kHalf).contiguous();
@@ -533,6 +557,7 @@ extern "C" int paro_torch_reset_workspaces() {
 TORCH_LIBRARY(paro_b200, m) {
   m.def("rotate(Tensor x, Tensor idx_ij, Tensor theta, Tensor? scales, int group_size) -> Tensor");
   m.def("prepare_rotation(Tensor pairs, Tensor theta, int group_size) -> Tensor");
+  m.def("prepare_rotation_matrices(Tensor rot_table) -> Tensor");
   m.def("rotq_int8(Tensor x, Tensor rot_table, Tensor? scales, int group_size, bool fp16_round) -> (Tensor, Tensor)");
   m.def("quant_int8(Tensor x) -> (Tensor, Tensor)");
   m.def("prepare_weights(Tensor qweight, Tensor scales, Tensor scaled_zeros, int N, int K) -> Tensor");
@@ -555,6 +580,7 @@ TORCH_LIBRARY(paro_b200, m) {
 TORCH_LIBRARY_IMPL(paro_b200, CUDA, m) {
   m.impl("rotate", &rotate);
   m.impl("prepare_rotation", &prepare_rotation);
+  m.impl("prepare_rotation_matrices", &prepare_rotation_matrices);
   m.impl("rotq_int8", &rotq_int8);
   m.impl("quant_int8", &quant_int8);
   m.impl("prepare_weights", &prepare_weights);

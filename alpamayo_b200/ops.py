@@ -27,6 +27,11 @@ def _prepare_rotation_fake(pairs, theta, group_size):
     return torch.empty(pairs.shape, dtype=torch.int32, device=pairs.device)
 
 
+@torch.library.register_fake("paro_b200::prepare_rotation_matrices")
+def _prepare_rotation_matrices_fake(rot_table):
+    return torch.empty((136, rot_table.shape[1]), dtype=torch.int32, device=rot_table.device)
+
+
 @torch.library.register_fake("paro_b200::rotq_int8")
 def _rotq_fake(x, rot_table, scales, group_size, fp16_round):
     q = torch.empty(x.shape, dtype=torch.int8, device=x.device)
@@ -74,11 +79,19 @@ def rotate(x, idx_ij, theta, scales=None, group_size=128):
     return _ops.rotate(x, idx_ij, theta, scales, group_size)
 
 
-def prepare_rotation(pairs, theta, group_size=128):
+def prepare_rotation(pairs, theta, group_size=128, matrices=False):
     """Validate the pair table (each layer-group a permutation of 0..127) and
     build the per-channel rotation table (int32 [krot, K]: partner channel,
-    role bit, fp16 angle bits) the fused kernel reads."""
-    return _ops.prepare_rotation(pairs, theta.to(torch.float16).contiguous(), group_size)
+    role bit, exchange slot, fp16 angle bits) the fused kernels read.
+
+    ``matrices=True`` (krot 8 only) also builds each 128-channel group's
+    rotation matrix once, into rows 8-135 of an int32 [136, K] table: the
+    prefill rotation then loads it instead of building it in every CTA
+    (bit-identical results; 512 bytes per channel of device memory)."""
+    table = _ops.prepare_rotation(pairs, theta.to(torch.float16).contiguous(), group_size)
+    if matrices:
+        table = _ops.prepare_rotation_matrices(table)
+    return table
 
 
 def rotq_int8(x, rot_table, scales=None, group_size=128, fp16_round=True):

@@ -61,11 +61,12 @@ class Rotation(nn.Module):
     def rot_table(self) -> torch.Tensor:
         """Per-channel rotation table (partner, role, fp16 angle) built from
         ``pairs`` / ``theta`` after checking that every layer's pairs are
-        disjoint; derived and cached, rebuilt if the buffers change."""
+        disjoint, with each group's rotation matrix for the prefill path
+        (int32 [136, K]); derived and cached, rebuilt if the buffers change."""
         key = (self.pairs.data_ptr(), self.pairs._version, self.theta.data_ptr(), self.theta._version,
                self.pairs.device)
         if self._rot_table is None or self._rot_key != key:
-            self._rot_table = ops.prepare_rotation(self.pairs.contiguous(), self.theta, 128)
+            self._rot_table = ops.prepare_rotation(self.pairs.contiguous(), self.theta, 128, matrices=True)
             self._rot_key = key
         return self._rot_table
 

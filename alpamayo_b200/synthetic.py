@@ -114,7 +114,7 @@ def make_layer(N, K, seed, device="cuda", checkpoint=True, keep_awq=False):
             layer["awq_qweight"], layer["awq_scales"], layer["awq_qzeros"] = awq
         del awq
     del codes
-    layer["rot_table"] = ops.prepare_rotation(pairs, theta, GROUP)
+    layer["rot_table"] = ops.prepare_rotation(pairs, theta, GROUP, matrices=True)
     layer["cs_vec"] = cs.reshape(-1).contiguous()
     return layer
 

@@ -88,6 +88,30 @@ int paro_prepare_rotation(const int16_t* pairs, const uint16_t* theta, int krot,
                           int group, uint32_t* out_table, int32_t* bad,
                           paro_stream_t stream);
 
+/*
+ * Words of a rotation table for K channels: 8·K (krot 8, group 128), or
+ * 136·K with with_matrices = 1.  0 when K is not a positive multiple of 128.
+ */
+size_t paro_rotation_table_words(int K, int with_matrices);
+
+/*
+ * Load-time, optional: extends a krot-8, group-128 table with each group's
+ * 128 x 128 rotation matrix (the eight Givens layers applied to the unit
+ * vectors, fp32, channel scales not included), so that the prefill
+ * activation path (paro_rotq_int8_ws and the linears from
+ * paro_rotq_int8_workspace_size tokens on, bf16 x) loads the matrix instead
+ * of building it in every CTA.  Every result is bit-identical with and
+ * without the matrices; the decode path ignores them.  The reference builds
+ * nothing ahead of time (its rotate kernel applies the layers one by one,
+ * rotation.cuh:280-334).
+ *   table : uint32 [136, K], 16-byte aligned; rows 0-7 from
+ *           paro_prepare_rotation (krot 8), rows 8-135 written here.  Bit 15
+ *           of word 0 (which paro_prepare_rotation never sets) is set to mark
+ *           the table as carrying the matrices: a table so marked must be
+ *           136·K words long.
+ */
+int paro_prepare_rotation_matrices(uint32_t* table, int K, paro_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Activation kernels
  * ------------------------------------------------------------------------ */
@@ -113,7 +137,8 @@ int paro_rotate(const void* x, int x_dtype, int64_t M, int K,
  * (int8_utils.py:106-128).
  *   x            : [M, K] of x_dtype (F32 / F16 / BF16).
  *   scales       : fp16 [K] channel scales or NULL.
- *   rot_table    : uint32 [krot, K] from paro_prepare_rotation.
+ *   rot_table    : uint32 [krot, K] from paro_prepare_rotation (or [136, K]
+ *                  with paro_prepare_rotation_matrices).
  *   fp16_round   : 1 = round the rotated value to fp16 before quantising,
  *                  as the reference does (its rotate kernel stores fp16,
  *                  rotation.cuh:333-334); 0 = quantise the float32 value.
@@ -274,7 +299,8 @@ int paro_selftest_wait_timeout(long long limit_cycles, paro_stream_t stream);
  * tensor-core kernel with 64-token tiles).  Otherwise it is the activation kernel(s)
  * followed by the GEMM.
  *   x             : [M, K] of x_dtype;  channel_scales : fp16 [K] or NULL.
- *   rot_table     : uint32 [8, K] from paro_prepare_rotation (group 128).
+ *   rot_table     : uint32 [8, K] from paro_prepare_rotation (group 128), or
+ *                   [136, K] with paro_prepare_rotation_matrices.
  *   workspace     : paro_w4a8_linear_workspace_size(M, N, K) bytes, 256-byte
  *                   aligned, ZERO-FILLED before first use and left zero-filled
  *                   by every call (as paro_w4a8_gemm's).
@@ -336,7 +362,8 @@ int paro_w4a8_linear_prologue(int prologue, const void* x, const void* residual_
  * y = [linear_0(x) | linear_1(x) | ...], the fused-projection layout
  * (patches.py:144-263).
  *   n_per_table   : host array of T output widths (each a multiple of 16).
- *   rot_tables    : host array of T device tables from paro_prepare_rotation.
+ *   rot_tables    : host array of T device tables from paro_prepare_rotation
+ *                   (each [8, K], or [136, K] with the matrices).
  *   channel_scales: host array of T device fp16 [K] pointers (entries may be
  *                   NULL), or NULL.
  *   packed        : the T layers' tile records concatenated (records are

@@ -62,6 +62,14 @@ def test_argument_validation_before_launch():
     assert L.paro_rotq_int8(dummy, 2, 4, 256, None, dummy, 4, 128, 1, dummy, dummy, None) == 3
     # the rotation table is only built for 128-channel groups
     assert L.paro_prepare_rotation(dummy, dummy, 8, 256, 64, dummy, dummy, None) == 3
+    # table sizes with and without the per-group matrices (128 x 128 fp32
+    # per 128 channels = 128 words per channel)
+    assert L.paro_rotation_table_words(3584, 0) == 8 * 3584
+    assert L.paro_rotation_table_words(3584, 1) == 136 * 3584
+    assert L.paro_rotation_table_words(200, 1) == 0
+    assert L.paro_prepare_rotation_matrices(None, 256, None) == 1
+    assert L.paro_prepare_rotation_matrices(dummy, 200, None) == 2
+    assert L.paro_prepare_rotation_matrices(ctypes.c_void_p(8), 256, None) == 4
     # GEMM shape checks
     assert L.paro_w4a8_gemm(dummy, dummy, 4, 100, 256, dummy, None, 0, dummy, 2, None, 0, None) == 2
     assert L.paro_w4a8_gemm(dummy, dummy, 4, 256, 200, dummy, None, 0, dummy, 2, None, 0, None) == 2
