@@ -34,10 +34,13 @@ constexpr int kRowsGB = 4;      // groups per CTA
 constexpr int kRowsR = 8;       // rows per register chunk
 constexpr int kRowsRB = 16;     // rows per CTA
 
+// Workspace: fp16 rows [M, K] (two-pass mode), row maxima [M], row-tile
+// counters [ceil(M / 128)] (single-pass mode); maxima and counters adjacent,
+// zeroed by one memset.
+static size_t rows_y_bytes(int64_t M, int K) { return ((size_t)M * K * sizeof(__half) + 255) & ~(size_t)255; }
+
 size_t rotq_rows_workspace(int64_t M, int K) {
-  size_t y = (size_t)M * K * sizeof(__half);
-  y = (y + 255) & ~(size_t)255;
-  return y + (size_t)M * sizeof(uint32_t);
+  return rows_y_bytes(M, K) + (size_t)M * sizeof(uint32_t) + (size_t)((M + 127) / 128) * sizeof(uint32_t);
 }
 
 template <typename InT>
@@ -163,20 +166,27 @@ quant_rows_kernel(const __half* __restrict__ y, const uint32_t* __restrict__ ama
 }
 
 cudaError_t launch_rot_tc(const void* x, int64_t M, int K, const uint16_t* scales, const uint32_t* rtab, __half* y,
-                          uint32_t* amax, cudaStream_t st);
+                          uint32_t* amax, int8_t* q, float* qscale, uint32_t* cnt, cudaStream_t st);
+bool rot_tc_single_pass_ok(int K, const void* q);
 
 template <typename InT>
 static cudaError_t launch_rows_t(const void* x, int64_t M, int K, const uint16_t* scales, const uint32_t* rtab,
                                  int8_t* q, float* s, void* ws, cudaStream_t st) {
   __half* y = static_cast<__half*>(ws);
-  uint32_t* amax = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(ws) + (rotq_rows_workspace(M, K) -
-                                                                           (size_t)M * sizeof(uint32_t)));
-  cudaError_t e = cudaMemsetAsync(amax, 0, (size_t)M * sizeof(uint32_t), st);
+  uint32_t* amax = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(ws) + rows_y_bytes(M, K));
+  uint32_t* cnt = amax + M;
+  cudaError_t e = cudaMemsetAsync(amax, 0, rotq_rows_workspace(M, K) - rows_y_bytes(M, K), st);
   if (e != cudaSuccess) return e;
   const int G = K / kGroup;
   if constexpr (std::is_same<InT, __nv_bfloat16>::value) {
-    // bf16 rows: the rotation on the tensor cores (rotq_tc.cu)
-    e = launch_rot_tc(x, M, K, scales, rtab, y, amax, st);
+    // bf16 rows: the rotation on the tensor cores (rotq_tc.cu), with the
+    // quantiser fused where every group's CTA fits the GPU at once
+    if (rot_tc_single_pass_ok(K, q)) {
+      e = launch_rot_tc(x, M, K, scales, rtab, y, amax, q, s, cnt, st);
+      if (e == cudaSuccess) return e;
+      cudaGetLastError();   // not launched (e.g. SMs held elsewhere): two passes
+    }
+    e = launch_rot_tc(x, M, K, scales, rtab, y, amax, nullptr, nullptr, nullptr, st);
   } else {
     dim3 grid1((unsigned)((G + kRowsGB - 1) / kRowsGB), (unsigned)((M + kRowsRB - 1) / kRowsRB));
     rot_rows_kernel<InT><<<grid1, 128 * kRowsGB, 0, st>>>(static_cast<const InT*>(x), M, K, scales, rtab, y, amax);

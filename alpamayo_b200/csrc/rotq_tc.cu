@@ -63,7 +63,8 @@ constexpr int kOffEx = kOffX + kRtStages * kRtTileBytes;   // build: [2 halves][
                                                             // epilogue: the fp16 output tile (32 KB)
 constexpr int kOffTab = kOffEx + 2 * 32 * 128 * 4;          // [8 layers][128] table words
 constexpr int kOffBar = kOffTab + 8 * 128 * 4;
-constexpr int kRtSmem = kOffBar + 256 + 1024;
+constexpr int kOffQ8 = kOffBar + 1024;          // single-pass mode: the int8 tile (16 KB, 1024-aligned)
+constexpr int kRtSmem = kOffQ8 + 16384 + 1024;
 
 // kind::f16 instruction descriptor: f32 accumulate, A and B bf16, both
 // K-major, N = 128, M = 128
@@ -181,20 +182,248 @@ struct RtParams {
   int splits;       // CTAs per group
   const uint16_t* scales;  // fp16 [K] or null
   const uint32_t* rtab;    // [8, K]
-  __half* y;               // [M, K] fp16 out
+  __half* y;               // [M, K] fp16 out (two-pass mode)
   uint32_t* amax;          // [M] row |max| bits (zero on entry)
+  // single-pass mode (quantiser fused): int8 codes, per-token scales, and a
+  // counter per row tile of the groups whose maxima are in (zero on entry)
+  int8_t* q;               // [M, K]
+  float* qscale;           // [M]
+  uint32_t* cnt;           // [tiles]
 };
 
-__global__ void __launch_bounds__(kRtThreads, 1) rot_tc_kernel(const __grid_constant__ CUtensorMap xmap,
-                                                               const __grid_constant__ CUtensorMap ymap, RtParams p) {
+// Round half away from zero, for |v| <= 255, as the low byte of the two's
+// complement integer, with float adds instead of conversions:
+//   s = |v| + 0.5 rounded toward zero lies in [floor(|v| + 0.5), |v| + 0.5]
+//     (the floor is an integer, representable, and rounding toward zero
+//     never passes it), so floor(s) = floor(|v| + 0.5) = round_half_away(|v|);
+//   m = s + 1.5·2^23 rounded toward zero lands in [2^23, 2^24), where the
+//     float32 spacing is 1, so m = 1.5·2^23 + floor(s) and the low byte of
+//     its bit pattern (0x4B400000 + n) is n;
+//   the sign is applied by negating the pattern for negative v (the low
+//   byte of -(0x4B400000 + n) is that of -n).
+// Equal to (int8) roundf(v) for every such v (the single-pass and
+// two-pass quantisers are tested bit-identical, ties included).
+__device__ __forceinline__ uint32_t round_half_away_byte(float v) {
+  const float s = __fadd_rz(fabsf(v), 0.5f);
+  const uint32_t m = __float_as_uint(__fadd_rz(s, 12582912.0f));
+  const uint32_t sg = (uint32_t)(__float_as_int(v) >> 31);
+  return (m ^ sg) - sg;
+}
+
+// Single-pass mode: 16 epilogue warps (warps 2-17), four per TMEM lane
+// quarter, thread = row r of the tile and columns 32·j .. 32·j + 31 of group
+// g (j = the warp's column slice); a signalling warp (18) and a waiting warp
+// (19).  Four TMEM accumulators, so a tile's values stay in tensor memory
+// until its codes are written.  Per tile i:
+//   epilogue A(i): the row's |max| over the 128 columns (the four slices'
+//     maxima combined in shared memory), fp16-rounded, folded into amax
+//     (atomicMax on the bit patterns); the combining warps arrive on
+//     `maxed`.
+//   signalling warp: after `maxed`, one release increment of cnt[tile] for
+//     the CTA.
+//   waiting warp: once cnt[tile] shows every group of the row range in, the
+//     final row maxima are read, 127/a goes to shared memory (and, in group
+//     0's CTAs, the per-token scale a/127 to memory); then `amax_ready`.
+//   epilogue B(i-2), after A(i): the codes of tile i-2 from its accumulator
+//     (fp16-rounded again) and 127/a, staged as an int8 tile (128-byte
+//     swizzle) and written by a tensor TMA store; the accumulator is freed.
+// The other groups' CTAs run the same tiles at the same pace, so a tile's
+// count is complete well before its codes are due and the epilogue never
+// waits on memory.  Every CTA counts itself in for a tile before it waits
+// for any later one's count, A(k) precedes B(k-2), and all CTAs are
+// co-resident (cooperative launch), so the waits always end; each is still
+// bounded (kErrMbarTimeout, kErrGridWait), and after a failure the warps
+// only pass the barriers.  The quantiser's arithmetic is
+// quant_rows_kernel's: a = max(|max|, 1e-10), q = round_half_away(y ·
+// 127/a), scale a/127.
+constexpr int kRtQuantThreads = 640;   // producer, MMA, 16 epilogue warps, signalling and waiting warps
+constexpr int kRtQuantEpi = 512;
+constexpr int kRtSignalWarp = 18;
+constexpr int kRtWaitWarp = 19;
+constexpr int kRtDefer = 2;            // tiles between a tile's maxima and its codes
+
+struct RtQuantBars {
+  uint64_t* maxed;        // [4] tile's maxima issued (4 combining warps)
+  uint64_t* amax_ready;   // [4] 127/a of the tile in shared memory (waiting warp)
+  uint64_t* amax_free;    // [4] the epilogue has read it (16 warps)
+};
+
+struct RtQuantCtx {
+  const RtParams* p;
+  const CUtensorMap* qmap;
+  uint8_t* q8;          // the int8 tile being stored (128 rows x 128 B, 128-byte swizzle)
+  uint32_t* pm;         // [4 slices][128 rows] row maxima
+  const float* inv;     // [4][128] 127/a per row
+  RtQuantBars bars;
+  uint64_t* acc_full;
+  uint64_t* acc_empty;
+  volatile uint32_t* wait_failed;
+  uint32_t tmem, lane_base;
+  int g, tb, ntile, r, j, lane;
+  bool issuer;
+};
+
+__device__ __forceinline__ void rtq_step(const RtQuantCtx& c, int i, bool& failed) {
+  const RtParams& p = *c.p;
+  if (i < c.ntile) {
+    const int b = i & 3;
+    if (!failed && !mbar_wait(&c.acc_full[b], (i >> 2) & 1)) failed = true;
+    uint32_t v[32];
+    if (!failed) {
+      fence_after();
+      tmem_ld32(c.tmem + c.lane_base + (uint32_t)(b * 128 + c.j * 32), v);
+      tmem_wait_ld();
+    }
+    // the |max| of the fp16-rounded values is the fp16 rounding of the
+    // float32 |max| (rounding is monotonic and symmetric); as float32 bits
+    // (non-negative floats order as unsigned integers)
+    float mx = 0.f;
+#pragma unroll
+    for (int k = 0; k < 32; ++k) mx = fmaxf(mx, fabsf(__uint_as_float(v[k])));
+    c.pm[c.j * 128 + c.r] = __float_as_uint(__half2float(__float2half_rn(mx)));
+    // the int8 tile's previous store has read it before B below writes it
+    if (c.issuer) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+    named_barrier(3, kRtQuantEpi);
+    if (c.j == 0) {
+      const uint32_t m = max(max(c.pm[c.r], c.pm[128 + c.r]), max(c.pm[256 + c.r], c.pm[384 + c.r]));
+      const int64_t row = (int64_t)(c.tb + i) * kRtRows + c.r;
+      if (!failed && row < p.M && m) atomicMax(p.amax + row, m);
+      __syncwarp();
+      if (c.lane == 0) mbar_arrive(&c.bars.maxed[b]);   // also after a failure
+    }
+  }
+  const int d = i - kRtDefer;
+  if (d >= 0 && d < c.ntile) {
+    const int tp = c.tb + d, b = d & 3;
+    if (!failed && !mbar_wait(&c.bars.amax_ready[b], (d >> 2) & 1)) failed = true;
+    if (*c.wait_failed) failed = true;
+    const float inv = c.inv[b * 128 + c.r];
+    uint32_t v[32];
+    if (!failed) {
+      tmem_ld32(c.tmem + c.lane_base + (uint32_t)(b * 128 + c.j * 32), v);
+      tmem_wait_ld();
+    }
+    fence_before();
+    __syncwarp();
+    if (c.lane == 0) {
+      mbar_arrive(&c.bars.amax_free[b]);
+      if (!failed) mbar_arrive(&c.acc_empty[b]);   // the MMA may reuse the accumulator
+    }
+    // after the last tile no A phase has waited for the int8 tile's previous
+    // store to read it
+    if (i >= c.ntile) {
+      if (c.issuer) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+      named_barrier(3, kRtQuantEpi);
+    }
+    const int64_t row = (int64_t)tp * kRtRows + c.r;
+    if (!failed && row < p.M) {
+      uint32_t w[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float2 f0 = __half22float2(__floats2half2_rn(__uint_as_float(v[4 * k]), __uint_as_float(v[4 * k + 1])));
+        const float2 f1 =
+            __half22float2(__floats2half2_rn(__uint_as_float(v[4 * k + 2]), __uint_as_float(v[4 * k + 3])));
+        const uint32_t q0 = round_half_away_byte(__fmul_rn(f0.x, inv)), q1 = round_half_away_byte(__fmul_rn(f0.y, inv));
+        const uint32_t q2 = round_half_away_byte(__fmul_rn(f1.x, inv)), q3 = round_half_away_byte(__fmul_rn(f1.y, inv));
+        w[k] = __byte_perm(__byte_perm(q0, q1, 0x0040), __byte_perm(q2, q3, 0x0040), 0x5410);
+      }
+      // row r's 32 bytes at chunks 2j, 2j + 1, swizzled by the row
+      uint8_t* srow = c.q8 + c.r * 128;
+      *reinterpret_cast<uint4*>(srow + (((2 * c.j) ^ (c.r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+      *reinterpret_cast<uint4*>(srow + (((2 * c.j + 1) ^ (c.r & 7)) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
+    }
+    fence_proxy_async_smem();
+    named_barrier(3, kRtQuantEpi);
+    // rows past M are clipped by the tensor map
+    if (c.issuer && !failed) {
+      asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(c.qmap),
+                   "r"(c.g * 128), "r"(tp * kRtRows), "r"(smem_u32(c.q8))
+                   : "memory");
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+    }
+  }
+}
+
+__device__ __forceinline__ void rt_epilogue_quant(const RtQuantCtx& c0, int warp, int lane, bool& failed) {
+  RtQuantCtx c = c0;
+  const int qd = warp & 3;
+  c.lane_base = (uint32_t)(qd * 32) << 16;
+  c.r = qd * 32 + lane;
+  c.j = (warp - 2) >> 2;
+  c.lane = lane;
+  c.issuer = warp == 2 && lane == 0;
+  for (int i = 0; i < c.ntile + kRtDefer; ++i) rtq_step(c, i, failed);
+  if (c.issuer) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// The signalling warp: counts the CTA in for each tile once the tile's
+// maxima are issued (the mbarrier orders them before the release).
+__device__ __forceinline__ void rt_signal_warp(const RtQuantCtx& c, int lane, bool& failed) {
+  const RtParams& p = *c.p;
+  for (int i = 0; i < c.ntile; ++i) {
+    if (!failed && !mbar_wait(&c.bars.maxed[i & 3], (i >> 2) & 1)) failed = true;
+    // counted in even after a failure, so the other CTAs do not wait for it
+    if (lane == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(p.cnt + c.tb + i) : "memory");
+  }
+}
+
+// The waiting warp: for each tile, waits for the count to complete and
+// publishes 127/a of its rows in shared memory.
+__device__ __forceinline__ void rt_wait_warp(const RtQuantCtx& c, float* inv, int lane, bool& failed) {
+  const RtParams& p = *c.p;
+  for (int i = 0; i < c.ntile; ++i) {
+    const int b = i & 3, t = c.tb + i;
+    if (lane == 0 && !*c.wait_failed) {
+      const long long t0 = clock64();
+      for (;;) {
+        uint32_t n;
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(n) : "l"(p.cnt + t) : "memory");
+        if (n >= (uint32_t)p.G) break;
+        if (clock64() - t0 > 1000000000LL) {
+          report_error(kErrGridWait);
+          *c.wait_failed = 1u;
+          break;
+        }
+        __nanosleep(32);
+      }
+    }
+    __syncwarp();
+    // the epilogue has read this slot's previous values (tile i-4)
+    if (!failed && !mbar_wait(&c.bars.amax_free[b], ((i >> 2) & 1) ^ 1)) failed = true;
+    if (!failed && !*c.wait_failed) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int rr = lane * 4 + k;
+        const int64_t row = (int64_t)t * kRtRows + rr;
+        if (row < p.M) {
+          uint32_t m;
+          asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(m) : "l"(p.amax + row) : "memory");
+          const float a = fmaxf(__uint_as_float(m), 1e-10f);
+          inv[b * 128 + rr] = __fdiv_rn(127.0f, a);
+          if (c.g == 0) p.qscale[row] = __fdiv_rn(a, 127.0f);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&c.bars.amax_ready[b]);
+  }
+}
+
+template <bool kQuant>
+__global__ void __launch_bounds__(kQuant ? kRtQuantThreads : kRtThreads, 1) rot_tc_kernel(const __grid_constant__ CUtensorMap xmap,
+                                                               const __grid_constant__ CUtensorMap ymap,
+                                                               const __grid_constant__ CUtensorMap qmap, RtParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBar);   // [3] tile landed
   uint64_t* freed = full + kRtStages;                               // [3] MMAs done with the tile
-  uint64_t* acc_full = freed + kRtStages;                           // [2]
-  uint64_t* acc_empty = acc_full + 2;                               // [2] 8 epilogue warps
-  uint64_t* mma_done = acc_empty + 2;                               // [1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  constexpr int kBufs = kQuant ? 4 : 2;                             // TMEM accumulators of 128 columns
+  uint64_t* acc_full = freed + kRtStages;                           // [kBufs]
+  uint64_t* acc_empty = acc_full + kBufs;                           // [kBufs] the epilogue warps
+  uint64_t* mma_done = acc_empty + kBufs;                           // [1]
+  uint64_t* qbars = mma_done + 1;                                   // [12] single-pass mode
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(qbars + 12);
+  volatile uint32_t* wait_failed = tmem_slot + 1;   // single-pass mode: a tile count wait gave up
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = threadIdx.x;
@@ -210,15 +439,24 @@ __global__ void __launch_bounds__(kRtThreads, 1) rot_tc_kernel(const __grid_cons
       mbar_init(&full[s], 1);
       mbar_init(&freed[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kBufs; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 8);
+      mbar_init(&acc_empty[b], kQuant ? 16 : 8);   // the epilogue warps
     }
     mbar_init(mma_done, 1);
+    if (kQuant) {
+      for (int b = 0; b < 4; ++b) {
+        mbar_init(&qbars[b], 4);       // maxed: the four combining warps
+        mbar_init(&qbars[4 + b], 1);   // amax_ready: the waiting warp
+        mbar_init(&qbars[8 + b], 16);  // amax_free: the epilogue warps
+      }
+    }
+    *wait_failed = 0u;
     fence_mbar_init();
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;" ::"r"(smem_u32(tmem_slot))
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kBufs * 128)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -228,14 +466,15 @@ __global__ void __launch_bounds__(kRtThreads, 1) rot_tc_kernel(const __grid_cons
       (__ldg(p.rtab) & kRotMatricesFlag) != 0 && (reinterpret_cast<uintptr_t>(p.rtab) & 15) == 0;
   uint32_t* tab = reinterpret_cast<uint32_t*>(smem + kOffTab);
   if (!prebuilt)
-    for (int i = t; i < 8 * 128; i += kRtThreads) tab[i] = __ldg(p.rtab + (size_t)(i >> 7) * p.K + g * 128 + (i & 127));
+    for (int i = t; i < 8 * 128; i += (int)blockDim.x) tab[i] = __ldg(p.rtab + (size_t)(i >> 7) * p.K + g * 128 + (i & 127));
   fence_before();
   __syncthreads();
   fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // the first tiles' loads go out before the build
-  if (t == 0) {
+  // the first tiles' loads go out before the build, from a thread that
+  // takes no part in it
+  if (t == 256) {
     for (int i = 0; i < kRtStages && i < ntile; ++i) {
       mbar_arrive_expect_tx(&full[i], kRtTileBytes);
       const int y0 = (tb + i) * kRtRows;
@@ -292,8 +531,8 @@ __global__ void __launch_bounds__(kRtThreads, 1) rot_tc_kernel(const __grid_cons
       const uint32_t x_base = smem_u32(smem + kOffX);
       const uint32_t rh = smem_u32(smem + kOffRhi), rl = smem_u32(smem + kOffRlo);
       for (int i = 0; i < ntile; ++i) {
-        const int s = i % kRtStages, b = i & 1;
-        if (!mbar_wait(&full[s], (i / kRtStages) & 1) || !mbar_wait(&acc_empty[b], ((i >> 1) & 1) ^ 1)) break;
+        const int s = i % kRtStages, b = i % kBufs;
+        if (!mbar_wait(&full[s], (i / kRtStages) & 1) || !mbar_wait(&acc_empty[b], ((i / kBufs) & 1) ^ 1)) break;
         fence_after();
         const uint32_t d = tmem + (uint32_t)(b * 128);
 #pragma unroll
@@ -312,6 +551,31 @@ __global__ void __launch_bounds__(kRtThreads, 1) rot_tc_kernel(const __grid_cons
       umma_commit(mma_done);
       mbar_wait(mma_done, 0);
     }
+  } else if (kQuant) {
+    // (the table area is free once R' is built: row maxima and 127/a)
+    RtQuantCtx c;
+    c.p = &p;
+    c.qmap = &qmap;
+    c.q8 = smem + kOffQ8;
+    c.pm = reinterpret_cast<uint32_t*>(smem + kOffTab);
+    float* inv = reinterpret_cast<float*>(smem + kOffTab + 2048);
+    c.inv = inv;
+    c.bars.maxed = qbars;
+    c.bars.amax_ready = qbars + 4;
+    c.bars.amax_free = qbars + 8;
+    c.acc_full = acc_full;
+    c.acc_empty = acc_empty;
+    c.wait_failed = wait_failed;
+    c.tmem = tmem;
+    c.g = g;
+    c.tb = tb;
+    c.ntile = ntile;
+    if (warp == kRtSignalWarp)
+      rt_signal_warp(c, lane, failed);
+    else if (warp == kRtWaitWarp)
+      rt_wait_warp(c, inv, lane, failed);
+    else
+      rt_epilogue_quant(c, warp, lane, failed);
   } else if (warp >= 4) {
     // epilogue: thread = row within the tile (TMEM lane), warps 4-7 take
     // channels 0-63, warps 8-11 channels 64-127.  The fp16 tile is staged in
@@ -381,7 +645,8 @@ __global__ void __launch_bounds__(kRtThreads, 1) rot_tc_kernel(const __grid_cons
   fence_before();
   __syncthreads();
   fence_after();
-  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;" ::"r"(tmem) : "memory");
+  if (warp == 1)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kBufs * 128) : "memory");
 }
 
 // ---------------------------------------------------------------------------
@@ -400,20 +665,45 @@ static PFN_cuTensorMapEncodeTiled_v12000 rt_encode() {
 }
 
 static int g_rt_sms = 0;
+static int g_rt_coresident = -1;   // CTAs of the single-pass kernel that fit the GPU at once
 
-// The rotation pass for bf16 x [M, K] (K % 128 == 0, 16-byte aligned rows):
-// y fp16 [M, K] and row maxima (amax zeroed by the caller).
-cudaError_t launch_rot_tc(const void* x, int64_t M, int K, const uint16_t* scales, const uint32_t* rtab, __half* y,
-                          uint32_t* amax, cudaStream_t st) {
-  if (M <= 0 || M > 0x7FFFFFFF) return cudaErrorInvalidValue;
-  auto encode = rt_encode();
-  if (!encode) return cudaErrorNotSupported;
+static void rt_init() {
   if (g_rt_sms == 0) {
     int dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&g_rt_sms, cudaDevAttrMultiProcessorCount, dev);
     if (g_rt_sms <= 0) g_rt_sms = 148;
   }
+  if (g_rt_coresident < 0) {
+    int per_sm = 0;
+    if (ensure_smem_limit((const void*)rot_tc_kernel<true>, kRtSmem) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rot_tc_kernel<true>, kRtQuantThreads, kRtSmem) !=
+            cudaSuccess)
+      per_sm = 0;
+    cudaGetLastError();
+    g_rt_coresident = per_sm * g_rt_sms;
+  }
+}
+
+// The single-pass mode needs every CTA resident at once (one group per CTA,
+// G <= resident CTAs) and 16-byte aligned int8 rows.
+bool rot_tc_single_pass_ok(int K, const void* q) {
+  rt_init();
+  return K % kGroup == 0 && K / kGroup <= g_rt_coresident && (reinterpret_cast<uintptr_t>(q) & 15) == 0;
+}
+
+// The rotation pass for bf16 x [M, K] (K % 128 == 0, 16-byte aligned rows).
+// q == nullptr: y fp16 [M, K] and row maxima (amax zeroed by the caller).
+// Otherwise the single-pass mode: int8 codes q and per-token scales qscale,
+// amax and cnt ([tiles] row-tile counters) zeroed by the caller; launched
+// cooperatively, so it either runs with every CTA resident or fails to
+// launch (the caller then takes the two-pass mode).
+cudaError_t launch_rot_tc(const void* x, int64_t M, int K, const uint16_t* scales, const uint32_t* rtab, __half* y,
+                          uint32_t* amax, int8_t* q, float* qscale, uint32_t* cnt, cudaStream_t st) {
+  if (M <= 0 || M > 0x7FFFFFFF) return cudaErrorInvalidValue;
+  auto encode = rt_encode();
+  if (!encode) return cudaErrorNotSupported;
+  rt_init();
   CUtensorMap xmap;
   const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
   const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
@@ -427,12 +717,23 @@ cudaError_t launch_rot_tc(const void* x, int64_t M, int K, const uint16_t* scale
   r = encode(&ymap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, y, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  // int8 codes (single-pass mode): 128-row x 128-byte boxes; else a copy of
+  // ymap (unused)
+  CUtensorMap qmap = ymap;
+  if (q) {
+    const cuuint64_t qstr[1] = {(cuuint64_t)K};
+    const cuuint32_t qbox[2] = {128, (cuuint32_t)kRtRows};
+    r = encode(&qmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, q, dims, qstr, qbox, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+  }
   RtParams p;
   p.M = M;
   p.K = K;
   p.G = K / kGroup;
   p.tiles = (int)((M + kRtRows - 1) / kRtRows);
-  int splits = g_rt_sms / p.G;
+  const int slots = q ? g_rt_coresident : g_rt_sms;
+  int splits = slots / p.G;
   if (splits < 1) splits = 1;
   if (splits > p.tiles) splits = p.tiles;
   p.splits = splits;
@@ -440,9 +741,28 @@ cudaError_t launch_rot_tc(const void* x, int64_t M, int K, const uint16_t* scale
   p.rtab = rtab;
   p.y = y;
   p.amax = amax;
-  cudaError_t e = ensure_smem_limit((const void*)rot_tc_kernel, kRtSmem);
+  p.q = q;
+  p.qscale = qscale;
+  p.cnt = cnt;
+  if (q) {
+    if (p.G * splits > g_rt_coresident) return cudaErrorCooperativeLaunchTooLarge;
+    cudaError_t e = ensure_smem_limit((const void*)rot_tc_kernel<true>, kRtSmem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(p.G * splits));
+    cfg.blockDim = dim3(kRtQuantThreads);
+    cfg.dynamicSmemBytes = kRtSmem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, rot_tc_kernel<true>, xmap, ymap, qmap, p);
+  }
+  cudaError_t e = ensure_smem_limit((const void*)rot_tc_kernel<false>, kRtSmem);
   if (e != cudaSuccess) return e;
-  rot_tc_kernel<<<(unsigned)(p.G * splits), kRtThreads, kRtSmem, st>>>(xmap, ymap, p);
+  rot_tc_kernel<false><<<(unsigned)(p.G * splits), kRtThreads, kRtSmem, st>>>(xmap, ymap, qmap, p);
   return cudaGetLastError();
 }
 

@@ -12,6 +12,7 @@ namespace paro {
 // by paro_device_error_word().
 constexpr uint32_t kErrMbarTimeout = 1u;
 constexpr uint32_t kErrTmemAlloc = 2u;
+constexpr uint32_t kErrGridWait = 4u;     // a wait for other CTAs of the same launch gave up
 
 // One error word per translation unit (no relocatable device code needed);
 // each .cu that uses these helpers exposes it through

@@ -190,7 +190,8 @@ def silu_mul(x):
 
 def device_error_word(clear=True):
     """Error bits the kernels raised instead of hanging (1 = a bounded
-    pipeline wait ran out, 2 = tensor-memory allocation failed); 0 when all
+    pipeline wait ran out, 2 = tensor-memory allocation failed, 4 = a wait
+    for the other CTAs of the same launch ran out); 0 when all
     is well, -1 if the word could not be read.  Synchronises the device.
 
     A non-zero word means the outputs of the calls since the last clean read

@@ -264,7 +264,8 @@ int paro_add_rmsnorm(const void* x, void* residual, const void* weight, int64_t 
 int paro_silu_mul(const void* x, int64_t M, int I, void* out, paro_stream_t stream);
 
 /* Error bits kernels raise instead of hanging (1 = a pipeline wait timed
- * out, 2 = tensor-memory allocation failed); synchronises with the device to
+ * out, 2 = tensor-memory allocation failed, 4 = a wait for the other CTAs of
+ * the same launch timed out); synchronises with the device to
  * read them.  clear != 0 resets the word.  Returns -1 if it cannot be read.
  *
  * Recovery: a kernel whose wait ran out stops where it was, so the outputs

@@ -98,3 +98,79 @@ def test_prepare_rotation_matrices_rejects(ops):
         ops._ops.prepare_rotation_matrices(torch.zeros(4, 256, dtype=torch.int32, device="cuda"))
     with pytest.raises(RuntimeError):
         ops._ops.prepare_rotation_matrices(torch.zeros(8, 200, dtype=torch.int32, device="cuda"))
+
+
+@pytest.mark.parametrize("M,K", [(512, 1024), (1000, 3584), (2047, 3584), (4100, 18944), (8192, 3584)])
+def test_single_pass_quantiser_equals_two_pass(ops, M, K):
+    """bf16 prefill rows: where every group's CTA fits the GPU at once the
+    quantiser runs inside the tensor-core rotation kernel (row maxima
+    exchanged between the groups' CTAs per 128-row tile); with int8 rows
+    that are not 16-byte aligned the fp16 rows go through the workspace and
+    a second kernel.  Same fp16 values, same quantiser arithmetic: the
+    codes and scales must be equal bit for bit."""
+    from alpamayo_b200 import _native
+    L = _native.capi()
+    pairs, theta, cs, plain, full = tables(ops, K, seed=3 * M + K)
+    x = torch.from_numpy(make_activations(M, K, seed=M)).to(torch.bfloat16).cuda()
+    x[3] = 0   # an all-zero row: absmax clamps to 1e-10
+    csd = dev(cs.reshape(-1))
+    wsb = L.paro_rotq_int8_workspace_size(M, K, 1)
+    assert wsb > 0
+    ws = torch.empty(wsb + 256, dtype=torch.uint8, device="cuda")
+    wsp = (ws.data_ptr() + 255) // 256 * 256
+    stream = torch.cuda.current_stream().cuda_stream
+    outs = []
+    for off in (0, 8):
+        qb = torch.empty(M * K + 16, dtype=torch.int8, device="cuda")
+        s = torch.empty(M, dtype=torch.float32, device="cuda")
+        st = L.paro_rotq_int8_ws(x.data_ptr(), 2, M, K, csd.data_ptr(), full.data_ptr(), 8, 128, 1,
+                                 qb.data_ptr() + off, s.data_ptr(), wsp, wsb, stream)
+        assert st == 0
+        torch.cuda.synchronize()
+        outs.append((qb[off:off + M * K].view(M, K).clone(), s.clone()))
+    assert ops.device_error_word() == 0
+    assert torch.equal(outs[0][0], outs[1][0]) and torch.equal(outs[0][1], outs[1][1])
+    assert outs[0][0][3].abs().max().item() == 0
+    # the torch operator takes the single-pass mode
+    q, s = ops.rotq_int8(x, full, csd, 128, True)
+    assert torch.equal(q, outs[0][0]) and torch.equal(s.reshape(-1), outs[0][1])
+
+
+def test_single_pass_quantiser_ties_round_half_away(ops):
+    """Zero angles (R = I) and unit channel scales: the rotated rows are the
+    inputs, so rows built from half-integers put exact ties under the
+    quantiser (row maxima 127 and 63.5: 127/a = 1 and 2).  Codes must be the
+    oracle's round-half-away codes bit for bit, in both the single-pass and
+    the two-pass mode."""
+    from alpamayo_b200 import _native
+    L = _native.capi()
+    M, K = 512, 1024
+    pairs, theta, _ = make_rotation(K, seed=5)
+    theta = np.zeros_like(theta)
+    table = ops.prepare_rotation(dev(pairs), dev(theta), 128, matrices=True)
+    x = make_activations(M, K, seed=6)
+    ties = np.array([127, 2.5, -3.5, 0.5, -0.5, 1.5, 126.5, -126.5, 4.5, -0.0, 63.5, -62.5], np.float32)
+    x[0, :] = 0
+    x[0, :len(ties)] = ties
+    x[1, :] = 0
+    x[1, :len(ties)] = ties / 2          # a = 63.5: inv = 2, ties again
+    x[2, 700:712] = ties                 # in another group
+    xt = torch.from_numpy(x).to(torch.bfloat16)
+    assert torch.equal(xt[:2].float(), torch.from_numpy(x[:2]))   # exact in bf16
+    assert torch.equal(xt[2, 700:712].float(), torch.from_numpy(ties))
+    q_ref, s_ref = O.per_token_quant_int8(O.round_to_fp16(xt.float().numpy()))
+    assert q_ref[0, :8].tolist() == [127, 3, -4, 1, -1, 2, 127, -127]
+    wsb = L.paro_rotq_int8_workspace_size(M, K, 1)
+    ws = torch.empty(wsb + 256, dtype=torch.uint8, device="cuda")
+    wsp = (ws.data_ptr() + 255) // 256 * 256
+    xd = xt.cuda()
+    for off in (0, 8):
+        qb = torch.empty(M * K + 16, dtype=torch.int8, device="cuda")
+        s = torch.empty(M, dtype=torch.float32, device="cuda")
+        st = L.paro_rotq_int8_ws(xd.data_ptr(), 2, M, K, None, table.data_ptr(), 8, 128, 1, qb.data_ptr() + off,
+                                 s.data_ptr(), wsp, wsb, torch.cuda.current_stream().cuda_stream)
+        assert st == 0
+        torch.cuda.synchronize()
+        q = qb[off:off + M * K].view(M, K).cpu().numpy()
+        assert np.array_equal(q, q_ref), f"offset {off}: {np.argwhere(q != q_ref)[:5]}"
+        assert np.array_equal(s.cpu().numpy(), s_ref.reshape(-1))
