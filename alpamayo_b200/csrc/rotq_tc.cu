@@ -23,19 +23,25 @@
 //  * Producer thread: tensor TMA of the 128-row x 128-channel bf16 tile
 //    (two 64-channel boxes, 128-byte swizzle), 3 stages.
 //  * MMA thread: 8 MMAs (M = 128 rows, N = 128 channels, K = 16) with R'_hi,
-//    then 8 with R'_lo, into one of two 128-column TMEM buffers.  x is exact
-//    in bf16, so Y = X hi^T + X lo^T carries R' to about 2^-16 relative:
-//    far below the fp16 spacing the result is rounded to.
-//  * Epilogue (8 warps, TMEM lanes = rows, two warps per lane quarter): each
-//    thread reads 64 of its row's 128 outputs, rounds them to fp16 — the
-//    value the reference's rotate kernel stores (rotation.cuh:333-334) —
-//    stores them, and folds their |max| into the row's maximum (atomicMax
-//    on the bit pattern).  quant_rows_kernel
-//    then quantises per token (rotq_rows.cu).
+//    then 8 with R'_lo, into a 128-column TMEM buffer (two buffers; four in
+//    the single-pass mode).  x is exact in bf16, so Y = X hi^T + X lo^T
+//    carries R' to about 2^-16 relative: far below the fp16 spacing the
+//    result is rounded to.
+//  * Two-pass mode (rot_tc_kernel<false>; 8 epilogue warps, TMEM lanes =
+//    rows, two warps per lane quarter): each thread reads 64 of its row's
+//    128 outputs, rounds them to fp16 — the value the reference's rotate
+//    kernel stores (rotation.cuh:333-334) — stores them, and folds their
+//    |max| into the row's maximum (atomicMax on the bit pattern).
+//    quant_rows_kernel then quantises per token (rotq_rows.cu).
+//  * Single-pass mode (rot_tc_kernel<true>, where every group's CTA fits the
+//    GPU at once): the kernel quantises its own tiles once every group's
+//    maximum of a row tile is in (described above rt_epilogue_quant), so
+//    the fp16 rows never leave the SM; same codes bit for bit.
 //
 // A CTA owns one group and a contiguous range of its row tiles (groups are
-// spread over the grid first).  Waits are bounded (kErrMbarTimeout), tensor
-// memory is freed on every exit.  No load uses cluster multicast.
+// spread over the grid first).  Waits are bounded (kErrMbarTimeout,
+// kErrGridWait), tensor memory is freed on every exit.  No load uses
+// cluster multicast.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
