@@ -55,6 +55,10 @@ namespace {
 
 constexpr int kRtThreads = 384;   // producer, MMA, 2 idle, 8 epilogue warps
 constexpr int kRtStages = 3;
+// tiles whose loads go out before R' is in shared memory: the first MMA
+// needs R' and one tile, and every CTA starts at once, so the others would
+// only compete with the matrix loads for DRAM
+constexpr int kRtEarly = 1;
 constexpr int kRtRows = 128;                     // rows per tile (MMA M)
 constexpr int kRtTileBytes = kRtRows * 128 * 2;  // 32 KB bf16 tile
 constexpr int kRtRBytes = 128 * 128 * 2;         // one bf16 128 x 128 matrix
@@ -478,10 +482,10 @@ __global__ void __launch_bounds__(kQuant ? kRtQuantThreads : kRtThreads, 1) rot_
   fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  // the first tiles' loads go out before the build, from a thread that
+  // the first tile's load goes out before the build, from a thread that
   // takes no part in it
   if (t == 256) {
-    for (int i = 0; i < kRtStages && i < ntile; ++i) {
+    for (int i = 0; i < kRtEarly && i < ntile; ++i) {
       mbar_arrive_expect_tx(&full[i], kRtTileBytes);
       const int y0 = (tb + i) * kRtRows;
       tma_load_2d(smem + kOffX + i * kRtTileBytes, &xmap, g * 128, y0, &full[i]);
@@ -522,10 +526,10 @@ __global__ void __launch_bounds__(kQuant ? kRtQuantThreads : kRtThreads, 1) rot_
   bool failed = false;
   if (warp == 0) {
     if (lane == 0) {
-      // producer: tiles kRtStages.. of this CTA's range
-      for (int i = kRtStages; i < ntile; ++i) {
+      // producer: tiles kRtEarly.. of this CTA's range
+      for (int i = kRtEarly; i < ntile; ++i) {
         const int s = i % kRtStages;
-        if (!mbar_wait(&freed[s], ((i / kRtStages) - 1) & 1)) break;
+        if (i >= kRtStages && !mbar_wait(&freed[s], ((i / kRtStages) - 1) & 1)) break;
         mbar_arrive_expect_tx(&full[s], kRtTileBytes);
         const int y0 = (tb + i) * kRtRows;
         tma_load_2d(smem + kOffX + s * kRtTileBytes, &xmap, g * 128, y0, &full[s]);
