@@ -437,6 +437,12 @@ __global__ void __launch_bounds__(kQuant ? kRtQuantThreads : kRtThreads, 1) rot_
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = threadIdx.x;
+  // the tensor maps' descriptors, fetched while the set-up runs (the first
+  // copies would otherwise wait for them)
+  if (t == 256) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&xmap) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(kQuant ? &qmap : &ymap) : "memory");
+  }
   // this CTA's group and row tiles
   const int part = blockIdx.x / p.G;
   const int g = blockIdx.x - part * p.G;
