@@ -174,3 +174,24 @@ def test_single_pass_quantiser_ties_round_half_away(ops):
         q = qb[off:off + M * K].view(M, K).cpu().numpy()
         assert np.array_equal(q, q_ref), f"offset {off}: {np.argwhere(q != q_ref)[:5]}"
         assert np.array_equal(s.cpu().numpy(), s_ref.reshape(-1))
+
+
+def test_wide_layer_takes_the_two_pass_path(ops):
+    """K = 20480: 160 groups, more than the GPU has SMs, so the single-pass
+    kernel cannot have every group's CTA resident and the fp16 rows go
+    through the workspace and a second kernel.  Codes bit-identical with and
+    without the matrices, within the code tolerance of the oracle."""
+    M, K = 600, 20480
+    pairs, theta, cs, plain, full = tables(ops, K, seed=9)
+    x = torch.from_numpy(make_activations(M, K, seed=10)).to(torch.bfloat16).cuda()
+    csd = dev(cs.reshape(-1))
+    q0, s0 = ops.rotq_int8(x, plain, csd, 128, True)
+    q1, s1 = ops.rotq_int8(x, full, csd, 128, True)
+    assert ops.device_error_word() == 0
+    assert torch.equal(q0, q1) and torch.equal(s0, s1)
+    rows = np.sort(np.random.default_rng(K).choice(M, size=16, replace=False))
+    q_ref, s_ref, _ = O.rot_quant_reference(x.float().cpu().numpy()[rows], pairs, theta.astype(np.float32),
+                                            cs.astype(np.float32))
+    d = np.abs(q1.cpu().numpy()[rows].astype(np.int32) - q_ref.astype(np.int32))
+    assert d.max() <= 1 and (d > 0).mean() <= 1e-3
+    assert np.allclose(s1.cpu().numpy().reshape(-1)[rows], s_ref, rtol=2 ** -10, atol=0)
